@@ -1,0 +1,190 @@
+/* libj1: B200-native (sm_100a) encoder forward for Julia-1 / ModernBERT decision models.
+ *
+ * C ABI replacing the reference's CUDA backend seam (julia1-rs):
+ *   enum Backend { Cpu(..), Cuda(Box<CudaModel>) }      src/engine.rs:67-71
+ *   CudaModel::new(cfg, &HostWeights, ordinal)           src/cuda/mod.rs:174
+ *   CudaModel::forward(&Batch) -> Vec<Vec<f32>>          src/cuda/mod.rs:400
+ *   CudaModel::name()                                    src/cuda/mod.rs:278
+ *   Engine::logits_encoded / batches / forward           src/engine.rs:191-235
+ *
+ * Plain pointers and sizes only. The caller owns every host array; the library
+ * owns device memory and pinned staging. Every call returns a j1_status and
+ * never aborts; j1_last_error() gives the calling thread's last message.
+ */
+#ifndef J1_H
+#define J1_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define J1_API __attribute__((visibility("default")))
+#else
+#define J1_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* anyhow::Result errors of the reference, as codes. */
+typedef enum j1_status {
+  J1_OK = 0,
+  J1_ERR_INVALID_ARG = 1,       /* bad batch / argument (e.g. marker outside its sequence) */
+  J1_ERR_UNSUPPORTED = 2,       /* config the kernels do not support (cf. src/cuda/mod.rs:175-176) */
+  J1_ERR_CUDA = 3,              /* CUDA runtime / driver failure; no usable device */
+  J1_ERR_OOM = 4,               /* device or pinned allocation failed */
+  J1_ERR_NONFINITE = 5,         /* "Inference returned nonfinite logits" (src/engine.rs:219-221) */
+  J1_ERR_DEVICE_TIMEOUT = 6,    /* a bounded device-side wait gave up; context still usable */
+  J1_ERR_IO = 7                 /* checkpoint / config could not be read or parsed (src/config.rs, src/weights.rs) */
+} j1_status;
+
+typedef struct j1_model j1_model;   /* one device replica: CudaModel */
+typedef struct j1_engine j1_engine; /* Engine over one or more replicas */
+
+/* Thread-local message of the last failing call on this thread; returns the full length. */
+J1_API size_t j1_last_error(char* buf, size_t cap);
+J1_API const char* j1_status_name(j1_status s);
+/* Library version string, e.g. "libj1 0.1.0 sm_100a". */
+J1_API const char* j1_version(void);
+
+/* ------------------------------------------------------------ configuration */
+/* ModelConfig (src/config.rs:6-24) as parsed from julia_config.json + encoder/config.json. */
+typedef struct j1_config {
+  int32_t hidden, heads, head_dim, intermediate, layers;
+  int32_t half_window;           /* local_attention / 2 */
+  int32_t vocab, max_positions;
+  int32_t head_layers, head_heads, head_ff;
+  float norm_eps;
+  int32_t n_global;              /* layers with i % global_attn_every_n_layers == 0 */
+} j1_config;
+
+/* ModelConfig::load (src/config.rs:36-40) without touching a GPU. */
+J1_API j1_status j1_config_load(const char* ckpt_dir, j1_config* out);
+
+/* ------------------------------------------------------------ model (one GPU) */
+/* CudaModel::new: parses both configs, memory-maps model.safetensors (F32), uploads
+ * GEMM weights as BF16 (norms, biases, embedding FP32) to device `ordinal`. */
+J1_API j1_status j1_model_create(const char* ckpt_dir, int ordinal, j1_model** out);
+J1_API void j1_model_destroy(j1_model* model);
+/* "cuda:N (<device name>)"; returns the full length. */
+J1_API size_t j1_model_name(const j1_model* model, char* buf, size_t cap);
+J1_API j1_status j1_model_config(const j1_model* model, j1_config* out);
+
+/* CudaModel::forward over one packed batch (model::Batch, src/model.rs:225-269):
+ *   ids[t]            token ids of all sequences, back to back
+ *   starts/lens[nseq] packed start row and length of each sequence (starts[s] == sum(lens[<s]))
+ *   qtypes[nseq]      question type (0..2) per sequence
+ *   marker_rows[m]    packed row of each option marker, grouped by sequence
+ *   marker_starts[nseq+1] first marker index of each sequence, marker_starts[nseq] == m
+ * scores_out[m] receives one logit per marker (flat; split with marker_starts).
+ * Blocking; thread-safe (one forward at a time per model). */
+J1_API j1_status j1_model_forward(j1_model* model, const uint32_t* ids, size_t t, const uint32_t* starts,
+                           const uint32_t* lens, const uint8_t* qtypes, size_t nseq, const uint32_t* marker_rows,
+                           const uint32_t* marker_starts, size_t m, float* scores_out);
+
+/* The same forward split in three so a caller can keep a batch resident on the device:
+ * stage (validate + pack + async H2D of the batch metadata), launch (enqueue all
+ * kernels on the model's stream; may be repeated on a staged batch), finish
+ * (D2H of the scores, synchronize, device-error and nonfinite checks). */
+J1_API j1_status j1_model_stage(j1_model* model, const uint32_t* ids, size_t t, const uint32_t* starts,
+                         const uint32_t* lens, const uint8_t* qtypes, size_t nseq, const uint32_t* marker_rows,
+                         const uint32_t* marker_starts, size_t m);
+J1_API j1_status j1_model_launch(j1_model* model);
+J1_API j1_status j1_model_finish(j1_model* model, float* scores_out, size_t m);
+/* cudaStream_t the model's kernels run on (for event timing by the caller). */
+J1_API void* j1_model_stream(j1_model* model);
+/* Number of kernel launches one j1_model_launch issues for the staged batch. */
+J1_API int64_t j1_model_launch_count(const j1_model* model);
+
+/* ------------------------------------------------------------ engine */
+/* EngineOptions (src/engine.rs:34-65), device-side subset. */
+typedef struct j1_engine_options {
+  const char* device;        /* "cuda", "cuda:N" (Device::from_str, src/engine.rs:20-31); "cpu" is rejected */
+  int32_t batch_size;        /* rows per forward, default 16 */
+  int64_t max_batch_tokens;  /* packed tokens per forward, default 65536 */
+  int32_t max_length;        /* 0 = checkpoint max_position_embeddings */
+} j1_engine_options;
+
+J1_API void j1_engine_options_default(j1_engine_options* out);
+/* Engine::load on one device. */
+J1_API j1_status j1_engine_create(const char* ckpt_dir, const j1_engine_options* opts, j1_engine** out);
+/* Engine over n device replicas (weights replicated); micro-batches are sharded
+ * across them, one host worker thread per device, logits gathered in row order. */
+J1_API j1_status j1_engine_create_pool(const char* ckpt_dir, const j1_engine_options* opts, const int* ordinals, int n,
+                                j1_engine** out);
+J1_API void j1_engine_destroy(j1_engine* engine);
+J1_API size_t j1_engine_device_name(const j1_engine* engine, char* buf, size_t cap);
+
+/* Engine::logits_encoded (src/engine.rs:225-235) over already-encoded rows
+ * (encode::Encoded: ids, marker positions within the row, qtype):
+ *   ids          concatenated token ids of all rows
+ *   row_lens[n]  tokens per row
+ *   markers      concatenated marker positions (relative to each row's first token)
+ *   row_markers[n] markers per row
+ *   qtypes[n]
+ * logits_out receives sum(row_markers) floats, row after row, in input order.
+ * Rows are length-sorted and cut into micro-batches of at most batch_size rows
+ * and max_batch_tokens tokens (src/engine.rs:191-210). */
+J1_API j1_status j1_engine_logits_encoded(j1_engine* engine, size_t n_rows, const uint32_t* ids, const uint32_t* row_lens,
+                                   const uint32_t* markers, const uint32_t* row_markers, const uint8_t* qtypes,
+                                   float* logits_out);
+
+/* ------------------------------------------------------------ kernel-level ops
+ * On caller device memory (e.g. torch tensors); `stream` is a cudaStream_t or NULL.
+ * With sync != 0 the call waits for completion and reports device-side timeouts. */
+
+/* Fused-epilogue GEMM: out = A[M,K] . W[N,K]^T, bf16 operands, fp32 accumulate. */
+typedef enum j1_epilogue {
+  J1_EPI_BF16 = 0,      /* out = bf16(acc (+bias)) (relu optional)                      */
+  J1_EPI_QKV_ROPE = 1,  /* out = bf16(rotate_half RoPE(acc)) on columns < rope_cols     */
+  J1_EPI_GEGLU = 2,     /* W rows interleaved per 128 (see j1_op_geglu_interleave);
+                           out[M, N/2] = bf16(gelu(a) * b)                             */
+  J1_EPI_RESID_LN = 3,  /* x[M,N] += acc (+bias) in fp32; xn = bf16(LayerNorm(x))       */
+  J1_EPI_RESID = 4,     /* x[M,N] += acc (+bias)                                       */
+  J1_EPI_SCORER = 5     /* scores[M] = sum_j gelu(acc + bias[j]) * w2[j] + b2           */
+} j1_epilogue;
+
+typedef struct j1_gemm_args {
+  int32_t epilogue;       /* j1_epilogue */
+  int32_t M, N, K;
+  const void* A;          /* bf16 [M, K], row stride K */
+  const void* W;          /* bf16 [N, K], row stride K */
+  void* out;              /* bf16 output (BF16 / QKV_ROPE / GEGLU) */
+  int32_t ldo;
+  const float* bias;      /* [N] or NULL */
+  int32_t relu;
+  float* x;               /* fp32 residual [M, N] (RESID*) */
+  int32_t ldx;
+  const float* ln_w;      /* [N] */
+  const float* ln_b;      /* [N] or NULL */
+  float ln_eps;
+  void* xn;               /* bf16 LayerNorm output */
+  int32_t ldxn;
+  const int32_t* pos;     /* [M] sequence position per row (QKV_ROPE) */
+  const float* rope_cos;  /* [positions, 32] */
+  const float* rope_sin;
+  int32_t rope_cols;      /* RoPE is applied on columns < rope_cols */
+  const float* w2;        /* [N] (SCORER) */
+  float b2;
+  float* scores;          /* [M] (SCORER) */
+  int32_t grid_limit;     /* max CTAs; 0 = number of SMs */
+} j1_gemm_args;
+
+J1_API j1_status j1_op_gemm(const j1_gemm_args* args, void* stream, int sync);
+
+/* Varlen attention over a packed qkv buffer [t, 3*hidden] (q | k | v, heads x 64 each):
+ * ctx[t, hidden]. seq_starts/seq_lens are host arrays; window < 0 = full attention,
+ * else |i - j| <= window (the reference's half_window). q/k are used as given
+ * (RoPE is applied by J1_EPI_QKV_ROPE). */
+J1_API j1_status j1_op_attention(const void* qkv, int64_t t, int32_t hidden, const uint32_t* seq_starts,
+                          const uint32_t* seq_lens, size_t nseq, int32_t window, void* ctx, void* stream, int sync);
+
+/* Host helper: dst rows of a [2*inter, K] Wi laid out for J1_EPI_GEGLU (FP32 -> BF16 on device). */
+J1_API j1_status j1_op_geglu_interleave(const float* src_dev, void* dst_dev, int32_t inter, int32_t k, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* J1_H */

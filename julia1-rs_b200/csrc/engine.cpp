@@ -1,0 +1,221 @@
+// Engine: Engine::logits_encoded semantics (src/engine.rs:190-235) over one or
+// more device replicas. Rows are length-sorted and cut into micro-batches
+// (batch_size rows, max_batch_tokens tokens); with several replicas the
+// micro-batches are dealt out by greedy token balance, one host worker thread
+// per device, and the logits are written back in the caller's row order.
+#include <algorithm>
+#include <atomic>
+#include <cstring>
+#include <memory>
+#include <numeric>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "model.h"
+
+using namespace j1rt;
+
+struct j1_engine {
+  std::vector<j1_model*> models;
+  j1_engine_options opts;
+  int max_length = 0;
+  std::string name;
+  std::mutex mu;  // Engine::lock (src/engine.rs:78,226)
+};
+
+namespace {
+
+j1_status parse_device(const char* s, int* ordinal) {
+  const std::string d = s ? s : "cuda";
+  if (d == "cpu")
+    return set_error(J1_ERR_UNSUPPORTED, "libj1 is the CUDA (sm_100a) backend; it has no CPU fallback");
+  if (d == "cuda") {
+    *ordinal = 0;
+    return J1_OK;
+  }
+  if (d.rfind("cuda:", 0) == 0 && d.size() > 5) {
+    const std::string n = d.substr(5);
+    if (n.find_first_not_of("0123456789") == std::string::npos && n.size() < 6) {
+      *ordinal = std::stoi(n);
+      return J1_OK;
+    }
+  }
+  return set_error(J1_ERR_INVALID_ARG, "device must be cpu, cuda or cuda:N");
+}
+
+j1_status check_options(j1_engine* e, const ModelConfig& c) {
+  const int ml = e->opts.max_length > 0 ? e->opts.max_length : c.max_positions;
+  if (ml < 1 || ml > c.max_positions)
+    return set_error(J1_ERR_INVALID_ARG,
+                     "max_length must be an integer between 1 and " + std::to_string(c.max_positions));
+  if (e->opts.batch_size < 1 || e->opts.max_batch_tokens < ml)
+    return set_error(J1_ERR_INVALID_ARG, "Invalid batch size / token budget");
+  e->max_length = ml;
+  return J1_OK;
+}
+
+struct Micro {
+  std::vector<size_t> rows;
+  size_t tokens = 0;
+};
+
+}  // namespace
+
+extern "C" {
+
+void j1_engine_options_default(j1_engine_options* o) {
+  if (!o) return;
+  o->device = "cuda";
+  o->batch_size = 16;
+  o->max_batch_tokens = 65536;
+  o->max_length = 0;
+}
+
+j1_status j1_engine_create_pool(const char* ckpt_dir, const j1_engine_options* opts, const int* ordinals, int n,
+                                j1_engine** out) {
+  if (!ckpt_dir || !out || n < 1 || !ordinals) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+  *out = nullptr;
+  std::unique_ptr<j1_engine> e(new j1_engine());
+  if (opts) e->opts = *opts;
+  else j1_engine_options_default(&e->opts);
+  e->opts.device = nullptr;  // not retained
+  for (int i = 0; i < n; ++i) {
+    j1_model* m = nullptr;
+    j1_status s = j1_model_create(ckpt_dir, ordinals[i], &m);
+    if (s) {
+      for (auto* x : e->models) j1_model_destroy(x);
+      return s;
+    }
+    e->models.push_back(m);
+  }
+  j1_status s = check_options(e.get(), e->models[0]->cfg);
+  if (s) {
+    for (auto* x : e->models) j1_model_destroy(x);
+    return s;
+  }
+  for (size_t i = 0; i < e->models.size(); ++i) e->name += (i ? ", " : "") + e->models[i]->name;
+  *out = e.release();
+  return J1_OK;
+}
+
+j1_status j1_engine_create(const char* ckpt_dir, const j1_engine_options* opts, j1_engine** out) {
+  int ordinal = 0;
+  j1_status s = parse_device(opts ? opts->device : "cuda", &ordinal);
+  if (s) return s;
+  return j1_engine_create_pool(ckpt_dir, opts, &ordinal, 1, out);
+}
+
+void j1_engine_destroy(j1_engine* e) {
+  if (!e) return;
+  for (auto* m : e->models) j1_model_destroy(m);
+  delete e;
+}
+
+size_t j1_engine_device_name(const j1_engine* e, char* buf, size_t cap) {
+  const std::string s = e ? e->name : std::string();
+  if (buf && cap) {
+    const size_t k = s.size() < cap - 1 ? s.size() : cap - 1;
+    std::memcpy(buf, s.data(), k);
+    buf[k] = 0;
+  }
+  return s.size();
+}
+
+j1_status j1_engine_logits_encoded(j1_engine* e, size_t n_rows, const uint32_t* ids, const uint32_t* row_lens,
+                                   const uint32_t* markers, const uint32_t* row_markers, const uint8_t* qtypes,
+                                   float* logits_out) {
+  if (!e) return set_error(J1_ERR_INVALID_ARG, "NULL engine");
+  if (n_rows == 0) return J1_OK;
+  if (!ids || !row_lens || !row_markers || !qtypes) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+  std::vector<size_t> tok_off(n_rows + 1, 0), mk_off(n_rows + 1, 0);
+  for (size_t r = 0; r < n_rows; ++r) {
+    if (row_lens[r] == 0 || row_lens[r] > static_cast<uint32_t>(e->max_length))
+      return set_error(J1_ERR_INVALID_ARG,
+                       "row " + std::to_string(r + 1) + ": length must be in 1.." + std::to_string(e->max_length));
+    if (qtypes[r] > 2) return set_error(J1_ERR_INVALID_ARG, "qtype must be 0, 1 or 2");
+    tok_off[r + 1] = tok_off[r] + row_lens[r];
+    mk_off[r + 1] = mk_off[r] + row_markers[r];
+  }
+  if (mk_off[n_rows] && (!markers || !logits_out)) return set_error(J1_ERR_INVALID_ARG, "NULL markers/logits");
+  for (size_t r = 0; r < n_rows; ++r)
+    for (size_t k = mk_off[r]; k < mk_off[r + 1]; ++k)
+      if (markers[k] >= row_lens[r]) return set_error(J1_ERR_INVALID_ARG, "marker outside its row");
+
+  std::lock_guard<std::mutex> lk(e->mu);
+  // Length-sorted micro-batches (src/engine.rs:191-210); stable sort keeps input order on ties.
+  std::vector<size_t> order(n_rows);
+  std::iota(order.begin(), order.end(), 0);
+  std::stable_sort(order.begin(), order.end(), [&](size_t a, size_t b) { return row_lens[a] < row_lens[b]; });
+  std::vector<Micro> micro;
+  Micro cur;
+  for (size_t i : order) {
+    const size_t n = row_lens[i];
+    if (!cur.rows.empty() &&
+        (cur.rows.size() == static_cast<size_t>(e->opts.batch_size) ||
+         cur.tokens + n > static_cast<size_t>(e->opts.max_batch_tokens))) {
+      micro.push_back(std::move(cur));
+      cur = Micro();
+    }
+    cur.rows.push_back(i);
+    cur.tokens += n;
+  }
+  if (!cur.rows.empty()) micro.push_back(std::move(cur));
+
+  // Greedy token balance across replicas, in batch order.
+  const size_t G = e->models.size();
+  std::vector<std::vector<size_t>> assign(G);
+  std::vector<size_t> load(G, 0);
+  for (size_t b = 0; b < micro.size(); ++b) {
+    const size_t g = static_cast<size_t>(std::min_element(load.begin(), load.end()) - load.begin());
+    assign[g].push_back(b);
+    load[g] += micro[b].tokens;
+  }
+
+  auto run = [&](size_t g, j1_status* status, std::string* msg) {
+    std::vector<uint32_t> bids, starts, lens, mrows, mstarts;
+    std::vector<uint8_t> qt;
+    std::vector<float> scores;
+    for (size_t b : assign[g]) {
+      const Micro& mb = micro[b];
+      bids.clear(), starts.clear(), lens.clear(), mrows.clear(), mstarts.assign(1, 0), qt.clear();
+      for (size_t r : mb.rows) {
+        const uint32_t start = static_cast<uint32_t>(bids.size());
+        starts.push_back(start);
+        lens.push_back(row_lens[r]);
+        qt.push_back(qtypes[r]);
+        bids.insert(bids.end(), ids + tok_off[r], ids + tok_off[r + 1]);
+        for (size_t k = mk_off[r]; k < mk_off[r + 1]; ++k) mrows.push_back(start + markers[k]);
+        mstarts.push_back(static_cast<uint32_t>(mrows.size()));
+      }
+      scores.assign(mrows.size(), 0.f);
+      j1_status s = j1_model_forward(e->models[g], bids.data(), bids.size(), starts.data(), lens.data(), qt.data(),
+                                     starts.size(), mrows.data(), mstarts.data(), mrows.size(), scores.data());
+      if (s) {
+        *status = s;
+        char buf[512];
+        j1_last_error(buf, sizeof(buf));
+        *msg = buf;
+        return;
+      }
+      size_t k = 0;
+      for (size_t r : mb.rows)
+        for (size_t j = mk_off[r]; j < mk_off[r + 1]; ++j) logits_out[j] = scores[k++];
+    }
+  };
+
+  std::vector<j1_status> st(G, J1_OK);
+  std::vector<std::string> msgs(G);
+  if (G == 1) {
+    run(0, &st[0], &msgs[0]);
+  } else {
+    std::vector<std::thread> workers;
+    for (size_t g = 0; g < G; ++g) workers.emplace_back(run, g, &st[g], &msgs[g]);
+    for (auto& w : workers) w.join();
+  }
+  for (size_t g = 0; g < G; ++g)
+    if (st[g]) return set_error(st[g], msgs[g]);
+  return J1_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,83 @@
+// Host-side launch interface of the device kernels (internal to libj1).
+#pragma once
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace j1rt {
+
+using bf16 = __nv_bfloat16;
+
+// ------------------------------------------------------------------ GEMM
+// out = A[M,K] . W[N,K]^T with a fused epilogue. A and W are bf16, row-major,
+// read through 128B-swizzled TMA maps (box 64 x 128 for A, 64 x BN for W).
+enum GemmEpi : int {
+  EPI_BF16 = 0,      // out = bf16(acc (+bias)) (relu when `relu`)
+  EPI_QKV_ROPE = 1,  // out = bf16(rope(acc)) on columns < rope_cols, bf16(acc) elsewhere
+  EPI_GEGLU = 2,     // W rows interleaved per 128: out[:, n/2 + j] = bf16(gelu(acc_a) * acc_b)
+  EPI_RESID_LN = 3,  // full row: x += acc (+bias); xn = bf16(LN(x; ln_w, ln_b, eps))
+  EPI_RESID = 4,     // full row: x += acc (+bias)
+  EPI_SCORER = 5,    // full row: scores[r] = sum_j gelu(acc + bias[j]) * w2[j] + b2
+};
+
+struct EpiParams {
+  int M, N, K;
+  bf16* out;
+  int ldo;
+  const float* bias;
+  int relu;
+  float* x;
+  int ldx;
+  const float* ln_w;
+  const float* ln_b;
+  float ln_eps;
+  bf16* xn;
+  int ldxn;
+  const int* pos;
+  const float* rope_cos;  // [max_pos, 32]
+  const float* rope_sin;
+  int rope_cols;
+  const float* w2;
+  float b2;
+  float* scores;
+  int* err;  // device error word
+};
+
+// Column width of one MMA tile for an N (or full-row width): 256 when N % 256 == 0, else 128.
+int gemm_bn_for(int n);
+// Returns 0 on success, or a cudaError_t value.
+int launch_gemm(GemmEpi epi, int bn, const CUtensorMap& tmA, const CUtensorMap& tmW, const EpiParams& p,
+                int grid_limit, cudaStream_t stream);
+// Validates shapes for an epilogue; returns nullptr when fine, else a message.
+const char* gemm_shape_error(GemmEpi epi, int bn, int M, int N, int K);
+
+// ------------------------------------------------------------------ attention
+// One 128-query tile of one sequence. Query row r of the tile is Q-buffer row
+// q_row0 + r at sequence position q_pos0 + r; keys/values are rows
+// kv_row0 .. kv_row0 + kv_len - 1 of the K/V buffer.
+struct AttnTile {
+  int q_row0, nq, kv_row0, kv_len, q_pos0, pad0, pad1, pad2;
+};
+// ctx[q_row0 + r, head*64 ..] = softmax(scale * q k^T [band]) v for every tile x head.
+// window < 0: full attention; else |qpos - kpos| <= window.
+int launch_attention(const CUtensorMap& tmQ, const CUtensorMap& tmKV, const AttnTile* tiles, int ntiles, int heads,
+                     int q_col0, int k_col0, int v_col0, bf16* out, int ldo, int window, float scale_log2, int* err,
+                     cudaStream_t stream);
+
+// ------------------------------------------------------------------ row kernels
+int launch_embed_ln(int hidden, const int* ids, const float* table, const float* w, float* x, bf16* xn, int rows,
+                    float eps, cudaStream_t stream);
+int launch_final_norm(int hidden, float* x, const float* fw, const float* type_emb, const int* qtype_tok,
+                      const float* hw, const float* hb, bf16* xn, int rows, float eps, cudaStream_t stream);
+int launch_gather_rows(const void* src, const int* idx, void* dst, int rows, int row_bytes, cudaStream_t stream);
+// dst = bf16(src) with an optional row permutation: dst row r <- src row perm(r) (GEGLU interleave).
+int launch_f32_to_bf16(const float* src, bf16* dst, long long rows, int cols, int geglu_inter, cudaStream_t stream);
+bool hidden_supported(int hidden);
+
+// ------------------------------------------------------------------ TMA maps
+// 2D bf16 row-major [rows, cols] with row stride `ld` elements; 128B swizzle box (64 x box_rows).
+bool make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld,
+                    uint32_t box_rows, const char** why);
+
+}  // namespace j1rt

@@ -1,0 +1,106 @@
+// Internal model / status helpers shared by model.cpp and engine.cpp.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/j1.h"
+#include "checkpoint.h"
+#include "kernels.h"
+
+namespace j1rt {
+
+j1_status set_error(j1_status s, const std::string& msg);
+j1_status cuda_error(cudaError_t e, const char* what);
+
+// Restores the calling thread's current device on scope exit.
+class DeviceGuard {
+ public:
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev_) != cudaSuccess) prev_ = -1;
+    ok_ = cudaSetDevice(dev) == cudaSuccess;
+  }
+  ~DeviceGuard() {
+    if (prev_ >= 0) cudaSetDevice(prev_);
+  }
+  bool ok() const { return ok_; }
+
+ private:
+  int prev_ = -1;
+  bool ok_ = false;
+};
+
+// A packed batch (model::Batch, src/model.rs:225-269) as host views.
+struct BatchView {
+  const uint32_t* ids;
+  size_t t;
+  const uint32_t* starts;
+  const uint32_t* lens;
+  const uint8_t* qtypes;
+  size_t nseq;
+  const uint32_t* marker_rows;
+  const uint32_t* marker_starts;
+  size_t m;
+};
+
+}  // namespace j1rt
+
+struct j1_model {
+  j1rt::ModelConfig cfg;
+  int device = 0;
+  int num_sms = 148;
+  cudaStream_t stream = nullptr;
+  std::string name;
+  std::mutex mu;
+  std::vector<void*> allocations;  // device memory owned by the model
+
+  // ---- weights (device)
+  float* emb = nullptr;
+  float* emb_norm = nullptr;
+  struct Layer {
+    float* attn_norm = nullptr;  // nullptr at layer 0 (nn.Identity)
+    float* mlp_norm = nullptr;
+    j1rt::bf16 *wqkv = nullptr, *wo = nullptr, *wi = nullptr, *wo2 = nullptr;  // wi interleaved for GEGLU
+    CUtensorMap tm_wqkv, tm_wo, tm_wi, tm_wo2;
+    int rope = 0;
+    bool global = false;
+  };
+  std::vector<Layer> layers;
+  float* final_norm = nullptr;
+  float* type_emb = nullptr;
+  struct Head {
+    float *norm1_w, *norm1_b, *in_b, *out_b, *norm2_w, *norm2_b, *lin1_b, *lin2_b;
+    j1rt::bf16 *in_w, *out_w, *lin1_w, *lin2_w;
+    CUtensorMap tm_in, tm_out, tm_lin1, tm_lin2;
+  };
+  std::vector<Head> head;
+  float *s_norm_w = nullptr, *s_norm_b = nullptr, *s_b1 = nullptr, *s_w2 = nullptr;
+  float s_b2 = 0.f;
+  j1rt::bf16* s_w1 = nullptr;
+  CUtensorMap tm_s_w1;
+  std::vector<float*> rope_cos, rope_sin;
+  int* err_dev = nullptr;
+
+  // ---- workspace (grows monotonically, like ensure_workspace in src/cuda/mod.rs:282-332)
+  size_t cap_tokens = 0, cap_markers = 0, cap_meta = 0;
+  float* x = nullptr;
+  j1rt::bf16 *xn = nullptr, *qkv = nullptr, *ctx = nullptr, *g = nullptr;
+  float* ym = nullptr;
+  j1rt::bf16 *ymb = nullptr, *cm = nullptr, *hm = nullptr;
+  float* scores = nullptr;
+  int* meta_dev = nullptr;
+  int* meta_host = nullptr;      // pinned
+  float* scores_host = nullptr;  // pinned
+  int* err_host = nullptr;       // pinned
+  std::vector<void*> ws_allocations;
+
+  // ---- staged batch
+  bool staged = false;
+  size_t t = 0, m = 0, nseq = 0, ntiles = 0;
+  int *d_ids = nullptr, *d_pos = nullptr, *d_qtype = nullptr, *d_markers = nullptr;
+  j1rt::AttnTile* d_tiles = nullptr;
+  CUtensorMap tm_xn, tm_ctx, tm_g, tm_h, tm_qkv, tm_cm, tm_ymb, tm_hm;
+  int64_t launches = 0;
+};

@@ -1,0 +1,404 @@
+"""Python host mirror of the julia1-rs engine API over libj1 (ctypes).
+
+The reference's Rust API (crate `julia1`, src/lib.rs) exposes `Engine`,
+`EngineOptions`, `Device` and, below the tokenizer, `Engine::logits_encoded`
+over `encode::Encoded` rows. This module mirrors those names on top of the C ABI
+in include/j1.h; all compute runs in libj1's CUDA kernels. There is no CPU
+fallback: if lib/libj1.so is missing or the device is not an sm_100 GPU, calls
+raise J1Error.
+"""
+import ctypes as C
+import os
+from dataclasses import dataclass, field
+from typing import List, Optional, Sequence
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(os.path.dirname(_HERE), "lib", "libj1.so")
+
+OK, INVALID_ARG, UNSUPPORTED, CUDA, OOM, NONFINITE, DEVICE_TIMEOUT, IO = range(8)
+STATUS_NAMES = ["J1_OK", "J1_ERR_INVALID_ARG", "J1_ERR_UNSUPPORTED", "J1_ERR_CUDA", "J1_ERR_OOM",
+                "J1_ERR_NONFINITE", "J1_ERR_DEVICE_TIMEOUT", "J1_ERR_IO"]
+
+# Every symbol include/j1.h declares (checked by tests against the built library).
+EXPORTS = [
+    "j1_last_error", "j1_status_name", "j1_version", "j1_config_load",
+    "j1_model_create", "j1_model_destroy", "j1_model_name", "j1_model_config", "j1_model_forward",
+    "j1_model_stage", "j1_model_launch", "j1_model_finish", "j1_model_stream", "j1_model_launch_count",
+    "j1_engine_options_default", "j1_engine_create", "j1_engine_create_pool", "j1_engine_destroy",
+    "j1_engine_device_name", "j1_engine_logits_encoded",
+    "j1_op_gemm", "j1_op_attention", "j1_op_geglu_interleave",
+]
+
+EPI_BF16, EPI_QKV_ROPE, EPI_GEGLU, EPI_RESID_LN, EPI_RESID, EPI_SCORER = range(6)
+
+
+class J1Error(RuntimeError):
+    def __init__(self, status, message):
+        self.status = status
+        super().__init__("%s: %s" % (STATUS_NAMES[status] if 0 <= status < len(STATUS_NAMES) else status, message))
+
+
+class J1Config(C.Structure):
+    _fields_ = [(n, C.c_int32) for n in ("hidden", "heads", "head_dim", "intermediate", "layers", "half_window",
+                                         "vocab", "max_positions", "head_layers", "head_heads", "head_ff")] + \
+               [("norm_eps", C.c_float), ("n_global", C.c_int32)]
+
+
+class J1EngineOptions(C.Structure):
+    _fields_ = [("device", C.c_char_p), ("batch_size", C.c_int32), ("max_batch_tokens", C.c_int64),
+                ("max_length", C.c_int32)]
+
+
+class J1GemmArgs(C.Structure):
+    _fields_ = [("epilogue", C.c_int32), ("M", C.c_int32), ("N", C.c_int32), ("K", C.c_int32),
+                ("A", C.c_void_p), ("W", C.c_void_p), ("out", C.c_void_p), ("ldo", C.c_int32),
+                ("bias", C.c_void_p), ("relu", C.c_int32), ("x", C.c_void_p), ("ldx", C.c_int32),
+                ("ln_w", C.c_void_p), ("ln_b", C.c_void_p), ("ln_eps", C.c_float), ("xn", C.c_void_p),
+                ("ldxn", C.c_int32), ("pos", C.c_void_p), ("rope_cos", C.c_void_p), ("rope_sin", C.c_void_p),
+                ("rope_cols", C.c_int32), ("w2", C.c_void_p), ("b2", C.c_float), ("scores", C.c_void_p),
+                ("grid_limit", C.c_int32)]
+
+
+_lib = None
+
+
+def lib():
+    """Load libj1.so once (raises if it was not built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise J1Error(CUDA, "libj1.so not built (run python julia1-rs_b200/build.py): %s" % LIB_PATH)
+    L = C.CDLL(LIB_PATH)
+    u32p, f32p, u8p = C.POINTER(C.c_uint32), C.POINTER(C.c_float), C.POINTER(C.c_uint8)
+    L.j1_last_error.argtypes = [C.c_char_p, C.c_size_t]
+    L.j1_last_error.restype = C.c_size_t
+    L.j1_status_name.restype = C.c_char_p
+    L.j1_version.restype = C.c_char_p
+    L.j1_config_load.argtypes = [C.c_char_p, C.POINTER(J1Config)]
+    L.j1_model_create.argtypes = [C.c_char_p, C.c_int, C.POINTER(C.c_void_p)]
+    L.j1_model_destroy.argtypes = [C.c_void_p]
+    L.j1_model_destroy.restype = None
+    L.j1_model_name.argtypes = [C.c_void_p, C.c_char_p, C.c_size_t]
+    L.j1_model_name.restype = C.c_size_t
+    L.j1_model_config.argtypes = [C.c_void_p, C.POINTER(J1Config)]
+    batch = [u32p, C.c_size_t, u32p, u32p, u8p, C.c_size_t, u32p, u32p, C.c_size_t]
+    L.j1_model_forward.argtypes = [C.c_void_p] + batch + [f32p]
+    L.j1_model_stage.argtypes = [C.c_void_p] + batch
+    L.j1_model_launch.argtypes = [C.c_void_p]
+    L.j1_model_finish.argtypes = [C.c_void_p, f32p, C.c_size_t]
+    L.j1_model_stream.argtypes = [C.c_void_p]
+    L.j1_model_stream.restype = C.c_void_p
+    L.j1_model_launch_count.argtypes = [C.c_void_p]
+    L.j1_model_launch_count.restype = C.c_int64
+    L.j1_engine_options_default.argtypes = [C.POINTER(J1EngineOptions)]
+    L.j1_engine_options_default.restype = None
+    L.j1_engine_create.argtypes = [C.c_char_p, C.POINTER(J1EngineOptions), C.POINTER(C.c_void_p)]
+    L.j1_engine_create_pool.argtypes = [C.c_char_p, C.POINTER(J1EngineOptions), C.POINTER(C.c_int), C.c_int,
+                                        C.POINTER(C.c_void_p)]
+    L.j1_engine_destroy.argtypes = [C.c_void_p]
+    L.j1_engine_destroy.restype = None
+    L.j1_engine_device_name.argtypes = [C.c_void_p, C.c_char_p, C.c_size_t]
+    L.j1_engine_device_name.restype = C.c_size_t
+    L.j1_engine_logits_encoded.argtypes = [C.c_void_p, C.c_size_t, u32p, u32p, u32p, u32p, u8p, f32p]
+    L.j1_op_gemm.argtypes = [C.POINTER(J1GemmArgs), C.c_void_p, C.c_int]
+    L.j1_op_attention.argtypes = [C.c_void_p, C.c_int64, C.c_int32, u32p, u32p, C.c_size_t, C.c_int32, C.c_void_p,
+                                  C.c_void_p, C.c_int]
+    L.j1_op_geglu_interleave.argtypes = [C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_void_p]
+    for fn in ("j1_config_load", "j1_model_create", "j1_model_config", "j1_model_forward", "j1_model_stage",
+               "j1_model_launch", "j1_model_finish", "j1_engine_create", "j1_engine_create_pool",
+               "j1_engine_logits_encoded", "j1_op_gemm", "j1_op_attention", "j1_op_geglu_interleave"):
+        getattr(L, fn).restype = C.c_int
+    _lib = L
+    return L
+
+
+def last_error():
+    buf = C.create_string_buffer(1024)
+    lib().j1_last_error(buf, 1024)
+    return buf.value.decode(errors="replace")
+
+
+def check(status):
+    if status != OK:
+        raise J1Error(status, last_error())
+
+
+def _u32(a):
+    a = np.ascontiguousarray(a, dtype=np.uint32)
+    return a, a.ctypes.data_as(C.POINTER(C.c_uint32))
+
+
+def _u8(a):
+    a = np.ascontiguousarray(a, dtype=np.uint8)
+    return a, a.ctypes.data_as(C.POINTER(C.c_uint8))
+
+
+# ------------------------------------------------------------------ Device / options
+@dataclass(frozen=True)
+class Device:
+    """Device::from_str (src/engine.rs:20-31): "cpu", "cuda", "cuda:N"."""
+    kind: str
+    index: int = 0
+
+    @staticmethod
+    def parse(s: str) -> "Device":
+        if s == "cpu":
+            return Device("cpu")
+        if s == "cuda":
+            return Device("cuda", 0)
+        if s.startswith("cuda:") and s[5:].isdigit():
+            return Device("cuda", int(s[5:]))
+        raise J1Error(INVALID_ARG, "device must be cpu, cuda or cuda:N")
+
+    def __str__(self):
+        return "cpu" if self.kind == "cpu" else "cuda:%d" % self.index
+
+
+@dataclass
+class EngineOptions:
+    """EngineOptions (src/engine.rs:34-65), device-side subset."""
+    device: str = "cuda"
+    batch_size: int = 16
+    max_batch_tokens: int = 65536
+    max_length: Optional[int] = None
+
+
+def load_config(ckpt_dir):
+    cfg = J1Config()
+    check(lib().j1_config_load(ckpt_dir.encode(), C.byref(cfg)))
+    return cfg
+
+
+# ------------------------------------------------------------------ Batch / CudaModel
+@dataclass
+class Encoded:
+    """encode::Encoded: token ids, marker positions within the row, question type."""
+    ids: np.ndarray
+    markers: np.ndarray
+    qtype: int = 0
+
+
+@dataclass
+class Batch:
+    """model::Batch (src/model.rs:225-269): sequences packed back to back, no padding."""
+    ids: np.ndarray
+    starts: np.ndarray
+    lens: np.ndarray
+    qtypes: np.ndarray
+    marker_rows: np.ndarray
+    marker_starts: np.ndarray
+
+    @staticmethod
+    def new(items: Sequence) -> "Batch":
+        ids, starts, lens, qtypes, mrows, mstarts = [], [], [], [], [], [0]
+        off = 0
+        for it in items:
+            e_ids, e_mk, e_qt = (it.ids, it.markers, it.qtype) if isinstance(it, Encoded) else it
+            e_ids = np.asarray(e_ids, dtype=np.uint32)
+            starts.append(off)
+            lens.append(len(e_ids))
+            qtypes.append(int(e_qt))
+            ids.append(e_ids)
+            mrows.extend(int(off + m) for m in np.asarray(e_mk).tolist())
+            mstarts.append(len(mrows))
+            off += len(e_ids)
+        cat = np.concatenate(ids) if ids else np.zeros(0, np.uint32)
+        return Batch(cat.astype(np.uint32), np.array(starts, np.uint32), np.array(lens, np.uint32),
+                     np.array(qtypes, np.uint8), np.array(mrows, np.uint32), np.array(mstarts, np.uint32))
+
+    def tokens(self):
+        return int(self.ids.size)
+
+    def split_scores(self, scores):
+        return [list(map(float, scores[a:b])) for a, b in zip(self.marker_starts[:-1], self.marker_starts[1:])]
+
+
+class CudaModel:
+    """CudaModel (src/cuda/mod.rs:141-521) on one device, via libj1."""
+
+    def __init__(self, ckpt_dir: str, ordinal: int = 0):
+        h = C.c_void_p()
+        check(lib().j1_model_create(ckpt_dir.encode(), int(ordinal), C.byref(h)))
+        self._h = h
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().j1_model_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def name(self):
+        buf = C.create_string_buffer(256)
+        lib().j1_model_name(self._h, buf, 256)
+        return buf.value.decode()
+
+    def config(self):
+        cfg = J1Config()
+        check(lib().j1_model_config(self._h, C.byref(cfg)))
+        return cfg
+
+    def _args(self, b: Batch):
+        keep = [_u32(b.ids), _u32(b.starts), _u32(b.lens), _u8(b.qtypes), _u32(b.marker_rows), _u32(b.marker_starts)]
+        p = [k[1] for k in keep]
+        return keep, [p[0], b.ids.size, p[1], p[2], p[3], b.lens.size, p[4], p[5], b.marker_rows.size]
+
+    def forward_flat(self, b: Batch) -> np.ndarray:
+        keep, args = self._args(b)
+        out = np.zeros(b.marker_rows.size, np.float32)
+        check(lib().j1_model_forward(self._h, *args, out.ctypes.data_as(C.POINTER(C.c_float))))
+        return out
+
+    def forward(self, b: Batch) -> List[List[float]]:
+        """Scores per sequence (Batch::split_scores)."""
+        return b.split_scores(self.forward_flat(b))
+
+    # resident-batch split used by the benchmark
+    def stage(self, b: Batch):
+        self._staged = self._args(b)
+        check(lib().j1_model_stage(self._h, *self._staged[1]))
+
+    def launch(self):
+        check(lib().j1_model_launch(self._h))
+
+    def finish(self, m):
+        out = np.zeros(m, np.float32)
+        check(lib().j1_model_finish(self._h, out.ctypes.data_as(C.POINTER(C.c_float)), m))
+        return out
+
+    def stream(self):
+        return lib().j1_model_stream(self._h)
+
+    def launch_count(self):
+        return int(lib().j1_model_launch_count(self._h))
+
+
+# ------------------------------------------------------------------ Engine
+class Engine:
+    """Engine (src/engine.rs:73-284) restricted to the encoded-row API (no tokenizer)."""
+
+    def __init__(self, handle):
+        self._h = handle
+
+    @staticmethod
+    def load(ckpt_dir: str, options: Optional[EngineOptions] = None, devices: Optional[Sequence[int]] = None):
+        o = options or EngineOptions()
+        Device.parse(o.device)  # same parse errors as the reference
+        copt = J1EngineOptions()
+        lib().j1_engine_options_default(C.byref(copt))
+        copt.device = o.device.encode()
+        copt.batch_size = int(o.batch_size)
+        copt.max_batch_tokens = int(o.max_batch_tokens)
+        copt.max_length = int(o.max_length or 0)
+        h = C.c_void_p()
+        if devices:
+            arr = (C.c_int * len(devices))(*devices)
+            check(lib().j1_engine_create_pool(ckpt_dir.encode(), C.byref(copt), arr, len(devices), C.byref(h)))
+        else:
+            check(lib().j1_engine_create(ckpt_dir.encode(), C.byref(copt), C.byref(h)))
+        return Engine(h)
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().j1_engine_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def device_name(self):
+        buf = C.create_string_buffer(1024)
+        lib().j1_engine_device_name(self._h, buf, 1024)
+        return buf.value.decode()
+
+    def logits_encoded(self, rows: Sequence) -> List[List[float]]:
+        """Raw option logits per row, in option order (Engine::logits_encoded)."""
+        if len(rows) == 0:
+            return []
+        items = [r if isinstance(r, Encoded) else Encoded(*r) for r in rows]
+        ids = np.concatenate([np.asarray(r.ids, np.uint32) for r in items])
+        lens = np.array([len(r.ids) for r in items], np.uint32)
+        mk = [np.asarray(r.markers, np.uint32) for r in items]
+        markers = np.concatenate(mk) if mk else np.zeros(0, np.uint32)
+        nmk = np.array([len(m) for m in mk], np.uint32)
+        qt = np.array([int(r.qtype) for r in items], np.uint8)
+        out = np.zeros(int(nmk.sum()), np.float32)
+        keep = [_u32(ids), _u32(lens), _u32(markers), _u32(nmk), _u8(qt)]
+        check(lib().j1_engine_logits_encoded(self._h, len(items), keep[0][1], keep[1][1], keep[2][1], keep[3][1],
+                                             keep[4][1], out.ctypes.data_as(C.POINTER(C.c_float))))
+        res, o = [], 0
+        for n in nmk.tolist():
+            res.append(list(map(float, out[o:o + n])))
+            o += n
+        return res
+
+    def predict_encoded(self, rows, probabilities=False):
+        """Engine::predict semantics on encoded rows: argmax index (+ softmax probabilities)."""
+        out = []
+        for z in self.logits_encoded(rows):
+            z = np.asarray(z, np.float32)
+            idx = int(np.argmax(z)) if z.size else 0
+            pr = None
+            if probabilities and z.size:
+                e = np.exp((z - z.max()).astype(np.float64))
+                pr = (e / e.sum()).tolist()
+            out.append((idx, pr))
+        return out
+
+
+# ------------------------------------------------------------------ kernel-level ops (torch tensors)
+def _ptr(t):
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def op_gemm(epilogue, A, W, out=None, bias=None, relu=False, x=None, ln_w=None, ln_b=None, ln_eps=1e-5, xn=None,
+            pos=None, rope_cos=None, rope_sin=None, rope_cols=0, w2=None, b2=0.0, scores=None, stream=None, sync=True,
+            grid_limit=0):
+    """Fused-epilogue GEMM on torch CUDA tensors (bf16 A [M,K], W [N,K])."""
+    M, K = A.shape
+    N = W.shape[0]
+    a = J1GemmArgs()
+    a.epilogue, a.M, a.N, a.K = epilogue, M, N, K
+    a.A, a.W = A.data_ptr(), W.data_ptr()
+    a.out = out.data_ptr() if out is not None else None
+    a.ldo = out.shape[1] if out is not None else 0
+    a.bias = bias.data_ptr() if bias is not None else None
+    a.relu = 1 if relu else 0
+    a.x = x.data_ptr() if x is not None else None
+    a.ldx = x.shape[1] if x is not None else 0
+    a.ln_w = ln_w.data_ptr() if ln_w is not None else None
+    a.ln_b = ln_b.data_ptr() if ln_b is not None else None
+    a.ln_eps = ln_eps
+    a.xn = xn.data_ptr() if xn is not None else None
+    a.ldxn = xn.shape[1] if xn is not None else 0
+    a.pos = pos.data_ptr() if pos is not None else None
+    a.rope_cos = rope_cos.data_ptr() if rope_cos is not None else None
+    a.rope_sin = rope_sin.data_ptr() if rope_sin is not None else None
+    a.rope_cols = rope_cols
+    a.w2 = w2.data_ptr() if w2 is not None else None
+    a.b2 = b2
+    a.scores = scores.data_ptr() if scores is not None else None
+    a.grid_limit = grid_limit
+    check(lib().j1_op_gemm(C.byref(a), C.c_void_p(stream) if stream else None, 1 if sync else 0))
+
+
+def op_attention(qkv, hidden, seq_starts, seq_lens, window, ctx, stream=None, sync=True):
+    s, sp = _u32(seq_starts)
+    l, lp = _u32(seq_lens)
+    check(lib().j1_op_attention(C.c_void_p(qkv.data_ptr()), qkv.shape[0], hidden, sp, lp, len(s), window,
+                                C.c_void_p(ctx.data_ptr()), C.c_void_p(stream) if stream else None, 1 if sync else 0))
+
+
+def op_geglu_interleave(src_f32, dst_bf16, inter, k, stream=None):
+    check(lib().j1_op_geglu_interleave(C.c_void_p(src_f32.data_ptr()), C.c_void_p(dst_bf16.data_ptr()), inter, k,
+                                       C.c_void_p(stream) if stream else None))
