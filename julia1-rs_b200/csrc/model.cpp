@@ -89,7 +89,10 @@ j1_status upload_f32(j1_model* model, SafeTensors& st, const std::string& name, 
   void* p;
   j1_status s = dalloc(model, &p, n * 4, model->allocations);
   if (s) return s;
-  J1_TRY_CUDA(cudaMemcpy(p, h, n * 4, cudaMemcpyHostToDevice), "weight upload");
+  // Ordered on the model's stream: a pageable cudaMemcpy may return before its DMA lands,
+  // and the model's non-blocking stream would not wait for it.
+  J1_TRY_CUDA(cudaMemcpyAsync(p, h, n * 4, cudaMemcpyHostToDevice, model->stream), "weight upload");
+  J1_TRY_CUDA(cudaStreamSynchronize(model->stream), "weight upload");
   *out = static_cast<T*>(p);
   return J1_OK;
 }
@@ -104,7 +107,7 @@ j1_status upload_bf16(j1_model* model, SafeTensors& st, const std::string& name,
   void* p;
   j1_status s = dalloc(model, &p, rows * cols * 2, model->allocations);
   if (s) return s;
-  J1_TRY_CUDA(cudaMemcpy(staging, h, rows * cols * 4, cudaMemcpyHostToDevice), "weight upload");
+  J1_TRY_CUDA(cudaMemcpyAsync(staging, h, rows * cols * 4, cudaMemcpyHostToDevice, model->stream), "weight upload");
   int rc = launch_f32_to_bf16(staging, static_cast<bf16*>(p), static_cast<long long>(rows), static_cast<int>(cols),
                               geglu_inter, model->stream);
   if (rc) return cuda_error(static_cast<cudaError_t>(rc), "weight conversion");
@@ -421,7 +424,7 @@ j1_status create_model(const char* ckpt_dir, int ordinal, j1_model** out) {
   j1_status s;
   if ((s = dalloc(M, &p, 4, M->allocations))) return s;
   M->err_dev = static_cast<int*>(p);
-  J1_TRY_CUDA(cudaMemset(M->err_dev, 0, 4), "memset");
+  J1_TRY_CUDA(cudaMemsetAsync(M->err_dev, 0, 4, M->stream), "memset");
   J1_TRY_CUDA(cudaMallocHost(&p, 16), "cudaMallocHost");
   M->err_host = static_cast<int*>(p);
 
@@ -453,8 +456,9 @@ j1_status create_model(const char* ckpt_dir, int ordinal, j1_model** out) {
       dc = static_cast<float*>(p);
       if ((s = dalloc(M, &p, sn.size() * 4, M->allocations))) return s;
       ds = static_cast<float*>(p);
-      J1_TRY_CUDA(cudaMemcpy(dc, ct.data(), ct.size() * 4, cudaMemcpyHostToDevice), "rope upload");
-      J1_TRY_CUDA(cudaMemcpy(ds, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice), "rope upload");
+      J1_TRY_CUDA(cudaMemcpyAsync(dc, ct.data(), ct.size() * 4, cudaMemcpyHostToDevice, M->stream), "rope upload");
+      J1_TRY_CUDA(cudaMemcpyAsync(ds, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice, M->stream), "rope upload");
+      J1_TRY_CUDA(cudaStreamSynchronize(M->stream), "rope upload");
       M->rope_cos.push_back(dc);
       M->rope_sin.push_back(ds);
       thetas.push_back(theta);

@@ -127,7 +127,7 @@ def read_safetensors(path):
 
 
 def synthetic_batch(lens, vocab=50368, markers_per_seq=4, seed=1, cls_id=1, sep_id=2, mask_id=4, qtype=0,
-                    option_block=None):
+                    option_block=None, mask_markers=True):
     """Encoded rows (ids, marker positions, qtype) with ids ~ U[5, vocab).
 
     Position 0 is CLS and the last position SEP. With option_block=None each row
@@ -135,6 +135,8 @@ def synthetic_batch(lens, vocab=50368, markers_per_seq=4, seed=1, cls_id=1, sep_
     option_block=(n_options, tokens_per_option, head_tokens) instead lays the row out as
     [CLS] head [SEP] n x ([MASK] + option tokens) [SEP] state ... [SEP]
     (the marker serialization of the reference's Encoder::sequence).
+    With mask_markers=False the marker positions keep their random ids: with random
+    weights, MASK markers give nearly tied logits, random ids spread them apart.
     """
     rng = np.random.default_rng(seed)
     rows = []
@@ -158,6 +160,7 @@ def synthetic_batch(lens, vocab=50368, markers_per_seq=4, seed=1, cls_id=1, sep_
             mk = np.array(mk, dtype=np.uint32)
             if pos < L - 1:
                 ids[pos] = sep_id
-        ids[mk] = mask_id
+        if mask_markers:
+            ids[mk] = mask_id
         rows.append((ids, mk, qtype))
     return rows
