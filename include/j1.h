@@ -97,6 +97,17 @@ J1_API void* j1_model_stream(j1_model* model);
 /* Number of kernel launches one j1_model_launch issues for the staged batch. */
 J1_API int64_t j1_model_launch_count(const j1_model* model);
 
+/* Optional device timing by kernel family: with profiling on, every launch is bracketed
+ * by CUDA events on the model's stream; j1_model_finish folds the elapsed times into
+ * per-family totals. enable != 0 turns it on and clears the totals. */
+#define J1_PROF_FAMILIES 12
+J1_API j1_status j1_model_profile(j1_model* model, int enable);
+/* Totals since the last j1_model_profile(model, 1): ms[J1_PROF_FAMILIES], launches[J1_PROF_FAMILIES]. */
+J1_API j1_status j1_model_profile_read(j1_model* model, double* ms, int64_t* launches);
+/* "embed_ln", "gemm_qkv_rope", "attn_local", "attn_global", "gemm_wo_resid_ln", "gemm_wi_geglu",
+ * "gemm_wo2_resid_ln", "final_norm", "head_gemm", "head_attn", "head_gather", "scorer_gemm". */
+J1_API const char* j1_profile_family_name(int family);
+
 /* ------------------------------------------------------------ engine */
 /* EngineOptions (src/engine.rs:34-65), device-side subset. */
 typedef struct j1_engine_options {

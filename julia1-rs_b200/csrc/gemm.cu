@@ -11,10 +11,16 @@
 // Structure: persistent CTAs (one per SM), 192 threads.
 //   warp 0      TMA producer: A (128 x 64) and W (BN x 64) boxes into a smem ring
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer (M=128, N=BN, K=16)
-//   warps 2..5  epilogue: tcgen05.ld of the FP32 accumulator (lane = row), fused math,
-//               direct global stores
-// The accumulator is double buffered in TMEM (2 x BN columns) so the epilogue
-// of one tile overlaps the main loop of the next.
+//   warps 2..5  epilogue: tcgen05.ld of the FP32 accumulator (TMEM lane = row), fused math
+// The accumulator is double buffered in TMEM (2 x BN columns) so the epilogue of one
+// tile overlaps the main loop of the next.
+//
+// Full-row epilogues (RESID*, SCORER) own whole rows: one work unit is 128 rows x H
+// columns, computed as H/BN sub-tiles. The residual stream x (FP32) moves through
+// shared memory in 128 x 32 chunks by TMA (load, in-place update, store), double
+// buffered and prefetched while the main loop runs; per-row LayerNorm statistics are
+// merged chunk by chunk (Welford/Chan), then the normalized BF16 row is produced from
+// the updated x with warp-coalesced loads.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -27,14 +33,19 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
+constexpr uint32_t XCHUNK = 128 * 32 * 4;  // one 128-row x 32-column FP32 residual chunk
 
-template <int BN>
+__host__ __device__ constexpr bool is_full_row(int epi) { return epi == EPI_RESID_LN || epi == EPI_RESID || epi == EPI_SCORER; }
+__host__ __device__ constexpr bool is_resid(int epi) { return epi == EPI_RESID_LN || epi == EPI_RESID; }
+
+template <int BN, int EPI>
 struct GemmCfg {
   static constexpr int STAGES = (BN == 256) ? 4 : 6;
   static constexpr uint32_t A_BYTES = BM * BK * 2;
   static constexpr uint32_t B_BYTES = BN * BK * 2;
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr uint32_t SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr uint32_t X_BYTES = is_resid(EPI) ? 2 * XCHUNK : 0;
+  static constexpr uint32_t SMEM = STAGES * STAGE_BYTES + X_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 };
 
 __device__ __forceinline__ float gelu_erf(float v) { return 0.5f * v * (1.f + erff(v * 0.70710678118654752f)); }
@@ -52,27 +63,33 @@ __device__ __forceinline__ void store_bf16x32(bf16* dst, const float (&v)[32]) {
   }
 }
 
-template <int BN, int EPI>
+// BN: MMA tile width; NSUB: sub-tiles per full-row unit (full-row width H = NSUB * BN).
+template <int BN, int EPI, int NSUB>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
-                   const EpiParams p) {
-  using C = GemmCfg<BN>;
-  constexpr bool FULL_ROW = (EPI == EPI_RESID_LN || EPI == EPI_RESID || EPI == EPI_SCORER);
+                   const __grid_constant__ CUtensorMap tmX, const EpiParams p) {
+  using C = GemmCfg<BN, EPI>;
+  constexpr bool FULL_ROW = is_full_row(EPI);
+  constexpr bool RES = is_resid(EPI);
+  constexpr int H = NSUB * BN;       // full-row width
+  constexpr int NCH = H / 32;        // residual chunks per row
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + C::STAGES * C::A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + C::STAGES * C::B_BYTES);
+  uint8_t* sX = sB + C::STAGES * C::B_BYTES;  // 2 x XCHUNK (1024-aligned) when RES
+  uint64_t* full = reinterpret_cast<uint64_t*>(sX + C::X_BYTES);
   uint64_t* empty = full + C::STAGES;
   uint64_t* tfull = empty + C::STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* xfull = drain + 1;  // 2 barriers
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xfull + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id(), lane = lane_id();
   const int m_tiles = (p.M + BM - 1) / BM;
-  const int n_sub = FULL_ROW ? p.N / BN : 1;
+  const int n_sub = FULL_ROW ? NSUB : 1;
   const int n_per_m = FULL_ROW ? 1 : p.N / BN;
   const int units = m_tiles * n_per_m;
   const int kblocks = p.K / BK;
@@ -91,6 +108,7 @@ __global__ void __launch_bounds__(192, 1)
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], 128);
+      mbar_init(&xfull[b], 1);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -99,6 +117,7 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmW);
+    if (RES) tma_prefetch_desc(&tmX);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, 2 * BN);
@@ -192,24 +211,48 @@ __global__ void __launch_bounds__(192, 1)
       mbar_wait(drain, 0, &no_abort, nullptr, 0);
     }
   } else {
-    // ------------------------------------------------------------ epilogue
+    // ------------------------------------------------------------ epilogue (warps 2..5)
+    // Control flow is uniform across the 128 epilogue threads (named barriers below):
+    // after an abort every wait returns at once and the loops run out without work.
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int trow = q * 32 + lane;
+    const bool xprod = (threadIdx.x == 64);  // issues the residual chunk TMA traffic
     int acc = 0;
-    bool ok = true;
-    for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+    uint32_t gch = 0;                     // residual chunks consumed so far (buffer = gch & 1)
+    uint32_t x_armed[2] = {0u, 0u};       // parity+1 of the last armed phase per buffer
+    for (int u = blockIdx.x; u < units; u += gridDim.x) {
       const int mt = u / n_per_m, nu = u % n_per_m;
-      const int row = mt * BM + trow;
+      const int m0 = mt * BM;
+      const int row = m0 + trow;
       const bool valid = row < p.M;
-      float rsum = 0.f;   // full-row residual sum (LN mean)
-      float score = 0.f;  // scorer dot product
+      float w_n = 0.f, w_mean = 0.f, w_m2 = 0.f;  // Welford state of this row
+      float score = 0.f;
+      if constexpr (RES) {
+        if (xprod && !*abort_flag) {  // prefetch the first two residual chunks of this unit
+#pragma unroll
+          for (int k = 0; k < 2 && k < NCH; ++k) {
+            const uint32_t b = (gch + k) & 1;
+            mbar_arrive_expect_tx(&xfull[b], XCHUNK);
+            tma_load_2d(&tmX, &xfull[b], sX + b * XCHUNK, k * 32, m0);
+            x_armed[b] = 1 + (((gch + k) >> 1) & 1);
+          }
+        }
+      }
+      float4 rc[8], rsn[8];  // RoPE cos/sin of this row's position (QKV epilogue)
+      if constexpr (EPI == EPI_QKV_ROPE) {
+        const int ps = valid ? p.pos[row] : 0;
+        const float4* c4 = reinterpret_cast<const float4*>(p.rope_cos + static_cast<size_t>(ps) * 32);
+        const float4* s4 = reinterpret_cast<const float4*>(p.rope_sin + static_cast<size_t>(ps) * 32);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          rc[i] = c4[i];
+          rsn[i] = s4[i];
+        }
+      }
       for (int s = 0; s < n_sub; ++s) {
         const int buf = acc & 1;
         const uint32_t aph = (acc >> 1) & 1;
-        if (!mbar_wait(&tfull[buf], aph, abort_flag, p.err, 4)) {
-          ok = false;
-          break;
-        }
+        mbar_wait(&tfull[buf], aph, abort_flag, p.err, 4);
         tc_fence_after();
         const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
         const int n0 = (FULL_ROW ? s : nu) * BN;
@@ -232,9 +275,6 @@ __global__ void __launch_bounds__(192, 1)
             if (valid) store_bf16x32(p.out + static_cast<size_t>(row) * p.ldo + col, v);
           }
         } else if constexpr (EPI == EPI_QKV_ROPE) {
-          const int ps = valid ? p.pos[row] : 0;
-          const float* cs = p.rope_cos + static_cast<size_t>(ps) * 32;
-          const float* sn = p.rope_sin + static_cast<size_t>(ps) * 32;
 #pragma unroll 1
           for (int g = 0; g < BN / 64; ++g) {
             uint32_t lo[32], hi[32];
@@ -245,11 +285,16 @@ __global__ void __launch_bounds__(192, 1)
             float a[32], b[32];
             if (col < p.rope_cols) {
 #pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                const float x = __uint_as_float(lo[j]), y = __uint_as_float(hi[j]);
-                const float c = cs[j], sv = sn[j];
-                a[j] = x * c - y * sv;
-                b[j] = y * c + x * sv;
+              for (int i = 0; i < 8; ++i) {
+                const float cc[4] = {rc[i].x, rc[i].y, rc[i].z, rc[i].w};
+                const float ss[4] = {rsn[i].x, rsn[i].y, rsn[i].z, rsn[i].w};
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                  const int j = 4 * i + k;
+                  const float x = __uint_as_float(lo[j]), y = __uint_as_float(hi[j]);
+                  a[j] = x * cc[k] - y * ss[k];
+                  b[j] = y * cc[k] + x * ss[k];
+                }
               }
             } else {
 #pragma unroll
@@ -277,33 +322,63 @@ __global__ void __launch_bounds__(192, 1)
             for (int j = 0; j < 32; ++j) v[j] = gelu_erf(__uint_as_float(ra[j])) * __uint_as_float(rb[j]);
             if (valid) store_bf16x32(p.out + static_cast<size_t>(row) * p.ldo + nu * 128 + c * 32, v);
           }
-        } else if constexpr (EPI == EPI_RESID_LN || EPI == EPI_RESID) {
+        } else if constexpr (RES) {
 #pragma unroll 1
-          for (int c = 0; c < BN / 32; ++c) {
+          for (int cc = 0; cc < BN / 32; ++cc) {
+            const int c = s * (BN / 32) + cc;  // chunk index within the row
+            const uint32_t b = gch & 1;
             uint32_t r[32];
-            tmem_ld32(tb + c * 32, r);
+            tmem_ld32(tb + cc * 32, r);
             tmem_ld_wait();
-            const int col = n0 + c * 32;
-            if (valid) {
-              float4* xr = reinterpret_cast<float4*>(p.x + static_cast<size_t>(row) * p.ldx + col);
+            mbar_wait(&xfull[b], (gch >> 1) & 1, abort_flag, p.err, 5);
+            // this row's 32 residual values, 128B-swizzled: 16-byte unit i sits at i ^ (row & 7)
+            uint8_t* xrow = sX + b * XCHUNK + trow * 128;
+            float v[32];
 #pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                float4 o = xr[i];
-                float b0 = 0.f, b1 = 0.f, b2 = 0.f, b3 = 0.f;
-                if (p.bias) {
-                  b0 = p.bias[col + 4 * i];
-                  b1 = p.bias[col + 4 * i + 1];
-                  b2 = p.bias[col + 4 * i + 2];
-                  b3 = p.bias[col + 4 * i + 3];
-                }
-                o.x += __uint_as_float(r[4 * i]) + b0;
-                o.y += __uint_as_float(r[4 * i + 1]) + b1;
-                o.z += __uint_as_float(r[4 * i + 2]) + b2;
-                o.w += __uint_as_float(r[4 * i + 3]) + b3;
-                xr[i] = o;
-                rsum += (o.x + o.y) + (o.z + o.w);
+            for (int i = 0; i < 8; ++i) {
+              float4* slot = reinterpret_cast<float4*>(xrow + ((static_cast<uint32_t>(i) ^ (trow & 7)) << 4));
+              float4 o = *slot;
+              const int col = c * 32 + 4 * i;
+              float4 bb = make_float4(0.f, 0.f, 0.f, 0.f);
+              if (p.bias) bb = *reinterpret_cast<const float4*>(p.bias + col);
+              o.x += __uint_as_float(r[4 * i + 0]) + bb.x;
+              o.y += __uint_as_float(r[4 * i + 1]) + bb.y;
+              o.z += __uint_as_float(r[4 * i + 2]) + bb.z;
+              o.w += __uint_as_float(r[4 * i + 3]) + bb.w;
+              *slot = o;
+              v[4 * i + 0] = o.x;
+              v[4 * i + 1] = o.y;
+              v[4 * i + 2] = o.z;
+              v[4 * i + 3] = o.w;
+            }
+            if constexpr (EPI == EPI_RESID_LN) {
+              // chunk mean / M2 (two-pass over registers), merged into the row's running state
+              float cs = 0.f;
+#pragma unroll
+              for (int j = 0; j < 32; ++j) cs += v[j];
+              const float cm = cs * (1.f / 32.f);
+              float c2 = 0.f;
+#pragma unroll
+              for (int j = 0; j < 32; ++j) c2 += (v[j] - cm) * (v[j] - cm);
+              const float n_new = w_n + 32.f;
+              const float delta = cm - w_mean;
+              w_mean += delta * (32.f / n_new);
+              w_m2 += c2 + delta * delta * (w_n * 32.f / n_new);
+              w_n = n_new;
+            }
+            fence_proxy_async_smem();
+            named_bar_sync(1, 128);
+            if (xprod && !*abort_flag) {
+              tma_store_2d(&tmX, sX + b * XCHUNK, c * 32, m0);
+              bulk_commit();
+              if (c + 2 < NCH) {
+                bulk_wait_read_all();  // buffer b free again
+                mbar_arrive_expect_tx(&xfull[b], XCHUNK);
+                tma_load_2d(&tmX, &xfull[b], sX + b * XCHUNK, (c + 2) * 32, m0);
+                x_armed[b] = 1 + (((gch + 2) >> 1) & 1);
               }
             }
+            ++gch;
           }
         } else if constexpr (EPI == EPI_SCORER) {
 #pragma unroll 1
@@ -321,36 +396,68 @@ __global__ void __launch_bounds__(192, 1)
         mbar_arrive(&tempty[buf]);
         ++acc;
       }
-      if (!ok) break;
+      if constexpr (RES) {
+        // the updated rows must be in global memory before they are re-read below / by the next kernel
+        if (xprod) {
+          bulk_wait_all();
+          fence_proxy_async_global();
+        }
+        named_bar_sync(1, 128);
+      }
       if constexpr (EPI == EPI_RESID_LN) {
-        if (valid) {
-          // Two-pass LayerNorm over the updated row (re-read from L1/L2).
-          const float inv_n = 1.f / static_cast<float>(p.N);
-          const float mean = rsum * inv_n;
-          const float4* xr = reinterpret_cast<const float4*>(p.x + static_cast<size_t>(row) * p.ldx);
-          float ss = 0.f;
-          for (int i = 0; i < p.N / 4; ++i) {
-            const float4 v = xr[i];
-            const float a = v.x - mean, b = v.y - mean, c = v.z - mean, d = v.w - mean;
-            ss += (a * a + b * b) + (c * c + d * d);
+        fence_proxy_async_global();
+        // per-row statistics live in the row's thread; the warp normalizes its 32 rows with
+        // coalesced loads (lane = 4 consecutive columns per 128-column slice), RB rows in flight
+        constexpr int NV = H / 128;
+        constexpr int RB = (NV <= 3) ? 8 : 4;
+        const float rstd = rsqrtf(w_m2 * (1.f / static_cast<float>(H)) + p.ln_eps);
+        float4 gw[NV], gb[NV];
+#pragma unroll
+        for (int v = 0; v < NV; ++v) {
+          gw[v] = reinterpret_cast<const float4*>(p.ln_w)[v * 32 + lane];
+          gb[v] = p.ln_b ? reinterpret_cast<const float4*>(p.ln_b)[v * 32 + lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        const int wrow0 = m0 + q * 32;
+#pragma unroll 1
+        for (int rr = 0; rr < 32; rr += RB) {
+          float4 xv[RB][NV];
+#pragma unroll
+          for (int k = 0; k < RB; ++k) {
+            const int rw = wrow0 + rr + k;
+            if (rw < p.M) {
+              const float4* src = reinterpret_cast<const float4*>(p.x + static_cast<size_t>(rw) * p.ldx);
+#pragma unroll
+              for (int v = 0; v < NV; ++v) xv[k][v] = __ldcg(src + v * 32 + lane);
+            }
           }
-          const float rstd = rsqrtf(ss * inv_n + p.ln_eps);
-          uint2* dst = reinterpret_cast<uint2*>(p.xn + static_cast<size_t>(row) * p.ldxn);
-          const float4* w4 = reinterpret_cast<const float4*>(p.ln_w);
-          const float4* b4 = reinterpret_cast<const float4*>(p.ln_b);
-          for (int i = 0; i < p.N / 4; ++i) {
-            const float4 v = xr[i];
-            const float4 g = w4[i];
-            float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (p.ln_b) b = b4[i];
-            uint2 o;
-            o.x = pack_bf16x2((v.x - mean) * rstd * g.x + b.x, (v.y - mean) * rstd * g.y + b.y);
-            o.y = pack_bf16x2((v.z - mean) * rstd * g.z + b.z, (v.w - mean) * rstd * g.w + b.w);
-            dst[i] = o;
+#pragma unroll
+          for (int k = 0; k < RB; ++k) {
+            const int rw = wrow0 + rr + k;
+            const float mu = __shfl_sync(0xffffffffu, w_mean, rr + k);
+            const float rs = __shfl_sync(0xffffffffu, rstd, rr + k);
+            if (rw < p.M) {
+              uint2* dst = reinterpret_cast<uint2*>(p.xn + static_cast<size_t>(rw) * p.ldxn);
+#pragma unroll
+              for (int v = 0; v < NV; ++v) {
+                const float4 a = xv[k][v], g = gw[v], bb = gb[v];
+                uint2 o;
+                o.x = pack_bf16x2((a.x - mu) * rs * g.x + bb.x, (a.y - mu) * rs * g.y + bb.y);
+                o.y = pack_bf16x2((a.z - mu) * rs * g.z + bb.z, (a.w - mu) * rs * g.w + bb.w);
+                dst[v * 32 + lane] = o;
+              }
+            }
           }
         }
       } else if constexpr (EPI == EPI_SCORER) {
         if (valid) p.scores[row] = score + p.b2;
+      }
+    }
+    if constexpr (RES) {
+      if (xprod) {  // nothing of ours may still be in flight into or out of smem at exit
+        bulk_wait_all();
+        volatile int no_abort = 0;
+        for (int b = 0; b < 2; ++b)
+          if (x_armed[b]) mbar_wait(&xfull[b], x_armed[b] - 1, &no_abort, nullptr, 0);
       }
     }
   }
@@ -361,22 +468,34 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 1) tmem_dealloc(tmem_base, 2 * BN);
 }
 
-template <int BN, int EPI>
-int launch_one(const CUtensorMap& tmA, const CUtensorMap& tmW, const EpiParams& p, int grid_limit,
-               cudaStream_t stream) {
-  static bool configured = false;  // per instantiation; attribute set is idempotent
-  auto kern = gemm_tc_kernel<BN, EPI>;
+template <int BN, int EPI, int NSUB>
+int launch_one(const CUtensorMap& tmA, const CUtensorMap& tmW, const CUtensorMap& tmX, const EpiParams& p,
+               int grid_limit, cudaStream_t stream) {
+  static bool configured = false;  // per instantiation; the attribute set is idempotent
+  auto kern = gemm_tc_kernel<BN, EPI, NSUB>;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<BN>::SMEM);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<BN, EPI>::SMEM);
     if (e != cudaSuccess) return static_cast<int>(e);
     configured = true;
   }
-  constexpr bool FULL_ROW = (EPI == EPI_RESID_LN || EPI == EPI_RESID || EPI == EPI_SCORER);
-  const int units = ((p.M + BM - 1) / BM) * (FULL_ROW ? 1 : p.N / BN);
+  const int units = ((p.M + BM - 1) / BM) * (is_full_row(EPI) ? 1 : p.N / BN);
   const int grid = units < grid_limit ? units : grid_limit;
   if (grid <= 0) return 0;
-  kern<<<grid, 192, GemmCfg<BN>::SMEM, stream>>>(tmA, tmW, p);
+  kern<<<grid, 192, GemmCfg<BN, EPI>::SMEM, stream>>>(tmA, tmW, tmX, p);
   return static_cast<int>(cudaGetLastError());
+}
+
+template <int EPI>
+int launch_full_row(int H, const CUtensorMap& tmA, const CUtensorMap& tmW, const CUtensorMap& tmX,
+                    const EpiParams& p, int grid_limit, cudaStream_t stream) {
+  switch (H) {
+    case 256: return launch_one<256, EPI, 1>(tmA, tmW, tmX, p, grid_limit, stream);
+    case 384: return launch_one<128, EPI, 3>(tmA, tmW, tmX, p, grid_limit, stream);
+    case 512: return launch_one<256, EPI, 2>(tmA, tmW, tmX, p, grid_limit, stream);
+    case 768: return launch_one<256, EPI, 3>(tmA, tmW, tmX, p, grid_limit, stream);
+    case 1024: return launch_one<256, EPI, 4>(tmA, tmW, tmX, p, grid_limit, stream);
+  }
+  return static_cast<int>(cudaErrorInvalidValue);
 }
 
 }  // namespace
@@ -389,27 +508,33 @@ const char* gemm_shape_error(GemmEpi epi, int bn, int M, int N, int K) {
   if (K % BK != 0) return "GEMM K must be a multiple of 64";
   if (N % bn != 0) return "GEMM N must be a multiple of the tile width";
   if (epi == EPI_GEGLU && bn != 256) return "GEGLU epilogue needs 256-wide tiles";
-  if (epi == EPI_QKV_ROPE && bn % 64 != 0) return "RoPE epilogue needs whole heads per tile";
+  if (is_full_row(epi) && !(N == 256 || N == 384 || N == 512 || N == 768 || N == 1024))
+    return "full-row epilogues support N in {256, 384, 512, 768, 1024}";
   return nullptr;
 }
 
-int launch_gemm(GemmEpi epi, int bn, const CUtensorMap& tmA, const CUtensorMap& tmW, const EpiParams& p,
-                int grid_limit, cudaStream_t stream) {
+int launch_gemm(GemmEpi epi, int bn, const CUtensorMap& tmA, const CUtensorMap& tmW, const CUtensorMap* tmX,
+                const EpiParams& p, int grid_limit, cudaStream_t stream) {
   if (p.M == 0) return 0;
-#define J1_GEMM_CASE(E)                                                                  \
-  case E:                                                                                \
-    return bn == 256 ? launch_one<256, E>(tmA, tmW, p, grid_limit, stream)               \
-                     : launch_one<128, E>(tmA, tmW, p, grid_limit, stream);
+  const CUtensorMap& X = tmX ? *tmX : tmA;  // unused by non-residual epilogues
   switch (epi) {
-    J1_GEMM_CASE(EPI_BF16)
-    J1_GEMM_CASE(EPI_QKV_ROPE)
-    J1_GEMM_CASE(EPI_RESID_LN)
-    J1_GEMM_CASE(EPI_RESID)
-    J1_GEMM_CASE(EPI_SCORER)
+    case EPI_BF16:
+      return bn == 256 ? launch_one<256, EPI_BF16, 1>(tmA, tmW, X, p, grid_limit, stream)
+                       : launch_one<128, EPI_BF16, 1>(tmA, tmW, X, p, grid_limit, stream);
+    case EPI_QKV_ROPE:
+      return bn == 256 ? launch_one<256, EPI_QKV_ROPE, 1>(tmA, tmW, X, p, grid_limit, stream)
+                       : launch_one<128, EPI_QKV_ROPE, 1>(tmA, tmW, X, p, grid_limit, stream);
     case EPI_GEGLU:
-      return launch_one<256, EPI_GEGLU>(tmA, tmW, p, grid_limit, stream);
+      return launch_one<256, EPI_GEGLU, 1>(tmA, tmW, X, p, grid_limit, stream);
+    case EPI_RESID_LN:
+      if (!tmX) return static_cast<int>(cudaErrorInvalidValue);
+      return launch_full_row<EPI_RESID_LN>(p.N, tmA, tmW, X, p, grid_limit, stream);
+    case EPI_RESID:
+      if (!tmX) return static_cast<int>(cudaErrorInvalidValue);
+      return launch_full_row<EPI_RESID>(p.N, tmA, tmW, X, p, grid_limit, stream);
+    case EPI_SCORER:
+      return launch_full_row<EPI_SCORER>(p.N, tmA, tmW, X, p, grid_limit, stream);
   }
-#undef J1_GEMM_CASE
   return static_cast<int>(cudaErrorInvalidValue);
 }
 
@@ -429,10 +554,9 @@ EncodeTiledFn encode_fn() {
   }();
   return fn;
 }
-}  // namespace
 
-bool make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld,
-                    uint32_t box_rows, const char** why) {
+bool make_tmap(CUtensorMap* map, CUtensorMapDataType dt, uint32_t esize, const void* base, uint64_t rows,
+               uint64_t cols, uint64_t ld, uint32_t box_cols, uint32_t box_rows, const char** why) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) {
     if (why) *why = "cuTensorMapEncodeTiled unavailable";
@@ -440,17 +564,27 @@ bool make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t 
   }
   if (rows == 0) rows = 1;  // an empty operand is never loaded; keep the map encodable
   const cuuint64_t dims[2] = {cols, rows};
-  const cuuint64_t strides[1] = {ld * 2};
-  const cuuint32_t box[2] = {64, box_rows};
+  const cuuint64_t strides[1] = {ld * esize};
+  const cuuint32_t box[2] = {box_cols, box_rows};
   const cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     if (why) *why = "cuTensorMapEncodeTiled failed (alignment or shape)";
     return false;
   }
   return true;
+}
+}  // namespace
+
+bool make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld,
+                    uint32_t box_rows, const char** why) {
+  return make_tmap(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, rows, cols, ld, 64, box_rows, why);
+}
+
+bool make_tmap_f32_resid(CUtensorMap* map, const float* base, uint64_t rows, uint64_t cols, uint64_t ld,
+                         const char** why) {
+  return make_tmap(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, rows, cols, ld, 32, 128, why);
 }
 
 }  // namespace j1rt

@@ -46,9 +46,10 @@ struct EpiParams {
 
 // Column width of one MMA tile for an N (or full-row width): 256 when N % 256 == 0, else 128.
 int gemm_bn_for(int n);
-// Returns 0 on success, or a cudaError_t value.
-int launch_gemm(GemmEpi epi, int bn, const CUtensorMap& tmA, const CUtensorMap& tmW, const EpiParams& p,
-                int grid_limit, cudaStream_t stream);
+// Returns 0 on success, or a cudaError_t value. tmX: FP32 residual map (make_tmap_f32_resid)
+// over p.x, required by EPI_RESID_LN / EPI_RESID, ignored otherwise (may be null).
+int launch_gemm(GemmEpi epi, int bn, const CUtensorMap& tmA, const CUtensorMap& tmW, const CUtensorMap* tmX,
+                const EpiParams& p, int grid_limit, cudaStream_t stream);
 // Validates shapes for an epilogue; returns nullptr when fine, else a message.
 const char* gemm_shape_error(GemmEpi epi, int bn, int M, int N, int K);
 
@@ -79,5 +80,8 @@ bool hidden_supported(int hidden);
 // 2D bf16 row-major [rows, cols] with row stride `ld` elements; 128B swizzle box (64 x box_rows).
 bool make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld,
                     uint32_t box_rows, const char** why);
+// 2D fp32 row-major residual [rows, cols] (row stride `ld` elements); 128B-swizzled 32 x 128 box.
+bool make_tmap_f32_resid(CUtensorMap* map, const float* base, uint64_t rows, uint64_t cols, uint64_t ld,
+                         const char** why);
 
 }  // namespace j1rt

@@ -62,11 +62,46 @@ namespace {
     if (e_ != cudaSuccess) return cuda_error(e_, what);  \
   } while (0)
 
-#define J1_TRY_LAUNCH(expr, what)                                                  \
-  do {                                                                             \
-    int rc_ = (expr);                                                              \
-    if (rc_ != 0) return cuda_error(static_cast<cudaError_t>(rc_), what);          \
-    ++model->launches;                                                             \
+// Kernel families for j1_model_profile (order of j1_profile_family_name).
+enum Family {
+  F_EMBED = 0, F_QKV, F_ATTN_LOCAL, F_ATTN_GLOBAL, F_WO, F_WI, F_WO2, F_FINAL, F_HEAD_GEMM, F_HEAD_ATTN,
+  F_HEAD_ROWS, F_SCORER
+};
+const char* const kFamilyNames[J1_PROF_FAMILIES] = {
+    "embed_ln", "gemm_qkv_rope", "attn_local", "attn_global", "gemm_wo_resid_ln", "gemm_wi_geglu",
+    "gemm_wo2_resid_ln", "final_norm", "head_gemm", "head_attn", "head_gather", "scorer_gemm"};
+
+cudaEvent_t* prof_slot(j1_model* model, int fam) {
+  const size_t need = 2 * (model->prof_used + 1);
+  while (model->prof_ev.size() < need) {
+    cudaEvent_t e;
+    if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+    model->prof_ev.push_back(e);
+  }
+  if (model->prof_fam.size() < model->prof_used + 1) model->prof_fam.resize(model->prof_used + 1);
+  model->prof_fam[model->prof_used] = fam;
+  return &model->prof_ev[2 * model->prof_used++];
+}
+
+void prof_fold(j1_model* model) {
+  for (size_t i = 0; i < model->prof_used; ++i) {
+    float ms = 0.f;
+    if (cudaEventElapsedTime(&ms, model->prof_ev[2 * i], model->prof_ev[2 * i + 1]) == cudaSuccess) {
+      model->prof_ms[model->prof_fam[i]] += ms;
+      model->prof_cnt[model->prof_fam[i]] += 1;
+    }
+  }
+  model->prof_used = 0;
+}
+
+#define J1_TRY_LAUNCH(fam, expr, what)                                                       \
+  do {                                                                                       \
+    cudaEvent_t* ev_ = model->prof_on ? prof_slot(model, (fam)) : nullptr;                   \
+    if (ev_) cudaEventRecord(ev_[0], model->stream);                                         \
+    int rc_ = (expr);                                                                        \
+    if (rc_ != 0) return cuda_error(static_cast<cudaError_t>(rc_), what);                    \
+    if (ev_) cudaEventRecord(ev_[1], model->stream);                                         \
+    ++model->launches;                                                                       \
   } while (0)
 
 j1_status dalloc(j1_model* model, void** p, size_t bytes, std::vector<void*>& list) {
@@ -257,7 +292,9 @@ j1_status stage_batch(j1_model* model, const BatchView& b) {
             make_tmap_bf16(&model->tm_qkv, model->qkv, t, 3 * H, 3 * H, 128, &why) &&
             make_tmap_bf16(&model->tm_cm, model->cm, m, H, H, 128, &why) &&
             make_tmap_bf16(&model->tm_ymb, model->ymb, m, H, H, 128, &why) &&
-            make_tmap_bf16(&model->tm_hm, model->hm, m, FF, FF, 128, &why);
+            make_tmap_bf16(&model->tm_hm, model->hm, m, FF, FF, 128, &why) &&
+            make_tmap_f32_resid(&model->tm_x, model->x, t, H, H, &why) &&
+            make_tmap_f32_resid(&model->tm_ym, model->ym, m, H, H, &why);
   if (!ok) return set_error(J1_ERR_CUDA, std::string("activation tensor map: ") + (why ? why : ""));
   model->staged = true;
   return J1_OK;
@@ -277,7 +314,7 @@ j1_status launch_forward(j1_model* model) {
   std::memset(&base, 0, sizeof(base));
   base.err = model->err_dev;
 
-  J1_TRY_LAUNCH(launch_embed_ln(H, model->d_ids, model->emb, model->emb_norm, model->x, model->xn, t, c.norm_eps, st),
+  J1_TRY_LAUNCH(F_EMBED, launch_embed_ln(H, model->d_ids, model->emb, model->emb_norm, model->x, model->xn, t, c.norm_eps, st),
                 "embed_ln");
   for (int l = 0; l < L; ++l) {
     const auto& ly = model->layers[l];
@@ -286,8 +323,9 @@ j1_status launch_forward(j1_model* model) {
     p.out = model->qkv, p.ldo = 3 * H;
     p.pos = model->d_pos, p.rope_cos = model->rope_cos[ly.rope], p.rope_sin = model->rope_sin[ly.rope];
     p.rope_cols = 2 * H;
-    J1_TRY_LAUNCH(launch_gemm(EPI_QKV_ROPE, bn_qkv, model->tm_xn, ly.tm_wqkv, p, nsm, st), "gemm qkv");
-    J1_TRY_LAUNCH(launch_attention(model->tm_qkv, model->tm_qkv, model->d_tiles, static_cast<int>(model->ntiles),
+    J1_TRY_LAUNCH(F_QKV, launch_gemm(EPI_QKV_ROPE, bn_qkv, model->tm_xn, ly.tm_wqkv, nullptr, p, nsm, st), "gemm qkv");
+    J1_TRY_LAUNCH(ly.global ? F_ATTN_GLOBAL : F_ATTN_LOCAL,
+                  launch_attention(model->tm_qkv, model->tm_qkv, model->d_tiles, static_cast<int>(model->ntiles),
                                    c.heads, 0, H, 2 * H, model->ctx, H, ly.global ? -1 : c.half_window, kScaleLog2,
                                    model->err_dev, st),
                   "attention");
@@ -295,23 +333,23 @@ j1_status launch_forward(j1_model* model) {
     p.M = t, p.N = H, p.K = H;
     p.x = model->x, p.ldx = H;
     p.ln_w = ly.mlp_norm, p.ln_eps = c.norm_eps, p.xn = model->xn, p.ldxn = H;
-    J1_TRY_LAUNCH(launch_gemm(EPI_RESID_LN, bn_full, model->tm_ctx, ly.tm_wo, p, nsm, st), "gemm wo");
+    J1_TRY_LAUNCH(F_WO, launch_gemm(EPI_RESID_LN, bn_full, model->tm_ctx, ly.tm_wo, &model->tm_x, p, nsm, st), "gemm wo");
     p = base;
     p.M = t, p.N = 2 * I, p.K = H;
     p.out = model->g, p.ldo = I;
-    J1_TRY_LAUNCH(launch_gemm(EPI_GEGLU, 256, model->tm_xn, ly.tm_wi, p, nsm, st), "gemm wi");
+    J1_TRY_LAUNCH(F_WI, launch_gemm(EPI_GEGLU, 256, model->tm_xn, ly.tm_wi, nullptr, p, nsm, st), "gemm wi");
     p = base;
     p.M = t, p.N = H, p.K = I;
     p.x = model->x, p.ldx = H;
     if (l + 1 < L) {
       p.ln_w = model->layers[l + 1].attn_norm, p.ln_eps = c.norm_eps, p.xn = model->xn, p.ldxn = H;
-      J1_TRY_LAUNCH(launch_gemm(EPI_RESID_LN, bn_full, model->tm_g, ly.tm_wo2, p, nsm, st), "gemm wo2");
+      J1_TRY_LAUNCH(F_WO2, launch_gemm(EPI_RESID_LN, bn_full, model->tm_g, ly.tm_wo2, &model->tm_x, p, nsm, st), "gemm wo2");
     } else {
-      J1_TRY_LAUNCH(launch_gemm(EPI_RESID, bn_full, model->tm_g, ly.tm_wo2, p, nsm, st), "gemm wo2");
+      J1_TRY_LAUNCH(F_WO2, launch_gemm(EPI_RESID, bn_full, model->tm_g, ly.tm_wo2, &model->tm_x, p, nsm, st), "gemm wo2");
     }
   }
   const auto& h0 = model->head[0];
-  J1_TRY_LAUNCH(launch_final_norm(H, model->x, model->final_norm, model->type_emb, model->d_qtype, h0.norm1_w,
+  J1_TRY_LAUNCH(F_FINAL, launch_final_norm(H, model->x, model->final_norm, model->type_emb, model->d_qtype, h0.norm1_w,
                                   h0.norm1_b, model->xn, t, c.norm_eps, st),
                 "final_norm");
   const int nh = static_cast<int>(model->head.size());
@@ -320,8 +358,9 @@ j1_status launch_forward(j1_model* model) {
     EpiParams p = base;
     p.M = t, p.N = 3 * H, p.K = H;
     p.out = model->qkv, p.ldo = 3 * H, p.bias = hl.in_b;
-    J1_TRY_LAUNCH(launch_gemm(EPI_BF16, bn_qkv, model->tm_xn, hl.tm_in, p, nsm, st), "gemm in_proj");
-    J1_TRY_LAUNCH(launch_attention(model->tm_qkv, model->tm_qkv, model->d_tiles, static_cast<int>(model->ntiles),
+    J1_TRY_LAUNCH(F_HEAD_GEMM, launch_gemm(EPI_BF16, bn_qkv, model->tm_xn, hl.tm_in, nullptr, p, nsm, st), "gemm in_proj");
+    J1_TRY_LAUNCH(F_HEAD_ATTN,
+                  launch_attention(model->tm_qkv, model->tm_qkv, model->d_tiles, static_cast<int>(model->ntiles),
                                    c.head_heads, 0, H, 2 * H, model->ctx, H, -1, kScaleLog2, model->err_dev, st),
                   "head attention");
     if (j + 1 < nh) {
@@ -329,38 +368,38 @@ j1_status launch_forward(j1_model* model) {
       p.M = t, p.N = H, p.K = H, p.bias = hl.out_b;
       p.x = model->x, p.ldx = H, p.ln_w = hl.norm2_w, p.ln_b = hl.norm2_b, p.ln_eps = 1e-5f;
       p.xn = model->xn, p.ldxn = H;
-      J1_TRY_LAUNCH(launch_gemm(EPI_RESID_LN, bn_full, model->tm_ctx, hl.tm_out, p, nsm, st), "gemm out_proj");
+      J1_TRY_LAUNCH(F_HEAD_GEMM, launch_gemm(EPI_RESID_LN, bn_full, model->tm_ctx, hl.tm_out, &model->tm_x, p, nsm, st), "gemm out_proj");
       p = base;
       p.M = t, p.N = FF, p.K = H, p.out = model->g, p.ldo = FF, p.bias = hl.lin1_b, p.relu = 1;
-      J1_TRY_LAUNCH(launch_gemm(EPI_BF16, bn_ff, model->tm_xn, hl.tm_lin1, p, nsm, st), "gemm linear1");
+      J1_TRY_LAUNCH(F_HEAD_GEMM, launch_gemm(EPI_BF16, bn_ff, model->tm_xn, hl.tm_lin1, nullptr, p, nsm, st), "gemm linear1");
       const auto& nx = model->head[j + 1];
       p = base;
       p.M = t, p.N = H, p.K = FF, p.bias = hl.lin2_b;
       p.x = model->x, p.ldx = H, p.ln_w = nx.norm1_w, p.ln_b = nx.norm1_b, p.ln_eps = 1e-5f;
       p.xn = model->xn, p.ldxn = H;
-      J1_TRY_LAUNCH(launch_gemm(EPI_RESID_LN, bn_full, model->tm_h, hl.tm_lin2, p, nsm, st), "gemm linear2");
+      J1_TRY_LAUNCH(F_HEAD_GEMM, launch_gemm(EPI_RESID_LN, bn_full, model->tm_h, hl.tm_lin2, &model->tm_x, p, nsm, st), "gemm linear2");
     } else {
       // Last head layer: only the option markers feed the scorer (src/cuda/mod.rs:496-506).
-      J1_TRY_LAUNCH(launch_gather_rows(model->ctx, model->d_markers, model->cm, m, H * 2, st), "gather ctx");
-      J1_TRY_LAUNCH(launch_gather_rows(model->x, model->d_markers, model->ym, m, H * 4, st), "gather x");
+      J1_TRY_LAUNCH(F_HEAD_ROWS, launch_gather_rows(model->ctx, model->d_markers, model->cm, m, H * 2, st), "gather ctx");
+      J1_TRY_LAUNCH(F_HEAD_ROWS, launch_gather_rows(model->x, model->d_markers, model->ym, m, H * 4, st), "gather x");
       p = base;
       p.M = m, p.N = H, p.K = H, p.bias = hl.out_b;
       p.x = model->ym, p.ldx = H, p.ln_w = hl.norm2_w, p.ln_b = hl.norm2_b, p.ln_eps = 1e-5f;
       p.xn = model->ymb, p.ldxn = H;
-      J1_TRY_LAUNCH(launch_gemm(EPI_RESID_LN, bn_full, model->tm_cm, hl.tm_out, p, nsm, st), "gemm out_proj");
+      J1_TRY_LAUNCH(F_HEAD_GEMM, launch_gemm(EPI_RESID_LN, bn_full, model->tm_cm, hl.tm_out, &model->tm_ym, p, nsm, st), "gemm out_proj");
       p = base;
       p.M = m, p.N = FF, p.K = H, p.out = model->hm, p.ldo = FF, p.bias = hl.lin1_b, p.relu = 1;
-      J1_TRY_LAUNCH(launch_gemm(EPI_BF16, bn_ff, model->tm_ymb, hl.tm_lin1, p, nsm, st), "gemm linear1");
+      J1_TRY_LAUNCH(F_HEAD_GEMM, launch_gemm(EPI_BF16, bn_ff, model->tm_ymb, hl.tm_lin1, nullptr, p, nsm, st), "gemm linear1");
       p = base;
       p.M = m, p.N = H, p.K = FF, p.bias = hl.lin2_b;
       p.x = model->ym, p.ldx = H, p.ln_w = model->s_norm_w, p.ln_b = model->s_norm_b, p.ln_eps = 1e-5f;
       p.xn = model->ymb, p.ldxn = H;
-      J1_TRY_LAUNCH(launch_gemm(EPI_RESID_LN, bn_full, model->tm_hm, hl.tm_lin2, p, nsm, st), "gemm linear2");
+      J1_TRY_LAUNCH(F_HEAD_GEMM, launch_gemm(EPI_RESID_LN, bn_full, model->tm_hm, hl.tm_lin2, &model->tm_ym, p, nsm, st), "gemm linear2");
     }
   }
   EpiParams p = base;
   p.M = m, p.N = H, p.K = H, p.bias = model->s_b1, p.w2 = model->s_w2, p.b2 = model->s_b2, p.scores = model->scores;
-  J1_TRY_LAUNCH(launch_gemm(EPI_SCORER, bn_full, model->tm_ymb, model->tm_s_w1, p, nsm, st), "gemm scorer");
+  J1_TRY_LAUNCH(F_SCORER, launch_gemm(EPI_SCORER, bn_full, model->tm_ymb, model->tm_s_w1, nullptr, p, nsm, st), "gemm scorer");
   return J1_OK;
 }
 
@@ -374,6 +413,7 @@ j1_status finish_forward(j1_model* model, float* scores_out, size_t m) {
   J1_TRY_CUDA(cudaMemcpyAsync(model->err_host, model->err_dev, 4, cudaMemcpyDeviceToHost, model->stream),
               "error word readback");
   J1_TRY_CUDA(cudaStreamSynchronize(model->stream), "forward");
+  prof_fold(model);
   if (*model->err_host != 0) {
     const int code = *model->err_host;
     cudaMemsetAsync(model->err_dev, 0, 4, model->stream);
@@ -519,6 +559,7 @@ void destroy_model(j1_model* model) {
   DeviceGuard guard(model->device);
   if (model->stream) cudaStreamSynchronize(model->stream);
   free_workspace(model);
+  for (cudaEvent_t e : model->prof_ev) cudaEventDestroy(e);
   for (void* p : model->allocations) cudaFree(p);
   if (model->err_host) cudaFreeHost(model->err_host);
   if (model->stream) cudaStreamDestroy(model->stream);
@@ -679,6 +720,28 @@ void* j1_model_stream(j1_model* model) { return model ? static_cast<void*>(model
 
 int64_t j1_model_launch_count(const j1_model* model) { return model ? model->launches : 0; }
 
+j1_status j1_model_profile(j1_model* model, int enable) {
+  if (!model) return set_error(J1_ERR_INVALID_ARG, "NULL model");
+  std::lock_guard<std::mutex> lk(model->mu);
+  DeviceGuard guard(model->device);
+  J1_TRY_CUDA(cudaStreamSynchronize(model->stream), "profile");
+  prof_fold(model);
+  model->prof_on = enable != 0;
+  for (int i = 0; i < J1_PROF_FAMILIES; ++i) model->prof_ms[i] = 0.0, model->prof_cnt[i] = 0;
+  return J1_OK;
+}
+
+j1_status j1_model_profile_read(j1_model* model, double* ms, int64_t* launches) {
+  if (!model || !ms || !launches) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+  std::lock_guard<std::mutex> lk(model->mu);
+  for (int i = 0; i < J1_PROF_FAMILIES; ++i) ms[i] = model->prof_ms[i], launches[i] = model->prof_cnt[i];
+  return J1_OK;
+}
+
+const char* j1_profile_family_name(int family) {
+  return (family >= 0 && family < J1_PROF_FAMILIES) ? kFamilyNames[family] : "";
+}
+
 j1_status j1_op_gemm(const j1_gemm_args* a, void* stream, int sync) {
   if (!a || !a->A || !a->W) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
   const GemmEpi epi = static_cast<GemmEpi>(a->epilogue);
@@ -686,7 +749,8 @@ j1_status j1_op_gemm(const j1_gemm_args* a, void* stream, int sync) {
   const int bn = (epi == EPI_GEGLU) ? 256 : gemm_bn_for(a->N);
   if (const char* why = gemm_shape_error(epi, bn, a->M, a->N, a->K)) return set_error(J1_ERR_UNSUPPORTED, why);
   const bool full_row = epi == EPI_RESID_LN || epi == EPI_RESID || epi == EPI_SCORER;
-  if (full_row && a->N / bn > 4) return set_error(J1_ERR_UNSUPPORTED, "full-row epilogue supports N <= 1024");
+  if (full_row && a->M > 0 && epi != EPI_SCORER && (a->ldx < a->N || a->ldx % 4 != 0))
+    return set_error(J1_ERR_INVALID_ARG, "ldx must be >= N and a multiple of 4");
   if ((epi == EPI_BF16 || epi == EPI_QKV_ROPE || epi == EPI_GEGLU) && !a->out)
     return set_error(J1_ERR_INVALID_ARG, "out is NULL");
   if ((epi == EPI_RESID_LN || epi == EPI_RESID) && !a->x) return set_error(J1_ERR_INVALID_ARG, "x is NULL");
@@ -697,10 +761,13 @@ j1_status j1_op_gemm(const j1_gemm_args* a, void* stream, int sync) {
   OpState* os;
   j1_status s = op_state(&os);
   if (s) return s;
-  CUtensorMap tmA, tmW;
+  CUtensorMap tmA, tmW, tmX;
   const char* why = nullptr;
   if (!make_tmap_bf16(&tmA, a->A, a->M, a->K, a->K, 128, &why) ||
       !make_tmap_bf16(&tmW, a->W, a->N, a->K, a->K, bn, &why))
+    return set_error(J1_ERR_INVALID_ARG, std::string("tensor map: ") + (why ? why : ""));
+  const bool resid = epi == EPI_RESID_LN || epi == EPI_RESID;
+  if (resid && !make_tmap_f32_resid(&tmX, a->x, a->M, a->N, a->ldx, &why))
     return set_error(J1_ERR_INVALID_ARG, std::string("tensor map: ") + (why ? why : ""));
   EpiParams p;
   std::memset(&p, 0, sizeof(p));
@@ -715,7 +782,7 @@ j1_status j1_op_gemm(const j1_gemm_args* a, void* stream, int sync) {
   p.err = os->err;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int grid = a->grid_limit > 0 ? a->grid_limit : os->num_sms;
-  int rc = launch_gemm(epi, bn, tmA, tmW, p, grid, st);
+  int rc = launch_gemm(epi, bn, tmA, tmW, resid ? &tmX : nullptr, p, grid, st);
   if (rc) return cuda_error(static_cast<cudaError_t>(rc), "gemm launch");
   return sync ? op_sync_check(os, st) : J1_OK;
 }

@@ -102,5 +102,14 @@ struct j1_model {
   int *d_ids = nullptr, *d_pos = nullptr, *d_qtype = nullptr, *d_markers = nullptr;
   j1rt::AttnTile* d_tiles = nullptr;
   CUtensorMap tm_xn, tm_ctx, tm_g, tm_h, tm_qkv, tm_cm, tm_ymb, tm_hm;
+  CUtensorMap tm_x, tm_ym;  // FP32 residual streams (tokens, markers)
   int64_t launches = 0;
+
+  // ---- optional per-launch CUDA-event timing by kernel family (j1_model_profile)
+  bool prof_on = false;
+  std::vector<cudaEvent_t> prof_ev;     // pool: 2 per recorded launch
+  std::vector<int> prof_fam;            // family of each recorded launch
+  size_t prof_used = 0;                 // recorded launches not yet accumulated
+  double prof_ms[J1_PROF_FAMILIES] = {0};
+  int64_t prof_cnt[J1_PROF_FAMILIES] = {0};
 };

@@ -29,7 +29,9 @@ EXPORTS = [
     "j1_engine_options_default", "j1_engine_create", "j1_engine_create_pool", "j1_engine_destroy",
     "j1_engine_device_name", "j1_engine_logits_encoded",
     "j1_op_gemm", "j1_op_attention", "j1_op_geglu_interleave",
+    "j1_model_profile", "j1_model_profile_read", "j1_profile_family_name",
 ]
+PROF_FAMILIES = 12
 
 EPI_BF16, EPI_QKV_ROPE, EPI_GEGLU, EPI_RESID_LN, EPI_RESID, EPI_SCORER = range(6)
 
@@ -103,13 +105,18 @@ def lib():
     L.j1_engine_device_name.argtypes = [C.c_void_p, C.c_char_p, C.c_size_t]
     L.j1_engine_device_name.restype = C.c_size_t
     L.j1_engine_logits_encoded.argtypes = [C.c_void_p, C.c_size_t, u32p, u32p, u32p, u32p, u8p, f32p]
+    L.j1_model_profile.argtypes = [C.c_void_p, C.c_int]
+    L.j1_model_profile_read.argtypes = [C.c_void_p, C.POINTER(C.c_double), C.POINTER(C.c_int64)]
+    L.j1_profile_family_name.argtypes = [C.c_int]
+    L.j1_profile_family_name.restype = C.c_char_p
     L.j1_op_gemm.argtypes = [C.POINTER(J1GemmArgs), C.c_void_p, C.c_int]
     L.j1_op_attention.argtypes = [C.c_void_p, C.c_int64, C.c_int32, u32p, u32p, C.c_size_t, C.c_int32, C.c_void_p,
                                   C.c_void_p, C.c_int]
     L.j1_op_geglu_interleave.argtypes = [C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_void_p]
     for fn in ("j1_config_load", "j1_model_create", "j1_model_config", "j1_model_forward", "j1_model_stage",
                "j1_model_launch", "j1_model_finish", "j1_engine_create", "j1_engine_create_pool",
-               "j1_engine_logits_encoded", "j1_op_gemm", "j1_op_attention", "j1_op_geglu_interleave"):
+               "j1_engine_logits_encoded", "j1_op_gemm", "j1_op_attention", "j1_op_geglu_interleave",
+               "j1_model_profile", "j1_model_profile_read"):
         getattr(L, fn).restype = C.c_int
     _lib = L
     return L
@@ -278,6 +285,17 @@ class CudaModel:
 
     def launch_count(self):
         return int(lib().j1_model_launch_count(self._h))
+
+    def profile(self, enable=True):
+        """Per-launch CUDA-event timing by kernel family (j1_model_profile)."""
+        check(lib().j1_model_profile(self._h, 1 if enable else 0))
+
+    def profile_read(self):
+        """{family: (total_ms, launches)} accumulated since profile(True)."""
+        ms = (C.c_double * PROF_FAMILIES)()
+        n = (C.c_int64 * PROF_FAMILIES)()
+        check(lib().j1_model_profile_read(self._h, ms, n))
+        return {lib().j1_profile_family_name(i).decode(): (ms[i], n[i]) for i in range(PROF_FAMILIES)}
 
 
 # ------------------------------------------------------------------ Engine
