@@ -54,7 +54,9 @@ int launch_gemm(GemmEpi epi, int bn, const CUtensorMap& tmA, const CUtensorMap& 
 const char* gemm_shape_error(GemmEpi epi, int bn, int M, int N, int K);
 
 // ------------------------------------------------------------------ attention
-// One 128-query tile of one sequence. Query row r of the tile is Q-buffer row
+// Queries covered by one attention CTA (two 128-query tiles).
+int attention_pair_queries();
+// One CTA's queries (up to attention_pair_queries()) of one sequence. Query row r of the tile is Q-buffer row
 // q_row0 + r at sequence position q_pos0 + r; keys/values are rows
 // kv_row0 .. kv_row0 + kv_len - 1 of the K/V buffer.
 struct AttnTile {
@@ -62,9 +64,10 @@ struct AttnTile {
 };
 // ctx[q_row0 + r, head*64 ..] = softmax(scale * q k^T [band]) v for every tile x head.
 // window < 0: full attention; else |qpos - kpos| <= window.
+// Persistent: min(ntiles * heads, grid_limit) CTAs walk the (tile pair, head) items.
 int launch_attention(const CUtensorMap& tmQ, const CUtensorMap& tmKV, const AttnTile* tiles, int ntiles, int heads,
                      int q_col0, int k_col0, int v_col0, bf16* out, int ldo, int window, float scale_log2, int* err,
-                     cudaStream_t stream);
+                     int grid_limit, cudaStream_t stream);
 
 // ------------------------------------------------------------------ row kernels
 int launch_embed_ln(int hidden, const int* ids, const float* table, const float* w, float* x, bf16* xn, int rows,

@@ -242,7 +242,8 @@ j1_status stage_batch(j1_model* model, const BatchView& b) {
   if (s) return s;
   J1_TRY_CUDA(cudaStreamSynchronize(model->stream), "stage");  // pinned staging is reused
   size_t ntiles = 0;
-  for (size_t q = 0; q < b.nseq; ++q) ntiles += (b.lens[q] + 127) / 128;
+  const int PQ = attention_pair_queries();  // queries per attention CTA (two 128-row tiles)
+  for (size_t q = 0; q < b.nseq; ++q) ntiles += (b.lens[q] + PQ - 1) / PQ;
   const size_t t = b.t, m = b.m;
   const size_t tiles_off = (3 * t + m + 7) / 8 * 8;
   const size_t meta_ints = tiles_off + ntiles * 8;
@@ -259,10 +260,10 @@ j1_status stage_batch(j1_model* model, const BatchView& b) {
       h[2 * t + o] = static_cast<int>(b.qtypes[q]);  // per-token qtype (src/cuda/mod.rs:428-432)
       ++o;
     }
-    for (int q0 = 0; q0 < len; q0 += 128) {
+    for (int q0 = 0; q0 < len; q0 += PQ) {
       AttnTile& tl = tiles[ti++];
       tl.q_row0 = start + q0;
-      tl.nq = len - q0 < 128 ? len - q0 : 128;
+      tl.nq = len - q0 < PQ ? len - q0 : PQ;
       tl.kv_row0 = start;
       tl.kv_len = len;
       tl.q_pos0 = q0;
@@ -327,7 +328,7 @@ j1_status launch_forward(j1_model* model) {
     J1_TRY_LAUNCH(ly.global ? F_ATTN_GLOBAL : F_ATTN_LOCAL,
                   launch_attention(model->tm_qkv, model->tm_qkv, model->d_tiles, static_cast<int>(model->ntiles),
                                    c.heads, 0, H, 2 * H, model->ctx, H, ly.global ? -1 : c.half_window, kScaleLog2,
-                                   model->err_dev, st),
+                                   model->err_dev, nsm, st),
                   "attention");
     p = base;
     p.M = t, p.N = H, p.K = H;
@@ -361,7 +362,7 @@ j1_status launch_forward(j1_model* model) {
     J1_TRY_LAUNCH(F_HEAD_GEMM, launch_gemm(EPI_BF16, bn_qkv, model->tm_xn, hl.tm_in, nullptr, p, nsm, st), "gemm in_proj");
     J1_TRY_LAUNCH(F_HEAD_ATTN,
                   launch_attention(model->tm_qkv, model->tm_qkv, model->d_tiles, static_cast<int>(model->ntiles),
-                                   c.head_heads, 0, H, 2 * H, model->ctx, H, -1, kScaleLog2, model->err_dev, st),
+                                   c.head_heads, 0, H, 2 * H, model->ctx, H, -1, kScaleLog2, model->err_dev, nsm, st),
                   "head attention");
     if (j + 1 < nh) {
       p = base;
@@ -795,10 +796,11 @@ j1_status j1_op_attention(const void* qkv, int64_t t, int32_t hidden, const uint
   for (size_t s = 0; s < nseq; ++s) {
     if (seq_lens[s] == 0 || static_cast<int64_t>(seq_starts[s]) + seq_lens[s] > t)
       return set_error(J1_ERR_INVALID_ARG, "sequence outside the qkv buffer");
-    for (uint32_t q0 = 0; q0 < seq_lens[s]; q0 += 128) {
+    const uint32_t PQ = static_cast<uint32_t>(attention_pair_queries());
+    for (uint32_t q0 = 0; q0 < seq_lens[s]; q0 += PQ) {
       AttnTile tl;
       tl.q_row0 = static_cast<int>(seq_starts[s] + q0);
-      tl.nq = static_cast<int>(std::min<uint32_t>(128, seq_lens[s] - q0));
+      tl.nq = static_cast<int>(std::min<uint32_t>(PQ, seq_lens[s] - q0));
       tl.kv_row0 = static_cast<int>(seq_starts[s]);
       tl.kv_len = static_cast<int>(seq_lens[s]);
       tl.q_pos0 = static_cast<int>(q0);
@@ -827,7 +829,7 @@ j1_status j1_op_attention(const void* qkv, int64_t t, int32_t hidden, const uint
   if (!make_tmap_bf16(&tm, qkv, static_cast<uint64_t>(t), 3 * static_cast<uint64_t>(hidden), 3 * hidden, 128, &why))
     return set_error(J1_ERR_INVALID_ARG, std::string("tensor map: ") + (why ? why : ""));
   int rc = launch_attention(tm, tm, os->tiles, static_cast<int>(tiles.size()), hidden / 64, 0, hidden, 2 * hidden,
-                            static_cast<bf16*>(ctx), hidden, window, kScaleLog2, os->err, st);
+                            static_cast<bf16*>(ctx), hidden, window, kScaleLog2, os->err, os->num_sms, st);
   if (rc) return cuda_error(static_cast<cudaError_t>(rc), "attention launch");
   if (sync || !tiles.empty()) return op_sync_check(os, st);  // tiles are host-owned: wait before returning
   return J1_OK;
