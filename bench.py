@@ -292,7 +292,7 @@ def main():
     barrier()
     e2e_s = max_over_ranks(h1 - h0)
     e2e = world * t * args.steps / e2e_s
-    ntiles = sum((n + 255) // 256 for n in batch.lens.tolist())  # attention tile pairs
+    ntiles = sum((n + 127) // 128 for n in batch.lens.tolist())  # 128-query attention tiles
     h2d = ((3 * t + m + 7) // 8 * 8 + 8 * ntiles) * 4
     d2h = m * 4 + 4
 

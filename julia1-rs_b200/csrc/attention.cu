@@ -6,19 +6,23 @@
 // kernels.cu:304-308,332), and P rounded to BF16 before P.V. RoPE is not applied here:
 // the Wqkv GEMM epilogue already rotated q and k.
 //
-// Work item = two consecutive 128-query tiles of one sequence x one head (a "tile pair").
-// The kernel is persistent: one CTA per SM walks items blockIdx.x, +gridDim.x, ... with
-// barrier phases, TMEM and smem set up once; Q is double buffered so the producer
-// fetches the next item's Q and K/V while the current item computes. 320 threads:
-//   warps 0..3  softmax of tile 0, warps 4..7 softmax of tile 1: thread r of a group owns
-//               query row r (TMEM lane r); reads S from TMEM, writes P (bf16, 128B-swizzled,
-//               K-major) to smem; O accumulates in TMEM across the item's key blocks
-//   warp 8      tcgen05.mma issuer: S_t = Q_t K^T (M=128, N=128, K=64) and
-//               O_t = P_t V (M=128, N=64, K=128; V read MN-major)
-//   warp 9      TMA producer: Q_0/Q_1 per item, K/V blocks of 128 keys, double buffered
-// The two tiles share every K/V block they both need; the issuer runs the P.V of one
-// tile and the next Q.K^T of that tile while the other tile's softmax is in flight.
-// TMEM (512 columns): S_0 [0,128), S_1 [128,256), O_0 [256,320), O_1 [320,384).
+// Work item = one 128-query tile of one sequence x one head. The kernel is persistent
+// with two CTAs per SM (their pipelines interleave: one CTA's softmax overlaps the
+// other's MMAs and loads); each CTA walks items blockIdx.x, +gridDim.x, ... with
+// barriers, TMEM and smem set up once. 192 threads per CTA:
+//   warps 0..3  softmax: thread r owns query row r (TMEM lane r); reads S from TMEM,
+//               writes P (bf16 pairs) back to TMEM; O accumulates in TMEM over key blocks
+//   warp 4      tcgen05.mma issuer: S = Q K^T (M=128, N=128, K=64, operands in smem) and
+//               O += P V (M=128, N=64, K=128; P from TMEM, V from smem read MN-major)
+//   warp 5      TMA producer: Q (double buffered across items), K/V blocks of 128 keys
+//               (two stages)
+// TMEM (256 columns): S [0,128), P [128,192) as packed bf16 pairs, O [192,256).
+//
+// Softmax: the first key block of an item computes the row max before the
+// exponentials; later blocks exponentiate with the running offset while tracking the
+// block max, and redo the block (and rescale O) only when the max grew by more than
+// 2^8. P <= 2^8 then, and BF16 rounding of P is relative, so results match the
+// always-rescaled online softmax to rounding.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -33,8 +37,8 @@ constexpr int QT = 128;   // queries per tile
 constexpr int KB = 128;   // keys per block
 constexpr int HD = 64;    // head dim
 constexpr uint32_t TILE_BYTES = 128 * HD * 2;  // 16 KB per Q/K/V box
-constexpr uint32_t P_BYTES = QT * KB * 2;      // 32 KB
-constexpr uint32_t ATT_SMEM = 8 * TILE_BYTES + 2 * P_BYTES + 1024 + 256;
+constexpr uint32_t ATT_SMEM = 6 * TILE_BYTES + 1024 + 256;  // Q x2, K x2, V x2
+constexpr uint32_t TS_COL = 0, TP_COL = 128, TO_COL = 192;
 
 __device__ __forceinline__ float ex2(float x) {
   float y;
@@ -49,70 +53,59 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
   return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, err, site));
 }
 
+// O (+)= P.V with P read from TMEM (A operand, K-major, two bf16 per 32-bit column).
+__device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n"
+      ::"r"(d_tmem), "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
 // Geometry of one work item (identical in every role of the CTA).
 struct Item {
   AttnTile tl;
   int head, kbeg, nb;
-  int jb0, je0, jb1, je1, nq0, nq1;
 };
 
-__device__ __forceinline__ Item item_geometry(const AttnTile* __restrict__ tiles, int npairs, int u, int window) {
+__device__ __forceinline__ Item item_geometry(const AttnTile* __restrict__ tiles, int ntiles, int u, int window) {
   Item it;
-  it.head = u / npairs;
-  it.tl = tiles[u % npairs];
-  const AttnTile& tl = it.tl;
-  int kend = tl.kv_len;
+  it.head = u / ntiles;
+  it.tl = tiles[u % ntiles];
+  int kend = it.tl.kv_len;
   it.kbeg = 0;
   if (window >= 0) {
-    it.kbeg = max(0, tl.q_pos0 - window);
-    kend = min(tl.kv_len, tl.q_pos0 + tl.nq + window);
+    it.kbeg = max(0, it.tl.q_pos0 - window);
+    kend = min(it.tl.kv_len, it.tl.q_pos0 + it.tl.nq + window);
   }
   it.nb = (kend - it.kbeg + KB - 1) / KB;
-  int jb[2], je[2], nq[2];
-#pragma unroll
-  for (int t = 0; t < 2; ++t) {
-    nq[t] = min(max(tl.nq - QT * t, 0), QT);
-    const int qp = tl.q_pos0 + QT * t;
-    if (nq[t] == 0) {
-      jb[t] = je[t] = 0;
-    } else if (window < 0) {
-      jb[t] = 0;
-      je[t] = it.nb;
-    } else {
-      const int lo = max(0, qp - window), hi = min(tl.kv_len, qp + nq[t] + window);
-      jb[t] = (lo - it.kbeg) / KB;
-      je[t] = (hi - it.kbeg + KB - 1) / KB;
-    }
-  }
-  it.jb0 = jb[0], it.je0 = je[0], it.jb1 = jb[1], it.je1 = je[1], it.nq0 = nq[0], it.nq1 = nq[1];
   return it;
 }
 
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(192, 2)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
-                   const AttnTile* __restrict__ tiles, int npairs, int heads, bf16* __restrict__ out, int ldo,
+                   const AttnTile* __restrict__ tiles, int ntiles, int heads, bf16* __restrict__ out, int ldo,
                    int q_col0, int k_col0, int v_col0, int window, float scale_log2, int* err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;                     // 2 buffers x 2 tiles
-  uint8_t* sK = sQ + 4 * TILE_BYTES;      // 2 stages
-  uint8_t* sV = sK + 2 * TILE_BYTES;      // 2 stages
-  uint8_t* sP = sV + 2 * TILE_BYTES;      // 2 tiles
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * P_BYTES);
-  uint64_t* kv_full = bars + 0;   // [2] per stage
-  uint64_t* kv_free = bars + 2;   // [2] per stage
-  uint64_t* s_full = bars + 4;    // [2] per tile
-  uint64_t* p_full = bars + 6;    // [2] per tile
-  uint64_t* o_full = bars + 8;    // [2] per tile
-  uint64_t* q_full = bars + 10;   // [2] per Q buffer
-  uint64_t* q_free = bars + 12;   // [2] per Q buffer
-  uint64_t* drain = bars + 14;
-  uint64_t* s_free = bars + 16;   // [2] per tile: the group has read S_t into registers
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
+  uint8_t* sQ = smem;                 // 2 buffers
+  uint8_t* sK = sQ + 2 * TILE_BYTES;  // 2 stages
+  uint8_t* sV = sK + 2 * TILE_BYTES;  // 2 stages
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + 2 * TILE_BYTES);
+  uint64_t* kv_full = bars + 0;  // [2] per stage
+  uint64_t* kv_free = bars + 2;  // [2] per stage
+  uint64_t* q_full = bars + 4;   // [2] per Q buffer
+  uint64_t* q_free = bars + 6;   // [2] per Q buffer
+  uint64_t* s_full = bars + 8;   // S of the next block in TMEM (and every earlier MMA done)
+  uint64_t* p_full = bars + 9;   // P of the current block in TMEM (128 arrivals)
+  uint64_t* o_full = bars + 10;  // last P.V of an item done
+  uint64_t* drain = bars + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id(), lane = lane_id();
-  const int items = npairs * heads;
+  const int items = ntiles * heads;
   {  // exit before allocating anything when an earlier CTA of this launch gave up
     __shared__ int s_abort;
     if (threadIdx.x == 0) s_abort = device_aborted(err) ? 1 : 0;
@@ -124,19 +117,18 @@ __global__ void __launch_bounds__(320, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_free[i], 1);
-      mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 128);
-      mbar_init(&o_full[i], 1);
       mbar_init(&q_full[i], 1);
       mbar_init(&q_free[i], 1);
-      mbar_init(&s_free[i], 128);
     }
+    mbar_init(s_full, 1);
+    mbar_init(p_full, 128);
+    mbar_init(o_full, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 8) {
-    tmem_alloc(tmem_slot, 512);
+  if (warp == 4) {
+    tmem_alloc(tmem_slot, 256);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -144,21 +136,19 @@ __global__ void __launch_bounds__(320, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (warp == 9) {
+  if (warp == 5) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      uint32_t kvb = 0;                           // K/V blocks loaded so far (stage = kvb & 1)
+      uint32_t kvb = 0;  // K/V blocks loaded so far (stage = kvb & 1)
       uint32_t armed_kv[2] = {0u, 0u}, armed_q[2] = {0u, 0u};  // parity+1 of the last armed phases
-      int n = 0;                                  // items handled by this CTA
+      int n = 0;         // items handled by this CTA
       bool ok = true;
       for (int u = blockIdx.x; u < items && ok; u += gridDim.x, ++n) {
-        const Item it = item_geometry(tiles, npairs, u, window);
+        const Item it = item_geometry(tiles, ntiles, u, window);
         const int qb = n & 1;
         if (n >= 2 && !mbar_wait(&q_free[qb], ((n - 2) >> 1) & 1, abort_flag, err, 10)) break;
-        mbar_arrive_expect_tx(&q_full[qb], it.nq1 > 0 ? 2 * TILE_BYTES : TILE_BYTES);
-        uint8_t* qdst = sQ + qb * 2 * TILE_BYTES;
-        tma_load_2d(&tmQ, &q_full[qb], qdst, q_col0 + it.head * HD, it.tl.q_row0);
-        if (it.nq1 > 0) tma_load_2d(&tmQ, &q_full[qb], qdst + TILE_BYTES, q_col0 + it.head * HD, it.tl.q_row0 + QT);
+        mbar_arrive_expect_tx(&q_full[qb], TILE_BYTES);
+        tma_load_2d(&tmQ, &q_full[qb], sQ + qb * TILE_BYTES, q_col0 + it.head * HD, it.tl.q_row0);
         armed_q[qb] = 1 + ((n >> 1) & 1);
         for (int j = 0; j < it.nb; ++j, ++kvb) {
           const int st = kvb & 1;
@@ -181,66 +171,52 @@ __global__ void __launch_bounds__(320, 1)
         }
       }
     }
-  } else if (warp == 8) {
+  } else if (warp == 4) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idS = idesc_bf16(128, 128, false, false);
       constexpr uint32_t idO = idesc_bf16(128, 64, false, true);
-      const uint32_t q0 = smem_u32(sQ), k0 = smem_u32(sK), v0 = smem_u32(sV), p0 = smem_u32(sP);
-      uint32_t pcnt0 = 0, pcnt1 = 0;  // p_full phases consumed per tile
-      uint32_t scnt[2] = {0u, 0u};    // S MMAs issued per tile (s_free phases trail by one)
-      uint32_t kvb = 0;               // K/V blocks consumed so far
+      const uint32_t q0 = smem_u32(sQ), k0 = smem_u32(sK), v0 = smem_u32(sV);
+      uint32_t pcnt = 0;  // p_full phases consumed
+      uint32_t kvb = 0;   // K/V blocks consumed
       int n = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < items && ok; u += gridDim.x, ++n) {
-        const Item it = item_geometry(tiles, npairs, u, window);
+        const Item it = item_geometry(tiles, ntiles, u, window);
         const int qb = n & 1;
         if (!mbar_wait(&q_full[qb], (n >> 1) & 1, abort_flag, err, 12)) break;
-        const uint32_t qbase = q0 + qb * 2 * TILE_BYTES;
-        auto issue_s = [&](int t, int j) -> bool {
-          // S_t is overwritten: the group must have read the previous S_t into registers
-          if (scnt[t] > 0 && !mbar_wait(&s_free[t], (scnt[t] - 1) & 1, abort_flag, err, 19)) return false;
-          ++scnt[t];
-          const uint32_t b = kvb + j;  // global block index of item block j
+        const uint32_t qa = q0 + qb * TILE_BYTES;
+        auto issue_s = [&](uint32_t b) -> bool {
           if (!mbar_wait(&kv_full[b & 1], (b >> 1) & 1, abort_flag, err, 13)) return false;
           tc_fence_after();
-          const uint32_t qa = qbase + t * TILE_BYTES, kb = k0 + (b & 1) * TILE_BYTES;
+          const uint32_t kb = k0 + (b & 1) * TILE_BYTES;
 #pragma unroll
           for (int k = 0; k < HD / 16; ++k)
-            umma_bf16(tmem_base + t * 128, sdesc_sw128(qa + k * 32, 16, 1024), sdesc_sw128(kb + k * 32, 16, 1024),
+            umma_bf16(tmem_base + TS_COL, sdesc_sw128(qa + k * 32, 16, 1024), sdesc_sw128(kb + k * 32, 16, 1024),
                       idS, k > 0);
-          umma_commit(&s_full[t]);
+          umma_commit(s_full);  // also covers the P.V issued before it
           return true;
         };
-        auto issue_pv = [&](int t, int j, uint32_t& pcnt, bool first) -> bool {
-          // P_t(j) is in smem (and O_t rescaled by the group when its offset moved)
-          if (!mbar_wait(&p_full[t], pcnt & 1, abort_flag, err, 14)) return false;
+        ok = issue_s(kvb);
+        for (int j = 0; j < it.nb && ok; ++j) {
+          // P(j) is in TMEM (the group has also finished reading S(j))
+          if (!mbar_wait(p_full, pcnt & 1, abort_flag, err, 14)) {
+            ok = false;
+            break;
+          }
           ++pcnt;
           tc_fence_after();
           const uint32_t b = kvb + j;
-          const uint32_t pa0 = p0 + t * P_BYTES, vb0 = v0 + (b & 1) * TILE_BYTES;
+          const uint32_t vb0 = v0 + (b & 1) * TILE_BYTES;
 #pragma unroll
-          for (int k = 0; k < KB / 16; ++k) {
-            const uint32_t pa = pa0 + (k >> 2) * (QT * 128) + (k & 3) * 32;
-            umma_bf16(tmem_base + 256 + t * 64, sdesc_sw128(pa, 16, 1024), sdesc_sw128(vb0 + k * 2048, 8192, 1024),
-                      idO, (k > 0 || !first) ? 1u : 0u);  // O_t accumulates over the item's blocks
-          }
-          umma_commit(&o_full[t]);
-          return true;
-        };
-        for (int j = 0; j < it.nb && ok; ++j) {
-          const bool a0 = j >= it.jb0 && j < it.je0, a1 = j >= it.jb1 && j < it.je1;
-          if (j == it.jb0 && a0) ok = issue_s(0, j);
-          if (ok && j == it.jb1 && a1) ok = issue_s(1, j);
-          // next Q.K^T of each tile as soon as its group has pulled S into registers ...
-          if (ok && a0 && j + 1 < it.je0) ok = issue_s(0, j + 1);
-          if (ok && a1 && j + 1 < it.je1) ok = issue_s(1, j + 1);
-          // ... then P.V once the group has written P
-          if (ok && a0) ok = issue_pv(0, j, pcnt0, j == it.jb0);
-          if (ok && a1) ok = issue_pv(1, j, pcnt1, j == it.jb1);
-          umma_commit(&kv_free[(kvb + j) & 1]);
+          for (int k = 0; k < KB / 16; ++k)
+            umma_bf16_ts(tmem_base + TO_COL, tmem_base + TP_COL + k * 8, sdesc_sw128(vb0 + k * 2048, 8192, 1024), idO,
+                         (k > 0 || j > 0) ? 1u : 0u);
+          umma_commit(&kv_free[b & 1]);
+          if (j + 1 < it.nb) ok = issue_s(b + 1);
         }
-        umma_commit(&q_free[qb]);  // every S of this item read Q[qb]
+        umma_commit(o_full);
+        umma_commit(&q_free[qb]);
         kvb += it.nb;
       }
       umma_commit(drain);
@@ -248,108 +224,89 @@ __global__ void __launch_bounds__(320, 1)
       mbar_wait(drain, 0, &no_abort, nullptr, 0);
     }
   } else {
-    // ------------------------------------------------------------ softmax warps (group t)
-    // S is read from TMEM once per block (128 columns -> registers). O stays in TMEM and is
-    // accumulated by the P.V MMAs; P and O share an offset u (base-2, scaled) that only
-    // moves when the running max exceeds it by more than 2^8, in which case the group
-    // rescales O in TMEM before releasing the next P. P <= 2^8 then, and BF16 rounding of
-    // P is relative, so the result matches always-rescaled online softmax to rounding.
-    const int t = warp >> 2;
-    const int r = threadIdx.x & 127;  // query row == TMEM lane
-    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const uint32_t tS = tmem_base + t * 128 + lane_off, tO = tmem_base + 256 + t * 64 + lane_off;
-    uint8_t* prow = sP + t * P_BYTES + r * 128;
-    const uint32_t sw = static_cast<uint32_t>(r & 7);
+    // ------------------------------------------------------------ softmax warps 0..3
+    const int r = threadIdx.x;  // query row == TMEM lane
+    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t tS = tmem_base + TS_COL + lane_off, tP = tmem_base + TP_COL + lane_off;
+    const uint32_t tO = tmem_base + TO_COL + lane_off;
     constexpr float kRescaleLog2 = 8.f;
-    uint32_t ns = 0;  // S / O phases consumed by this group
+    uint32_t ns = 0, no = 0;  // s_full / o_full phases consumed
     bool ok = true;
     for (int u = blockIdx.x; u < items && ok; u += gridDim.x) {
-      const Item it = item_geometry(tiles, npairs, u, window);
-      const int jb = t ? it.jb1 : it.jb0, je = t ? it.je1 : it.je0, nq = t ? it.nq1 : it.nq0;
-      if (jb >= je) continue;  // this tile of the pair is empty
-      const int qpos = it.tl.q_pos0 + QT * t + r;
+      const Item it = item_geometry(tiles, ntiles, u, window);
+      const int qpos = it.tl.q_pos0 + r;
       // this row's valid keys: [klo, khi)
       const int klo = window >= 0 ? max(0, qpos - window) : 0;
       const int khi = window >= 0 ? min(it.tl.kv_len, qpos + window + 1) : it.tl.kv_len;
       float m_used = -INFINITY;  // offset of P and O (scaled, base 2)
       float l = 0.f;
-      for (int j = jb; j < je; ++j, ++ns) {
-        if (!warp_wait(&s_full[t], ns & 1, abort_flag, err, 16)) {
+      for (int j = 0; j < it.nb; ++j, ++ns) {
+        if (!warp_wait(s_full, ns & 1, abort_flag, err, 16)) {  // also: P.V(j-1) is done
           ok = false;
           break;
         }
         tc_fence_after();
-        uint32_t sr[KB / 32][32];
-#pragma unroll
-        for (int c = 0; c < KB / 32; ++c) tmem_ld32(tS + c * 32, sr[c]);
-        tmem_ld_wait();
-        tc_fence_before();
-        mbar_arrive(&s_free[t]);  // S_t may be overwritten by the next Q.K^T
         const int key0 = it.kbeg + j * KB;
-        const int lo = klo - key0, hi = khi - key0;  // valid columns c: lo <= c < hi
-        const bool all_valid = lo <= 0 && hi >= KB;
-        float mxp[8];  // independent partial maxima (short dependency chains)
+        // valid columns c of this block: lo <= c < hi, tested as (unsigned)(c - lo) < span.
+        // Masked scores become -inf *before* the exponential (a select around ex2 would
+        // cost ~3x in issue slots).
+        const int lo = klo - key0;
+        const unsigned span = static_cast<unsigned>(max(khi - klo, 0));
+        if (j == 0) {
+          // first block: exact row max before the exponentials
+          float mxp[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll 1
+          for (int c = 0; c < KB / 32; ++c) {
+            uint32_t sr[32];
+            tmem_ld32(tS + c * 32, sr);
+            tmem_ld_wait();
 #pragma unroll
-        for (int k = 0; k < 8; ++k) mxp[k] = -INFINITY;
-#pragma unroll
-        for (int c = 0; c < KB / 32; ++c)
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int col = c * 32 + i;
-            const float v = __uint_as_float(sr[c][i]);
-            mxp[i & 7] = (all_valid || (col >= lo && col < hi)) ? fmaxf(mxp[i & 7], v) : mxp[i & 7];
+            for (int i = 0; i < 32; ++i) {
+              const bool v = static_cast<unsigned>(c * 32 + i - lo) < span;
+              mxp[i & 3] = fmaxf(mxp[i & 3], v ? __uint_as_float(sr[i]) : -INFINITY);
+            }
           }
-        const float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
-                               fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
-        const float m_cand = fmaxf(m_used, mx * scale_log2);
-        float alpha = 1.f;
-        bool moved = false;
-        if (m_cand > m_used + kRescaleLog2) {
-          alpha = ex2(m_used - m_cand);
+          m_used = fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])) * scale_log2;
+        }
+        // exponentiate with the current offset; redo once if the block max moved it too far
+        float lb = 0.f;
+        for (int attempt = 0; attempt < 2; ++attempt) {
+          const float uu = (m_used == -INFINITY) ? 0.f : m_used;
+          float lp[4] = {0.f, 0.f, 0.f, 0.f};
+          float bm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll 1
+          for (int c = 0; c < KB / 64; ++c) {
+            uint32_t sa[32], sb[32];
+            tmem_ld32(tS + c * 64, sa);
+            tmem_ld32(tS + c * 64 + 32, sb);
+            tmem_ld_wait();
+            uint32_t pk[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const int col = c * 64 + 2 * i;
+              const float s0 = __uint_as_float(i < 16 ? sa[2 * i] : sb[2 * i - 32]);
+              const float s1 = __uint_as_float(i < 16 ? sa[2 * i + 1] : sb[2 * i - 31]);
+              const float a0 = static_cast<unsigned>(col - lo) < span ? s0 : -INFINITY;
+              const float a1 = static_cast<unsigned>(col + 1 - lo) < span ? s1 : -INFINITY;
+              const float p0 = ex2(fmaf(a0, scale_log2, -uu));
+              const float p1 = ex2(fmaf(a1, scale_log2, -uu));
+              bm[i & 3] = fmaxf(bm[i & 3], a0);
+              bm[(i + 2) & 3] = fmaxf(bm[(i + 2) & 3], a1);
+              lp[i & 3] += p0 + p1;
+              pk[i] = pack_bf16x2(p0, p1);
+            }
+            tmem_st32(tP + c * 32, pk);
+          }
+          tmem_st_wait();
+          lb = (lp[0] + lp[1]) + (lp[2] + lp[3]);
+          const float bmax = fmaxf(fmaxf(bm[0], bm[1]), fmaxf(bm[2], bm[3])) * scale_log2;
+          const bool moved = bmax > m_used + kRescaleLog2;  // never on the first block
+          if (!__any_sync(0xffffffffu, moved)) break;
+          // some row of this warp needs a larger offset: rescale its O and l, redo the block
+          const float m_new = moved ? bmax : m_used;
+          const float alpha = moved ? ex2(m_used - m_new) : 1.f;
           l *= alpha;
-          m_used = m_cand;
-          moved = true;
-        }
-        const float uu = (m_used == -INFINITY) ? 0.f : m_used;
-        // P_t(j) replaces P_t(j-1): the P.V of the previous block must be complete
-        if (j > jb) {
-          if (!warp_wait(&o_full[t], (ns - 1) & 1, abort_flag, err, 17)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-        }
-        // P = 2^(s*scale - u) as bf16 into the swizzled K-major P tile
-        float lp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // partial row sums
-#pragma unroll
-        for (int c = 0; c < KB / 32; ++c) {
-          float pv[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int col = c * 32 + i;
-            const float e = ex2(fmaf(__uint_as_float(sr[c][i]), scale_log2, -uu));
-            pv[i] = (all_valid || (col >= lo && col < hi)) ? e : 0.f;
-            lp[i & 7] += pv[i];
-          }
-          // keys c*32 .. c*32+31 live in K-chunk c/2 (64 keys), 16-byte units (c&1)*4 .. +3
-          uint8_t* chunk = prow + (c >> 1) * (QT * 128);
-#pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            const uint32_t unit = static_cast<uint32_t>((c & 1) * 4 + g);
-            uint4 w;
-            w.x = pack_bf16x2(pv[8 * g + 0], pv[8 * g + 1]);
-            w.y = pack_bf16x2(pv[8 * g + 2], pv[8 * g + 3]);
-            w.z = pack_bf16x2(pv[8 * g + 4], pv[8 * g + 5]);
-            w.w = pack_bf16x2(pv[8 * g + 6], pv[8 * g + 7]);
-            *reinterpret_cast<uint4*>(chunk + ((unit ^ sw) << 4)) = w;
-          }
-        }
-        l += ((lp[0] + lp[1]) + (lp[2] + lp[3])) + ((lp[4] + lp[5]) + (lp[6] + lp[7]));
-        // O_t(j-1) is complete (waited above): move it to the new offset before P_t(j).V accumulates.
-        // tcgen05.ld/st are warp-collective (.sync.aligned): the whole warp takes this branch
-        // when any of its rows moved; rows that did not move scale by 1.
-        if (j > jb && __any_sync(0xffffffffu, moved)) {
-          if (!moved) alpha = 1.f;
+          m_used = m_new;
 #pragma unroll 1
           for (int h = 0; h < 2; ++h) {
             uint32_t orr[32];
@@ -361,23 +318,23 @@ __global__ void __launch_bounds__(320, 1)
           }
           tmem_st_wait();
         }
-        fence_proxy_async_smem();
+        l += lb;
         tc_fence_before();
-        mbar_arrive(&p_full[t]);
+        mbar_arrive(p_full);
       }
-      if (!ok || !warp_wait(&o_full[t], (ns - 1) & 1, abort_flag, err, 18)) {
+      if (!ok || !warp_wait(o_full, no & 1, abort_flag, err, 18)) {
         ok = false;
         break;
       }
+      ++no;
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       uint32_t orr[2][32];
       tmem_ld32(tO, orr[0]);
       tmem_ld32(tO + 32, orr[1]);
       tmem_ld_wait();
-      if (r < nq) {
-        uint4* dst =
-            reinterpret_cast<uint4*>(out + static_cast<size_t>(it.tl.q_row0 + QT * t + r) * ldo + it.head * HD);
+      if (r < it.tl.nq) {
+        uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(it.tl.q_row0 + r) * ldo + it.head * HD);
 #pragma unroll
         for (int g = 0; g < 8; ++g) {
           const uint32_t* v = &orr[g >> 2][(g & 3) * 8];
@@ -389,7 +346,7 @@ __global__ void __launch_bounds__(320, 1)
           dst[g] = w;
         }
       }
-      // O_t is reused by the next item's first P.V (issued after this group's next p_full)
+      // O is overwritten by the next item's first P.V, issued after this warp's next p_full
       tc_fence_before();
     }
   }
@@ -397,12 +354,12 @@ __global__ void __launch_bounds__(320, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 8) tmem_dealloc(tmem_base, 512);
+  if (warp == 4) tmem_dealloc(tmem_base, 256);
 }
 
 }  // namespace
 
-int attention_pair_queries() { return 2 * QT; }
+int attention_pair_queries() { return QT; }
 
 int launch_attention(const CUtensorMap& tmQ, const CUtensorMap& tmKV, const AttnTile* tiles, int ntiles, int heads,
                      int q_col0, int k_col0, int v_col0, bf16* out, int ldo, int window, float scale_log2, int* err,
@@ -415,8 +372,9 @@ int launch_attention(const CUtensorMap& tmQ, const CUtensorMap& tmKV, const Attn
   }
   if (ntiles == 0 || heads == 0) return 0;
   const int items = ntiles * heads;
-  const int grid = items < grid_limit ? items : grid_limit;
-  attn_tc_kernel<<<grid, 320, ATT_SMEM, stream>>>(tmQ, tmKV, tiles, ntiles, heads, out, ldo, q_col0, k_col0, v_col0,
+  const int limit = 2 * grid_limit;  // two CTAs per SM
+  const int grid = items < limit ? items : limit;
+  attn_tc_kernel<<<grid, 192, ATT_SMEM, stream>>>(tmQ, tmKV, tiles, ntiles, heads, out, ldo, q_col0, k_col0, v_col0,
                                                    window, scale_log2, err);
   return static_cast<int>(cudaGetLastError());
 }
