@@ -232,6 +232,7 @@ def main():
     import torch.distributed as dist
     import julia1 as j1
     from julia1 import synthetic
+    from julia1.replicas import aggregate_rate, max_over_ranks
 
     torch.cuda.set_device(local)
     if world > 1:
@@ -251,13 +252,6 @@ def main():
             dist.barrier()
         torch.cuda.synchronize()
 
-    def max_over_ranks(x):
-        if world == 1:
-            return x
-        v = torch.tensor([x], device="cuda", dtype=torch.float64)
-        dist.all_reduce(v, op=dist.ReduceOp.MAX)
-        return float(v.item())
-
     # ---------------- value: batch resident in HBM, device-timed
     model.stage(batch)
     for _ in range(args.warmup):
@@ -275,11 +269,11 @@ def main():
     scores = model.finish(m)
     barrier()
     clk = clocks.stop() if clocks else None
-    dev_ms = max_over_ranks(e0.elapsed_time(e1))
+    dev_ms = max_over_ranks(e0.elapsed_time(e1), device="cuda")
+    value = aggregate_rate(t * args.steps, e0.elapsed_time(e1) / 1e3, device="cuda")
     fam = model.profile_read()
     model.profile(False)
     assert np.isfinite(scores).all()
-    value = world * t * args.steps / (dev_ms / 1e3)
 
     # ---------------- e2e: public C ABI with host buffers (pack + H2D + kernels + D2H + sync)
     for _ in range(2):
@@ -290,8 +284,7 @@ def main():
         model.forward_flat(batch)
     h1 = time.perf_counter()
     barrier()
-    e2e_s = max_over_ranks(h1 - h0)
-    e2e = world * t * args.steps / e2e_s
+    e2e = aggregate_rate(t * args.steps, h1 - h0, device="cuda")
     ntiles = sum((n + 127) // 128 for n in batch.lens.tolist())  # 128-query attention tiles
     h2d = ((3 * t + m + 7) // 8 * 8 + 8 * ntiles) * 4
     d2h = m * 4 + 4

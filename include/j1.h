@@ -141,6 +141,14 @@ J1_API j1_status j1_engine_logits_encoded(j1_engine* engine, size_t n_rows, cons
                                    const uint32_t* markers, const uint32_t* row_markers, const uint8_t* qtypes,
                                    float* logits_out);
 
+/* Host-only: the micro-batch plan j1_engine_logits_encoded uses (src/engine.rs:191-210):
+ * rows stable-sorted by length, cut at batch_size rows or max_batch_tokens tokens, each
+ * micro-batch assigned to the replica with the fewest tokens so far.
+ * batch_of_row[n_rows]; device_of_batch must hold n_rows entries (the most batches possible). */
+J1_API j1_status j1_plan_batches(size_t n_rows, const uint32_t* row_lens, int32_t batch_size, int64_t max_batch_tokens,
+                                 int32_t n_devices, uint32_t* batch_of_row, uint32_t* device_of_batch,
+                                 size_t* n_batches);
+
 /* ------------------------------------------------------------ kernel-level ops
  * On caller device memory (e.g. torch tensors); `stream` is a cudaStream_t or NULL.
  * With sync != 0 the call waits for completion and reports device-side timeouts. */

@@ -60,6 +60,35 @@ struct Micro {
   size_t tokens = 0;
 };
 
+// Engine::batches (src/engine.rs:191-210): rows sorted by length (stable), cut when a
+// micro-batch reaches batch_size rows or would exceed max_batch_tokens. Then each
+// micro-batch goes to the replica with the fewest tokens so far (ties: lowest index).
+void plan(size_t n_rows, const uint32_t* row_lens, size_t batch_size, size_t max_batch_tokens, size_t n_devices,
+          std::vector<Micro>& micro, std::vector<size_t>& device_of) {
+  std::vector<size_t> order(n_rows);
+  std::iota(order.begin(), order.end(), 0);
+  std::stable_sort(order.begin(), order.end(), [&](size_t a, size_t b) { return row_lens[a] < row_lens[b]; });
+  micro.clear();
+  Micro cur;
+  for (size_t i : order) {
+    const size_t n = row_lens[i];
+    if (!cur.rows.empty() && (cur.rows.size() == batch_size || cur.tokens + n > max_batch_tokens)) {
+      micro.push_back(std::move(cur));
+      cur = Micro();
+    }
+    cur.rows.push_back(i);
+    cur.tokens += n;
+  }
+  if (!cur.rows.empty()) micro.push_back(std::move(cur));
+  std::vector<size_t> load(n_devices, 0);
+  device_of.assign(micro.size(), 0);
+  for (size_t b = 0; b < micro.size(); ++b) {
+    const size_t g = static_cast<size_t>(std::min_element(load.begin(), load.end()) - load.begin());
+    device_of[b] = g;
+    load[g] += micro[b].tokens;
+  }
+}
+
 }  // namespace
 
 extern "C" {
@@ -143,34 +172,13 @@ j1_status j1_engine_logits_encoded(j1_engine* e, size_t n_rows, const uint32_t* 
       if (markers[k] >= row_lens[r]) return set_error(J1_ERR_INVALID_ARG, "marker outside its row");
 
   std::lock_guard<std::mutex> lk(e->mu);
-  // Length-sorted micro-batches (src/engine.rs:191-210); stable sort keeps input order on ties.
-  std::vector<size_t> order(n_rows);
-  std::iota(order.begin(), order.end(), 0);
-  std::stable_sort(order.begin(), order.end(), [&](size_t a, size_t b) { return row_lens[a] < row_lens[b]; });
-  std::vector<Micro> micro;
-  Micro cur;
-  for (size_t i : order) {
-    const size_t n = row_lens[i];
-    if (!cur.rows.empty() &&
-        (cur.rows.size() == static_cast<size_t>(e->opts.batch_size) ||
-         cur.tokens + n > static_cast<size_t>(e->opts.max_batch_tokens))) {
-      micro.push_back(std::move(cur));
-      cur = Micro();
-    }
-    cur.rows.push_back(i);
-    cur.tokens += n;
-  }
-  if (!cur.rows.empty()) micro.push_back(std::move(cur));
-
-  // Greedy token balance across replicas, in batch order.
   const size_t G = e->models.size();
+  std::vector<Micro> micro;
+  std::vector<size_t> device_of;
+  plan(n_rows, row_lens, static_cast<size_t>(e->opts.batch_size), static_cast<size_t>(e->opts.max_batch_tokens), G,
+       micro, device_of);
   std::vector<std::vector<size_t>> assign(G);
-  std::vector<size_t> load(G, 0);
-  for (size_t b = 0; b < micro.size(); ++b) {
-    const size_t g = static_cast<size_t>(std::min_element(load.begin(), load.end()) - load.begin());
-    assign[g].push_back(b);
-    load[g] += micro[b].tokens;
-  }
+  for (size_t b = 0; b < micro.size(); ++b) assign[device_of[b]].push_back(b);
 
   auto run = [&](size_t g, j1_status* status, std::string* msg) {
     std::vector<uint32_t> bids, starts, lens, mrows, mstarts;
@@ -215,6 +223,24 @@ j1_status j1_engine_logits_encoded(j1_engine* e, size_t n_rows, const uint32_t* 
   }
   for (size_t g = 0; g < G; ++g)
     if (st[g]) return set_error(st[g], msgs[g]);
+  return J1_OK;
+}
+
+j1_status j1_plan_batches(size_t n_rows, const uint32_t* row_lens, int32_t batch_size, int64_t max_batch_tokens,
+                          int32_t n_devices, uint32_t* batch_of_row, uint32_t* device_of_batch, size_t* n_batches) {
+  if (!n_batches || (n_rows && (!row_lens || !batch_of_row || !device_of_batch)))
+    return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+  if (batch_size < 1 || max_batch_tokens < 1 || n_devices < 1)
+    return set_error(J1_ERR_INVALID_ARG, "batch_size, max_batch_tokens and n_devices must be positive");
+  std::vector<Micro> micro;
+  std::vector<size_t> device_of;
+  plan(n_rows, row_lens, static_cast<size_t>(batch_size), static_cast<size_t>(max_batch_tokens),
+       static_cast<size_t>(n_devices), micro, device_of);
+  for (size_t b = 0; b < micro.size(); ++b) {
+    device_of_batch[b] = static_cast<uint32_t>(device_of[b]);
+    for (size_t r : micro[b].rows) batch_of_row[r] = static_cast<uint32_t>(b);
+  }
+  *n_batches = micro.size();
   return J1_OK;
 }
 

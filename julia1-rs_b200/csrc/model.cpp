@@ -429,11 +429,49 @@ j1_status finish_forward(j1_model* model, float* scores_out, size_t m) {
   return J1_OK;
 }
 
+// Every tensor HostWeights::load reads (src/model.rs:55-110), with its shape; checked
+// before any device work so a bad checkpoint fails fast (and without a GPU).
+j1_status validate_checkpoint(SafeTensors& st, const ModelConfig& c) {
+  const size_t H = c.hidden, I = c.intermediate, FF = c.head_ff;
+  std::vector<std::pair<std::string, std::vector<size_t>>> want = {
+      {"encoder.embeddings.tok_embeddings.weight", {size_t(c.vocab), H}},
+      {"encoder.embeddings.norm.weight", {H}},
+      {"encoder.final_norm.weight", {H}},
+      {"type_emb.weight", {3, H}},
+      {"scorer.0.weight", {H}}, {"scorer.0.bias", {H}}, {"scorer.1.weight", {H, H}}, {"scorer.1.bias", {H}},
+      {"scorer.3.weight", {1, H}}, {"scorer.3.bias", {1}}};
+  for (int l = 0; l < c.layers; ++l) {
+    const std::string pre = "encoder.layers." + std::to_string(l) + ".";
+    if (l > 0) want.push_back({pre + "attn_norm.weight", {H}});
+    want.push_back({pre + "attn.Wqkv.weight", {3 * H, H}});
+    want.push_back({pre + "attn.Wo.weight", {H, H}});
+    want.push_back({pre + "mlp_norm.weight", {H}});
+    want.push_back({pre + "mlp.Wi.weight", {2 * I, H}});
+    want.push_back({pre + "mlp.Wo.weight", {H, I}});
+  }
+  for (int j = 0; j < c.head_layers; ++j) {
+    const std::string pre = "head.layers." + std::to_string(j) + ".";
+    for (auto& kv : std::vector<std::pair<const char*, std::vector<size_t>>>{
+             {"norm1.weight", {H}}, {"norm1.bias", {H}}, {"self_attn.in_proj_weight", {3 * H, H}},
+             {"self_attn.in_proj_bias", {3 * H}}, {"self_attn.out_proj.weight", {H, H}},
+             {"self_attn.out_proj.bias", {H}}, {"norm2.weight", {H}}, {"norm2.bias", {H}},
+             {"linear1.weight", {FF, H}}, {"linear1.bias", {FF}}, {"linear2.weight", {H, FF}},
+             {"linear2.bias", {H}}})
+      want.push_back({pre + kv.first, kv.second});
+  }
+  std::string err;
+  for (const auto& w : want)
+    if (!st.f32(w.first, w.second, err)) return set_error(J1_ERR_IO, err);
+  return J1_OK;
+}
+
+void destroy_model(j1_model* model);
+
 j1_status create_model(const char* ckpt_dir, int ordinal, j1_model** out) {
   if (!ckpt_dir || !out) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
   *out = nullptr;
   const std::string root(ckpt_dir);
-  std::unique_ptr<j1_model> model(new j1_model());
+  std::unique_ptr<j1_model, void (*)(j1_model*)> model(new j1_model(), destroy_model);
   std::string err;
   if (!config_load(root, model->cfg, err)) return set_error(J1_ERR_IO, err);
   if (file_exists(root + "/INCOMPLETE") || file_exists(root + "/quantization.json"))
@@ -445,6 +483,9 @@ j1_status create_model(const char* ckpt_dir, int ordinal, j1_model** out) {
   if (c.intermediate % 128 != 0) return set_error(J1_ERR_UNSUPPORTED, "intermediate_size must be a multiple of 128");
   if (c.head_heads != c.heads || c.head_layers < 1)
     return set_error(J1_ERR_UNSUPPORTED, "Unsupported decision head layout");
+  SafeTensors st;
+  if (!st.open(root + "/model.safetensors", err)) return set_error(J1_ERR_IO, err);
+  if (j1_status v = validate_checkpoint(st, c)) return v;
   int ndev = 0;
   if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0)
     return set_error(J1_ERR_CUDA, "CUDA device unavailable");
@@ -469,8 +510,6 @@ j1_status create_model(const char* ckpt_dir, int ordinal, j1_model** out) {
   J1_TRY_CUDA(cudaMallocHost(&p, 16), "cudaMallocHost");
   M->err_host = static_cast<int*>(p);
 
-  SafeTensors st;
-  if (!st.open(root + "/model.safetensors", err)) return set_error(J1_ERR_IO, err);
   const size_t H = c.hidden, I = c.intermediate, FF = c.head_ff;
   // staging for FP32 -> BF16 conversion, sized for the largest GEMM weight
   const size_t stage_elems = std::max({3 * H * H, 2 * I * H, FF * H});

@@ -29,7 +29,7 @@ EXPORTS = [
     "j1_engine_options_default", "j1_engine_create", "j1_engine_create_pool", "j1_engine_destroy",
     "j1_engine_device_name", "j1_engine_logits_encoded",
     "j1_op_gemm", "j1_op_attention", "j1_op_geglu_interleave",
-    "j1_model_profile", "j1_model_profile_read", "j1_profile_family_name",
+    "j1_model_profile", "j1_model_profile_read", "j1_profile_family_name", "j1_plan_batches",
 ]
 PROF_FAMILIES = 12
 
@@ -109,6 +109,9 @@ def lib():
     L.j1_model_profile_read.argtypes = [C.c_void_p, C.POINTER(C.c_double), C.POINTER(C.c_int64)]
     L.j1_profile_family_name.argtypes = [C.c_int]
     L.j1_profile_family_name.restype = C.c_char_p
+    L.j1_plan_batches.argtypes = [C.c_size_t, u32p, C.c_int32, C.c_int64, C.c_int32, u32p, u32p,
+                                  C.POINTER(C.c_size_t)]
+    L.j1_plan_batches.restype = C.c_int
     L.j1_op_gemm.argtypes = [C.POINTER(J1GemmArgs), C.c_void_p, C.c_int]
     L.j1_op_attention.argtypes = [C.c_void_p, C.c_int64, C.c_int32, u32p, u32p, C.c_size_t, C.c_int32, C.c_void_p,
                                   C.c_void_p, C.c_int]
@@ -372,6 +375,24 @@ class Engine:
                 pr = (e / e.sum()).tolist()
             out.append((idx, pr))
         return out
+
+
+def plan_batches(row_lens, batch_size=16, max_batch_tokens=65536, n_devices=1):
+    """The engine's micro-batch plan (j1_plan_batches): ([rows of batch b], [device of batch b])."""
+    lens, lp = _u32(row_lens)
+    n = lens.size
+    bor = np.zeros(max(n, 1), np.uint32)
+    dob = np.zeros(max(n, 1), np.uint32)
+    nb = C.c_size_t()
+    check(lib().j1_plan_batches(n, lp, int(batch_size), int(max_batch_tokens), int(n_devices),
+                                bor.ctypes.data_as(C.POINTER(C.c_uint32)), dob.ctypes.data_as(C.POINTER(C.c_uint32)),
+                                C.byref(nb)))
+    batches = [[] for _ in range(nb.value)]
+    for r in range(n):
+        batches[int(bor[r])].append(r)
+    # rows inside a batch keep the length-sorted order of the plan
+    batches = [sorted(b, key=lambda r: (int(lens[r]), r)) for b in batches]
+    return batches, [int(d) for d in dob[:nb.value]]
 
 
 # ------------------------------------------------------------------ kernel-level ops (torch tensors)
