@@ -3,7 +3,8 @@
   python oracle/build.py          -> oracle/_build/libj1oracle.so  (CPU restatement, j1_oracle.cpp)
   python oracle/build.py --ref    -> also oracle/_ref/kernels.cubin (the reference's own
                                      src/cuda/kernels.cu, compiled unmodified for sm_100a
-                                     from /root/reference when that tree is present)
+                                     from the reference tree when it is present; the
+                                     GPU box has no reference tree and uses the prebuilt cubin)
 
 Outputs are git-ignored but travel to the GPU box with the repository snapshot.
 """
@@ -16,7 +17,7 @@ BUILD = os.path.join(HERE, "_build")
 REF = os.path.join(HERE, "_ref")
 LIB = os.path.join(BUILD, "libj1oracle.so")
 CUBIN = os.path.join(REF, "kernels.cubin")
-REFERENCE_KERNELS = "/root/reference/src/cuda/kernels.cu"
+REFERENCE_KERNELS = os.path.join(os.environ.get("J1_REFERENCE_DIR", "/root/reference"), "src", "cuda", "kernels.cu")
 
 
 def build_oracle(force=False):
