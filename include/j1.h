@@ -199,6 +199,18 @@ J1_API j1_status j1_op_gemm(const j1_gemm_args* args, void* stream, int sync);
 J1_API j1_status j1_op_attention(const void* qkv, int64_t t, int32_t hidden, const uint32_t* seq_starts,
                           const uint32_t* seq_lens, size_t nseq, int32_t window, void* ctx, void* stream, int sync);
 
+/* j1_op_attention with no run-time allocation (no counterpart in the reference).
+ * Same arguments, results and errors as j1_op_attention, but the tile list and the
+ * error word live in a fixed device array of this library, so callers that cannot
+ * allocate device memory (a pool that owns all free HBM; a loop that must not hit
+ * cudaMalloc's device-wide synchronisation) can use it. At most 8192 query tiles
+ * (sum of ceil(len / 128)) per call, else J1_ERR_INVALID_ARG. All calls on a device
+ * share that array: calls on one stream are ordered, overlapping calls race. The
+ * first call on each device does its set-up and should precede any stream capture. */
+J1_API j1_status j1_op_attention_noalloc(const void* qkv, int64_t t, int32_t hidden, const uint32_t* seq_starts,
+                                         const uint32_t* seq_lens, size_t nseq, int32_t window, void* ctx,
+                                         void* stream, int sync);
+
 /* Host helper: dst rows of a [2*inter, K] Wi laid out for J1_EPI_GEGLU (FP32 -> BF16 on device). */
 J1_API j1_status j1_op_geglu_interleave(const float* src_dev, void* dst_dev, int32_t inter, int32_t k, void* stream);
 

@@ -28,7 +28,7 @@ EXPORTS = [
     "j1_model_stage", "j1_model_launch", "j1_model_finish", "j1_model_stream", "j1_model_launch_count",
     "j1_engine_options_default", "j1_engine_create", "j1_engine_create_pool", "j1_engine_destroy",
     "j1_engine_device_name", "j1_engine_logits_encoded",
-    "j1_op_gemm", "j1_op_attention", "j1_op_geglu_interleave",
+    "j1_op_gemm", "j1_op_attention", "j1_op_attention_noalloc", "j1_op_geglu_interleave",
     "j1_model_profile", "j1_model_profile_read", "j1_profile_family_name", "j1_plan_batches",
 ]
 PROF_FAMILIES = 12
@@ -115,11 +115,12 @@ def lib():
     L.j1_op_gemm.argtypes = [C.POINTER(J1GemmArgs), C.c_void_p, C.c_int]
     L.j1_op_attention.argtypes = [C.c_void_p, C.c_int64, C.c_int32, u32p, u32p, C.c_size_t, C.c_int32, C.c_void_p,
                                   C.c_void_p, C.c_int]
+    L.j1_op_attention_noalloc.argtypes = L.j1_op_attention.argtypes
     L.j1_op_geglu_interleave.argtypes = [C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_void_p]
     for fn in ("j1_config_load", "j1_model_create", "j1_model_config", "j1_model_forward", "j1_model_stage",
                "j1_model_launch", "j1_model_finish", "j1_engine_create", "j1_engine_create_pool",
-               "j1_engine_logits_encoded", "j1_op_gemm", "j1_op_attention", "j1_op_geglu_interleave",
-               "j1_model_profile", "j1_model_profile_read"):
+               "j1_engine_logits_encoded", "j1_op_gemm", "j1_op_attention", "j1_op_attention_noalloc",
+               "j1_op_geglu_interleave", "j1_model_profile", "j1_model_profile_read"):
         getattr(L, fn).restype = C.c_int
     _lib = L
     return L
@@ -436,6 +437,15 @@ def op_attention(qkv, hidden, seq_starts, seq_lens, window, ctx, stream=None, sy
     l, lp = _u32(seq_lens)
     check(lib().j1_op_attention(C.c_void_p(qkv.data_ptr()), qkv.shape[0], hidden, sp, lp, len(s), window,
                                 C.c_void_p(ctx.data_ptr()), C.c_void_p(stream) if stream else None, 1 if sync else 0))
+
+
+def op_attention_noalloc(qkv, hidden, seq_starts, seq_lens, window, ctx, stream=None, sync=True):
+    """j1_op_attention_noalloc: op_attention with its scratch in a fixed device array."""
+    s, sp = _u32(seq_starts)
+    l, lp = _u32(seq_lens)
+    check(lib().j1_op_attention_noalloc(C.c_void_p(qkv.data_ptr()), qkv.shape[0], hidden, sp, lp, len(s), window,
+                                        C.c_void_p(ctx.data_ptr()), C.c_void_p(stream) if stream else None,
+                                        1 if sync else 0))
 
 
 def op_geglu_interleave(src_f32, dst_bf16, inter, k, stream=None):
