@@ -364,12 +364,9 @@ int attention_pair_queries() { return QT; }
 int launch_attention(const CUtensorMap& tmQ, const CUtensorMap& tmKV, const AttnTile* tiles, int ntiles, int heads,
                      int q_col0, int k_col0, int v_col0, bf16* out, int ldo, int window, float scale_log2, int* err,
                      int grid_limit, cudaStream_t stream) {
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ATT_SMEM);
-    if (e != cudaSuccess) return static_cast<int>(e);
-    configured = true;
-  }
+  static std::atomic<unsigned long long> configured{0};  // one bit per device
+  const cudaError_t e = set_smem_once(attn_tc_kernel, ATT_SMEM, configured);
+  if (e != cudaSuccess) return static_cast<int>(e);
   if (ntiles == 0 || heads == 0) return 0;
   const int items = ntiles * heads;
   const int limit = 2 * grid_limit;  // two CTAs per SM

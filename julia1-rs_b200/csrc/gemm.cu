@@ -471,13 +471,10 @@ __global__ void __launch_bounds__(192, 1)
 template <int BN, int EPI, int NSUB>
 int launch_one(const CUtensorMap& tmA, const CUtensorMap& tmW, const CUtensorMap& tmX, const EpiParams& p,
                int grid_limit, cudaStream_t stream) {
-  static bool configured = false;  // per instantiation; the attribute set is idempotent
+  static std::atomic<unsigned long long> configured{0};  // per instantiation, one bit per device
   auto kern = gemm_tc_kernel<BN, EPI, NSUB>;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<BN, EPI>::SMEM);
-    if (e != cudaSuccess) return static_cast<int>(e);
-    configured = true;
-  }
+  const cudaError_t e = set_smem_once(kern, GemmCfg<BN, EPI>::SMEM, configured);
+  if (e != cudaSuccess) return static_cast<int>(e);
   const int units = ((p.M + BM - 1) / BM) * (is_full_row(EPI) ? 1 : p.N / BN);
   const int grid = units < grid_limit ? units : grid_limit;
   if (grid <= 0) return 0;

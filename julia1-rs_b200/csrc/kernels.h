@@ -5,9 +5,27 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 namespace j1rt {
 
 using bf16 = __nv_bfloat16;
+
+// cudaFuncSetAttribute acts on the kernel as loaded in the current device's
+// context, so a process that drives several GPUs (the engine pool) must raise the
+// dynamic shared-memory limit once per device. `done` keeps one bit per device
+// ordinal; ordinals of 64 and above set the attribute on every launch.
+template <typename Kernel>
+inline cudaError_t set_smem_once(Kernel kern, int bytes, std::atomic<unsigned long long>& done) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const unsigned long long bit = dev < 64 ? 1ull << dev : 0ull;
+  if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && bit) done.fetch_or(bit, std::memory_order_acq_rel);
+  return e;
+}
 
 // ------------------------------------------------------------------ GEMM
 // out = A[M,K] . W[N,K]^T with a fused epilogue. A and W are bf16, row-major,

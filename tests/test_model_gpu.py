@@ -137,6 +137,23 @@ def test_engine_micro_batching_matches_model(torch_cuda, ckpt768, model768):
     assert got[5] == []  # a 1-token row has no markers
 
 
+def test_engine_pool_matches_model(torch_cuda, ckpt768, model768):
+    """A pool engine (one replica + host worker per device) gives the single-model
+    logits bit for bit; with one visible GPU the pool holds two replicas on it."""
+    n = torch_cuda.cuda.device_count()
+    devices = list(range(min(n, 4))) if n >= 2 else [0, 0]
+    lens = np.random.default_rng(5).integers(1, 900, size=23).tolist()
+    rows = synthetic.synthetic_batch(lens, markers_per_seq=2, seed=112, mask_markers=False)
+    eng = j1.Engine.load(ckpt768, j1.EngineOptions(batch_size=2, max_batch_tokens=4096, max_length=1024),
+                      devices=devices)
+    try:
+        got = eng.logits_encoded([j1.Encoded(*r) for r in rows])
+    finally:
+        eng.close()
+    want = model768.forward(rows_to_batch(rows))
+    assert got == [list(w) for w in want]
+
+
 def test_forward_rejects_bad_batches(model768):
     rows = synthetic.synthetic_batch([64, 64], markers_per_seq=2, seed=113)
     b = rows_to_batch(rows)
