@@ -8,19 +8,24 @@
 //   head in_proj/lin1    -> EPI_BF16 with bias (+relu)  (kernels.cu:158-172)
 //   scorer W1 + scorer   -> EPI_SCORER   (kernels.cu:186-194)
 //
-// Structure: persistent CTAs (one per SM), 192 threads.
+// Structure: persistent CTAs (one per SM), 224 threads.
 //   warp 0      TMA producer: A (128 x 64) and W (BN x 64) boxes into a smem ring
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer (M=128, N=BN, K=16)
 //   warps 2..5  epilogue: tcgen05.ld of the FP32 accumulator (TMEM lane = row), fused math
+//   warp 6      residual producer (RESID*): TMA loads of x chunks into a smem ring
 // The accumulator is double buffered in TMEM (2 x BN columns) so the epilogue of one
 // tile overlaps the main loop of the next.
 //
+// BF16 outputs (BF16, QKV_ROPE, GEGLU) are written row-per-thread into 128 x 64
+// 128B-swizzled smem boxes (three in rotation) and leave by TMA store, so global
+// writes are whole lines instead of 16-byte pieces of 32 different rows.
+//
 // Full-row epilogues (RESID*, SCORER) own whole rows: one work unit is 128 rows x H
 // columns, computed as H/BN sub-tiles. The residual stream x (FP32) moves through
-// shared memory in 128 x 32 chunks by TMA (load, in-place update, store), double
-// buffered and prefetched while the main loop runs; per-row LayerNorm statistics are
-// merged chunk by chunk (Welford/Chan), then the normalized BF16 row is produced from
-// the updated x with warp-coalesced loads.
+// shared memory in 128 x 32 chunks (load by warp 6, in-place update, TMA store), with
+// NXB chunks in flight so that HBM latency is covered; per-row LayerNorm statistics
+// are merged chunk by chunk (Welford/Chan), then the normalized BF16 row is produced
+// from the updated x with warp-coalesced loads.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -34,24 +39,34 @@ namespace {
 constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr uint32_t XCHUNK = 128 * 32 * 4;  // one 128-row x 32-column FP32 residual chunk
+constexpr uint32_t NXB = 4;                // residual chunks in flight per CTA (64 KB)
+constexpr uint32_t OBUF = 128 * 64 * 2;    // one 128-row x 64-column BF16 output box
+constexpr int GEMM_THREADS = 224;
 
 __host__ __device__ constexpr bool is_full_row(int epi) { return epi == EPI_RESID_LN || epi == EPI_RESID || epi == EPI_SCORER; }
 __host__ __device__ constexpr bool is_resid(int epi) { return epi == EPI_RESID_LN || epi == EPI_RESID; }
+__host__ __device__ constexpr bool is_tile_out(int epi) {
+  return epi == EPI_BF16 || epi == EPI_QKV_ROPE || epi == EPI_GEGLU;
+}
 
 template <int BN, int EPI>
 struct GemmCfg {
-  static constexpr int STAGES = (BN == 256) ? 4 : 6;
+  // main-loop ring depth: what is left of 227 KB after the x ring / output boxes
+  static constexpr int STAGES = (EPI == EPI_SCORER) ? (BN == 256 ? 4 : 6) : (BN == 256 ? 3 : 5);
   static constexpr uint32_t A_BYTES = BM * BK * 2;
   static constexpr uint32_t B_BYTES = BN * BK * 2;
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr uint32_t X_BYTES = is_resid(EPI) ? 2 * XCHUNK : 0;
-  static constexpr uint32_t SMEM = STAGES * STAGE_BYTES + X_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr uint32_t X_BYTES = is_resid(EPI) ? NXB * XCHUNK : 0;
+  static constexpr uint32_t O_BYTES = is_tile_out(EPI) ? 3 * OBUF : 0;
+  static constexpr uint32_t SMEM = STAGES * STAGE_BYTES + X_BYTES + O_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static_assert(SMEM <= 232448, "shared memory budget");
 };
 
 __device__ __forceinline__ float gelu_erf(float v) { return 0.5f * v * (1.f + erff(v * 0.70710678118654752f)); }
 
-__device__ __forceinline__ void store_bf16x32(bf16* dst, const float (&v)[32]) {
-  uint4* d = reinterpret_cast<uint4*>(dst);
+// 32 values of one row -> four 16-byte units (unit0 .. unit0+3) of a 128B-swizzled box
+// row: unit i of row r sits at (i ^ (r & 7)) * 16 within the row's 128 bytes.
+__device__ __forceinline__ void put_row32(uint8_t* srow, int r, int unit0, const float (&v)[32]) {
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     uint4 q;
@@ -59,13 +74,13 @@ __device__ __forceinline__ void store_bf16x32(bf16* dst, const float (&v)[32]) {
     q.y = pack_bf16x2(v[8 * i + 2], v[8 * i + 3]);
     q.z = pack_bf16x2(v[8 * i + 4], v[8 * i + 5]);
     q.w = pack_bf16x2(v[8 * i + 6], v[8 * i + 7]);
-    d[i] = q;
+    *reinterpret_cast<uint4*>(srow + ((static_cast<uint32_t>(unit0 + i) ^ (r & 7)) << 4)) = q;
   }
 }
 
 // BN: MMA tile width; NSUB: sub-tiles per full-row unit (full-row width H = NSUB * BN).
 template <int BN, int EPI, int NSUB>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                    const __grid_constant__ CUtensorMap tmX, const EpiParams p) {
   using C = GemmCfg<BN, EPI>;
@@ -77,14 +92,16 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + C::STAGES * C::A_BYTES;
-  uint8_t* sX = sB + C::STAGES * C::B_BYTES;  // 2 x XCHUNK (1024-aligned) when RES
-  uint64_t* full = reinterpret_cast<uint64_t*>(sX + C::X_BYTES);
+  uint8_t* sX = sB + C::STAGES * C::B_BYTES;  // NXB x XCHUNK (1024-aligned) when RES
+  uint8_t* sO = sX + C::X_BYTES;              // 3 x OBUF output boxes when tile-out
+  uint64_t* full = reinterpret_cast<uint64_t*>(sO + C::O_BYTES);
   uint64_t* empty = full + C::STAGES;
   uint64_t* tfull = empty + C::STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint64_t* xfull = drain + 1;  // 2 barriers
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xfull + 2);
+  uint64_t* xfull = drain + 1;     // NXB barriers
+  uint64_t* xempty = xfull + NXB;  // NXB barriers
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xempty + NXB);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id(), lane = lane_id();
@@ -108,7 +125,10 @@ __global__ void __launch_bounds__(192, 1)
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], 128);
+    }
+    for (uint32_t b = 0; b < NXB; ++b) {
       mbar_init(&xfull[b], 1);
+      mbar_init(&xempty[b], 1);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -210,16 +230,34 @@ __global__ void __launch_bounds__(192, 1)
       volatile int no_abort = 0;
       mbar_wait(drain, 0, &no_abort, nullptr, 0);
     }
-  } else {
+  } else if (warp <= 5) {
     // ------------------------------------------------------------ epilogue (warps 2..5)
     // Control flow is uniform across the 128 epilogue threads (named barriers below):
     // after an abort every wait returns at once and the loops run out without work.
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int trow = q * 32 + lane;
-    const bool xprod = (threadIdx.x == 64);  // issues the residual chunk TMA traffic
+    const bool storer = (threadIdx.x == 64);  // issues the TMA stores of the epilogue
     int acc = 0;
-    uint32_t gch = 0;                     // residual chunks consumed so far (buffer = gch & 1)
-    uint32_t x_armed[2] = {0u, 0u};       // parity+1 of the last armed phase per buffer
+    uint32_t gch = 0;  // residual chunks consumed so far (ring slot = gch % NXB)
+    int xpend = -1;    // ring slot whose store may still be reading smem
+    int ob = 0;        // output box in use (of three)
+    // BF16 output: this thread's 64 values of row trow -> box `ob` (128B swizzle), then
+    // one TMA store of the 128 x 64 box at (col, m0). Three boxes rotate: after issuing
+    // a store the storer waits until only that store may still read smem, so the box
+    // written next-but-one is free before any thread passes the next barrier.
+    auto store_box = [&](const float (&a)[32], const float (&b)[32], int col, int m0) {
+      uint8_t* srow = sO + ob * OBUF + trow * 128;
+      put_row32(srow, trow, 0, a);
+      put_row32(srow, trow, 4, b);
+      fence_proxy_async_smem();
+      named_bar_sync(1, 128);
+      if (storer && !*abort_flag) {
+        tma_store_2d(&tmX, sO + ob * OBUF, col, m0);
+        bulk_commit();
+        bulk_wait_read_1();
+      }
+      ob = (ob == 2) ? 0 : ob + 1;
+    };
     for (int u = blockIdx.x; u < units; u += gridDim.x) {
       const int mt = u / n_per_m, nu = u % n_per_m;
       const int m0 = mt * BM;
@@ -227,17 +265,6 @@ __global__ void __launch_bounds__(192, 1)
       const bool valid = row < p.M;
       float w_n = 0.f, w_mean = 0.f, w_m2 = 0.f;  // Welford state of this row
       float score = 0.f;
-      if constexpr (RES) {
-        if (xprod && !*abort_flag) {  // prefetch the first two residual chunks of this unit
-#pragma unroll
-          for (int k = 0; k < 2 && k < NCH; ++k) {
-            const uint32_t b = (gch + k) & 1;
-            mbar_arrive_expect_tx(&xfull[b], XCHUNK);
-            tma_load_2d(&tmX, &xfull[b], sX + b * XCHUNK, k * 32, m0);
-            x_armed[b] = 1 + (((gch + k) >> 1) & 1);
-          }
-        }
-      }
       float4 rc[8], rsn[8];  // RoPE cos/sin of this row's position (QKV epilogue)
       if constexpr (EPI == EPI_QKV_ROPE) {
         const int ps = valid ? p.pos[row] : 0;
@@ -259,20 +286,28 @@ __global__ void __launch_bounds__(192, 1)
 
         if constexpr (EPI == EPI_BF16) {
 #pragma unroll 1
-          for (int c = 0; c < BN / 32; ++c) {
-            uint32_t r[32];
-            tmem_ld32(tb + c * 32, r);
+          for (int g = 0; g < BN / 64; ++g) {
+            uint32_t lo[32], hi[32];
+            tmem_ld32(tb + g * 64, lo);
+            tmem_ld32(tb + g * 64 + 32, hi);
             tmem_ld_wait();
-            float v[32];
-            const int col = n0 + c * 32;
+            const int col = n0 + g * 64;
+            float a[32], b[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
-              float a = __uint_as_float(r[j]);
-              if (p.bias) a += p.bias[col + j];
-              if (p.relu) a = fmaxf(a, 0.f);
-              v[j] = a;
+              float x = __uint_as_float(lo[j]), y = __uint_as_float(hi[j]);
+              if (p.bias) {
+                x += p.bias[col + j];
+                y += p.bias[col + 32 + j];
+              }
+              if (p.relu) {
+                x = fmaxf(x, 0.f);
+                y = fmaxf(y, 0.f);
+              }
+              a[j] = x;
+              b[j] = y;
             }
-            if (valid) store_bf16x32(p.out + static_cast<size_t>(row) * p.ldo + col, v);
+            store_box(a, b, col, m0);
           }
         } else if constexpr (EPI == EPI_QKV_ROPE) {
 #pragma unroll 1
@@ -303,34 +338,40 @@ __global__ void __launch_bounds__(192, 1)
                 b[j] = __uint_as_float(hi[j]);
               }
             }
-            if (valid) {
-              bf16* dst = p.out + static_cast<size_t>(row) * p.ldo + col;
-              store_bf16x32(dst, a);
-              store_bf16x32(dst + 32, b);
-            }
+            store_box(a, b, col, m0);
           }
         } else if constexpr (EPI == EPI_GEGLU) {
           static_assert(BN == 256, "GEGLU tiles hold 128 gate-input + 128 gate columns");
 #pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
-            uint32_t ra[32], rb[32];
-            tmem_ld32(tb + c * 32, ra);
-            tmem_ld32(tb + 128 + c * 32, rb);
-            tmem_ld_wait();
-            float v[32];
+          for (int h = 0; h < 2; ++h) {
+            float a[32], b[32];
+            {
+              uint32_t ra[32], rb[32];
+              tmem_ld32(tb + h * 64, ra);
+              tmem_ld32(tb + 128 + h * 64, rb);
+              tmem_ld_wait();
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = gelu_erf(__uint_as_float(ra[j])) * __uint_as_float(rb[j]);
-            if (valid) store_bf16x32(p.out + static_cast<size_t>(row) * p.ldo + nu * 128 + c * 32, v);
+              for (int j = 0; j < 32; ++j) a[j] = gelu_erf(__uint_as_float(ra[j])) * __uint_as_float(rb[j]);
+            }
+            {
+              uint32_t ra[32], rb[32];
+              tmem_ld32(tb + h * 64 + 32, ra);
+              tmem_ld32(tb + 128 + h * 64 + 32, rb);
+              tmem_ld_wait();
+#pragma unroll
+              for (int j = 0; j < 32; ++j) b[j] = gelu_erf(__uint_as_float(ra[j])) * __uint_as_float(rb[j]);
+            }
+            store_box(a, b, nu * 128 + h * 64, m0);
           }
         } else if constexpr (RES) {
 #pragma unroll 1
           for (int cc = 0; cc < BN / 32; ++cc) {
             const int c = s * (BN / 32) + cc;  // chunk index within the row
-            const uint32_t b = gch & 1;
+            const uint32_t b = gch % NXB;
             uint32_t r[32];
             tmem_ld32(tb + cc * 32, r);
             tmem_ld_wait();
-            mbar_wait(&xfull[b], (gch >> 1) & 1, abort_flag, p.err, 5);
+            mbar_wait(&xfull[b], (gch / NXB) & 1, abort_flag, p.err, 5);
             // this row's 32 residual values, 128B-swizzled: 16-byte unit i sits at i ^ (row & 7)
             uint8_t* xrow = sX + b * XCHUNK + trow * 128;
             float v[32];
@@ -368,15 +409,12 @@ __global__ void __launch_bounds__(192, 1)
             }
             fence_proxy_async_smem();
             named_bar_sync(1, 128);
-            if (xprod && !*abort_flag) {
+            if (storer && !*abort_flag) {
               tma_store_2d(&tmX, sX + b * XCHUNK, c * 32, m0);
               bulk_commit();
-              if (c + 2 < NCH) {
-                bulk_wait_read_all();  // buffer b free again
-                mbar_arrive_expect_tx(&xfull[b], XCHUNK);
-                tma_load_2d(&tmX, &xfull[b], sX + b * XCHUNK, (c + 2) * 32, m0);
-                x_armed[b] = 1 + (((gch + 2) >> 1) & 1);
-              }
+              bulk_wait_read_1();  // the previous chunk's store has read its slot: hand it back
+              if (xpend >= 0) mbar_arrive(&xempty[xpend]);
+              xpend = static_cast<int>(b);
             }
             ++gch;
           }
@@ -398,9 +436,11 @@ __global__ void __launch_bounds__(192, 1)
       }
       if constexpr (RES) {
         // the updated rows must be in global memory before they are re-read below / by the next kernel
-        if (xprod) {
+        if (storer) {
           bulk_wait_all();
           fence_proxy_async_global();
+          if (xpend >= 0) mbar_arrive(&xempty[xpend]);
+          xpend = -1;
         }
         named_bar_sync(1, 128);
       }
@@ -452,12 +492,33 @@ __global__ void __launch_bounds__(192, 1)
         if (valid) p.scores[row] = score + p.b2;
       }
     }
+    if (storer) bulk_wait_all();  // no store of ours may still read smem at exit
+  } else if (warp == 6) {
+    // ------------------------------------------------------------ residual producer (RESID*)
     if constexpr (RES) {
-      if (xprod) {  // nothing of ours may still be in flight into or out of smem at exit
-        bulk_wait_all();
-        volatile int no_abort = 0;
-        for (int b = 0; b < 2; ++b)
-          if (x_armed[b]) mbar_wait(&xfull[b], x_armed[b] - 1, &no_abort, nullptr, 0);
+      if (lane == 0) {
+        uint32_t gx = 0;                    // chunks issued so far (ring slot = gx % NXB)
+        uint32_t armed = 0, armed_par = 0;  // per slot: armed bit and the parity it was armed with
+        bool ok = true;
+        for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+          const int m0 = (u / n_per_m) * BM;
+          for (int c = 0; c < NCH; ++c, ++gx) {
+            const uint32_t b = gx % NXB, ph = (gx / NXB) & 1;
+            if (!mbar_wait(&xempty[b], ph ^ 1, abort_flag, p.err, 6)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&xfull[b], XCHUNK);
+            tma_load_2d(&tmX, &xfull[b], sX + b * XCHUNK, c * 32, m0);
+            armed |= 1u << b;
+            armed_par = (armed_par & ~(1u << b)) | (ph << b);
+          }
+        }
+        if (!ok) {  // unwinding: every load already issued must land before smem is released
+          volatile int no_abort = 0;
+          for (uint32_t b = 0; b < NXB; ++b)
+            if (armed & (1u << b)) mbar_wait(&xfull[b], (armed_par >> b) & 1u, &no_abort, nullptr, 0);
+        }
       }
     }
   }
@@ -478,7 +539,7 @@ int launch_one(const CUtensorMap& tmA, const CUtensorMap& tmW, const CUtensorMap
   const int units = ((p.M + BM - 1) / BM) * (is_full_row(EPI) ? 1 : p.N / BN);
   const int grid = units < grid_limit ? units : grid_limit;
   if (grid <= 0) return 0;
-  kern<<<grid, 192, GemmCfg<BN, EPI>::SMEM, stream>>>(tmA, tmW, tmX, p);
+  kern<<<grid, GEMM_THREADS, GemmCfg<BN, EPI>::SMEM, stream>>>(tmA, tmW, tmX, p);
   return static_cast<int>(cudaGetLastError());
 }
 
@@ -513,7 +574,8 @@ const char* gemm_shape_error(GemmEpi epi, int bn, int M, int N, int K) {
 int launch_gemm(GemmEpi epi, int bn, const CUtensorMap& tmA, const CUtensorMap& tmW, const CUtensorMap* tmX,
                 const EpiParams& p, int grid_limit, cudaStream_t stream) {
   if (p.M == 0) return 0;
-  const CUtensorMap& X = tmX ? *tmX : tmA;  // unused by non-residual epilogues
+  if (!tmX && epi != EPI_SCORER) return static_cast<int>(cudaErrorInvalidValue);
+  const CUtensorMap& X = tmX ? *tmX : tmA;  // unused by the scorer epilogue
   switch (epi) {
     case EPI_BF16:
       return bn == 256 ? launch_one<256, EPI_BF16, 1>(tmA, tmW, X, p, grid_limit, stream)
@@ -524,10 +586,8 @@ int launch_gemm(GemmEpi epi, int bn, const CUtensorMap& tmA, const CUtensorMap& 
     case EPI_GEGLU:
       return launch_one<256, EPI_GEGLU, 1>(tmA, tmW, X, p, grid_limit, stream);
     case EPI_RESID_LN:
-      if (!tmX) return static_cast<int>(cudaErrorInvalidValue);
       return launch_full_row<EPI_RESID_LN>(p.N, tmA, tmW, X, p, grid_limit, stream);
     case EPI_RESID:
-      if (!tmX) return static_cast<int>(cudaErrorInvalidValue);
       return launch_full_row<EPI_RESID>(p.N, tmA, tmW, X, p, grid_limit, stream);
     case EPI_SCORER:
       return launch_full_row<EPI_SCORER>(p.N, tmA, tmW, X, p, grid_limit, stream);

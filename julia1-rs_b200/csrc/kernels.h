@@ -64,15 +64,17 @@ struct EpiParams {
 
 // Column width of one MMA tile for an N (or full-row width): 256 when N % 256 == 0, else 128.
 int gemm_bn_for(int n);
-// Returns 0 on success, or a cudaError_t value. tmX: FP32 residual map (make_tmap_f32_resid)
-// over p.x, required by EPI_RESID_LN / EPI_RESID, ignored otherwise (may be null).
+// Returns 0 on success, or a cudaError_t value. tmX: the map of the epilogue's global tensor:
+// the FP32 residual map (make_tmap_f32_resid) over p.x for EPI_RESID_LN / EPI_RESID; the
+// BF16 output map over p.out (make_tmap_bf16, box 64 x 128, N columns -- N/2 for GEGLU --
+// and row stride p.ldo) for EPI_BF16 / EPI_QKV_ROPE / EPI_GEGLU; ignored by EPI_SCORER.
 int launch_gemm(GemmEpi epi, int bn, const CUtensorMap& tmA, const CUtensorMap& tmW, const CUtensorMap* tmX,
                 const EpiParams& p, int grid_limit, cudaStream_t stream);
 // Validates shapes for an epilogue; returns nullptr when fine, else a message.
 const char* gemm_shape_error(GemmEpi epi, int bn, int M, int N, int K);
 
 // ------------------------------------------------------------------ attention
-// Queries covered by one attention CTA (two 128-query tiles).
+// Queries covered by one attention work item (one 128-query tile).
 int attention_pair_queries();
 // One CTA's queries (up to attention_pair_queries()) of one sequence. Query row r of the tile is Q-buffer row
 // q_row0 + r at sequence position q_pos0 + r; keys/values are rows

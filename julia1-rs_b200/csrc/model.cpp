@@ -324,7 +324,7 @@ j1_status launch_forward(j1_model* model) {
     p.out = model->qkv, p.ldo = 3 * H;
     p.pos = model->d_pos, p.rope_cos = model->rope_cos[ly.rope], p.rope_sin = model->rope_sin[ly.rope];
     p.rope_cols = 2 * H;
-    J1_TRY_LAUNCH(F_QKV, launch_gemm(EPI_QKV_ROPE, bn_qkv, model->tm_xn, ly.tm_wqkv, nullptr, p, nsm, st), "gemm qkv");
+    J1_TRY_LAUNCH(F_QKV, launch_gemm(EPI_QKV_ROPE, bn_qkv, model->tm_xn, ly.tm_wqkv, &model->tm_qkv, p, nsm, st), "gemm qkv");
     J1_TRY_LAUNCH(ly.global ? F_ATTN_GLOBAL : F_ATTN_LOCAL,
                   launch_attention(model->tm_qkv, model->tm_qkv, model->d_tiles, static_cast<int>(model->ntiles),
                                    c.heads, 0, H, 2 * H, model->ctx, H, ly.global ? -1 : c.half_window, kScaleLog2,
@@ -338,7 +338,7 @@ j1_status launch_forward(j1_model* model) {
     p = base;
     p.M = t, p.N = 2 * I, p.K = H;
     p.out = model->g, p.ldo = I;
-    J1_TRY_LAUNCH(F_WI, launch_gemm(EPI_GEGLU, 256, model->tm_xn, ly.tm_wi, nullptr, p, nsm, st), "gemm wi");
+    J1_TRY_LAUNCH(F_WI, launch_gemm(EPI_GEGLU, 256, model->tm_xn, ly.tm_wi, &model->tm_g, p, nsm, st), "gemm wi");
     p = base;
     p.M = t, p.N = H, p.K = I;
     p.x = model->x, p.ldx = H;
@@ -359,7 +359,7 @@ j1_status launch_forward(j1_model* model) {
     EpiParams p = base;
     p.M = t, p.N = 3 * H, p.K = H;
     p.out = model->qkv, p.ldo = 3 * H, p.bias = hl.in_b;
-    J1_TRY_LAUNCH(F_HEAD_GEMM, launch_gemm(EPI_BF16, bn_qkv, model->tm_xn, hl.tm_in, nullptr, p, nsm, st), "gemm in_proj");
+    J1_TRY_LAUNCH(F_HEAD_GEMM, launch_gemm(EPI_BF16, bn_qkv, model->tm_xn, hl.tm_in, &model->tm_qkv, p, nsm, st), "gemm in_proj");
     J1_TRY_LAUNCH(F_HEAD_ATTN,
                   launch_attention(model->tm_qkv, model->tm_qkv, model->d_tiles, static_cast<int>(model->ntiles),
                                    c.head_heads, 0, H, 2 * H, model->ctx, H, -1, kScaleLog2, model->err_dev, nsm, st),
@@ -372,7 +372,7 @@ j1_status launch_forward(j1_model* model) {
       J1_TRY_LAUNCH(F_HEAD_GEMM, launch_gemm(EPI_RESID_LN, bn_full, model->tm_ctx, hl.tm_out, &model->tm_x, p, nsm, st), "gemm out_proj");
       p = base;
       p.M = t, p.N = FF, p.K = H, p.out = model->g, p.ldo = FF, p.bias = hl.lin1_b, p.relu = 1;
-      J1_TRY_LAUNCH(F_HEAD_GEMM, launch_gemm(EPI_BF16, bn_ff, model->tm_xn, hl.tm_lin1, nullptr, p, nsm, st), "gemm linear1");
+      J1_TRY_LAUNCH(F_HEAD_GEMM, launch_gemm(EPI_BF16, bn_ff, model->tm_xn, hl.tm_lin1, &model->tm_h, p, nsm, st), "gemm linear1");
       const auto& nx = model->head[j + 1];
       p = base;
       p.M = t, p.N = H, p.K = FF, p.bias = hl.lin2_b;
@@ -390,7 +390,7 @@ j1_status launch_forward(j1_model* model) {
       J1_TRY_LAUNCH(F_HEAD_GEMM, launch_gemm(EPI_RESID_LN, bn_full, model->tm_cm, hl.tm_out, &model->tm_ym, p, nsm, st), "gemm out_proj");
       p = base;
       p.M = m, p.N = FF, p.K = H, p.out = model->hm, p.ldo = FF, p.bias = hl.lin1_b, p.relu = 1;
-      J1_TRY_LAUNCH(F_HEAD_GEMM, launch_gemm(EPI_BF16, bn_ff, model->tm_ymb, hl.tm_lin1, nullptr, p, nsm, st), "gemm linear1");
+      J1_TRY_LAUNCH(F_HEAD_GEMM, launch_gemm(EPI_BF16, bn_ff, model->tm_ymb, hl.tm_lin1, &model->tm_hm, p, nsm, st), "gemm linear1");
       p = base;
       p.M = m, p.N = H, p.K = FF, p.bias = hl.lin2_b;
       p.x = model->ym, p.ldx = H, p.ln_w = model->s_norm_w, p.ln_b = model->s_norm_b, p.ln_eps = 1e-5f;
@@ -809,6 +809,12 @@ j1_status j1_op_gemm(const j1_gemm_args* a, void* stream, int sync) {
   const bool resid = epi == EPI_RESID_LN || epi == EPI_RESID;
   if (resid && !make_tmap_f32_resid(&tmX, a->x, a->M, a->N, a->ldx, &why))
     return set_error(J1_ERR_INVALID_ARG, std::string("tensor map: ") + (why ? why : ""));
+  const bool tile_out = epi == EPI_BF16 || epi == EPI_QKV_ROPE || epi == EPI_GEGLU;
+  const int out_cols = epi == EPI_GEGLU ? a->N / 2 : a->N;
+  if (tile_out && (a->ldo < out_cols || a->ldo % 8 != 0))
+    return set_error(J1_ERR_INVALID_ARG, "ldo must be >= the output width and a multiple of 8");
+  if (tile_out && !make_tmap_bf16(&tmX, a->out, a->M, out_cols, a->ldo, 128, &why))
+    return set_error(J1_ERR_INVALID_ARG, std::string("tensor map: ") + (why ? why : ""));
   EpiParams p;
   std::memset(&p, 0, sizeof(p));
   p.M = a->M, p.N = a->N, p.K = a->K;
@@ -822,7 +828,7 @@ j1_status j1_op_gemm(const j1_gemm_args* a, void* stream, int sync) {
   p.err = os->err;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int grid = a->grid_limit > 0 ? a->grid_limit : os->num_sms;
-  int rc = launch_gemm(epi, bn, tmA, tmW, resid ? &tmX : nullptr, p, grid, st);
+  int rc = launch_gemm(epi, bn, tmA, tmW, (resid || tile_out) ? &tmX : nullptr, p, grid, st);
   if (rc) return cuda_error(static_cast<cudaError_t>(rc), "gemm launch");
   return sync ? op_sync_check(os, st) : J1_OK;
 }
