@@ -75,7 +75,9 @@ def family_model(t, seqs, m):
                                   bound="hbm"),
         "attn_global": dict(flops=4.0 * H * pg, bytes=t * 3 * H * 2 + t * H * 2, bound="tensor"),
         "attn_local": dict(flops=4.0 * H * pl, bytes=t * 3 * H * 2 + t * H * 2, bound="tensor"),
-        "head_attn": dict(flops=4.0 * H * pg, bytes=t * 3 * H * 2 + t * H * 2, bound="tensor"),
+        # two head layers: full attention over every row, then marker queries only (per-launch mean)
+        "head_attn": dict(flops=4.0 * H * (pg + m * SEQ) / 2, bytes=(t * 3 * H * 2 + t * H * 2 + t * 2 * H * 2 +
+                                                                     m * H * 4) / 2, bound="tensor"),
     }
 
 

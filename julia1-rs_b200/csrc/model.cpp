@@ -191,6 +191,7 @@ j1_status ensure_workspace(j1_model* model, size_t tokens, size_t markers, size_
     J1_WS(ymb, bf16*, M * H * 2)
     J1_WS(cm, bf16*, M * H * 2)
     J1_WS(hm, bf16*, M * FF * 2)
+    J1_WS(qm, bf16*, M * H * 2)
     J1_WS(scores, float*, M * 4)
     J1_WS(meta_dev, int*, E * 4)
 #undef J1_WS
@@ -241,12 +242,15 @@ j1_status stage_batch(j1_model* model, const BatchView& b) {
   j1_status s = validate_batch(model, b);
   if (s) return s;
   J1_TRY_CUDA(cudaStreamSynchronize(model->stream), "stage");  // pinned staging is reused
-  size_t ntiles = 0;
-  const int PQ = attention_pair_queries();  // queries per attention CTA (two 128-row tiles)
-  for (size_t q = 0; q < b.nseq; ++q) ntiles += (b.lens[q] + PQ - 1) / PQ;
+  size_t ntiles = 0, nmtiles = 0;
+  const int PQ = attention_pair_queries();  // queries per attention work item
+  for (size_t q = 0; q < b.nseq; ++q) {
+    ntiles += (b.lens[q] + PQ - 1) / PQ;
+    nmtiles += (b.marker_starts[q + 1] - b.marker_starts[q] + PQ - 1) / PQ;
+  }
   const size_t t = b.t, m = b.m;
   const size_t tiles_off = (3 * t + m + 7) / 8 * 8;
-  const size_t meta_ints = tiles_off + ntiles * 8;
+  const size_t meta_ints = tiles_off + (ntiles + nmtiles) * 8;
   if ((s = ensure_workspace(model, t, m, meta_ints))) return s;
   int* h = model->meta_host;
   for (size_t i = 0; i < t; ++i) h[i] = static_cast<int>(b.ids[i]);
@@ -270,6 +274,20 @@ j1_status stage_batch(j1_model* model, const BatchView& b) {
       tl.pad0 = tl.pad1 = tl.pad2 = 0;
     }
   }
+  // last head layer: the marker rows of each sequence as query tiles (rows of qm) over
+  // all of that sequence's keys
+  for (size_t q = 0; q < b.nseq; ++q) {
+    const int k0 = static_cast<int>(b.marker_starts[q]), k1 = static_cast<int>(b.marker_starts[q + 1]);
+    for (int r0 = k0; r0 < k1; r0 += PQ) {
+      AttnTile& tl = tiles[ti++];
+      tl.q_row0 = r0;
+      tl.nq = k1 - r0 < PQ ? k1 - r0 : PQ;
+      tl.kv_row0 = static_cast<int>(b.starts[q]);
+      tl.kv_len = static_cast<int>(b.lens[q]);
+      tl.q_pos0 = 0;
+      tl.pad0 = tl.pad1 = tl.pad2 = 0;
+    }
+  }
   for (size_t k = 0; k < m; ++k) h[3 * t + k] = static_cast<int>(b.marker_rows[k]);
   if (meta_ints)
     J1_TRY_CUDA(cudaMemcpyAsync(model->meta_dev, h, meta_ints * 4, cudaMemcpyHostToDevice, model->stream),
@@ -278,11 +296,13 @@ j1_status stage_batch(j1_model* model, const BatchView& b) {
   model->m = m;
   model->nseq = b.nseq;
   model->ntiles = ntiles;
+  model->nmtiles = nmtiles;
   model->d_ids = model->meta_dev;
   model->d_pos = model->meta_dev + t;
   model->d_qtype = model->meta_dev + 2 * t;
   model->d_markers = model->meta_dev + 3 * t;
   model->d_tiles = reinterpret_cast<AttnTile*>(model->meta_dev + tiles_off);
+  model->d_mtiles = model->d_tiles + ntiles;
   const ModelConfig& c = model->cfg;
   const size_t H = c.hidden, I = c.intermediate, FF = c.head_ff;
   const char* why = nullptr;
@@ -294,6 +314,8 @@ j1_status stage_batch(j1_model* model, const BatchView& b) {
             make_tmap_bf16(&model->tm_cm, model->cm, m, H, H, 128, &why) &&
             make_tmap_bf16(&model->tm_ymb, model->ymb, m, H, H, 128, &why) &&
             make_tmap_bf16(&model->tm_hm, model->hm, m, FF, FF, 128, &why) &&
+            make_tmap_bf16(&model->tm_qm, model->qm, m, H, H, 128, &why) &&
+            make_tmap_bf16(&model->tm_qkv_kv, model->qkv + H, t, 2 * H, 3 * H, 128, &why) &&
             make_tmap_f32_resid(&model->tm_x, model->x, t, H, H, &why) &&
             make_tmap_f32_resid(&model->tm_ym, model->ym, m, H, H, &why);
   if (!ok) return set_error(J1_ERR_CUDA, std::string("activation tensor map: ") + (why ? why : ""));
@@ -357,21 +379,21 @@ j1_status launch_forward(j1_model* model) {
   for (int j = 0; j < nh; ++j) {
     const auto& hl = model->head[j];
     EpiParams p = base;
-    p.M = t, p.N = 3 * H, p.K = H;
-    p.out = model->qkv, p.ldo = 3 * H, p.bias = hl.in_b;
-    J1_TRY_LAUNCH(F_HEAD_GEMM, launch_gemm(EPI_BF16, bn_qkv, model->tm_xn, hl.tm_in, &model->tm_qkv, p, nsm, st), "gemm in_proj");
-    J1_TRY_LAUNCH(F_HEAD_ATTN,
-                  launch_attention(model->tm_qkv, model->tm_qkv, model->d_tiles, static_cast<int>(model->ntiles),
-                                   c.head_heads, 0, H, 2 * H, model->ctx, H, -1, kScaleLog2, model->err_dev, nsm, st),
-                  "head attention");
     if (j + 1 < nh) {
+      p.M = t, p.N = 3 * H, p.K = H;
+      p.bias = hl.in_b;
+      J1_TRY_LAUNCH(F_HEAD_GEMM, launch_gemm(EPI_BF16, bn_qkv, model->tm_xn, hl.tm_in, &model->tm_qkv, p, nsm, st), "gemm in_proj");
+      J1_TRY_LAUNCH(F_HEAD_ATTN,
+                    launch_attention(model->tm_qkv, model->tm_qkv, model->d_tiles, static_cast<int>(model->ntiles),
+                                     c.head_heads, 0, H, 2 * H, model->ctx, H, -1, kScaleLog2, model->err_dev, nsm, st),
+                    "head attention");
       p = base;
       p.M = t, p.N = H, p.K = H, p.bias = hl.out_b;
       p.x = model->x, p.ldx = H, p.ln_w = hl.norm2_w, p.ln_b = hl.norm2_b, p.ln_eps = 1e-5f;
       p.xn = model->xn, p.ldxn = H;
       J1_TRY_LAUNCH(F_HEAD_GEMM, launch_gemm(EPI_RESID_LN, bn_full, model->tm_ctx, hl.tm_out, &model->tm_x, p, nsm, st), "gemm out_proj");
       p = base;
-      p.M = t, p.N = FF, p.K = H, p.out = model->g, p.ldo = FF, p.bias = hl.lin1_b, p.relu = 1;
+      p.M = t, p.N = FF, p.K = H, p.bias = hl.lin1_b, p.relu = 1;
       J1_TRY_LAUNCH(F_HEAD_GEMM, launch_gemm(EPI_BF16, bn_ff, model->tm_xn, hl.tm_lin1, &model->tm_h, p, nsm, st), "gemm linear1");
       const auto& nx = model->head[j + 1];
       p = base;
@@ -379,9 +401,22 @@ j1_status launch_forward(j1_model* model) {
       p.x = model->x, p.ldx = H, p.ln_w = nx.norm1_w, p.ln_b = nx.norm1_b, p.ln_eps = 1e-5f;
       p.xn = model->xn, p.ldxn = H;
       J1_TRY_LAUNCH(F_HEAD_GEMM, launch_gemm(EPI_RESID_LN, bn_full, model->tm_h, hl.tm_lin2, &model->tm_x, p, nsm, st), "gemm linear2");
-    } else {
-      // Last head layer: only the option markers feed the scorer (src/cuda/mod.rs:496-506).
-      J1_TRY_LAUNCH(F_HEAD_ROWS, launch_gather_rows(model->ctx, model->d_markers, model->cm, m, H * 2, st), "gather ctx");
+    } else if (m > 0) {
+      // Last head layer: only the option markers feed the scorer, so the queries, the
+      // attention rows and everything after them are computed for the m marker rows
+      // alone (the reference's CPU path does the same, src/cpu/mod.rs:293-321; its CUDA
+      // path computes all t rows and gathers, src/cuda/mod.rs:480-507 -- rows are
+      // independent, so the marker rows agree). Keys and values still cover every token.
+      J1_TRY_LAUNCH(F_HEAD_ROWS, launch_gather_rows(model->xn, model->d_markers, model->ymb, m, H * 2, st), "gather xn");
+      p.M = m, p.N = H, p.K = H, p.bias = hl.in_b;
+      J1_TRY_LAUNCH(F_HEAD_GEMM, launch_gemm(EPI_BF16, bn_full, model->tm_ymb, hl.tm_in_q, &model->tm_qm, p, nsm, st), "gemm in_proj q");
+      p = base;
+      p.M = t, p.N = 2 * H, p.K = H, p.bias = hl.in_b + H;
+      J1_TRY_LAUNCH(F_HEAD_GEMM, launch_gemm(EPI_BF16, gemm_bn_for(2 * H), model->tm_xn, hl.tm_in_kv, &model->tm_qkv_kv, p, nsm, st), "gemm in_proj kv");
+      J1_TRY_LAUNCH(F_HEAD_ATTN,
+                    launch_attention(model->tm_qm, model->tm_qkv, model->d_mtiles, static_cast<int>(model->nmtiles),
+                                     c.head_heads, 0, H, 2 * H, model->cm, H, -1, kScaleLog2, model->err_dev, nsm, st),
+                    "head attention (markers)");
       J1_TRY_LAUNCH(F_HEAD_ROWS, launch_gather_rows(model->x, model->d_markers, model->ym, m, H * 4, st), "gather x");
       p = base;
       p.M = m, p.N = H, p.K = H, p.bias = hl.out_b;
@@ -389,7 +424,7 @@ j1_status launch_forward(j1_model* model) {
       p.xn = model->ymb, p.ldxn = H;
       J1_TRY_LAUNCH(F_HEAD_GEMM, launch_gemm(EPI_RESID_LN, bn_full, model->tm_cm, hl.tm_out, &model->tm_ym, p, nsm, st), "gemm out_proj");
       p = base;
-      p.M = m, p.N = FF, p.K = H, p.out = model->hm, p.ldo = FF, p.bias = hl.lin1_b, p.relu = 1;
+      p.M = m, p.N = FF, p.K = H, p.bias = hl.lin1_b, p.relu = 1;
       J1_TRY_LAUNCH(F_HEAD_GEMM, launch_gemm(EPI_BF16, bn_ff, model->tm_ymb, hl.tm_lin1, &model->tm_hm, p, nsm, st), "gemm linear1");
       p = base;
       p.M = m, p.N = H, p.K = FF, p.bias = hl.lin2_b;
@@ -576,6 +611,10 @@ j1_status create_model(const char* ckpt_dir, int ordinal, j1_model** out) {
         (s = upload_bf16(M, st, pre + "linear1.weight", FF, H, 0, staging, &hl.lin1_w, &hl.tm_lin1, bn_ff)) ||
         (s = upload_bf16(M, st, pre + "linear2.weight", H, FF, 0, staging, &hl.lin2_w, &hl.tm_lin2, bn_full)))
       return s;
+    const char* why = nullptr;
+    if (!make_tmap_bf16(&hl.tm_in_q, hl.in_w, H, H, H, bn_full, &why) ||
+        !make_tmap_bf16(&hl.tm_in_kv, hl.in_w + static_cast<size_t>(H) * H, 2 * H, H, H, gemm_bn_for(2 * H), &why))
+      return set_error(J1_ERR_CUDA, std::string("weight tensor map: ") + (why ? why : ""));
     M->head.push_back(hl);
   }
   if ((s = upload_f32(M, st, "scorer.0.weight", {H}, &M->s_norm_w)) ||

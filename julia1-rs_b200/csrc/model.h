@@ -74,6 +74,7 @@ struct j1_model {
     float *norm1_w, *norm1_b, *in_b, *out_b, *norm2_w, *norm2_b, *lin1_b, *lin2_b;
     j1rt::bf16 *in_w, *out_w, *lin1_w, *lin2_w;
     CUtensorMap tm_in, tm_out, tm_lin1, tm_lin2;
+    CUtensorMap tm_in_q, tm_in_kv;  // in_proj rows [0, H) (queries) and [H, 3H) (keys, values)
   };
   std::vector<Head> head;
   float *s_norm_w = nullptr, *s_norm_b = nullptr, *s_b1 = nullptr, *s_w2 = nullptr;
@@ -88,7 +89,7 @@ struct j1_model {
   float* x = nullptr;
   j1rt::bf16 *xn = nullptr, *qkv = nullptr, *ctx = nullptr, *g = nullptr;
   float* ym = nullptr;
-  j1rt::bf16 *ymb = nullptr, *cm = nullptr, *hm = nullptr;
+  j1rt::bf16 *ymb = nullptr, *cm = nullptr, *hm = nullptr, *qm = nullptr;
   float* scores = nullptr;
   int* meta_dev = nullptr;
   int* meta_host = nullptr;      // pinned
@@ -98,10 +99,12 @@ struct j1_model {
 
   // ---- staged batch
   bool staged = false;
-  size_t t = 0, m = 0, nseq = 0, ntiles = 0;
+  size_t t = 0, m = 0, nseq = 0, ntiles = 0, nmtiles = 0;
   int *d_ids = nullptr, *d_pos = nullptr, *d_qtype = nullptr, *d_markers = nullptr;
   j1rt::AttnTile* d_tiles = nullptr;
+  j1rt::AttnTile* d_mtiles = nullptr;  // marker-query tiles of the last head layer
   CUtensorMap tm_xn, tm_ctx, tm_g, tm_h, tm_qkv, tm_cm, tm_ymb, tm_hm;
+  CUtensorMap tm_qm, tm_qkv_kv;  // marker queries [m, H]; the k|v columns of qkv
   CUtensorMap tm_x, tm_ym;  // FP32 residual streams (tokens, markers)
   int64_t launches = 0;
 

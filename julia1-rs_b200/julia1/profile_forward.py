@@ -4,7 +4,7 @@
 
 Creates a seeded synthetic checkpoint (ModernBERT-base shape), stages one batch of
 R rows x S tokens (20 options per row, as in bench.py) and runs F forwards through
-the C ABI. Kernel launches per forward: 125 for the default 2-layer head. Weight
+the C ABI. Kernel launches per forward: 126 for the default 2-layer head. Weight
 conversion at load issues 97 launches before the first forward.
 """
 import argparse
