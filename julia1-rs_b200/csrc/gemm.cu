@@ -8,9 +8,11 @@
 //   head in_proj/lin1    -> EPI_BF16 with bias (+relu)  (kernels.cu:158-172)
 //   scorer W1 + scorer   -> EPI_SCORER   (kernels.cu:186-194)
 //
-// Structure: persistent CTAs (one per SM), 224 threads.
+// Structure: persistent CTA pairs (clusters of two CTAs on two SMs), 224 threads per CTA;
+// the pair shares each 256-row tile through tcgen05 .cta_group::2 (see gemm_tc_kernel).
 //   warp 0      TMA producer: A (128 x 64) and W (BN x 64) boxes into a smem ring
-//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer (M=128, N=BN, K=16)
+//   warp 1      TMEM allocator; in the even CTA also the single-thread tcgen05.mma issuer
+//               (M=256 over the pair, N=BN, K=16)
 //   warps 2..5  epilogue: tcgen05.ld of the FP32 accumulator (TMEM lane = row), fused math
 //   warp 6      residual producer (RESID*): TMA loads of x chunks into a smem ring
 // The accumulator is double buffered in TMEM (2 x BN columns) so the epilogue of one
@@ -51,15 +53,19 @@ __host__ __device__ constexpr bool is_tile_out(int epi) {
 
 template <int BN, int EPI>
 struct GemmCfg {
-  // main-loop ring depth: what is left of 227 KB after the x ring / output boxes
-  static constexpr int STAGES = (EPI == EPI_SCORER) ? (BN == 256 ? 4 : 6) : (BN == 256 ? 3 : 5);
+  // per CTA of a pair: 128 rows of A and BN/2 rows of W per stage; the ring takes what is
+  // left of 227 KB after the x ring / output boxes
+  static constexpr int STAGES = (EPI == EPI_SCORER) ? (BN == 256 ? 6 : 8)
+                                : is_resid(EPI)     ? (BN == 256 ? 5 : 6)
+                                                    : (BN == 256 ? 5 : 7);
   static constexpr uint32_t A_BYTES = BM * BK * 2;
-  static constexpr uint32_t B_BYTES = BN * BK * 2;
+  static constexpr uint32_t B_BYTES = (BN / 2) * BK * 2;
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr uint32_t X_BYTES = is_resid(EPI) ? NXB * XCHUNK : 0;
   static constexpr uint32_t O_BYTES = is_tile_out(EPI) ? 3 * OBUF : 0;
   static constexpr uint32_t SMEM = STAGES * STAGE_BYTES + X_BYTES + O_BYTES + 1024 /*align*/ + 256 /*barriers*/;
   static_assert(SMEM <= 232448, "shared memory budget");
+  static_assert(2 * STAGES + 4 + 1 + 2 * NXB <= 30, "barrier area");
 };
 
 __device__ __forceinline__ float gelu_erf(float v) { return 0.5f * v * (1.f + erff(v * 0.70710678118654752f)); }
@@ -79,8 +85,13 @@ __device__ __forceinline__ void put_row32(uint8_t* srow, int r, int unit0, const
 }
 
 // BN: MMA tile width; NSUB: sub-tiles per full-row unit (full-row width H = NSUB * BN).
+// Launched as clusters of two CTAs (a pair). A pair computes 256-row tiles: each CTA
+// loads its own 128 rows of A and its own half (BN/2 rows) of the W tile into smem, the
+// even CTA issues tcgen05.mma.cta_group::2 (M = 256, N = BN) over both CTAs' operands,
+// and each CTA's TMEM receives the accumulator of its 128 rows, which its own epilogue
+// warps consume. Per 128 x BN of output a CTA thus moves A + W/2 instead of A + W.
 template <int BN, int EPI, int NSUB>
-__global__ void __launch_bounds__(GEMM_THREADS, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                    const __grid_constant__ CUtensorMap tmX, const EpiParams p) {
   using C = GemmCfg<BN, EPI>;
@@ -105,15 +116,23 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id(), lane = lane_id();
-  const int m_tiles = (p.M + BM - 1) / BM;
+  const uint32_t rank = cluster_ctarank();  // 0: the CTA that issues the pair's MMAs
+  const bool leader = rank == 0;
+  const int pair = static_cast<int>(blockIdx.x >> 1), npairs = static_cast<int>(gridDim.x >> 1);
+  const int m_tiles = (p.M + 2 * BM - 1) / (2 * BM);
   const int n_sub = FULL_ROW ? NSUB : 1;
   const int n_per_m = FULL_ROW ? 1 : p.N / BN;
   const int units = m_tiles * n_per_m;
   const int kblocks = p.K / BK;
-  {  // exit before allocating anything when an earlier CTA of this launch gave up
+  {  // exit before allocating anything when an earlier CTA of this launch gave up; the
+     // leader decides for both CTAs so that the pair stays together
     __shared__ int s_abort;
-    if (threadIdx.x == 0) s_abort = device_aborted(p.err) ? 1 : 0;
-    __syncthreads();
+    if (leader && threadIdx.x == 0) {
+      const int a = device_aborted(p.err) ? 1 : 0;
+      s_abort = a;
+      st_shared_cluster_u32(mapa_shared(smem_u32(&s_abort), 1), static_cast<uint32_t>(a));
+    }
+    cluster_sync();
     if (s_abort) return;
   }
 
@@ -124,7 +143,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 128);
+      mbar_init(&tempty[b], 8);  // one arrival per epilogue warp of both CTAs
     }
     for (uint32_t b = 0; b < NXB; ++b) {
       mbar_init(&xfull[b], 1);
@@ -137,38 +156,38 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmW);
-    if (RES) tma_prefetch_desc(&tmX);
+    if (RES || is_tile_out(EPI)) tma_prefetch_desc(&tmX);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 2 * BN);
-    tmem_relinquish();
+    tmem_alloc_pair(tmem_slot, 2 * BN);
+    tmem_relinquish_pair();
   }
   tc_fence_before();
-  __syncthreads();
+  cluster_sync();  // barriers of both CTAs initialised, TMEM allocated in both
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
-    // ------------------------------------------------------------ producer
+    // ------------------------------------------------------------ producer (both CTAs)
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      uint32_t armed = 0, armed_par = 0;  // per stage: armed bit and the parity it was armed with
       bool ok = true;
-      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+      for (int u = pair; u < units && ok; u += npairs) {
         const int mt = u / n_per_m, nu = u % n_per_m;
+        const int m0 = mt * 2 * BM + static_cast<int>(rank) * BM;
         for (int s = 0; s < n_sub && ok; ++s) {
-          const int n0 = (FULL_ROW ? s : nu) * BN;
+          const int n0 = (FULL_ROW ? s : nu) * BN + static_cast<int>(rank) * (BN / 2);
           for (int kb = 0; kb < kblocks; ++kb) {
             if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.err, 1)) {
               ok = false;
               break;
             }
-            mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
-            tma_load_2d(&tmA, &full[stage], sA + stage * C::A_BYTES, kb * BK, mt * BM);
-            tma_load_2d(&tmW, &full[stage], sB + stage * C::B_BYTES, kb * BK, n0);
-            armed |= 1u << stage;
-            armed_par = (armed_par & ~(1u << stage)) | (phase << stage);
+            // both CTAs' boxes of this stage complete on the leader's barrier
+            if (leader) mbar_arrive_expect_tx(&full[stage], 2 * C::STAGE_BYTES);
+            const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
+            tma_load_2d_pair(&tmA, fb, sA + stage * C::A_BYTES, kb * BK, m0);
+            tma_load_2d_pair(&tmW, fb, sB + stage * C::B_BYTES, kb * BK, n0);
             if (++stage == C::STAGES) {
               stage = 0;
               phase ^= 1;
@@ -177,21 +196,22 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
       }
       if (!ok) {
-        // Unwinding: let every copy already in flight land before smem is released.
-        volatile int no_abort = 0;
-        for (int s = 0; s < C::STAGES; ++s)
-          if (armed & (1u << s)) mbar_wait(&full[s], (armed_par >> s) & 1u, &no_abort, nullptr, 0);
+        // Unwinding: loads of this CTA may complete on the other CTA's barrier, so they
+        // cannot all be waited for here; give any copy in flight ample time to land
+        // before the CTA releases its shared memory (this path only follows a timeout).
+        const long long t0 = clock64();
+        while (clock64() - t0 < 2000000) __nanosleep(1000);
       }
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16(BM, BN, false, false);
+    // ------------------------------------------------------------ MMA issuer (even CTA)
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16(2 * BM, BN, false, false);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+      for (int u = pair; u < units && ok; u += npairs) {
         for (int s = 0; s < n_sub && ok; ++s) {
           const int buf = acc & 1;
           const uint32_t aph = (acc >> 1) & 1;
@@ -211,22 +231,24 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             const uint32_t b0 = smem_u32(sB + stage * C::B_BYTES);
 #pragma unroll
             for (int k = 0; k < BK / 16; ++k) {
-              umma_bf16(d, sdesc_sw128(a0 + k * 32, 16, 1024), sdesc_sw128(b0 + k * 32, 16, 1024), idesc,
-                        (kb | k) != 0);
+              umma_bf16_pair(d, sdesc_sw128(a0 + k * 32, 16, 1024), sdesc_sw128(b0 + k * 32, 16, 1024), idesc,
+                             (kb | k) != 0);
             }
-            umma_commit(&empty[stage]);
+            umma_commit_pair(mapa_shared(smem_u32(&empty[stage]), 0));
+            umma_commit_pair(mapa_shared(smem_u32(&empty[stage]), 1));
             if (++stage == C::STAGES) {
               stage = 0;
               phase ^= 1;
             }
           }
           if (!ok) break;
-          umma_commit(&tfull[buf]);
+          umma_commit_pair(mapa_shared(smem_u32(&tfull[buf]), 0));
+          umma_commit_pair(mapa_shared(smem_u32(&tfull[buf]), 1));
           ++acc;
         }
       }
-      // All MMAs of this thread must have finished before TMEM is released.
-      umma_commit(drain);
+      // All MMAs of this thread must have finished before TMEM is released (in both CTAs).
+      umma_commit_pair(mapa_shared(smem_u32(drain), 0));
       volatile int no_abort = 0;
       mbar_wait(drain, 0, &no_abort, nullptr, 0);
     }
@@ -258,9 +280,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       }
       ob = (ob == 2) ? 0 : ob + 1;
     };
-    for (int u = blockIdx.x; u < units; u += gridDim.x) {
+    for (int u = pair; u < units; u += npairs) {
       const int mt = u / n_per_m, nu = u % n_per_m;
-      const int m0 = mt * BM;
+      const int m0 = mt * 2 * BM + static_cast<int>(rank) * BM;  // this CTA's 128 rows
       const int row = m0 + trow;
       const bool valid = row < p.M;
       float w_n = 0.f, w_mean = 0.f, w_m2 = 0.f;  // Welford state of this row
@@ -430,8 +452,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
               score += gelu_erf(__uint_as_float(r[j]) + p.bias[col + j]) * p.w2[col + j];
           }
         }
+        // this warp has read its lanes of the buffer: release it to the leader's MMA
         tc_fence_before();
-        mbar_arrive(&tempty[buf]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&tempty[buf]), 0));
         ++acc;
       }
       if constexpr (RES) {
@@ -500,8 +524,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         uint32_t gx = 0;                    // chunks issued so far (ring slot = gx % NXB)
         uint32_t armed = 0, armed_par = 0;  // per slot: armed bit and the parity it was armed with
         bool ok = true;
-        for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-          const int m0 = (u / n_per_m) * BM;
+        for (int u = pair; u < units && ok; u += npairs) {
+          const int m0 = (u / n_per_m) * 2 * BM + static_cast<int>(rank) * BM;
           for (int c = 0; c < NCH; ++c, ++gx) {
             const uint32_t b = gx % NXB, ph = (gx / NXB) & 1;
             if (!mbar_wait(&xempty[b], ph ^ 1, abort_flag, p.err, 6)) {
@@ -524,9 +548,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   }
 
   tc_fence_before();
-  __syncthreads();
+  cluster_sync();  // every role of both CTAs is done and the leader's MMAs have drained
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem_base, 2 * BN);
+  if (warp == 1) tmem_dealloc_pair(tmem_base, 2 * BN);
 }
 
 template <int BN, int EPI, int NSUB>
@@ -536,10 +560,12 @@ int launch_one(const CUtensorMap& tmA, const CUtensorMap& tmW, const CUtensorMap
   auto kern = gemm_tc_kernel<BN, EPI, NSUB>;
   const cudaError_t e = set_smem_once(kern, GemmCfg<BN, EPI>::SMEM, configured);
   if (e != cudaSuccess) return static_cast<int>(e);
-  const int units = ((p.M + BM - 1) / BM) * (is_full_row(EPI) ? 1 : p.N / BN);
-  const int grid = units < grid_limit ? units : grid_limit;
-  if (grid <= 0) return 0;
-  kern<<<grid, GEMM_THREADS, GemmCfg<BN, EPI>::SMEM, stream>>>(tmA, tmW, tmX, p);
+  // work units are 256-row tiles of CTA pairs; grid_limit counts CTAs (SMs)
+  const int units = ((p.M + 2 * BM - 1) / (2 * BM)) * (is_full_row(EPI) ? 1 : p.N / BN);
+  const int max_pairs = grid_limit / 2 > 0 ? grid_limit / 2 : 1;
+  const int pairs = units < max_pairs ? units : max_pairs;
+  if (pairs <= 0) return 0;
+  kern<<<2 * pairs, GEMM_THREADS, GemmCfg<BN, EPI>::SMEM, stream>>>(tmA, tmW, tmX, p);
   return static_cast<int>(cudaGetLastError());
 }
 

@@ -29,7 +29,8 @@ inline cudaError_t set_smem_once(Kernel kern, int bytes, std::atomic<unsigned lo
 
 // ------------------------------------------------------------------ GEMM
 // out = A[M,K] . W[N,K]^T with a fused epilogue. A and W are bf16, row-major,
-// read through 128B-swizzled TMA maps (box 64 x 128 for A, 64 x BN for W).
+// read through 128B-swizzled TMA maps (box 64 x 128 for A, 64 x BN/2 for W: each CTA of a
+// pair loads half of the tile's W rows; see gemm_w_box_rows).
 enum GemmEpi : int {
   EPI_BF16 = 0,      // out = bf16(acc (+bias)) (relu when `relu`)
   EPI_QKV_ROPE = 1,  // out = bf16(rope(acc)) on columns < rope_cols, bf16(acc) elsewhere
@@ -64,6 +65,8 @@ struct EpiParams {
 
 // Column width of one MMA tile for an N (or full-row width): 256 when N % 256 == 0, else 128.
 int gemm_bn_for(int n);
+// Rows of one W box for tile width bn (the two CTAs of a pair each load half of the tile).
+inline uint32_t gemm_w_box_rows(int bn) { return static_cast<uint32_t>(bn / 2); }
 // Returns 0 on success, or a cudaError_t value. tmX: the map of the epilogue's global tensor:
 // the FP32 residual map (make_tmap_f32_resid) over p.x for EPI_RESID_LN / EPI_RESID; the
 // BF16 output map over p.out (make_tmap_bf16, box 64 x 128, N columns -- N/2 for GEGLU --

@@ -135,7 +135,7 @@ j1_status upload_f32(j1_model* model, SafeTensors& st, const std::string& name, 
 // GEMM weight: F32 on disk -> BF16 on device (round-to-nearest-even, as half::bf16::from_f32
 // in src/cuda/mod.rs:36-39), optionally with the GEGLU row interleave; plus its TMA map.
 j1_status upload_bf16(j1_model* model, SafeTensors& st, const std::string& name, size_t rows, size_t cols,
-                      int geglu_inter, float* staging, bf16** out, CUtensorMap* tm, uint32_t box_rows) {
+                      int geglu_inter, float* staging, bf16** out, CUtensorMap* tm, uint32_t tile_n) {
   std::string err;
   const float* h = st.f32(name, {rows, cols}, err);
   if (!h) return set_error(J1_ERR_IO, err);
@@ -149,7 +149,7 @@ j1_status upload_bf16(j1_model* model, SafeTensors& st, const std::string& name,
   J1_TRY_CUDA(cudaStreamSynchronize(model->stream), "weight conversion");
   *out = static_cast<bf16*>(p);
   const char* why = nullptr;
-  if (!make_tmap_bf16(tm, p, rows, cols, cols, box_rows, &why))
+  if (!make_tmap_bf16(tm, p, rows, cols, cols, gemm_w_box_rows(static_cast<int>(tile_n)), &why))
     return set_error(J1_ERR_CUDA, std::string(name) + ": " + (why ? why : "tensor map"));
   return J1_OK;
 }
@@ -612,8 +612,9 @@ j1_status create_model(const char* ckpt_dir, int ordinal, j1_model** out) {
         (s = upload_bf16(M, st, pre + "linear2.weight", H, FF, 0, staging, &hl.lin2_w, &hl.tm_lin2, bn_full)))
       return s;
     const char* why = nullptr;
-    if (!make_tmap_bf16(&hl.tm_in_q, hl.in_w, H, H, H, bn_full, &why) ||
-        !make_tmap_bf16(&hl.tm_in_kv, hl.in_w + static_cast<size_t>(H) * H, 2 * H, H, H, gemm_bn_for(2 * H), &why))
+    if (!make_tmap_bf16(&hl.tm_in_q, hl.in_w, H, H, H, gemm_w_box_rows(bn_full), &why) ||
+        !make_tmap_bf16(&hl.tm_in_kv, hl.in_w + static_cast<size_t>(H) * H, 2 * H, H, H,
+                        gemm_w_box_rows(gemm_bn_for(static_cast<int>(2 * H))), &why))
       return set_error(J1_ERR_CUDA, std::string("weight tensor map: ") + (why ? why : ""));
     M->head.push_back(hl);
   }
@@ -843,7 +844,7 @@ j1_status j1_op_gemm(const j1_gemm_args* a, void* stream, int sync) {
   CUtensorMap tmA, tmW, tmX;
   const char* why = nullptr;
   if (!make_tmap_bf16(&tmA, a->A, a->M, a->K, a->K, 128, &why) ||
-      !make_tmap_bf16(&tmW, a->W, a->N, a->K, a->K, bn, &why))
+      !make_tmap_bf16(&tmW, a->W, a->N, a->K, a->K, gemm_w_box_rows(bn), &why))
     return set_error(J1_ERR_INVALID_ARG, std::string("tensor map: ") + (why ? why : ""));
   const bool resid = epi == EPI_RESID_LN || epi == EPI_RESID;
   if (resid && !make_tmap_f32_resid(&tmX, a->x, a->M, a->N, a->ldx, &why))
