@@ -85,8 +85,9 @@ __device__ __forceinline__ Item item_geometry(const AttnTile* __restrict__ tiles
 
 __global__ void __launch_bounds__(192, 2)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
-                   const AttnTile* __restrict__ tiles, int ntiles, int heads, bf16* __restrict__ out, int ldo,
-                   int q_col0, int k_col0, int v_col0, int window, float scale_log2, int* err) {
+                   const __grid_constant__ CUtensorMap tmO, int use_tma_out, const AttnTile* __restrict__ tiles,
+                   int ntiles, int heads, bf16* __restrict__ out, int ldo, int q_col0, int k_col0, int v_col0,
+                   int window, float scale_log2, int* err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                 // 2 buffers
@@ -97,11 +98,12 @@ __global__ void __launch_bounds__(192, 2)
   uint64_t* kv_free = bars + 2;  // [2] per stage
   uint64_t* q_full = bars + 4;   // [2] per Q buffer
   uint64_t* q_free = bars + 6;   // [2] per Q buffer
-  uint64_t* s_full = bars + 8;   // S of the next block in TMEM (and every earlier MMA done)
-  uint64_t* p_full = bars + 9;   // P of the current block in TMEM (128 arrivals)
+  uint64_t* s_full = bars + 8;   // S of the next block in TMEM (and the P.V before the previous one)
+  uint64_t* p_full = bars + 9;   // P of the current block in TMEM (one arrival per softmax warp)
   uint64_t* o_full = bars + 10;  // last P.V of an item done
   uint64_t* drain = bars + 11;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* pv_full = bars + 12;  // P.V of a block other than an item's last done (P may be rewritten)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id(), lane = lane_id();
@@ -118,10 +120,11 @@ __global__ void __launch_bounds__(192, 2)
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_free[i], 1);
       mbar_init(&q_full[i], 1);
-      mbar_init(&q_free[i], 1);
+      mbar_init(&q_free[i], 4);  // one arrival per softmax warp (its rows of O have left)
     }
     mbar_init(s_full, 1);
-    mbar_init(p_full, 128);
+    mbar_init(p_full, 4);
+    mbar_init(pv_full, 1);
     mbar_init(o_full, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -146,6 +149,7 @@ __global__ void __launch_bounds__(192, 2)
       for (int u = blockIdx.x; u < items && ok; u += gridDim.x, ++n) {
         const Item it = item_geometry(tiles, ntiles, u, window);
         const int qb = n & 1;
+        // the Q buffer of item n - 2 is free once its O has left through it (softmax storer)
         if (n >= 2 && !mbar_wait(&q_free[qb], ((n - 2) >> 1) & 1, abort_flag, err, 10)) break;
         mbar_arrive_expect_tx(&q_full[qb], TILE_BYTES);
         tma_load_2d(&tmQ, &q_full[qb], sQ + qb * TILE_BYTES, q_col0 + it.head * HD, it.tl.q_row0);
@@ -173,33 +177,34 @@ __global__ void __launch_bounds__(192, 2)
     }
   } else if (warp == 4) {
     // ------------------------------------------------------------ MMA issuer
+    // Per block: wait for P(j); issue the next S (S(j+1), or S(0) of the next item) so that
+    // the softmax can start on it at once; then P(j).V(j) into O.
     if (lane == 0) {
       constexpr uint32_t idS = idesc_bf16(128, 128, false, false);
       constexpr uint32_t idO = idesc_bf16(128, 64, false, true);
       const uint32_t q0 = smem_u32(sQ), k0 = smem_u32(sK), v0 = smem_u32(sV);
       uint32_t pcnt = 0;  // p_full phases consumed
-      uint32_t kvb = 0;   // K/V blocks consumed
-      int n = 0;
+      uint32_t kvb = 0;   // K/V blocks of earlier items
       bool ok = true;
+      auto issue_s = [&](int n, uint32_t b) -> bool {  // S = Q(item n) K(block b)^T
+        if (!mbar_wait(&kv_full[b & 1], (b >> 1) & 1, abort_flag, err, 13)) return false;
+        tc_fence_after();
+        const uint32_t qa = q0 + (n & 1) * TILE_BYTES, kb = k0 + (b & 1) * TILE_BYTES;
+#pragma unroll
+        for (int k = 0; k < HD / 16; ++k)
+          umma_bf16(tmem_base + TS_COL, sdesc_sw128(qa + k * 32, 16, 1024), sdesc_sw128(kb + k * 32, 16, 1024), idS,
+                    k > 0);
+        umma_commit(s_full);  // also covers every P.V issued before it
+        return true;
+      };
+      auto wait_q = [&](int n) { return mbar_wait(&q_full[n & 1], (n >> 1) & 1, abort_flag, err, 12); };
+      int n = 0;
+      if (blockIdx.x < items) ok = wait_q(0) && issue_s(0, 0);
       for (int u = blockIdx.x; u < items && ok; u += gridDim.x, ++n) {
         const Item it = item_geometry(tiles, ntiles, u, window);
-        const int qb = n & 1;
-        if (!mbar_wait(&q_full[qb], (n >> 1) & 1, abort_flag, err, 12)) break;
-        const uint32_t qa = q0 + qb * TILE_BYTES;
-        auto issue_s = [&](uint32_t b) -> bool {
-          if (!mbar_wait(&kv_full[b & 1], (b >> 1) & 1, abort_flag, err, 13)) return false;
-          tc_fence_after();
-          const uint32_t kb = k0 + (b & 1) * TILE_BYTES;
-#pragma unroll
-          for (int k = 0; k < HD / 16; ++k)
-            umma_bf16(tmem_base + TS_COL, sdesc_sw128(qa + k * 32, 16, 1024), sdesc_sw128(kb + k * 32, 16, 1024),
-                      idS, k > 0);
-          umma_commit(s_full);  // also covers the P.V issued before it
-          return true;
-        };
-        ok = issue_s(kvb);
-        for (int j = 0; j < it.nb && ok; ++j) {
-          // P(j) is in TMEM (the group has also finished reading S(j))
+        const bool has_next = u + static_cast<int>(gridDim.x) < items;
+        for (int j = 0; j < it.nb; ++j) {
+          // P(j) is in TMEM and the group has finished reading S(j)
           if (!mbar_wait(p_full, pcnt & 1, abort_flag, err, 14)) {
             ok = false;
             break;
@@ -207,16 +212,18 @@ __global__ void __launch_bounds__(192, 2)
           ++pcnt;
           tc_fence_after();
           const uint32_t b = kvb + j;
+          if (j + 1 < it.nb) ok = issue_s(n, b + 1);
+          else if (has_next) ok = wait_q(n + 1) && issue_s(n + 1, b + 1);
+          if (!ok) break;
           const uint32_t vb0 = v0 + (b & 1) * TILE_BYTES;
 #pragma unroll
           for (int k = 0; k < KB / 16; ++k)
             umma_bf16_ts(tmem_base + TO_COL, tmem_base + TP_COL + k * 8, sdesc_sw128(vb0 + k * 2048, 8192, 1024), idO,
                          (k > 0 || j > 0) ? 1u : 0u);
           umma_commit(&kv_free[b & 1]);
-          if (j + 1 < it.nb) ok = issue_s(b + 1);
+          // P(j) consumed: the softmax may write P(j+1); after the last block, O is final
+          umma_commit(j + 1 < it.nb ? pv_full : o_full);
         }
-        umma_commit(o_full);
-        umma_commit(&q_free[qb]);
         kvb += it.nb;
       }
       umma_commit(drain);
@@ -230,9 +237,64 @@ __global__ void __launch_bounds__(192, 2)
     const uint32_t tS = tmem_base + TS_COL + lane_off, tP = tmem_base + TP_COL + lane_off;
     const uint32_t tO = tmem_base + TO_COL + lane_off;
     constexpr float kRescaleLog2 = 8.f;
-    uint32_t ns = 0, no = 0;  // s_full / o_full phases consumed
+    uint32_t ns = 0, no = 0, npv = 0;  // s_full / o_full / pv_full phases consumed
     bool ok = true;
-    for (int u = blockIdx.x; u < items && ok; u += gridDim.x) {
+    // The epilogue of an item (O / l -> ctx) runs while the next item's first block is in
+    // progress: its O is complete once o_full fires, and it must be read before this
+    // group's next p_full lets P.V(0) of the next item overwrite it.
+    struct Pending {
+      bool on;
+      float l;
+      int row0, nq, head, qb;
+    } pend = {false, 0.f, 0, 0, 0, 0};
+    auto epilogue = [&]() {
+      const float inv = pend.l > 0.f ? 1.f / pend.l : 0.f;
+      uint32_t orr[2][32];
+      tmem_ld32(tO, orr[0]);
+      tmem_ld32(tO + 32, orr[1]);
+      tmem_ld_wait();
+      uint4 w[8];
+#pragma unroll
+      for (int g = 0; g < 8; ++g) {
+        const uint32_t* v = &orr[g >> 2][(g & 3) * 8];
+        w[g].x = pack_bf16x2(__uint_as_float(v[0]) * inv, __uint_as_float(v[1]) * inv);
+        w[g].y = pack_bf16x2(__uint_as_float(v[2]) * inv, __uint_as_float(v[3]) * inv);
+        w[g].z = pack_bf16x2(__uint_as_float(v[4]) * inv, __uint_as_float(v[5]) * inv);
+        w[g].w = pack_bf16x2(__uint_as_float(v[6]) * inv, __uint_as_float(v[7]) * inv);
+      }
+      tc_fence_before();  // O read before the next p_full
+      const int w0 = warp * 32;  // this warp's 32 rows of the tile
+      if (use_tma_out && w0 + 32 <= pend.nq) {
+        // stage the warp's 32 x 64 rows in the item's Q buffer (128B swizzle, the TMA
+        // layout) and write them with one TMA store; lane 0 hands its part of the buffer
+        // back to the producer once the store has read it
+        uint8_t* row = sQ + pend.qb * TILE_BYTES + r * 128;
+#pragma unroll
+        for (int g = 0; g < 8; ++g)
+          *reinterpret_cast<uint4*>(row + ((static_cast<uint32_t>(g) ^ (r & 7)) << 4)) = w[g];
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if (!*abort_flag) {
+            tma_store_2d(&tmO, sQ + pend.qb * TILE_BYTES + w0 * 128, pend.head * HD, pend.row0 + w0);
+            bulk_commit();
+            bulk_wait_read_all();
+          }
+          mbar_arrive(&q_free[pend.qb]);
+        }
+      } else {  // rows past the tile's end (ragged tail) or no output map: plain stores
+        if (r < pend.nq) {
+          uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(pend.row0 + r) * ldo + pend.head * HD);
+#pragma unroll
+          for (int g = 0; g < 8; ++g) dst[g] = w[g];
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&q_free[pend.qb]);
+      }
+      pend.on = false;
+    };
+    int n = 0;
+    for (int u = blockIdx.x; u < items && ok; u += gridDim.x, ++n) {
       const Item it = item_geometry(tiles, ntiles, u, window);
       const int qpos = it.tl.q_pos0 + r;
       // this row's valid keys: [klo, khi)
@@ -241,7 +303,7 @@ __global__ void __launch_bounds__(192, 2)
       float m_used = -INFINITY;  // offset of P and O (scaled, base 2)
       float l = 0.f;
       for (int j = 0; j < it.nb; ++j, ++ns) {
-        if (!warp_wait(s_full, ns & 1, abort_flag, err, 16)) {  // also: P.V(j-1) is done
+        if (!warp_wait(s_full, ns & 1, abort_flag, err, 16)) {
           ok = false;
           break;
         }
@@ -270,6 +332,8 @@ __global__ void __launch_bounds__(192, 2)
         }
         // exponentiate with the current offset; redo once if the block max moved it too far
         float lb = 0.f;
+        // before P is written: the previous P.V must have read P (and finished adding to O)
+        bool p_wait = j > 0 || pend.on;
         for (int attempt = 0; attempt < 2; ++attempt) {
           const float uu = (m_used == -INFINITY) ? 0.f : m_used;
           float lp[4] = {0.f, 0.f, 0.f, 0.f};
@@ -295,6 +359,15 @@ __global__ void __launch_bounds__(192, 2)
               lp[i & 3] += p0 + p1;
               pk[i] = pack_bf16x2(p0, p1);
             }
+            if (p_wait) {
+              const bool w = j > 0 ? warp_wait(pv_full, npv & 1, abort_flag, err, 15)
+                                   : warp_wait(o_full, no & 1, abort_flag, err, 18);
+              if (j > 0) ++npv;
+              else ++no;
+              if (!w) ok = false;
+              p_wait = false;
+              tc_fence_after();
+            }
             tmem_st32(tP + c * 32, pk);
           }
           tmem_st_wait();
@@ -318,39 +391,24 @@ __global__ void __launch_bounds__(192, 2)
           }
           tmem_st_wait();
         }
+        if (!ok) break;
         l += lb;
+        if (pend.on) epilogue();  // previous item's O (complete: o_full was waited above)
         tc_fence_before();
-        mbar_arrive(p_full);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_full);
       }
-      if (!ok || !warp_wait(o_full, no & 1, abort_flag, err, 18)) {
-        ok = false;
-        break;
-      }
-      ++no;
-      tc_fence_after();
-      const float inv = l > 0.f ? 1.f / l : 0.f;
-      uint32_t orr[2][32];
-      tmem_ld32(tO, orr[0]);
-      tmem_ld32(tO + 32, orr[1]);
-      tmem_ld_wait();
-      if (r < it.tl.nq) {
-        uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(it.tl.q_row0 + r) * ldo + it.head * HD);
-#pragma unroll
-        for (int g = 0; g < 8; ++g) {
-          const uint32_t* v = &orr[g >> 2][(g & 3) * 8];
-          uint4 w;
-          w.x = pack_bf16x2(__uint_as_float(v[0]) * inv, __uint_as_float(v[1]) * inv);
-          w.y = pack_bf16x2(__uint_as_float(v[2]) * inv, __uint_as_float(v[3]) * inv);
-          w.z = pack_bf16x2(__uint_as_float(v[4]) * inv, __uint_as_float(v[5]) * inv);
-          w.w = pack_bf16x2(__uint_as_float(v[6]) * inv, __uint_as_float(v[7]) * inv);
-          dst[g] = w;
-        }
-      }
-      // O is overwritten by the next item's first P.V, issued after this warp's next p_full
-      tc_fence_before();
+      pend = {true, l, it.tl.q_row0, it.tl.nq, it.head, n & 1};
     }
+    if (ok && pend.on) {
+      if (warp_wait(o_full, no & 1, abort_flag, err, 18)) {
+        ++no;
+        tc_fence_after();
+        epilogue();
+      }
+    }
+    if (lane == 0) bulk_wait_all();  // no store of ours may still read smem at exit
   }
-
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -361,9 +419,9 @@ __global__ void __launch_bounds__(192, 2)
 
 int attention_pair_queries() { return QT; }
 
-int launch_attention(const CUtensorMap& tmQ, const CUtensorMap& tmKV, const AttnTile* tiles, int ntiles, int heads,
-                     int q_col0, int k_col0, int v_col0, bf16* out, int ldo, int window, float scale_log2, int* err,
-                     int grid_limit, cudaStream_t stream) {
+int launch_attention(const CUtensorMap& tmQ, const CUtensorMap& tmKV, const CUtensorMap* tmO, const AttnTile* tiles,
+                     int ntiles, int heads, int q_col0, int k_col0, int v_col0, bf16* out, int ldo, int window,
+                     float scale_log2, int* err, int grid_limit, cudaStream_t stream) {
   static std::atomic<unsigned long long> configured{0};  // one bit per device
   const cudaError_t e = set_smem_once(attn_tc_kernel, ATT_SMEM, configured);
   if (e != cudaSuccess) return static_cast<int>(e);
@@ -371,8 +429,8 @@ int launch_attention(const CUtensorMap& tmQ, const CUtensorMap& tmKV, const Attn
   const int items = ntiles * heads;
   const int limit = 2 * grid_limit;  // two CTAs per SM
   const int grid = items < limit ? items : limit;
-  attn_tc_kernel<<<grid, 192, ATT_SMEM, stream>>>(tmQ, tmKV, tiles, ntiles, heads, out, ldo, q_col0, k_col0, v_col0,
-                                                   window, scale_log2, err);
+  attn_tc_kernel<<<grid, 192, ATT_SMEM, stream>>>(tmQ, tmKV, tmO ? *tmO : tmQ, tmO ? 1 : 0, tiles, ntiles, heads,
+                                                   out, ldo, q_col0, k_col0, v_col0, window, scale_log2, err);
   return static_cast<int>(cudaGetLastError());
 }
 

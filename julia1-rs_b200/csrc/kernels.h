@@ -87,10 +87,12 @@ struct AttnTile {
 };
 // ctx[q_row0 + r, head*64 ..] = softmax(scale * q k^T [band]) v for every tile x head.
 // window < 0: full attention; else |qpos - kpos| <= window.
-// Persistent: min(ntiles * heads, grid_limit) CTAs walk the (tile pair, head) items.
-int launch_attention(const CUtensorMap& tmQ, const CUtensorMap& tmKV, const AttnTile* tiles, int ntiles, int heads,
-                     int q_col0, int k_col0, int v_col0, bf16* out, int ldo, int window, float scale_log2, int* err,
-                     int grid_limit, cudaStream_t stream);
+// tmO (optional): bf16 map over out with 64 x 32 boxes (make_tmap_bf16(..., box_rows 32));
+// full 32-row slices of O leave through it by TMA store, the rest by plain stores.
+// Persistent: min(ntiles * heads, 2 * grid_limit) CTAs walk the (tile, head) items.
+int launch_attention(const CUtensorMap& tmQ, const CUtensorMap& tmKV, const CUtensorMap* tmO, const AttnTile* tiles,
+                     int ntiles, int heads, int q_col0, int k_col0, int v_col0, bf16* out, int ldo, int window,
+                     float scale_log2, int* err, int grid_limit, cudaStream_t stream);
 
 // ------------------------------------------------------------------ row kernels
 int launch_embed_ln(int hidden, const int* ids, const float* table, const float* w, float* x, bf16* xn, int rows,
