@@ -94,8 +94,10 @@ extern "C" j1_status j1_op_attention_noalloc(const void* qkv, int64_t t, int32_t
   const char* why = nullptr;
   if (!make_tmap_bf16(&tm, qkv, static_cast<uint64_t>(t), 3 * static_cast<uint64_t>(hidden), 3 * hidden, 128, &why))
     return set_error(J1_ERR_INVALID_ARG, std::string("tensor map: ") + (why ? why : ""));
-  CUtensorMap tmO;
-  if (!make_tmap_bf16(&tmO, ctx, static_cast<uint64_t>(t), static_cast<uint64_t>(hidden), hidden, 32, &why))
+  CUtensorMap tmO, tmKV;
+  if (!make_tmap_bf16(&tmO, ctx, static_cast<uint64_t>(t), static_cast<uint64_t>(hidden), hidden, 32, &why) ||
+      !make_tmap_bf16(&tmKV, qkv, static_cast<uint64_t>(t), 3 * static_cast<uint64_t>(hidden), 3 * hidden,
+                      attention_kv_box_rows(), &why))
     return set_error(J1_ERR_INVALID_ARG, std::string("tensor map: ") + (why ? why : ""));
   DeviceSetup* ds = nullptr;
   j1_status st = setup_device(&ds);
@@ -129,7 +131,7 @@ extern "C" j1_status j1_op_attention_noalloc(const void* qkv, int64_t t, int32_t
     NA_TRY(cudaMemcpyAsync(tiles + done, chunk, fill * sizeof(AttnTile), cudaMemcpyHostToDevice, cs),
                 "tile upload");
   NA_TRY(cudaMemsetAsync(err, 0, sizeof(int), cs), "clear error word");
-  const int rc = launch_attention(tm, tm, &tmO, tiles, static_cast<int>(ntiles), hidden / 64, 0, hidden, 2 * hidden,
+  const int rc = launch_attention(tm, tmKV, &tmO, tiles, static_cast<int>(ntiles), hidden / 64, 0, hidden, 2 * hidden,
                                   static_cast<bf16*>(ctx), hidden, window, kScaleLog2, err, ds->num_sms, cs);
   if (rc) return cuda_error(static_cast<cudaError_t>(rc), "attention launch");
   if (!sync) return J1_OK;

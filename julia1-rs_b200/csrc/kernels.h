@@ -79,6 +79,8 @@ const char* gemm_shape_error(GemmEpi epi, int bn, int M, int N, int K);
 // ------------------------------------------------------------------ attention
 // Queries covered by one attention work item (one 128-query tile).
 int attention_pair_queries();
+// Rows of one K/V box: the tmKV map given to launch_attention uses boxes of 64 x this.
+int attention_kv_box_rows();
 // One CTA's queries (up to attention_pair_queries()) of one sequence. Query row r of the tile is Q-buffer row
 // q_row0 + r at sequence position q_pos0 + r; keys/values are rows
 // kv_row0 .. kv_row0 + kv_len - 1 of the K/V buffer.
@@ -86,6 +88,7 @@ struct AttnTile {
   int q_row0, nq, kv_row0, kv_len, q_pos0, pad0, pad1, pad2;
 };
 // ctx[q_row0 + r, head*64 ..] = softmax(scale * q k^T [band]) v for every tile x head.
+// tmQ: bf16 map with 64 x 128 boxes; tmKV: 64 x attention_kv_box_rows() boxes.
 // window < 0: full attention; else |qpos - kpos| <= window.
 // tmO (optional): bf16 map over out with 64 x 32 boxes (make_tmap_bf16(..., box_rows 32));
 // full 32-row slices of O leave through it by TMA store, the rest by plain stores.

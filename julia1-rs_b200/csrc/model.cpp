@@ -317,6 +317,7 @@ j1_status stage_batch(j1_model* model, const BatchView& b) {
             make_tmap_bf16(&model->tm_qm, model->qm, m, H, H, 128, &why) &&
             make_tmap_bf16(&model->tm_qkv_kv, model->qkv + H, t, 2 * H, 3 * H, 128, &why) &&
             make_tmap_bf16(&model->tm_ctx_o, model->ctx, t, H, H, 32, &why) &&
+            make_tmap_bf16(&model->tm_kv, model->qkv, t, 3 * H, 3 * H, attention_kv_box_rows(), &why) &&
             make_tmap_bf16(&model->tm_cm_o, model->cm, m, H, H, 32, &why) &&
             make_tmap_f32_resid(&model->tm_x, model->x, t, H, H, &why) &&
             make_tmap_f32_resid(&model->tm_ym, model->ym, m, H, H, &why);
@@ -350,7 +351,7 @@ j1_status launch_forward(j1_model* model) {
     p.rope_cols = 2 * H;
     J1_TRY_LAUNCH(F_QKV, launch_gemm(EPI_QKV_ROPE, bn_qkv, model->tm_xn, ly.tm_wqkv, &model->tm_qkv, p, nsm, st), "gemm qkv");
     J1_TRY_LAUNCH(ly.global ? F_ATTN_GLOBAL : F_ATTN_LOCAL,
-                  launch_attention(model->tm_qkv, model->tm_qkv, &model->tm_ctx_o, model->d_tiles, static_cast<int>(model->ntiles),
+                  launch_attention(model->tm_qkv, model->tm_kv, &model->tm_ctx_o, model->d_tiles, static_cast<int>(model->ntiles),
                                    c.heads, 0, H, 2 * H, model->ctx, H, ly.global ? -1 : c.half_window, kScaleLog2,
                                    model->err_dev, nsm, st),
                   "attention");
@@ -386,7 +387,7 @@ j1_status launch_forward(j1_model* model) {
       p.bias = hl.in_b;
       J1_TRY_LAUNCH(F_HEAD_GEMM, launch_gemm(EPI_BF16, bn_qkv, model->tm_xn, hl.tm_in, &model->tm_qkv, p, nsm, st), "gemm in_proj");
       J1_TRY_LAUNCH(F_HEAD_ATTN,
-                    launch_attention(model->tm_qkv, model->tm_qkv, &model->tm_ctx_o, model->d_tiles, static_cast<int>(model->ntiles),
+                    launch_attention(model->tm_qkv, model->tm_kv, &model->tm_ctx_o, model->d_tiles, static_cast<int>(model->ntiles),
                                      c.head_heads, 0, H, 2 * H, model->ctx, H, -1, kScaleLog2, model->err_dev, nsm, st),
                     "head attention");
       p = base;
@@ -416,7 +417,7 @@ j1_status launch_forward(j1_model* model) {
       p.M = t, p.N = 2 * H, p.K = H, p.bias = hl.in_b + H;
       J1_TRY_LAUNCH(F_HEAD_GEMM, launch_gemm(EPI_BF16, gemm_bn_for(2 * H), model->tm_xn, hl.tm_in_kv, &model->tm_qkv_kv, p, nsm, st), "gemm in_proj kv");
       J1_TRY_LAUNCH(F_HEAD_ATTN,
-                    launch_attention(model->tm_qm, model->tm_qkv, &model->tm_cm_o, model->d_mtiles, static_cast<int>(model->nmtiles),
+                    launch_attention(model->tm_qm, model->tm_kv, &model->tm_cm_o, model->d_mtiles, static_cast<int>(model->nmtiles),
                                      c.head_heads, 0, H, 2 * H, model->cm, H, -1, kScaleLog2, model->err_dev, nsm, st),
                     "head attention (markers)");
       J1_TRY_LAUNCH(F_HEAD_ROWS, launch_gather_rows(model->x, model->d_markers, model->ym, m, H * 4, st), "gather x");
@@ -915,10 +916,12 @@ j1_status j1_op_attention(const void* qkv, int64_t t, int32_t hidden, const uint
   const char* why = nullptr;
   if (!make_tmap_bf16(&tm, qkv, static_cast<uint64_t>(t), 3 * static_cast<uint64_t>(hidden), 3 * hidden, 128, &why))
     return set_error(J1_ERR_INVALID_ARG, std::string("tensor map: ") + (why ? why : ""));
-  CUtensorMap tmO;
-  if (!make_tmap_bf16(&tmO, ctx, static_cast<uint64_t>(t), static_cast<uint64_t>(hidden), hidden, 32, &why))
+  CUtensorMap tmO, tmKV;
+  if (!make_tmap_bf16(&tmO, ctx, static_cast<uint64_t>(t), static_cast<uint64_t>(hidden), hidden, 32, &why) ||
+      !make_tmap_bf16(&tmKV, qkv, static_cast<uint64_t>(t), 3 * static_cast<uint64_t>(hidden), 3 * hidden,
+                      attention_kv_box_rows(), &why))
     return set_error(J1_ERR_INVALID_ARG, std::string("tensor map: ") + (why ? why : ""));
-  int rc = launch_attention(tm, tm, &tmO, os->tiles, static_cast<int>(tiles.size()), hidden / 64, 0, hidden, 2 * hidden,
+  int rc = launch_attention(tm, tmKV, &tmO, os->tiles, static_cast<int>(tiles.size()), hidden / 64, 0, hidden, 2 * hidden,
                             static_cast<bf16*>(ctx), hidden, window, kScaleLog2, os->err, os->num_sms, st);
   if (rc) return cuda_error(static_cast<cudaError_t>(rc), "attention launch");
   if (sync || !tiles.empty()) return op_sync_check(os, st);  // tiles are host-owned: wait before returning

@@ -106,6 +106,7 @@ struct j1_model {
   CUtensorMap tm_xn, tm_ctx, tm_g, tm_h, tm_qkv, tm_cm, tm_ymb, tm_hm;
   CUtensorMap tm_qm, tm_qkv_kv;  // marker queries [m, H]; the k|v columns of qkv
   CUtensorMap tm_ctx_o, tm_cm_o;  // attention outputs, 64 x 32 boxes (TMA stores of O)
+  CUtensorMap tm_kv;              // qkv with K/V-block boxes for attention
   CUtensorMap tm_x, tm_ym;  // FP32 residual streams (tokens, markers)
   int64_t launches = 0;
 
