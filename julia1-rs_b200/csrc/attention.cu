@@ -77,10 +77,10 @@ struct Item {
   int head, kbeg, nb;
 };
 
-__device__ __forceinline__ Item item_geometry(const AttnTile* __restrict__ tiles, int ntiles, int u, int window) {
+__device__ __forceinline__ Item item_geometry(const AttnTile& tl, int ntiles, int u, int window) {
   Item it;
   it.head = u / ntiles;
-  it.tl = tiles[u % ntiles];
+  it.tl = tl;
   int kend = it.tl.kv_len;
   it.kbeg = 0;
   if (window >= 0) {
@@ -91,23 +91,35 @@ __device__ __forceinline__ Item item_geometry(const AttnTile* __restrict__ tiles
   return it;
 }
 
+__device__ __forceinline__ AttnTile load_tile(const AttnTile* __restrict__ tiles, int ntiles, int u, int items) {
+  AttnTile t = {0, 0, 0, 0, 0, 0, 0, 0};
+  if (u < items) t = tiles[u % ntiles];
+  return t;
+}
+
 // Walks the (item, block) stream of one CTA: item u (the n-th of this CTA), block j.
+// The tile record of the following item is fetched one item ahead.
 struct Cursor {
   int u, n, j;
   Item it;
+  AttnTile next;
 };
 __device__ __forceinline__ void cursor_start(Cursor& c, const AttnTile* tiles, int ntiles, int items, int window) {
   c.u = blockIdx.x;
   c.n = 0;
   c.j = 0;
-  if (c.u < items) c.it = item_geometry(tiles, ntiles, c.u, window);
+  if (c.u < items) c.it = item_geometry(tiles[c.u % ntiles], ntiles, c.u, window);
+  c.next = load_tile(tiles, ntiles, c.u + static_cast<int>(gridDim.x), items);
 }
 __device__ __forceinline__ void cursor_next(Cursor& c, const AttnTile* tiles, int ntiles, int items, int window) {
   if (++c.j < c.it.nb) return;
   c.j = 0;
   c.u += gridDim.x;
   ++c.n;
-  if (c.u < items) c.it = item_geometry(tiles, ntiles, c.u, window);
+  if (c.u < items) {
+    c.it = item_geometry(c.next, ntiles, c.u, window);
+    c.next = load_tile(tiles, ntiles, c.u + static_cast<int>(gridDim.x), items);
+  }
 }
 
 __global__ void __launch_bounds__(192, 2)
@@ -176,7 +188,7 @@ __global__ void __launch_bounds__(192, 2)
       int n = 0;       // items handled by this CTA
       bool ok = true;
       for (int u = blockIdx.x; u < items && ok; u += gridDim.x, ++n) {
-        const Item it = item_geometry(tiles, ntiles, u, window);
+        const Item it = item_geometry(tiles[u % ntiles], ntiles, u, window);
         const int qb = n & 1;
         // the Q buffer of item n - 2 is free once its O has left through it (softmax)
         if (n >= 2 && !mbar_wait(&q_free[qb], ((n - 2) >> 1) & 1, abort_flag, err, 10)) break;
