@@ -15,6 +15,8 @@
 //               (M=256 over the pair, N=BN, K=16)
 //   warps 2..5  epilogue: tcgen05.ld of the FP32 accumulator (TMEM lane = row), fused math
 //   warp 6      residual producer (RESID*): TMA loads of x chunks into a smem ring
+//   warps 7..10 LayerNorm (RESID_LN only): normalise the previous unit's updated rows
+//               while warps 2..5 work on the next unit
 // The accumulator is double buffered in TMEM (2 x BN columns) so the epilogue of one
 // tile overlaps the main loop of the next.
 //
@@ -26,8 +28,8 @@
 // columns, computed as H/BN sub-tiles. The residual stream x (FP32) moves through
 // shared memory in 128 x 32 chunks (load by warp 6, in-place update, TMA store), with
 // NXB chunks in flight so that HBM latency is covered; per-row LayerNorm statistics
-// are merged chunk by chunk (Welford/Chan), then the normalized BF16 row is produced
-// from the updated x with warp-coalesced loads.
+// are merged chunk by chunk (Welford/Chan) and handed over in smem, and the LayerNorm
+// warps produce the normalized BF16 rows from the updated x with warp-coalesced loads.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -43,7 +45,6 @@ constexpr int BK = 64;
 constexpr uint32_t XCHUNK = 128 * 32 * 4;  // one 128-row x 32-column FP32 residual chunk
 constexpr uint32_t NXB = 4;                // residual chunks in flight per CTA (64 KB)
 constexpr uint32_t OBUF = 128 * 64 * 2;    // one 128-row x 64-column BF16 output box
-constexpr int GEMM_THREADS = 224;
 
 __host__ __device__ constexpr bool is_full_row(int epi) { return epi == EPI_RESID_LN || epi == EPI_RESID || epi == EPI_SCORER; }
 __host__ __device__ constexpr bool is_resid(int epi) { return epi == EPI_RESID_LN || epi == EPI_RESID; }
@@ -55,17 +56,22 @@ template <int BN, int EPI>
 struct GemmCfg {
   // per CTA of a pair: 128 rows of A and BN/2 rows of W per stage; the ring takes what is
   // left of 227 KB after the x ring / output boxes
-  static constexpr int STAGES = (EPI == EPI_SCORER) ? (BN == 256 ? 6 : 8)
-                                : is_resid(EPI)     ? (BN == 256 ? 5 : 6)
-                                                    : (BN == 256 ? 5 : 7);
+  static constexpr int STAGES = (EPI == EPI_SCORER)   ? (BN == 256 ? 6 : 8)
+                                : (EPI == EPI_RESID_LN) ? (BN == 256 ? 4 : 6)
+                                : is_resid(EPI)       ? (BN == 256 ? 5 : 6)
+                                                      : (BN == 256 ? 5 : 7);
+  // RESID_LN adds four LayerNorm warps (7..10) that normalise the previous unit's rows
+  static constexpr int THREADS = (EPI == EPI_RESID_LN) ? 352 : 224;
+  static constexpr uint32_t STATS_BYTES = (EPI == EPI_RESID_LN) ? 2 * BM * 8 : 0;  // 2 slots x (mean, rstd)
   static constexpr uint32_t A_BYTES = BM * BK * 2;
   static constexpr uint32_t B_BYTES = (BN / 2) * BK * 2;
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr uint32_t X_BYTES = is_resid(EPI) ? NXB * XCHUNK : 0;
   static constexpr uint32_t O_BYTES = is_tile_out(EPI) ? 3 * OBUF : 0;
-  static constexpr uint32_t SMEM = STAGES * STAGE_BYTES + X_BYTES + O_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr uint32_t SMEM =
+      STAGES * STAGE_BYTES + X_BYTES + O_BYTES + STATS_BYTES + 1024 /*align*/ + 512 /*barriers*/;
   static_assert(SMEM <= 232448, "shared memory budget");
-  static_assert(2 * STAGES + 4 + 1 + 2 * NXB <= 30, "barrier area");
+  static_assert(2 * STAGES + 4 + 1 + 2 * NXB + 4 <= 62, "barrier area");
 };
 
 __device__ __forceinline__ float gelu_erf(float v) { return 0.5f * v * (1.f + erff(v * 0.70710678118654752f)); }
@@ -91,7 +97,7 @@ __device__ __forceinline__ void put_row32(uint8_t* srow, int r, int unit0, const
 // and each CTA's TMEM receives the accumulator of its 128 rows, which its own epilogue
 // warps consume. Per 128 x BN of output a CTA thus moves A + W/2 instead of A + W.
 template <int BN, int EPI, int NSUB>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GemmCfg<BN, EPI>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                    const __grid_constant__ CUtensorMap tmX, const EpiParams p) {
   using C = GemmCfg<BN, EPI>;
@@ -105,14 +111,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
   uint8_t* sB = smem + C::STAGES * C::A_BYTES;
   uint8_t* sX = sB + C::STAGES * C::B_BYTES;  // NXB x XCHUNK (1024-aligned) when RES
   uint8_t* sO = sX + C::X_BYTES;              // 3 x OBUF output boxes when tile-out
-  uint64_t* full = reinterpret_cast<uint64_t*>(sO + C::O_BYTES);
+  float2* stats = reinterpret_cast<float2*>(sO + C::O_BYTES);  // [2][128] (mean, rstd) when RESID_LN
+  uint64_t* full = reinterpret_cast<uint64_t*>(sO + C::O_BYTES + C::STATS_BYTES);
   uint64_t* empty = full + C::STAGES;
   uint64_t* tfull = empty + C::STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
   uint64_t* xfull = drain + 1;     // NXB barriers
   uint64_t* xempty = xfull + NXB;  // NXB barriers
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xempty + NXB);
+  uint64_t* lnfull = xempty + NXB;  // [2] a unit's row statistics are in `stats` (RESID_LN)
+  uint64_t* lnempty = lnfull + 2;   // [2] the LayerNorm warps are done with a stats slot
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(lnempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id(), lane = lane_id();
@@ -148,6 +157,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     for (uint32_t b = 0; b < NXB; ++b) {
       mbar_init(&xfull[b], 1);
       mbar_init(&xempty[b], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&lnfull[b], 1);
+      mbar_init(&lnempty[b], 4);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -263,6 +276,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     uint32_t gch = 0;  // residual chunks consumed so far (ring slot = gch % NXB)
     int xpend = -1;    // ring slot whose store may still be reading smem
     int ob = 0;        // output box in use (of three)
+    int nunit = 0;     // units done by this CTA
     // BF16 output: this thread's 64 values of row trow -> box `ob` (128B swizzle), then
     // one TMA store of the 128 x 64 box at (col, m0). Three boxes rotate: after issuing
     // a store the storer waits until only that store may still read smem, so the box
@@ -416,13 +430,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
             }
             if constexpr (EPI == EPI_RESID_LN) {
               // chunk mean / M2 (two-pass over registers), merged into the row's running state
-              float cs = 0.f;
+              float cs4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-              for (int j = 0; j < 32; ++j) cs += v[j];
-              const float cm = cs * (1.f / 32.f);
-              float c2 = 0.f;
+              for (int j = 0; j < 32; ++j) cs4[j & 3] += v[j];
+              const float cm = ((cs4[0] + cs4[1]) + (cs4[2] + cs4[3])) * (1.f / 32.f);
+              float c24[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-              for (int j = 0; j < 32; ++j) c2 += (v[j] - cm) * (v[j] - cm);
+              for (int j = 0; j < 32; ++j) c24[j & 3] += (v[j] - cm) * (v[j] - cm);
+              const float c2 = (c24[0] + c24[1]) + (c24[2] + c24[3]);
               const float n_new = w_n + 32.f;
               const float delta = cm - w_mean;
               w_mean += delta * (32.f / n_new);
@@ -459,62 +474,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
         ++acc;
       }
       if constexpr (RES) {
-        // the updated rows must be in global memory before they are re-read below / by the next kernel
+        // the updated rows must be in global memory before they are re-read (LayerNorm
+        // warps) or read by the next kernel
         if (storer) {
           bulk_wait_all();
           fence_proxy_async_global();
           if (xpend >= 0) mbar_arrive(&xempty[xpend]);
           xpend = -1;
         }
-        named_bar_sync(1, 128);
       }
       if constexpr (EPI == EPI_RESID_LN) {
-        fence_proxy_async_global();
-        // per-row statistics live in the row's thread; the warp normalizes its 32 rows with
-        // coalesced loads (lane = 4 consecutive columns per 128-column slice), RB rows in flight
-        constexpr int NV = H / 128;
-        constexpr int RB = (NV <= 3) ? 8 : 4;
-        const float rstd = rsqrtf(w_m2 * (1.f / static_cast<float>(H)) + p.ln_eps);
-        float4 gw[NV], gb[NV];
-#pragma unroll
-        for (int v = 0; v < NV; ++v) {
-          gw[v] = reinterpret_cast<const float4*>(p.ln_w)[v * 32 + lane];
-          gb[v] = p.ln_b ? reinterpret_cast<const float4*>(p.ln_b)[v * 32 + lane] : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-        const int wrow0 = m0 + q * 32;
-#pragma unroll 1
-        for (int rr = 0; rr < 32; rr += RB) {
-          float4 xv[RB][NV];
-#pragma unroll
-          for (int k = 0; k < RB; ++k) {
-            const int rw = wrow0 + rr + k;
-            if (rw < p.M) {
-              const float4* src = reinterpret_cast<const float4*>(p.x + static_cast<size_t>(rw) * p.ldx);
-#pragma unroll
-              for (int v = 0; v < NV; ++v) xv[k][v] = __ldcg(src + v * 32 + lane);
-            }
-          }
-#pragma unroll
-          for (int k = 0; k < RB; ++k) {
-            const int rw = wrow0 + rr + k;
-            const float mu = __shfl_sync(0xffffffffu, w_mean, rr + k);
-            const float rs = __shfl_sync(0xffffffffu, rstd, rr + k);
-            if (rw < p.M) {
-              uint2* dst = reinterpret_cast<uint2*>(p.xn + static_cast<size_t>(rw) * p.ldxn);
-#pragma unroll
-              for (int v = 0; v < NV; ++v) {
-                const float4 a = xv[k][v], g = gw[v], bb = gb[v];
-                uint2 o;
-                o.x = pack_bf16x2((a.x - mu) * rs * g.x + bb.x, (a.y - mu) * rs * g.y + bb.y);
-                o.y = pack_bf16x2((a.z - mu) * rs * g.z + bb.z, (a.w - mu) * rs * g.w + bb.w);
-                dst[v * 32 + lane] = o;
-              }
-            }
-          }
-        }
+        // hand this unit's row statistics to the LayerNorm warps (slot = unit parity)
+        const int slot = nunit & 1;
+        if (nunit >= 2) mbar_wait(&lnempty[slot], ((nunit - 2) >> 1) & 1, abort_flag, p.err, 7);
+        stats[slot * BM + trow] = make_float2(w_mean, rsqrtf(w_m2 * (1.f / static_cast<float>(H)) + p.ln_eps));
+        named_bar_sync(1, 128);  // every row's statistics written; the unit's x stores complete
+        if (storer) mbar_arrive(&lnfull[slot]);
+      } else if constexpr (RES) {
+        named_bar_sync(1, 128);
       } else if constexpr (EPI == EPI_SCORER) {
         if (valid) p.scores[row] = score + p.b2;
       }
+      ++nunit;
     }
     if (storer) bulk_wait_all();  // no store of ours may still read smem at exit
   } else if (warp == 6) {
@@ -545,6 +526,63 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
         }
       }
     }
+  } else if (warp >= 7) {
+    // ------------------------------------------------------------ LayerNorm warps (RESID_LN)
+    // Warp 7 + k normalises rows 32k .. 32k+31 of each unit once warps 2..5 have stored
+    // the unit's updated x and its row statistics: coalesced loads of x (lane = 4
+    // consecutive columns per 128-column slice), RB rows in flight, BF16 xn out.
+    if constexpr (EPI == EPI_RESID_LN) {
+      const int k = warp - 7;
+      constexpr int NV = H / 128;
+      constexpr int RB = (NV <= 3) ? 8 : (NV <= 6 ? 4 : 2);
+      float4 gw[NV], gb[NV];
+#pragma unroll
+      for (int v = 0; v < NV; ++v) {
+        gw[v] = reinterpret_cast<const float4*>(p.ln_w)[v * 32 + lane];
+        gb[v] = p.ln_b ? reinterpret_cast<const float4*>(p.ln_b)[v * 32 + lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      int nunit = 0;
+      for (int u = pair; u < units; u += npairs, ++nunit) {
+        const int m0 = (u / n_per_m) * 2 * BM + static_cast<int>(rank) * BM;
+        const int slot = nunit & 1;
+        if (!__all_sync(0xffffffffu, mbar_wait(&lnfull[slot], (nunit >> 1) & 1, abort_flag, p.err, 8))) break;
+        fence_proxy_async_global();
+        const float2 my = stats[slot * BM + k * 32 + lane];  // (mean, rstd) of row 32k + lane
+        const int wrow0 = m0 + k * 32;
+#pragma unroll 1
+        for (int rr = 0; rr < 32; rr += RB) {
+          float4 xv[RB][NV];
+#pragma unroll
+          for (int i = 0; i < RB; ++i) {
+            const int rw = wrow0 + rr + i;
+            if (rw < p.M) {
+              const float4* src = reinterpret_cast<const float4*>(p.x + static_cast<size_t>(rw) * p.ldx);
+#pragma unroll
+              for (int v = 0; v < NV; ++v) xv[i][v] = __ldcg(src + v * 32 + lane);
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < RB; ++i) {
+            const int rw = wrow0 + rr + i;
+            const float mu = __shfl_sync(0xffffffffu, my.x, rr + i);
+            const float rs = __shfl_sync(0xffffffffu, my.y, rr + i);
+            if (rw < p.M) {
+              uint2* dst = reinterpret_cast<uint2*>(p.xn + static_cast<size_t>(rw) * p.ldxn);
+#pragma unroll
+              for (int v = 0; v < NV; ++v) {
+                const float4 a = xv[i][v], g = gw[v], bb = gb[v];
+                uint2 o;
+                o.x = pack_bf16x2((a.x - mu) * rs * g.x + bb.x, (a.y - mu) * rs * g.y + bb.y);
+                o.y = pack_bf16x2((a.z - mu) * rs * g.z + bb.z, (a.w - mu) * rs * g.w + bb.w);
+                dst[v * 32 + lane] = o;
+              }
+            }
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&lnempty[slot]);
+      }
+    }
   }
 
   tc_fence_before();
@@ -565,7 +603,7 @@ int launch_one(const CUtensorMap& tmA, const CUtensorMap& tmW, const CUtensorMap
   const int max_pairs = grid_limit / 2 > 0 ? grid_limit / 2 : 1;
   const int pairs = units < max_pairs ? units : max_pairs;
   if (pairs <= 0) return 0;
-  kern<<<2 * pairs, GEMM_THREADS, GemmCfg<BN, EPI>::SMEM, stream>>>(tmA, tmW, tmX, p);
+  kern<<<2 * pairs, GemmCfg<BN, EPI>::THREADS, GemmCfg<BN, EPI>::SMEM, stream>>>(tmA, tmW, tmX, p);
   return static_cast<int>(cudaGetLastError());
 }
 
