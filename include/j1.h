@@ -94,6 +94,27 @@ J1_API j1_status j1_model_launch(j1_model* model);
 J1_API j1_status j1_model_finish(j1_model* model, float* scores_out, size_t m);
 /* cudaStream_t the model's kernels run on (for event timing by the caller). */
 J1_API void* j1_model_stream(j1_model* model);
+
+/* One packed batch, as the arguments of j1_model_forward. */
+typedef struct j1_batch {
+  const uint32_t* ids;
+  size_t t;
+  const uint32_t* starts;
+  const uint32_t* lens;
+  const uint8_t* qtypes;
+  size_t nseq;
+  const uint32_t* marker_rows;
+  const uint32_t* marker_starts;
+  size_t m;
+} j1_batch;
+
+/* nbatch forwards back to back, as j1_model_forward on each (scores_out[k] receives batch
+ * k's m scores), pipelined: batch k+1 is validated, packed and uploaded while batch k
+ * computes, and scores are read back one batch behind, so the device does not idle
+ * between micro-batches (the engine's per-device loop, src/engine.rs:212-233). Every
+ * batch is validated before the first launch; blocking. */
+J1_API j1_status j1_model_forward_many(j1_model* model, size_t nbatch, const j1_batch* batches,
+                                       float* const* scores_out);
 /* Number of kernel launches one j1_model_launch issues for the staged batch. */
 J1_API int64_t j1_model_launch_count(const j1_model* model);
 

@@ -180,35 +180,48 @@ j1_status j1_engine_logits_encoded(j1_engine* e, size_t n_rows, const uint32_t* 
   std::vector<std::vector<size_t>> assign(G);
   for (size_t b = 0; b < micro.size(); ++b) assign[device_of[b]].push_back(b);
 
-  auto run = [&](size_t g, j1_status* status, std::string* msg) {
-    std::vector<uint32_t> bids, starts, lens, mrows, mstarts;
+  // One worker per replica packs its micro-batches (Batch::new, src/model.rs:225-269) and
+  // runs them through j1_model_forward_many, which overlaps the staging of batch k+1
+  // with the forward of batch k; logits go back in the caller's row order.
+  struct Packed {
+    std::vector<uint32_t> ids, starts, lens, mrows, mstarts;
     std::vector<uint8_t> qt;
     std::vector<float> scores;
-    for (size_t b : assign[g]) {
-      const Micro& mb = micro[b];
-      bids.clear(), starts.clear(), lens.clear(), mrows.clear(), mstarts.assign(1, 0), qt.clear();
+  };
+  auto run = [&](size_t g, j1_status* status, std::string* msg) {
+    std::vector<Packed> pk(assign[g].size());
+    std::vector<j1_batch> jb(pk.size());
+    std::vector<float*> outs(pk.size());
+    for (size_t i = 0; i < pk.size(); ++i) {
+      const Micro& mb = micro[assign[g][i]];
+      Packed& P = pk[i];
+      P.mstarts.assign(1, 0);
       for (size_t r : mb.rows) {
-        const uint32_t start = static_cast<uint32_t>(bids.size());
-        starts.push_back(start);
-        lens.push_back(row_lens[r]);
-        qt.push_back(qtypes[r]);
-        bids.insert(bids.end(), ids + tok_off[r], ids + tok_off[r + 1]);
-        for (size_t k = mk_off[r]; k < mk_off[r + 1]; ++k) mrows.push_back(start + markers[k]);
-        mstarts.push_back(static_cast<uint32_t>(mrows.size()));
+        const uint32_t start = static_cast<uint32_t>(P.ids.size());
+        P.starts.push_back(start);
+        P.lens.push_back(row_lens[r]);
+        P.qt.push_back(qtypes[r]);
+        P.ids.insert(P.ids.end(), ids + tok_off[r], ids + tok_off[r + 1]);
+        for (size_t k = mk_off[r]; k < mk_off[r + 1]; ++k) P.mrows.push_back(start + markers[k]);
+        P.mstarts.push_back(static_cast<uint32_t>(P.mrows.size()));
       }
-      scores.assign(mrows.size(), 0.f);
-      j1_status s = j1_model_forward(e->models[g], bids.data(), bids.size(), starts.data(), lens.data(), qt.data(),
-                                     starts.size(), mrows.data(), mstarts.data(), mrows.size(), scores.data());
-      if (s) {
-        *status = s;
-        char buf[512];
-        j1_last_error(buf, sizeof(buf));
-        *msg = buf;
-        return;
-      }
+      P.scores.assign(P.mrows.size(), 0.f);
+      jb[i] = j1_batch{P.ids.data(), P.ids.size(), P.starts.data(), P.lens.data(), P.qt.data(), P.starts.size(),
+                       P.mrows.data(), P.mstarts.data(), P.mrows.size()};
+      outs[i] = P.scores.data();
+    }
+    j1_status s = j1_model_forward_many(e->models[g], jb.size(), jb.data(), outs.data());
+    if (s) {
+      *status = s;
+      char buf[512];
+      j1_last_error(buf, sizeof(buf));
+      *msg = buf;
+      return;
+    }
+    for (size_t i = 0; i < pk.size(); ++i) {
       size_t k = 0;
-      for (size_t r : mb.rows)
-        for (size_t j = mk_off[r]; j < mk_off[r + 1]; ++j) logits_out[j] = scores[k++];
+      for (size_t r : micro[assign[g][i]].rows)
+        for (size_t j = mk_off[r]; j < mk_off[r + 1]; ++j) logits_out[j] = pk[i].scores[k++];
     }
   };
 

@@ -157,10 +157,14 @@ j1_status upload_bf16(j1_model* model, SafeTensors& st, const std::string& name,
 void free_workspace(j1_model* model) {
   for (void* p : model->ws_allocations) cudaFree(p);
   model->ws_allocations.clear();
-  if (model->meta_host) cudaFreeHost(model->meta_host);
-  if (model->scores_host) cudaFreeHost(model->scores_host);
-  model->meta_host = nullptr;
-  model->scores_host = nullptr;
+  for (int k = 0; k < 2; ++k) {
+    if (model->meta_host[k]) cudaFreeHost(model->meta_host[k]);
+    if (model->scores_host[k]) cudaFreeHost(model->scores_host[k]);
+    model->meta_host[k] = nullptr;
+    model->scores_host[k] = nullptr;
+    model->meta_dev[k] = nullptr;
+    model->slot_busy[k] = false;
+  }
   model->cap_tokens = model->cap_markers = model->cap_meta = 0;
 }
 
@@ -193,12 +197,15 @@ j1_status ensure_workspace(j1_model* model, size_t tokens, size_t markers, size_
     J1_WS(hm, bf16*, M * FF * 2)
     J1_WS(qm, bf16*, M * H * 2)
     J1_WS(scores, float*, M * 4)
-    J1_WS(meta_dev, int*, E * 4)
+    J1_WS(meta_dev[0], int*, E * 4)
+    J1_WS(meta_dev[1], int*, E * 4)
 #undef J1_WS
-    J1_TRY_CUDA(cudaMallocHost(&p, E * 4), "cudaMallocHost");
-    model->meta_host = static_cast<int*>(p);
-    J1_TRY_CUDA(cudaMallocHost(&p, M * 4), "cudaMallocHost");
-    model->scores_host = static_cast<float*>(p);
+    for (int k = 0; k < 2; ++k) {
+      J1_TRY_CUDA(cudaMallocHost(&p, E * 4), "cudaMallocHost");
+      model->meta_host[k] = static_cast<int*>(p);
+      J1_TRY_CUDA(cudaMallocHost(&p, M * 4), "cudaMallocHost");
+      model->scores_host[k] = static_cast<float*>(p);
+    }
     model->cap_tokens = T;
     model->cap_markers = M;
     model->cap_meta = E;
@@ -238,21 +245,38 @@ j1_status validate_batch(const j1_model* model, const BatchView& b) {
   return J1_OK;
 }
 
-j1_status stage_batch(j1_model* model, const BatchView& b) {
-  j1_status s = validate_batch(model, b);
-  if (s) return s;
-  J1_TRY_CUDA(cudaStreamSynchronize(model->stream), "stage");  // pinned staging is reused
-  size_t ntiles = 0, nmtiles = 0;
+// Layout of a batch's metadata (ints): ids[t] | pos[t] | qtype per token[t] | markers[m]
+// | pad to 8 | attention tiles | marker-query tiles (8 ints per tile).
+struct MetaLayout {
+  size_t ntiles = 0, nmtiles = 0, tiles_off = 0, ints = 0;
+};
+MetaLayout meta_layout(const BatchView& b) {
+  MetaLayout L;
   const int PQ = attention_pair_queries();  // queries per attention work item
   for (size_t q = 0; q < b.nseq; ++q) {
-    ntiles += (b.lens[q] + PQ - 1) / PQ;
-    nmtiles += (b.marker_starts[q + 1] - b.marker_starts[q] + PQ - 1) / PQ;
+    L.ntiles += (b.lens[q] + PQ - 1) / PQ;
+    L.nmtiles += (b.marker_starts[q + 1] - b.marker_starts[q] + PQ - 1) / PQ;
   }
+  L.tiles_off = (3 * b.t + b.m + 7) / 8 * 8;
+  L.ints = L.tiles_off + (L.ntiles + L.nmtiles) * 8;
+  return L;
+}
+
+// Packs a validated batch into staging slot `slot` and uploads it (async, model stream).
+// The slot's pinned buffer may only be rewritten once its previous use has completed:
+// with `sync` the whole stream is drained first (single-batch calls), otherwise the
+// slot's completion event is awaited (pipelined calls).
+j1_status stage_batch(j1_model* model, const BatchView& b, int slot = 0, bool sync = true) {
+  j1_status s = validate_batch(model, b);
+  if (s) return s;
+  if (sync) J1_TRY_CUDA(cudaStreamSynchronize(model->stream), "stage");
+  else if (model->slot_busy[slot]) J1_TRY_CUDA(cudaEventSynchronize(model->slot_done[slot]), "stage");
+  const MetaLayout L = meta_layout(b);
+  const size_t ntiles = L.ntiles, nmtiles = L.nmtiles, tiles_off = L.tiles_off, meta_ints = L.ints;
+  const int PQ = attention_pair_queries();
   const size_t t = b.t, m = b.m;
-  const size_t tiles_off = (3 * t + m + 7) / 8 * 8;
-  const size_t meta_ints = tiles_off + (ntiles + nmtiles) * 8;
   if ((s = ensure_workspace(model, t, m, meta_ints))) return s;
-  int* h = model->meta_host;
+  int* h = model->meta_host[slot];
   for (size_t i = 0; i < t; ++i) h[i] = static_cast<int>(b.ids[i]);
   size_t o = 0;
   AttnTile* tiles = reinterpret_cast<AttnTile*>(h + tiles_off);
@@ -290,18 +314,20 @@ j1_status stage_batch(j1_model* model, const BatchView& b) {
   }
   for (size_t k = 0; k < m; ++k) h[3 * t + k] = static_cast<int>(b.marker_rows[k]);
   if (meta_ints)
-    J1_TRY_CUDA(cudaMemcpyAsync(model->meta_dev, h, meta_ints * 4, cudaMemcpyHostToDevice, model->stream),
+    J1_TRY_CUDA(cudaMemcpyAsync(model->meta_dev[slot], h, meta_ints * 4, cudaMemcpyHostToDevice, model->stream),
                 "meta upload");
+  model->slot = slot;
   model->t = t;
   model->m = m;
   model->nseq = b.nseq;
   model->ntiles = ntiles;
   model->nmtiles = nmtiles;
-  model->d_ids = model->meta_dev;
-  model->d_pos = model->meta_dev + t;
-  model->d_qtype = model->meta_dev + 2 * t;
-  model->d_markers = model->meta_dev + 3 * t;
-  model->d_tiles = reinterpret_cast<AttnTile*>(model->meta_dev + tiles_off);
+  int* md = model->meta_dev[slot];
+  model->d_ids = md;
+  model->d_pos = md + t;
+  model->d_qtype = md + 2 * t;
+  model->d_markers = md + 3 * t;
+  model->d_tiles = reinterpret_cast<AttnTile*>(md + tiles_off);
   model->d_mtiles = model->d_tiles + ntiles;
   const ModelConfig& c = model->cfg;
   const size_t H = c.hidden, I = c.intermediate, FF = c.head_ff;
@@ -442,29 +468,82 @@ j1_status launch_forward(j1_model* model) {
   return J1_OK;
 }
 
+// Queues the readback of the launched forward's scores and error word into the staged
+// slot's pinned buffers and marks the slot's completion.
+j1_status enqueue_readback(j1_model* model) {
+  const int slot = model->slot;
+  if (model->m)
+    J1_TRY_CUDA(cudaMemcpyAsync(model->scores_host[slot], model->scores, model->m * 4, cudaMemcpyDeviceToHost,
+                                model->stream),
+                "scores readback");
+  J1_TRY_CUDA(cudaMemcpyAsync(model->err_host + slot, model->err_dev, 4, cudaMemcpyDeviceToHost, model->stream),
+              "error word readback");
+  J1_TRY_CUDA(cudaEventRecord(model->slot_done[slot], model->stream), "event");
+  model->slot_busy[slot] = true;
+  return J1_OK;
+}
+
+// Waits for a slot's forward and copies its m scores out (checking the error word and
+// finiteness, as Engine::forward does with the logits, src/engine.rs:219-221).
+j1_status collect(j1_model* model, int slot, float* scores_out, size_t m) {
+  J1_TRY_CUDA(cudaEventSynchronize(model->slot_done[slot]), "forward");
+  if (model->err_host[slot] != 0) {
+    const int code = model->err_host[slot];
+    cudaStreamSynchronize(model->stream);
+    cudaMemsetAsync(model->err_dev, 0, 4, model->stream);
+    cudaStreamSynchronize(model->stream);
+    model->err_host[slot] = 0;
+    return set_error(J1_ERR_DEVICE_TIMEOUT,
+                     "device-side wait timed out (site " + std::to_string(code >> 16) + "); results discarded");
+  }
+  const float* sc = model->scores_host[slot];
+  for (size_t i = 0; i < m; ++i)
+    if (!std::isfinite(sc[i])) return set_error(J1_ERR_NONFINITE, "Inference returned nonfinite logits");
+  if (m) std::memcpy(scores_out, sc, m * 4);
+  return J1_OK;
+}
+
 j1_status finish_forward(j1_model* model, float* scores_out, size_t m) {
   if (!model->staged) return set_error(J1_ERR_INVALID_ARG, "no staged batch");
   if (m != model->m) return set_error(J1_ERR_INVALID_ARG, "scores length does not match the staged batch");
   if (m && !scores_out) return set_error(J1_ERR_INVALID_ARG, "scores_out is NULL");
-  if (m)
-    J1_TRY_CUDA(cudaMemcpyAsync(model->scores_host, model->scores, m * 4, cudaMemcpyDeviceToHost, model->stream),
-                "scores readback");
-  J1_TRY_CUDA(cudaMemcpyAsync(model->err_host, model->err_dev, 4, cudaMemcpyDeviceToHost, model->stream),
-              "error word readback");
-  J1_TRY_CUDA(cudaStreamSynchronize(model->stream), "forward");
+  j1_status s = enqueue_readback(model);
+  if (s) return s;
+  s = collect(model, model->slot, scores_out, m);
   prof_fold(model);
-  if (*model->err_host != 0) {
-    const int code = *model->err_host;
-    cudaMemsetAsync(model->err_dev, 0, 4, model->stream);
-    cudaStreamSynchronize(model->stream);
-    return set_error(J1_ERR_DEVICE_TIMEOUT,
-                     "device-side wait timed out (site " + std::to_string(code >> 16) + "); results discarded");
+  return s;
+}
+
+// Several batches back to back: batch k + 1 is validated, packed and uploaded while batch
+// k computes (two staging slots); scores are collected one batch behind.
+j1_status forward_many(j1_model* model, const std::vector<BatchView>& batches, float* const* outs) {
+  size_t T = 0, Mk = 0, E = 0;
+  for (size_t k = 0; k < batches.size(); ++k) {
+    j1_status s = validate_batch(model, batches[k]);
+    if (s) return set_error(s, "batch " + std::to_string(k) + ": " + t_last_error);
+    if (batches[k].m && !outs[k]) return set_error(J1_ERR_INVALID_ARG, "scores_out is NULL");
+    T = std::max(T, batches[k].t);
+    Mk = std::max(Mk, batches[k].m);
+    E = std::max(E, meta_layout(batches[k]).ints);
   }
-  for (size_t i = 0; i < m; ++i)
-    if (!std::isfinite(model->scores_host[i]))
-      return set_error(J1_ERR_NONFINITE, "Inference returned nonfinite logits");
-  if (m) std::memcpy(scores_out, model->scores_host, m * 4);
-  return J1_OK;
+  J1_TRY_CUDA(cudaStreamSynchronize(model->stream), "forward");
+  j1_status s = ensure_workspace(model, T, Mk, E);  // no growth (and no reallocation) below
+  if (s) return s;
+  model->slot_busy[0] = model->slot_busy[1] = false;
+  int prev = -1;
+  for (size_t k = 0; k < batches.size(); ++k) {
+    const int slot = static_cast<int>(k & 1);
+    if ((s = stage_batch(model, batches[k], slot, false)) || (s = launch_forward(model)) ||
+        (s = enqueue_readback(model)))
+      break;
+    if (prev >= 0 && (s = collect(model, prev & 1, outs[prev], batches[prev].m))) break;
+    prev = static_cast<int>(k);
+  }
+  if (!s && prev >= 0) s = collect(model, prev & 1, outs[prev], batches[prev].m);
+  cudaStreamSynchronize(model->stream);  // nothing of this call stays in flight
+  model->slot_busy[0] = model->slot_busy[1] = false;
+  prof_fold(model);
+  return s;
 }
 
 // Every tensor HostWeights::load reads (src/model.rs:55-110), with its shape; checked
@@ -547,6 +626,9 @@ j1_status create_model(const char* ckpt_dir, int ordinal, j1_model** out) {
   J1_TRY_CUDA(cudaMemsetAsync(M->err_dev, 0, 4, M->stream), "memset");
   J1_TRY_CUDA(cudaMallocHost(&p, 16), "cudaMallocHost");
   M->err_host = static_cast<int*>(p);
+  std::memset(M->err_host, 0, 16);
+  for (int k = 0; k < 2; ++k)
+    J1_TRY_CUDA(cudaEventCreateWithFlags(&M->slot_done[k], cudaEventDisableTiming), "event");
 
   const size_t H = c.hidden, I = c.intermediate, FF = c.head_ff;
   // staging for FP32 -> BF16 conversion, sized for the largest GEMM weight
@@ -643,6 +725,8 @@ void destroy_model(j1_model* model) {
   if (model->stream) cudaStreamSynchronize(model->stream);
   free_workspace(model);
   for (cudaEvent_t e : model->prof_ev) cudaEventDestroy(e);
+  for (cudaEvent_t e : model->slot_done)
+    if (e) cudaEventDestroy(e);
   for (void* p : model->allocations) cudaFree(p);
   if (model->err_host) cudaFreeHost(model->err_host);
   if (model->stream) cudaStreamDestroy(model->stream);
@@ -797,6 +881,20 @@ j1_status j1_model_forward(j1_model* model, const uint32_t* ids, size_t t, const
   if (s) return s;
   if ((s = launch_forward(model))) return s;
   return finish_forward(model, scores_out, m);
+}
+
+j1_status j1_model_forward_many(j1_model* model, size_t nbatch, const j1_batch* batches, float* const* scores_out) {
+  if (!model) return set_error(J1_ERR_INVALID_ARG, "NULL model");
+  if (nbatch && (!batches || !scores_out)) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+  std::lock_guard<std::mutex> lk(model->mu);
+  DeviceGuard guard(model->device);
+  std::vector<BatchView> v;
+  v.reserve(nbatch);
+  for (size_t k = 0; k < nbatch; ++k) {
+    const j1_batch& b = batches[k];
+    v.push_back(BatchView{b.ids, b.t, b.starts, b.lens, b.qtypes, b.nseq, b.marker_rows, b.marker_starts, b.m});
+  }
+  return forward_many(model, v, scores_out);
 }
 
 void* j1_model_stream(j1_model* model) { return model ? static_cast<void*>(model->stream) : nullptr; }

@@ -91,14 +91,20 @@ struct j1_model {
   float* ym = nullptr;
   j1rt::bf16 *ymb = nullptr, *cm = nullptr, *hm = nullptr, *qm = nullptr;
   float* scores = nullptr;
-  int* meta_dev = nullptr;
-  int* meta_host = nullptr;      // pinned
-  float* scores_host = nullptr;  // pinned
-  int* err_host = nullptr;       // pinned
+  // Two staging slots (batch metadata in/out), so that the next batch can be packed and
+  // uploaded while the current one computes (j1_model_forward_many); the single-batch
+  // calls use slot 0. err_host holds one error word per slot.
+  int* meta_dev[2] = {nullptr, nullptr};
+  int* meta_host[2] = {nullptr, nullptr};      // pinned
+  float* scores_host[2] = {nullptr, nullptr};  // pinned
+  cudaEvent_t slot_done[2] = {nullptr, nullptr};  // the slot's forward and readback completed
+  bool slot_busy[2] = {false, false};
+  int* err_host = nullptr;  // pinned
   std::vector<void*> ws_allocations;
 
   // ---- staged batch
   bool staged = false;
+  int slot = 0;  // staging slot of the staged batch
   size_t t = 0, m = 0, nseq = 0, ntiles = 0, nmtiles = 0;
   int *d_ids = nullptr, *d_pos = nullptr, *d_qtype = nullptr, *d_markers = nullptr;
   j1rt::AttnTile* d_tiles = nullptr;

@@ -26,6 +26,7 @@ EXPORTS = [
     "j1_last_error", "j1_status_name", "j1_version", "j1_config_load",
     "j1_model_create", "j1_model_destroy", "j1_model_name", "j1_model_config", "j1_model_forward",
     "j1_model_stage", "j1_model_launch", "j1_model_finish", "j1_model_stream", "j1_model_launch_count",
+    "j1_model_forward_many",
     "j1_engine_options_default", "j1_engine_create", "j1_engine_create_pool", "j1_engine_destroy",
     "j1_engine_device_name", "j1_engine_logits_encoded",
     "j1_op_gemm", "j1_op_attention", "j1_op_attention_noalloc", "j1_op_geglu_interleave",
@@ -46,6 +47,12 @@ class J1Config(C.Structure):
     _fields_ = [(n, C.c_int32) for n in ("hidden", "heads", "head_dim", "intermediate", "layers", "half_window",
                                          "vocab", "max_positions", "head_layers", "head_heads", "head_ff")] + \
                [("norm_eps", C.c_float), ("n_global", C.c_int32)]
+
+
+class J1Batch(C.Structure):
+    _fields_ = [("ids", C.POINTER(C.c_uint32)), ("t", C.c_size_t), ("starts", C.POINTER(C.c_uint32)),
+                ("lens", C.POINTER(C.c_uint32)), ("qtypes", C.POINTER(C.c_uint8)), ("nseq", C.c_size_t),
+                ("marker_rows", C.POINTER(C.c_uint32)), ("marker_starts", C.POINTER(C.c_uint32)), ("m", C.c_size_t)]
 
 
 class J1EngineOptions(C.Structure):
@@ -91,6 +98,8 @@ def lib():
     L.j1_model_stage.argtypes = [C.c_void_p] + batch
     L.j1_model_launch.argtypes = [C.c_void_p]
     L.j1_model_finish.argtypes = [C.c_void_p, f32p, C.c_size_t]
+    L.j1_model_forward_many.argtypes = [C.c_void_p, C.c_size_t, C.POINTER(J1Batch), C.POINTER(f32p)]
+    L.j1_model_forward_many.restype = C.c_int
     L.j1_model_stream.argtypes = [C.c_void_p]
     L.j1_model_stream.restype = C.c_void_p
     L.j1_model_launch_count.argtypes = [C.c_void_p]
@@ -270,6 +279,18 @@ class CudaModel:
     def forward(self, b: Batch) -> List[List[float]]:
         """Scores per sequence (Batch::split_scores)."""
         return b.split_scores(self.forward_flat(b))
+
+    def forward_many(self, batches: Sequence[Batch]) -> List[np.ndarray]:
+        """j1_model_forward_many: the flat scores of each batch (pipelined staging)."""
+        keep, jb, outs = [], (J1Batch * len(batches))(), []
+        for i, b in enumerate(batches):
+            k, a = self._args(b)
+            keep.append(k)
+            jb[i] = J1Batch(*a)
+            outs.append(np.zeros(b.marker_rows.size, np.float32))
+        po = (C.POINTER(C.c_float) * len(batches))(*[o.ctypes.data_as(C.POINTER(C.c_float)) for o in outs])
+        check(lib().j1_model_forward_many(self._h, len(batches), jb, po))
+        return outs
 
     # resident-batch split used by the benchmark
     def stage(self, b: Batch):

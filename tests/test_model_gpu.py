@@ -154,6 +154,32 @@ def test_engine_pool_matches_model(torch_cuda, ckpt768, model768):
     assert got == [list(w) for w in want]
 
 
+def test_forward_many_matches_single_forwards(model768):
+    """j1_model_forward_many (staging of batch k+1 overlapped with forward k) gives each
+    batch's single-forward scores bit for bit, for batches of different sizes."""
+    rng = np.random.default_rng(7)
+    batches = []
+    for i in range(5):
+        lens = rng.integers(1, 700, size=int(rng.integers(1, 9))).tolist()
+        batches.append(rows_to_batch(synthetic.synthetic_batch(lens, markers_per_seq=3, seed=120 + i,
+                                                               mask_markers=False)))
+    got = model768.forward_many(batches)
+    for b, g in zip(batches, got):
+        assert np.array_equal(g, model768.forward_flat(b))
+    assert model768.forward_many([]) == []
+
+
+def test_forward_many_validates_every_batch_first(model768):
+    good = rows_to_batch(synthetic.synthetic_batch([64, 64], markers_per_seq=2, seed=131))
+    ids = good.ids.copy()
+    ids[0] = 50368  # out of vocabulary
+    bad = j1.Batch(ids, good.starts, good.lens, good.qtypes, good.marker_rows, good.marker_starts)
+    with pytest.raises(j1.J1Error) as e:
+        model768.forward_many([good, bad, good])
+    assert e.value.status == j1.INVALID_ARG and "batch 1" in str(e.value)
+    assert np.array_equal(model768.forward_many([good])[0], model768.forward_flat(good))
+
+
 def test_forward_rejects_bad_batches(model768):
     rows = synthetic.synthetic_batch([64, 64], markers_per_seq=2, seed=113)
     b = rows_to_batch(rows)
