@@ -379,9 +379,9 @@ __global__ void __launch_bounds__(192, 2)
         }
         float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          mx[i & 3] = fmaxf(mx[i & 3], __uint_as_float(sa[i]));
-          mx[(i + 2) & 3] = fmaxf(mx[(i + 2) & 3], __uint_as_float(sb[i]));
+        for (int i = 0; i < 32; i += 2) {
+          mx[(i >> 1) & 3] = max3(mx[(i >> 1) & 3], __uint_as_float(sa[i]), __uint_as_float(sa[i + 1]));
+          mx[((i >> 1) + 2) & 3] = max3(mx[((i >> 1) + 2) & 3], __uint_as_float(sb[i]), __uint_as_float(sb[i + 1]));
         }
         const float bmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * scale_log2;
         const bool moved = bmax > m_used + kRescaleLog2;  // also the row's first valid block
@@ -406,17 +406,23 @@ __global__ void __launch_bounds__(192, 2)
         }
         if (moved) m_used = bmax;
         const float uu = (m_used == -INFINITY) ? 0.f : m_used;
-        float lp[4] = {0.f, 0.f, 0.f, 0.f};
+        // pairs of keys: one packed FMA for both exponents, one packed add into the sums
+        const uint64_t sc2 = f2pack(scale_log2, scale_log2), nu2 = f2pack(-uu, -uu);
+        uint64_t lp2[4] = {0ull, 0ull, 0ull, 0ull};
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const uint32_t s0 = i < 16 ? sa[2 * i] : sb[2 * i - 32];
           const uint32_t s1 = i < 16 ? sa[2 * i + 1] : sb[2 * i - 31];
-          const float p0 = ex2(fmaf(__uint_as_float(s0), scale_log2, -uu));
-          const float p1 = ex2(fmaf(__uint_as_float(s1), scale_log2, -uu));
-          lp[i & 3] += p0 + p1;
+          float a0, a1;
+          f2unpack(fma2(f2pack(__uint_as_float(s0), __uint_as_float(s1)), sc2, nu2), a0, a1);
+          const float p0 = ex2(a0), p1 = ex2(a1);
+          lp2[i & 3] = add2(lp2[i & 3], f2pack(p0, p1));
           pk[i] = pack_bf16x2(p0, p1);
         }
-        lb = (lp[0] + lp[1]) + (lp[2] + lp[3]);
+        float lq[8];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) f2unpack(lp2[k], lq[2 * k], lq[2 * k + 1]);
+        lb = ((lq[0] + lq[1]) + (lq[2] + lq[3])) + ((lq[4] + lq[5]) + (lq[6] + lq[7]));
       } else {
 #pragma unroll
         for (int i = 0; i < 32; ++i) pk[i] = 0u;

@@ -76,6 +76,36 @@ struct GemmCfg {
 
 __device__ __forceinline__ float gelu_erf(float v) { return 0.5f * v * (1.f + erff(v * 0.70710678118654752f)); }
 
+// GEGLU outputs gelu(h0) * g0 and gelu(h1) * g1, evaluated pairwise with packed FP32
+// arithmetic. erf(x) uses the rational approximation of the reference's CPU path
+// (src/cpu/fastmath.rs:27-43; the Eigen/XLA float erf): x clamped to [-4, 4],
+// erf = x p(x^2) / q(x^2) with p of degree 6 and q of degree 4 in x^2; the division is a
+// reciprocal estimate (about 1 ulp). It agrees with erff to about 1e-7, far below the
+// BF16 rounding of the output, at half the instructions.
+__device__ __forceinline__ void geglu2(float h0, float h1, float g0, float g1, float& o0, float& o1) {
+  const float x0 = fminf(fmaxf(h0 * 0.70710678118654752f, -4.f), 4.f);
+  const float x1 = fminf(fmaxf(h1 * 0.70710678118654752f, -4.f), 4.f);
+  const uint64_t x = f2pack(x0, x1), x2 = mul2(x, x);
+  auto c2 = [](float c) { return f2pack(c, c); };
+  uint64_t p = c2(-2.7261423e-10f);
+  p = fma2(p, x2, c2(2.7706814e-8f));
+  p = fma2(p, x2, c2(-2.101024e-6f));
+  p = fma2(p, x2, c2(-5.6925064e-5f));
+  p = fma2(p, x2, c2(-7.3499063e-4f));
+  p = fma2(p, x2, c2(-2.9546e-3f));
+  p = fma2(p, x2, c2(-1.6096033e-2f));
+  uint64_t q = c2(-1.4566072e-5f);
+  q = fma2(q, x2, c2(-2.1337406e-4f));
+  q = fma2(q, x2, c2(-1.682827e-3f));
+  q = fma2(q, x2, c2(-7.373329e-3f));
+  q = fma2(q, x2, c2(-1.426474e-2f));
+  float q0, q1;
+  f2unpack(q, q0, q1);
+  const uint64_t erf = mul2(mul2(x, p), f2pack(rcp_approx(q0), rcp_approx(q1)));
+  const uint64_t hh = mul2(f2pack(h0, h1), c2(0.5f));
+  f2unpack(mul2(fma2(hh, erf, hh), f2pack(g0, g1)), o0, o1);
+}
+
 // 32 values of one row -> four 16-byte units (unit0 .. unit0+3) of a 128B-swizzled box
 // row: unit i of row r sits at (i ^ (r & 7)) * 16 within the row's 128 bytes.
 __device__ __forceinline__ void put_row32(uint8_t* srow, int r, int unit0, const float (&v)[32]) {
@@ -387,7 +417,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GemmCfg<BN, EPI>::TH
               tmem_ld32(tb + 128 + h * 64, rb);
               tmem_ld_wait();
 #pragma unroll
-              for (int j = 0; j < 32; ++j) a[j] = gelu_erf(__uint_as_float(ra[j])) * __uint_as_float(rb[j]);
+              for (int j = 0; j < 32; j += 2)
+                geglu2(__uint_as_float(ra[j]), __uint_as_float(ra[j + 1]), __uint_as_float(rb[j]),
+                       __uint_as_float(rb[j + 1]), a[j], a[j + 1]);
             }
             {
               uint32_t ra[32], rb[32];
@@ -395,7 +427,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GemmCfg<BN, EPI>::TH
               tmem_ld32(tb + 128 + h * 64 + 32, rb);
               tmem_ld_wait();
 #pragma unroll
-              for (int j = 0; j < 32; ++j) b[j] = gelu_erf(__uint_as_float(ra[j])) * __uint_as_float(rb[j]);
+              for (int j = 0; j < 32; j += 2)
+                geglu2(__uint_as_float(ra[j]), __uint_as_float(ra[j + 1]), __uint_as_float(rb[j]),
+                       __uint_as_float(rb[j + 1]), b[j], b[j + 1]);
             }
             store_box(a, b, nu * 128 + h * 64, m0);
           }
