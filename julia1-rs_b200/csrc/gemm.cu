@@ -385,16 +385,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GemmCfg<BN, EPI>::TH
             const int col = n0 + g * 64;
             float a[32], b[32];
             if (col < p.rope_cols) {
+              // rotate-half on pairs of dimensions at once (packed FP32):
+              //   a = x c - y s,  b = y c + x s   for x = q[d], y = q[d + 32]
 #pragma unroll
               for (int i = 0; i < 8; ++i) {
-                const float cc[4] = {rc[i].x, rc[i].y, rc[i].z, rc[i].w};
-                const float ss[4] = {rsn[i].x, rsn[i].y, rsn[i].z, rsn[i].w};
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
+                for (int k = 0; k < 4; k += 2) {
                   const int j = 4 * i + k;
-                  const float x = __uint_as_float(lo[j]), y = __uint_as_float(hi[j]);
-                  a[j] = x * cc[k] - y * ss[k];
-                  b[j] = y * cc[k] + x * ss[k];
+                  const uint64_t cc = k == 0 ? f2pack(rc[i].x, rc[i].y) : f2pack(rc[i].z, rc[i].w);
+                  const uint64_t ss = k == 0 ? f2pack(rsn[i].x, rsn[i].y) : f2pack(rsn[i].z, rsn[i].w);
+                  const uint64_t ns = k == 0 ? f2pack(-rsn[i].x, -rsn[i].y) : f2pack(-rsn[i].z, -rsn[i].w);
+                  const uint64_t x = f2pack(__uint_as_float(lo[j]), __uint_as_float(lo[j + 1]));
+                  const uint64_t y = f2pack(__uint_as_float(hi[j]), __uint_as_float(hi[j + 1]));
+                  f2unpack(fma2(y, ns, mul2(x, cc)), a[j], a[j + 1]);
+                  f2unpack(fma2(x, ss, mul2(y, cc)), b[j], b[j + 1]);
                 }
               }
             } else {
