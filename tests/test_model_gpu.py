@@ -104,6 +104,35 @@ def test_long_sequence_2048_parity(model768, oracle768):
     assert np.abs(gpu - ref32).max() <= TOL_FP32
 
 
+def test_c3_ragged_64_full_size(model768, oracle768):
+    """Config 3 at full size: 64 sequences, lengths U[16, 1024], packed varlen (~33K tokens),
+    against the BF16-chain oracle; every row's argmax where the top-2 gap is resolvable."""
+    rng = np.random.default_rng(2024)
+    lens = rng.integers(16, 1025, size=64).tolist()
+    rows = synthetic.synthetic_batch(lens, markers_per_seq=4, seed=140, mask_markers=False)
+    b = rows_to_batch(rows)
+    gpu = model768.forward_flat(b)
+    ref16 = oracle768.forward_flat(b, mode="bf16")
+    d = np.abs(gpu - ref16)
+    print("C3 t=%d max|gpu-bf16| %.5f mean %.6f" % (b.tokens(), d.max(), d.mean()))
+    assert d.max() <= TOL_BF16
+    assert np.abs(gpu - ref16).max() <= 2e-2 * max(1.0, np.abs(ref16).max())
+    agree, total = argmax_agreement(gpu, ref16, b.marker_starts, TOL_BF16)
+    assert agree == total
+
+
+def test_c4_8192_parity(model768, oracle768):
+    """Config 4 sequence length (8192 = max_position_embeddings): global layers attend over
+    all 8192 keys (128 key blocks of 64 per query tile); against the BF16-chain oracle."""
+    rows = synthetic.synthetic_batch([8192], markers_per_seq=24, seed=141, mask_markers=False)
+    b = rows_to_batch(rows)
+    gpu = model768.forward_flat(b)
+    ref16 = oracle768.forward_flat(b, mode="bf16")
+    d = np.abs(gpu - ref16)
+    print("C4 max|gpu-bf16| %.5f mean %.6f" % (d.max(), d.mean()))
+    assert d.max() <= TOL_BF16
+
+
 def test_batching_invariance_exact(model768):
     """tests/checkpoint.rs:91-105 property; here the per-row math is independent of the batch: exact."""
     rows = synthetic.synthetic_batch([300, 17, 129, 512, 1000, 64], markers_per_seq=5, seed=107, mask_markers=False)
