@@ -81,6 +81,19 @@ def family_model(t, seqs, m):
     }
 
 
+def gemm_peak_share(timed, model_f, sustained):
+    """The metric's "GEMM % tensor peak": the four encoder GEMM families' FLOPs over their
+    summed device time, against the measured sustained and the nominal dense bf16 peak."""
+    fams = ["gemm_qkv_rope", "gemm_wo_resid_ln", "gemm_wi_geglu", "gemm_wo2_resid_ln"]
+    flops = sum(model_f[f]["flops"] * timed[f][1] for f in fams if f in timed)
+    ms = sum(timed[f][0] for f in fams if f in timed)
+    if ms <= 0:
+        return None
+    tf = flops / (ms / 1e3) / 1e12
+    return {"tflops": round(tf, 1), "frac_of_measured_sustained": round(tf / sustained, 4),
+            "frac_of_nominal": round(tf / 2250.0, 4)}
+
+
 def encoder_flops_per_token(S):
     return 2.0 * L * (H * 3 * H + H * H + H * 2 * I + I * H) + 4.0 * H * (N_GLOBAL * S + (L - N_GLOBAL) *
                                                                           local_pairs(S) / S)
@@ -153,11 +166,11 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def cpu_sample(ckpt, target_s=12.0, max_rows=64):
+def cpu_sample(ckpt, target_s=12.0, max_rows=64, threads=None):
     """Time the reference CPU path (FP32 restatement) on a bounded sample of the same workload."""
     from oracle import oracle as orc
     import julia1 as j1
-    threads = len(os.sched_getaffinity(0))
+    threads = threads or len(os.sched_getaffinity(0))
     o = orc.Oracle(ckpt)
     rows = make_rows(seed=77)
     b = j1.Batch.new([j1.Encoded(*r) for r in rows[:1]])
@@ -312,6 +325,8 @@ def main():
                 roof = {"kernel": dom, "bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
                         "frac": round(ach / hbm, 4), "traffic": traffic, "peak_kind": "%s HBM copy" % kind}
             roof["algorithmic_per_launch"] = fm["flops"] if fm["bound"] == "tensor" else fm["bytes"]
+            # against the nominal B200 figures as well (2.25 PF/s dense bf16, 8 TB/s HBM3e)
+            roof["frac_of_nominal"] = round(ach / (2250.0 if fm["bound"] == "tensor" else 8000.0), 4)
             roof["avg_launch_ms"] = round(avg_ms, 4)
             roof["share_of_step"] = round(timed[dom][0] / total, 4)
         breakdown = {}
@@ -328,6 +343,7 @@ def main():
                 "data": "synthetic (seeded ids, random-init weights)", "config": workload_config(),
                 "roofline": roof,
                 "encoder_tflops": round(value / world * fpt / 1e12, 1),
+                "gemm_tensor_peak": gemm_peak_share(timed, model_f, tf_sust),
                 "kernel_breakdown": breakdown,
                 "e2e": {"value": round(e2e, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                         "d2h_bytes_per_step": d2h},
@@ -337,6 +353,9 @@ def main():
             model.close()
             cb, _, _ = cpu_sample(ckpt)
             line["cpu_baseline"] = cb
+            # the reference engine's default CPU thread count (src/engine.rs:160-162)
+            cb4, _, _ = cpu_sample(ckpt, target_s=8.0, max_rows=16, threads=4)
+            line["cpu_baseline_4_threads"] = cb4
         print(json.dumps(line), flush=True)
     model.close()
     if world > 1:

@@ -200,3 +200,11 @@ def test_plan_errors():
     with pytest.raises(j1.J1Error):
         j1.plan_batches([1, 2], 0, 100, 1)
     assert j1.plan_batches([], 4, 100, 2) == ([], [])
+
+
+def test_null_handles_are_rejected():
+    L = j1.lib()
+    assert L.j1_model_forward_many(None, 0, None, None) == j1.INVALID_ARG
+    assert L.j1_model_launch(None) == j1.INVALID_ARG
+    assert L.j1_engine_logits_encoded(None, 0, None, None, None, None, None, None) == j1.INVALID_ARG
+    assert "NULL" in j1.last_error()
