@@ -222,7 +222,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GemmCfg<BN, EPI>::TH
         for (int s = 0; s < n_sub && ok; ++s) {
           const int n0 = (FULL_ROW ? s : nu) * BN + static_cast<int>(rank) * (BN / 2);
           for (int kb = 0; kb < kblocks; ++kb) {
-            if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.err, 1)) {
+            if (!mbar_wait<true>(&empty[stage], phase ^ 1, abort_flag, p.err, 1)) {
               ok = false;
               break;
             }
@@ -258,14 +258,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GemmCfg<BN, EPI>::TH
         for (int s = 0; s < n_sub && ok; ++s) {
           const int buf = acc & 1;
           const uint32_t aph = (acc >> 1) & 1;
-          if (!mbar_wait(&tempty[buf], aph ^ 1, abort_flag, p.err, 2)) {
+          if (!mbar_wait<true>(&tempty[buf], aph ^ 1, abort_flag, p.err, 2)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t d = tmem_base + buf * BN;
           for (int kb = 0; kb < kblocks; ++kb) {
-            if (!mbar_wait(&full[stage], phase, abort_flag, p.err, 3)) {
+            if (!mbar_wait<true>(&full[stage], phase, abort_flag, p.err, 3)) {
               ok = false;
               break;
             }
@@ -293,7 +293,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GemmCfg<BN, EPI>::TH
       // All MMAs of this thread must have finished before TMEM is released (in both CTAs).
       umma_commit_pair(mapa_shared(smem_u32(drain), 0));
       volatile int no_abort = 0;
-      mbar_wait(drain, 0, &no_abort, nullptr, 0);
+      mbar_wait<true>(drain, 0, &no_abort, nullptr, 0);
     }
   } else if (warp <= 5) {
     // ------------------------------------------------------------ epilogue (warps 2..5)
@@ -345,7 +345,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GemmCfg<BN, EPI>::TH
       for (int s = 0; s < n_sub; ++s) {
         const int buf = acc & 1;
         const uint32_t aph = (acc >> 1) & 1;
-        mbar_wait(&tfull[buf], aph, abort_flag, p.err, 4);
+        mbar_wait<true>(&tfull[buf], aph, abort_flag, p.err, 4);
         tc_fence_after();
         const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
         const int n0 = (FULL_ROW ? s : nu) * BN;
@@ -445,7 +445,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GemmCfg<BN, EPI>::TH
             uint32_t r[32];
             tmem_ld32(tb + cc * 32, r);
             tmem_ld_wait();
-            mbar_wait(&xfull[b], (gch / NXB) & 1, abort_flag, p.err, 5);
+            mbar_wait<true>(&xfull[b], (gch / NXB) & 1, abort_flag, p.err, 5);
             // this row's 32 residual values, 128B-swizzled: 16-byte unit i sits at i ^ (row & 7)
             uint8_t* xrow = sX + b * XCHUNK + trow * 128;
             float v[32];
@@ -524,7 +524,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GemmCfg<BN, EPI>::TH
       if constexpr (EPI == EPI_RESID_LN) {
         // hand this unit's row statistics to the LayerNorm warps (slot = unit parity)
         const int slot = nunit & 1;
-        if (nunit >= 2) mbar_wait(&lnempty[slot], ((nunit - 2) >> 1) & 1, abort_flag, p.err, 7);
+        if (nunit >= 2) mbar_wait<true>(&lnempty[slot], ((nunit - 2) >> 1) & 1, abort_flag, p.err, 7);
         stats[slot * BM + trow] = make_float2(w_mean, rsqrtf(w_m2 * (1.f / static_cast<float>(H)) + p.ln_eps));
         named_bar_sync(1, 128);  // every row's statistics written; the unit's x stores complete
         if (storer) mbar_arrive(&lnfull[slot]);
@@ -547,7 +547,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GemmCfg<BN, EPI>::TH
           const int m0 = (u / n_per_m) * 2 * BM + static_cast<int>(rank) * BM;
           for (int c = 0; c < NCH; ++c, ++gx) {
             const uint32_t b = gx % NXB, ph = (gx / NXB) & 1;
-            if (!mbar_wait(&xempty[b], ph ^ 1, abort_flag, p.err, 6)) {
+            if (!mbar_wait<true>(&xempty[b], ph ^ 1, abort_flag, p.err, 6)) {
               ok = false;
               break;
             }
@@ -560,7 +560,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GemmCfg<BN, EPI>::TH
         if (!ok) {  // unwinding: every load already issued must land before smem is released
           volatile int no_abort = 0;
           for (uint32_t b = 0; b < NXB; ++b)
-            if (armed & (1u << b)) mbar_wait(&xfull[b], (armed_par >> b) & 1u, &no_abort, nullptr, 0);
+            if (armed & (1u << b)) mbar_wait<true>(&xfull[b], (armed_par >> b) & 1u, &no_abort, nullptr, 0);
         }
       }
     }
@@ -583,7 +583,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GemmCfg<BN, EPI>::TH
       for (int u = pair; u < units; u += npairs, ++nunit) {
         const int m0 = (u / n_per_m) * 2 * BM + static_cast<int>(rank) * BM;
         const int slot = nunit & 1;
-        if (!__all_sync(0xffffffffu, mbar_wait(&lnfull[slot], (nunit >> 1) & 1, abort_flag, p.err, 8))) break;
+        if (!__all_sync(0xffffffffu, mbar_wait<true>(&lnfull[slot], (nunit >> 1) & 1, abort_flag, p.err, 8))) break;
         fence_proxy_async_global();
         const float2 my = stats[slot * BM + k * 32 + lane];  // (mean, rstd) of row 32k + lane
         const int wrow0 = m0 + k * 32;

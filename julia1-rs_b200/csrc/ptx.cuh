@@ -44,17 +44,33 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// The same test, allowing the hardware to suspend the thread for up to 20 us until the
+// phase completes: a waiting thread then takes no issue slots from warps that compute.
+__device__ __forceinline__ bool mbar_test_suspend(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(20000u)
+      : "memory");
+  return ok != 0;
+}
 
 // Wait until the phase with the given parity has completed. Returns false when
 // the CTA is aborting (another role timed out) or this wait timed out.
 // `err` is a device error word the host reads after the forward (0 = ok; low
 // 16 bits = code 1 "wait timeout", high bits = the site tag of the wait).
+// SUSPEND: let the thread sleep inside each test (for waits off the latency-critical
+// path, e.g. the GEMM producer / MMA threads sharing an SM with epilogue warps).
+template <bool SUSPEND = false>
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err,
                                           int site) {
   if (mbar_test(bar, parity)) return true;
   const long long t0 = clock64();
   for (uint32_t it = 1;; ++it) {
-    if (mbar_test(bar, parity)) return true;
+    if (SUSPEND ? mbar_test_suspend(bar, parity) : mbar_test(bar, parity)) return true;
     if (*abort_flag) return false;
     if ((it & 255u) == 0 && err && *reinterpret_cast<volatile int*>(err) != 0) {  // another CTA gave up
       *abort_flag = 1;
