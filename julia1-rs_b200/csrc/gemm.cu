@@ -485,7 +485,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GemmCfg<BN, EPI>::TH
             fence_proxy_async_smem();
             named_bar_sync(1, 128);
             if (storer && !*abort_flag) {
-              tma_store_2d(&tmX, sX + b * XCHUNK, c * 32, m0);
+              // the LayerNorm warps re-read the updated rows one unit later: ask L2 to keep them
+              if constexpr (EPI == EPI_RESID_LN)
+                tma_store_2d_hint(&tmX, sX + b * XCHUNK, c * 32, m0, l2_policy_evict_last());
+              else
+                tma_store_2d(&tmX, sX + b * XCHUNK, c * 32, m0);
               bulk_commit();
               bulk_wait_read_1();  // the previous chunk's store has read its slot: hand it back
               if (xpend >= 0) mbar_arrive(&xempty[xpend]);
@@ -579,6 +583,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GemmCfg<BN, EPI>::TH
         gw[v] = reinterpret_cast<const float4*>(p.ln_w)[v * 32 + lane];
         gb[v] = p.ln_b ? reinterpret_cast<const float4*>(p.ln_b)[v * 32 + lane] : make_float4(0.f, 0.f, 0.f, 0.f);
       }
+      const uint64_t pol_first = l2_policy_evict_first();  // last read of these rows here
       int nunit = 0;
       for (int u = pair; u < units; u += npairs, ++nunit) {
         const int m0 = (u / n_per_m) * 2 * BM + static_cast<int>(rank) * BM;
@@ -596,7 +601,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GemmCfg<BN, EPI>::TH
             if (rw < p.M) {
               const float4* src = reinterpret_cast<const float4*>(p.x + static_cast<size_t>(rw) * p.ldx);
 #pragma unroll
-              for (int v = 0; v < NV; ++v) xv[i][v] = __ldcg(src + v * 32 + lane);
+              for (int v = 0; v < NV; ++v) xv[i][v] = ld_cg_hint(src + v * 32 + lane, pol_first);
             }
           }
 #pragma unroll
