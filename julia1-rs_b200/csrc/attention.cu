@@ -16,9 +16,11 @@
 //   warp 4      tcgen05.mma issuer: S = Q K^T (M=128, N=64, K=64, operands in smem) and
 //               O += P V (M=128, N=64, K=64; P from TMEM, V from smem read MN-major)
 //   warp 5      TMA producer: Q (double buffered across items), K/V blocks (4 stages)
-// TMEM (256 columns): S(g) in [64 (g&1), +64), P(g) in [128 + 32 (g&1), +32), O in
-// [192, 256). With S and P double buffered the MMA runs two blocks ahead of the
-// softmax: S(g+2) is issued as soon as P(g) is in, so the softmax rarely waits for S.
+// TMEM (256 columns): S(g) in [64 (g&1), +64); P(g) overwrites the first 32 of those
+// columns once the row's scores are in registers; O of the CTA's n-th item in
+// [128 + 64 (n&1), +64). With S double buffered the MMA runs two blocks ahead of the
+// softmax: S(g+2) is issued once P(g).V(g) has read P(g), so the softmax rarely waits
+// for S. With O double buffered the next item's P.V never waits for an epilogue.
 //
 // Softmax per block: the 64 scores of the row are loaded once and their exact maximum
 // is taken first; the running offset only moves (rescaling O and l) when the maximum
@@ -27,8 +29,9 @@
 // for all 32 rows of a warp skip the exponentials (P = 0).
 //
 // The epilogue of an item (O / l -> out) runs during the first block of the next item,
-// after o_full; full 32-row slices leave by TMA store, staged in the item's Q buffer,
-// which then goes back to the producer.
+// after that block's P is handed over; full 32-row slices leave by TMA store, staged in
+// the item's Q buffer, which goes back to the producer one block later (once the store
+// has read it), or before the next S wait when that S needs the buffer's next Q.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -46,7 +49,7 @@ constexpr int NKV = 4;   // K/V stages
 constexpr uint32_t Q_BYTES = QT * HD * 2;   // 16 KB Q box
 constexpr uint32_t KV_BYTES = KB * HD * 2;  // 8 KB K or V box
 constexpr uint32_t ATT_SMEM = 2 * Q_BYTES + NKV * 2 * KV_BYTES + 1024 + 256;
-constexpr uint32_t TS_COL = 0, TP_COL = 128, TO_COL = 192;
+constexpr uint32_t TS_COL = 0, TO_COL = 128;
 
 __device__ __forceinline__ float ex2(float x) {
   float y;
@@ -139,9 +142,9 @@ __global__ void __launch_bounds__(192, 2)
   uint64_t* q_free = q_full + 2;      // [2] per Q buffer (one arrival per softmax warp)
   uint64_t* s_full = q_free + 2;      // [2] per S buffer: S(g) in TMEM
   uint64_t* p_full = s_full + 2;      // [2] per P buffer: P(g) in TMEM and S(g) read (4 arrivals)
-  uint64_t* pv_done = p_full + 2;     // [2] per P buffer: P(g).V(g) done
-  uint64_t* o_full = pv_done + 2;     // last P.V of an item done
-  uint64_t* drain = o_full + 1;
+  uint64_t* pv_done = p_full + 2;     // [2] per S buffer: P(g).V(g) done
+  uint64_t* o_full = pv_done + 2;     // [2] per O buffer: last P.V of an item done
+  uint64_t* drain = o_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -165,8 +168,8 @@ __global__ void __launch_bounds__(192, 2)
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 4);
       mbar_init(&pv_done[i], 1);
+      mbar_init(&o_full[i], 1);
     }
-    mbar_init(o_full, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -256,16 +259,20 @@ __global__ void __launch_bounds__(192, 2)
         if (!mbar_wait(&p_full[g & 1], (g >> 1) & 1, abort_flag, err, 14)) break;
         tc_fence_after();
         const uint32_t vb0 = v0 + (g % NKV) * KV_BYTES;
+        const uint32_t ob = static_cast<uint32_t>(cp.n & 1);
 #pragma unroll
         for (int k = 0; k < KB / 16; ++k)
-          umma_bf16_ts(tmem_base + TO_COL, tmem_base + TP_COL + (g & 1) * (KB / 2) + k * 8,
+          umma_bf16_ts(tmem_base + TO_COL + ob * HD, tmem_base + TS_COL + (g & 1) * KB + k * 8,
                        sdesc_sw128(vb0 + k * 2048, 8192, 1024), idO, (k > 0 || cp.j > 0) ? 1u : 0u);
         umma_commit(&kv_free[g % NKV]);
         umma_commit(&pv_done[g & 1]);
-        if (cp.j + 1 == cp.it.nb) umma_commit(o_full);  // O of the item is final
+        if (cp.j + 1 == cp.it.nb) umma_commit(&o_full[ob]);  // O of the item is final
         cursor_next(cp, tiles, ntiles, items, window);
         if (cs.u < items) {
-          ok = issue_s(cs, gs);  // into S buffer g&1, which S(g) no longer needs
+          // S(g+2) goes into the columns that hold P(g): P(g).V(g) must have read them
+          if (!mbar_wait(&pv_done[g & 1], (g >> 1) & 1, abort_flag, err, 19)) break;
+          tc_fence_after();
+          ok = issue_s(cs, gs);
           cursor_next(cs, tiles, ntiles, items, window);
           ++gs;
         }
@@ -278,19 +285,30 @@ __global__ void __launch_bounds__(192, 2)
     // ------------------------------------------------------------ softmax warps 0..3
     const int r = threadIdx.x;  // query row == TMEM lane
     const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
-    const uint32_t tO = tmem_base + TO_COL + lane_off;
     constexpr float kRescaleLog2 = 8.f;
     bool ok = true;
-    uint32_t no = 0;  // o_full phases consumed
     // The epilogue of an item (O / l -> out) runs during the first block of the next
-    // item: its O is final once o_full fires, and it must be read before this group's
-    // next p_full lets P.V(0) of the next item overwrite it.
+    // item, after that block's P is handed over: the next item accumulates into the
+    // other O buffer, and o_full of this one has fired by then.
     struct Pending {
       bool on;
       float l;
-      int row0, nq, head, qb;
+      int row0, nq, head, n;  // n: the item's index in this CTA (O and Q buffer n & 1)
     } pend = {false, 0.f, 0, 0, 0, 0};
+    int qrel = -1;  // Q buffer that a TMA store of ours may still be reading (warp-uniform)
+    // Lane 0 hands the buffer back to the producer once the store has read it.
+    auto release_q = [&]() {
+      if (qrel >= 0) {
+        if (lane == 0) {
+          bulk_wait_read_all();
+          mbar_arrive(&q_free[qrel]);
+        }
+        qrel = -1;
+      }
+    };
     auto epilogue = [&]() {
+      const int ob = pend.n & 1;
+      const uint32_t tO = tmem_base + TO_COL + ob * HD + lane_off;
       const float inv = pend.l > 0.f ? 1.f / pend.l : 0.f;
       uint32_t orr[2][32];
       tmem_ld32(tO, orr[0]);
@@ -309,22 +327,19 @@ __global__ void __launch_bounds__(192, 2)
       const int w0 = warp * 32;  // this warp's 32 rows of the tile
       if (use_tma_out && w0 + 32 <= pend.nq) {
         // stage the warp's 32 x 64 rows in the item's Q buffer (128B swizzle, the TMA
-        // layout) and write them with one TMA store; lane 0 hands its part of the buffer
-        // back to the producer once the store has read it
-        uint8_t* row = sQ + pend.qb * Q_BYTES + r * 128;
+        // layout) and write them with one TMA store; the buffer goes back to the producer
+        // one block later (release_q)
+        uint8_t* row = sQ + ob * Q_BYTES + r * 128;
 #pragma unroll
         for (int q = 0; q < 8; ++q)
           *reinterpret_cast<uint4*>(row + ((static_cast<uint32_t>(q) ^ (r & 7)) << 4)) = w[q];
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) {
-          if (!*abort_flag) {
-            tma_store_2d(&tmO, sQ + pend.qb * Q_BYTES + w0 * 128, pend.head * HD, pend.row0 + w0);
-            bulk_commit();
-            bulk_wait_read_all();
-          }
-          mbar_arrive(&q_free[pend.qb]);
+        if (lane == 0 && !*abort_flag) {
+          tma_store_2d(&tmO, sQ + ob * Q_BYTES + w0 * 128, pend.head * HD, pend.row0 + w0);
+          bulk_commit();
         }
+        qrel = ob;
       } else {  // rows past the tile's end (ragged tail) or no output map: plain stores
         if (r < pend.nq) {
           uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(pend.row0 + r) * ldo + pend.head * HD);
@@ -332,7 +347,7 @@ __global__ void __launch_bounds__(192, 2)
           for (int q = 0; q < 8; ++q) dst[q] = w[q];
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&q_free[pend.qb]);
+        if (lane == 0) mbar_arrive(&q_free[ob]);
       }
       pend.on = false;
     };
@@ -344,6 +359,7 @@ __global__ void __launch_bounds__(192, 2)
     for (uint32_t g = 0; c.u < items && ok; ++g) {
       const Item& it = c.it;
       if (c.j == 0) {
+        release_q();  // this item's S may need the Q buffer of that store (the item after next)
         const int qpos = it.tl.q_pos0 + r;
         klo = window >= 0 ? max(0, qpos - window) : 0;
         khi = window >= 0 ? min(it.tl.kv_len, qpos + window + 1) : it.tl.kv_len;
@@ -357,7 +373,7 @@ __global__ void __launch_bounds__(192, 2)
       const bool any = __any_sync(0xffffffffu, span > 0);
       const bool full = __all_sync(0xffffffffu, span == static_cast<unsigned>(KB));
       const uint32_t tS = tmem_base + TS_COL + (g & 1) * KB + lane_off;
-      const uint32_t tP = tmem_base + TP_COL + (g & 1) * (KB / 2) + lane_off;
+      const uint32_t tO = tmem_base + TO_COL + (c.n & 1) * HD + lane_off;
       if (!warp_wait(&s_full[g & 1], (g >> 1) & 1, abort_flag, err, 16)) {
         ok = false;
         break;
@@ -427,35 +443,34 @@ __global__ void __launch_bounds__(192, 2)
 #pragma unroll
         for (int i = 0; i < 32; ++i) pk[i] = 0u;
       }
-      // P buffer g&1 was last read by P(g-2).V(g-2)
-      if (g >= 2 && !warp_wait(&pv_done[g & 1], ((g - 2) >> 1) & 1, abort_flag, err, 17)) ok = false;
-      tc_fence_after();
-      tmem_st32(tP, pk);
+      release_q();  // the store issued during the previous block has had that block to read
+      // P(g) overwrites S(g) in place: this thread's scores are in registers, and the MMA
+      // issues nothing into these columns before P(g).V(g) has completed
+      tmem_st32(tS, pk);
       tmem_st_wait();
       if (!ok) break;
       l += lb;
-      if (pend.on) {  // previous item's O: final once o_full fires
-        if (!warp_wait(o_full, no & 1, abort_flag, err, 18)) {
-          ok = false;
-          break;
-        }
-        ++no;
-        tc_fence_after();
-        epilogue();
-      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[g & 1]);
-      if (c.j + 1 == it.nb) pend = {true, l, it.tl.q_row0, it.tl.nq, it.head, c.n & 1};
+      if (pend.on) {  // previous item's O: final once its o_full fires
+        if (!warp_wait(&o_full[pend.n & 1], (pend.n >> 1) & 1, abort_flag, err, 18)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        epilogue();
+      }
+      if (c.j + 1 == it.nb) pend = {true, l, it.tl.q_row0, it.tl.nq, it.head, c.n};
       cursor_next(c, tiles, ntiles, items, window);
     }
     if (ok && pend.on) {
-      if (warp_wait(o_full, no & 1, abort_flag, err, 18)) {
-        ++no;
+      if (warp_wait(&o_full[pend.n & 1], (pend.n >> 1) & 1, abort_flag, err, 18)) {
         tc_fence_after();
         epilogue();
       }
     }
+    release_q();
     if (lane == 0) bulk_wait_all();  // no store of ours may still read smem at exit
   }
 
