@@ -137,13 +137,12 @@ __global__ void __launch_bounds__(192, 2)
   uint8_t* sV = sK + NKV * KV_BYTES;  // NKV stages
   uint64_t* bars = reinterpret_cast<uint64_t*>(sV + NKV * KV_BYTES);
   uint64_t* kv_full = bars;           // [NKV]
-  uint64_t* kv_free = bars + NKV;     // [NKV]
+  uint64_t* pv_done = bars + NKV;     // [NKV] per K/V stage: P(g).V(g) done (stage g % NKV free)
   uint64_t* q_full = bars + 2 * NKV;  // [2] per Q buffer
   uint64_t* q_free = q_full + 2;      // [2] per Q buffer (one arrival per softmax warp)
   uint64_t* s_full = q_free + 2;      // [2] per S buffer: S(g) in TMEM
   uint64_t* p_full = s_full + 2;      // [2] per P buffer: P(g) in TMEM and S(g) read (4 arrivals)
-  uint64_t* pv_done = p_full + 2;     // [2] per S buffer: P(g).V(g) done
-  uint64_t* o_full = pv_done + 2;     // [2] per O buffer: last P.V of an item done
+  uint64_t* o_full = p_full + 2;      // [2] per O buffer: last P.V of an item done
   uint64_t* drain = o_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -160,14 +159,13 @@ __global__ void __launch_bounds__(192, 2)
   if (threadIdx.x == 0) {
     for (int i = 0; i < NKV; ++i) {
       mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_free[i], 1);
+      mbar_init(&pv_done[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&q_full[i], 1);
       mbar_init(&q_free[i], 4);
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 4);
-      mbar_init(&pv_done[i], 1);
       mbar_init(&o_full[i], 1);
     }
     mbar_init(drain, 1);
@@ -200,7 +198,7 @@ __global__ void __launch_bounds__(192, 2)
         armed_q[qb] = 1 + ((n >> 1) & 1);
         for (int j = 0; j < it.nb; ++j, ++g) {
           const uint32_t st = g % NKV;
-          if (g >= NKV && !mbar_wait(&kv_free[st], ((g - NKV) / NKV) & 1, abort_flag, err, 11)) {
+          if (g >= NKV && !mbar_wait(&pv_done[st], ((g - NKV) / NKV) & 1, abort_flag, err, 11)) {
             ok = false;
             break;
           }
@@ -264,13 +262,12 @@ __global__ void __launch_bounds__(192, 2)
         for (int k = 0; k < KB / 16; ++k)
           umma_bf16_ts(tmem_base + TO_COL + ob * HD, tmem_base + TS_COL + (g & 1) * KB + k * 8,
                        sdesc_sw128(vb0 + k * 2048, 8192, 1024), idO, (k > 0 || cp.j > 0) ? 1u : 0u);
-        umma_commit(&kv_free[g % NKV]);
-        umma_commit(&pv_done[g & 1]);
+        umma_commit(&pv_done[g % NKV]);  // frees K/V stage g % NKV and S buffer g & 1
         if (cp.j + 1 == cp.it.nb) umma_commit(&o_full[ob]);  // O of the item is final
         cursor_next(cp, tiles, ntiles, items, window);
         if (cs.u < items) {
           // S(g+2) goes into the columns that hold P(g): P(g).V(g) must have read them
-          if (!mbar_wait(&pv_done[g & 1], (g >> 1) & 1, abort_flag, err, 19)) break;
+          if (!mbar_wait(&pv_done[g % NKV], (g / NKV) & 1, abort_flag, err, 19)) break;
           tc_fence_after();
           ok = issue_s(cs, gs);
           cursor_next(cs, tiles, ntiles, items, window);
@@ -405,7 +402,7 @@ __global__ void __launch_bounds__(192, 2)
         if (__any_sync(0xffffffffu, rescale)) {
           // O must be stable first: every P.V of this item issued so far has completed
           // (m_used is finite only after a block of this item, so g >= 1 here)
-          if (!warp_wait(&pv_done[(g - 1) & 1], ((g - 1) >> 1) & 1, abort_flag, err, 15)) ok = false;
+          if (!warp_wait(&pv_done[(g - 1) % NKV], ((g - 1) / NKV) & 1, abort_flag, err, 15)) ok = false;
           tc_fence_after();
           const float alpha = rescale ? ex2(m_used - bmax) : 1.f;
 #pragma unroll 1
