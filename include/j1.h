@@ -170,6 +170,93 @@ J1_API j1_status j1_plan_batches(size_t n_rows, const uint32_t* row_lens, int32_
                                  int32_t n_devices, uint32_t* batch_of_row, uint32_t* device_of_batch,
                                  size_t* n_batches);
 
+/* The engine's row limit (EngineOptions::max_length, or the checkpoint's max_position_embeddings). */
+J1_API int32_t j1_engine_max_length(const j1_engine* engine);
+
+/* ------------------------------------------------------------ requests below the tokenizer
+ * The reference turns a Request (state, question, options, qtype; src/request.rs:77-82) into
+ * model rows with Encoder::sequence (src/encode.rs:138-195). Text -> token ids is the
+ * caller's part (the checkpoint's tokenizer.json), using the reference's text forms:
+ *   head_ids    tokens of "<choice|score|noul> question: <question>"     (encode.rs:146)
+ *   option k    tokens of " <option k>"                                   (encode.rs:147)
+ *   state_ids   tokens of the rendered state (State::render)              (encode.rs:180)
+ * each with the mask token's text replaced by a space first (encode.rs:145); a mask id in
+ * the tokens is refused ("Reserved model marker in request" in strict mode). */
+typedef struct j1_encoder_options {
+  uint32_t cls_id, sep_id, mask_id; /* tokenizer_config.json cls/sep/mask tokens (encode.rs:74-85) */
+  int32_t max_length;               /* tokens per row; 0 = the engine's max_length (engine calls only) */
+  int32_t head_length;              /* question + options budget, default 256 (engine.rs:55) */
+  int32_t strict;                   /* strict_encoding: refuse instead of truncating */
+} j1_encoder_options;
+
+typedef struct j1_tokenized_request {
+  const uint32_t* head_ids;
+  size_t head_len;
+  const uint32_t* option_ids;  /* all options' tokens, concatenated */
+  const uint32_t* option_lens; /* tokens per option [n_options] */
+  size_t n_options;
+  const uint32_t* state_ids;
+  size_t state_len;
+  uint8_t qtype; /* QType: 0 choice, 1 score, 2 noul */
+} j1_tokenized_request;
+
+J1_API void j1_encoder_options_default(j1_encoder_options* out);
+/* Encoder::sequence on ids: [CLS] head [SEP] ([MASK] option)... [SEP] state [SEP]; options cut
+ * to 48 tokens, the head to its budget, the state to the room left. Writes the row
+ * (ids_cap >= max_length), each option's marker position (markers_out[n_options]) and
+ * whether the state was cut. Strict mode returns the reference's refusals instead. */
+J1_API j1_status j1_encode_sequence(const j1_encoder_options* opts, const j1_tokenized_request* req,
+                                    uint32_t* ids_out, size_t ids_cap, size_t* ids_len, uint32_t* markers_out,
+                                    int32_t* truncated);
+/* Engine::logits (src/engine.rs:236-243) on tokenized requests: Request::validate for every
+ * row (2-20 options; noul = 2), encode, logits_encoded. logits_out: sum(n_options) floats. */
+J1_API j1_status j1_engine_logits_tokenized(j1_engine* engine, const j1_encoder_options* opts, size_t n_rows,
+                                            const j1_tokenized_request* rows, float* logits_out);
+
+/* ------------------------------------------------------------ router
+ * Router (src/router.rs): up to `width` options, one model row; larger choice requests keep
+ * `survivors` per group of `width` (one if its local softmax is confident) and rerank until
+ * one group remains; all groups of all requests of a call are scored together, identical
+ * jobs once, and an optional LRU cache (cache_size entries) keeps logits across calls. */
+typedef struct j1_router j1_router;
+typedef struct j1_router_options {
+  int32_t width;       /* 2..20, default 20 */
+  int32_t survivors;   /* 1..width-1, default 2 */
+  int32_t batch_size;  /* accepted for the reference's signature; a round's jobs go to the engine together */
+  int32_t cache_size;  /* 0 = no cache */
+  int32_t max_options; /* default 4096 */
+} j1_router_options;
+
+/* RouteResult (src/router.rs:15-26); candidates/probabilities hold n_candidates (<= width)
+ * entries. probability_scope is "final_candidates" when hierarchical, else "all_options". */
+typedef struct j1_route_result {
+  uint32_t index;            /* chosen option, index into the request's options */
+  uint32_t n_candidates;     /* options of the final group */
+  uint32_t candidates[20];   /* in the order the final group was scored */
+  double probabilities[20];  /* display_probabilities of the final group's softmax */
+  uint32_t rounds;
+  int32_t hierarchical;      /* more than width options */
+} j1_route_result;
+
+/* Scores encoded rows (layout of j1_engine_logits_encoded); returns 0 on success. */
+typedef int (*j1_scorer_fn)(void* user, size_t n_rows, const uint32_t* ids, const uint32_t* row_lens,
+                            const uint32_t* markers, const uint32_t* row_markers, const uint8_t* qtypes,
+                            float* logits_out);
+
+J1_API void j1_router_options_default(j1_router_options* out);
+/* Router::new over an engine (the engine must outlive the router). */
+J1_API j1_status j1_router_create(j1_engine* engine, const j1_encoder_options* enc, const j1_router_options* opts,
+                                  j1_router** out);
+/* The same router over a caller's scorer (e.g. another backend, or a test double). */
+J1_API j1_status j1_router_create_with_scorer(j1_scorer_fn fn, void* user, const j1_encoder_options* enc,
+                                              const j1_router_options* opts, j1_router** out);
+J1_API void j1_router_destroy(j1_router* router);
+J1_API void j1_router_clear_cache(j1_router* router);
+/* Router::route_many: results[n] in request order; model_rows and cache_hits are the call's
+ * totals (RouteResult::model_rows / cache_hits). */
+J1_API j1_status j1_router_route_many(j1_router* router, size_t n, const j1_tokenized_request* rows,
+                                      j1_route_result* results, uint64_t* model_rows, uint64_t* cache_hits);
+
 /* ------------------------------------------------------------ kernel-level ops
  * On caller device memory (e.g. torch tensors); `stream` is a cudaStream_t or NULL.
  * With sync != 0 the call waits for completion and reports device-side timeouts. */

@@ -239,6 +239,8 @@ j1_status j1_engine_logits_encoded(j1_engine* e, size_t n_rows, const uint32_t* 
   return J1_OK;
 }
 
+int32_t j1_engine_max_length(const j1_engine* e) { return e ? e->max_length : 0; }
+
 j1_status j1_plan_batches(size_t n_rows, const uint32_t* row_lens, int32_t batch_size, int64_t max_batch_tokens,
                           int32_t n_devices, uint32_t* batch_of_row, uint32_t* device_of_batch, size_t* n_batches) {
   if (!n_batches || (n_rows && (!row_lens || !batch_of_row || !device_of_batch)))

@@ -31,6 +31,9 @@ EXPORTS = [
     "j1_engine_device_name", "j1_engine_logits_encoded",
     "j1_op_gemm", "j1_op_attention", "j1_op_attention_noalloc", "j1_op_geglu_interleave",
     "j1_model_profile", "j1_model_profile_read", "j1_profile_family_name", "j1_plan_batches",
+    "j1_engine_max_length", "j1_encoder_options_default", "j1_encode_sequence", "j1_engine_logits_tokenized",
+    "j1_router_options_default", "j1_router_create", "j1_router_create_with_scorer", "j1_router_destroy",
+    "j1_router_clear_cache", "j1_router_route_many",
 ]
 PROF_FAMILIES = 12
 
@@ -69,6 +72,30 @@ class J1GemmArgs(C.Structure):
                 ("rope_cols", C.c_int32), ("w2", C.c_void_p), ("b2", C.c_float), ("scores", C.c_void_p),
                 ("grid_limit", C.c_int32)]
 
+
+class J1EncoderOptions(C.Structure):
+    _fields_ = [("cls_id", C.c_uint32), ("sep_id", C.c_uint32), ("mask_id", C.c_uint32), ("max_length", C.c_int32),
+                ("head_length", C.c_int32), ("strict", C.c_int32)]
+
+
+class J1TokenizedRequest(C.Structure):
+    _fields_ = [("head_ids", C.POINTER(C.c_uint32)), ("head_len", C.c_size_t),
+                ("option_ids", C.POINTER(C.c_uint32)), ("option_lens", C.POINTER(C.c_uint32)),
+                ("n_options", C.c_size_t), ("state_ids", C.POINTER(C.c_uint32)), ("state_len", C.c_size_t),
+                ("qtype", C.c_uint8)]
+
+
+class J1RouterOptions(C.Structure):
+    _fields_ = [(n, C.c_int32) for n in ("width", "survivors", "batch_size", "cache_size", "max_options")]
+
+
+class J1RouteResult(C.Structure):
+    _fields_ = [("index", C.c_uint32), ("n_candidates", C.c_uint32), ("candidates", C.c_uint32 * 20),
+                ("probabilities", C.c_double * 20), ("rounds", C.c_uint32), ("hierarchical", C.c_int32)]
+
+
+SCORER_FN = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_size_t, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32),
+                        C.POINTER(C.c_uint32), C.POINTER(C.c_uint32), C.POINTER(C.c_uint8), C.POINTER(C.c_float))
 
 _lib = None
 
@@ -121,6 +148,26 @@ def lib():
     L.j1_plan_batches.argtypes = [C.c_size_t, u32p, C.c_int32, C.c_int64, C.c_int32, u32p, u32p,
                                   C.POINTER(C.c_size_t)]
     L.j1_plan_batches.restype = C.c_int
+    L.j1_engine_max_length.argtypes = [C.c_void_p]
+    L.j1_engine_max_length.restype = C.c_int32
+    L.j1_encoder_options_default.argtypes = [C.POINTER(J1EncoderOptions)]
+    L.j1_encoder_options_default.restype = None
+    L.j1_encode_sequence.argtypes = [C.POINTER(J1EncoderOptions), C.POINTER(J1TokenizedRequest), u32p, C.c_size_t,
+                                     C.POINTER(C.c_size_t), u32p, C.POINTER(C.c_int32)]
+    L.j1_engine_logits_tokenized.argtypes = [C.c_void_p, C.POINTER(J1EncoderOptions), C.c_size_t,
+                                             C.POINTER(J1TokenizedRequest), f32p]
+    L.j1_router_options_default.argtypes = [C.POINTER(J1RouterOptions)]
+    L.j1_router_options_default.restype = None
+    L.j1_router_create.argtypes = [C.c_void_p, C.POINTER(J1EncoderOptions), C.POINTER(J1RouterOptions),
+                                   C.POINTER(C.c_void_p)]
+    L.j1_router_create_with_scorer.argtypes = [SCORER_FN, C.c_void_p, C.POINTER(J1EncoderOptions),
+                                               C.POINTER(J1RouterOptions), C.POINTER(C.c_void_p)]
+    L.j1_router_destroy.argtypes = [C.c_void_p]
+    L.j1_router_destroy.restype = None
+    L.j1_router_clear_cache.argtypes = [C.c_void_p]
+    L.j1_router_clear_cache.restype = None
+    L.j1_router_route_many.argtypes = [C.c_void_p, C.c_size_t, C.POINTER(J1TokenizedRequest),
+                                       C.POINTER(J1RouteResult), C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]
     L.j1_op_gemm.argtypes = [C.POINTER(J1GemmArgs), C.c_void_p, C.c_int]
     L.j1_op_attention.argtypes = [C.c_void_p, C.c_int64, C.c_int32, u32p, u32p, C.c_size_t, C.c_int32, C.c_void_p,
                                   C.c_void_p, C.c_int]
@@ -129,7 +176,9 @@ def lib():
     for fn in ("j1_config_load", "j1_model_create", "j1_model_config", "j1_model_forward", "j1_model_stage",
                "j1_model_launch", "j1_model_finish", "j1_engine_create", "j1_engine_create_pool",
                "j1_engine_logits_encoded", "j1_op_gemm", "j1_op_attention", "j1_op_attention_noalloc",
-               "j1_op_geglu_interleave", "j1_model_profile", "j1_model_profile_read"):
+               "j1_op_geglu_interleave", "j1_model_profile", "j1_model_profile_read", "j1_encode_sequence",
+               "j1_engine_logits_tokenized", "j1_router_create", "j1_router_create_with_scorer",
+               "j1_router_route_many"):
         getattr(L, fn).restype = C.c_int
     _lib = L
     return L
@@ -415,6 +464,182 @@ def plan_batches(row_lens, batch_size=16, max_batch_tokens=65536, n_devices=1):
     # rows inside a batch keep the length-sorted order of the plan
     batches = [sorted(b, key=lambda r: (int(lens[r]), r)) for b in batches]
     return batches, [int(d) for d in dob[:nb.value]]
+
+
+# ------------------------------------------------------------------ requests below the tokenizer, router
+@dataclass
+class EncoderOptions:
+    """Encoder settings (src/encode.rs:25-38) without the tokenizer: special token ids and budgets.
+    max_length 0 = the engine's max_length."""
+    cls_id: int
+    sep_id: int
+    mask_id: int
+    max_length: int = 0
+    head_length: int = 256
+    strict: bool = False
+
+    def c(self):
+        o = J1EncoderOptions()
+        lib().j1_encoder_options_default(C.byref(o))
+        o.cls_id, o.sep_id, o.mask_id = int(self.cls_id), int(self.sep_id), int(self.mask_id)
+        o.max_length, o.head_length, o.strict = int(self.max_length), int(self.head_length), int(bool(self.strict))
+        return o
+
+
+@dataclass
+class TokenizedRequest:
+    """A Request (src/request.rs:77-82) after tokenization: tokens of
+    "<qtype> question: <question>", of " <option>" per option, and of the rendered state."""
+    head: Sequence[int]
+    options: Sequence[Sequence[int]]
+    state: Sequence[int]
+    qtype: int = 0  # 0 choice, 1 score, 2 noul
+
+
+class _Requests:
+    """C views of a list of TokenizedRequest (keeps the arrays alive)."""
+
+    def __init__(self, rows: Sequence[TokenizedRequest]):
+        self.keep = []
+        self.arr = (J1TokenizedRequest * max(len(rows), 1))()
+        for i, r in enumerate(rows):
+            head = np.ascontiguousarray(np.asarray(r.head, np.uint32).reshape(-1))
+            state = np.ascontiguousarray(np.asarray(r.state, np.uint32).reshape(-1))
+            opts = [np.asarray(x, np.uint32).reshape(-1) for x in r.options]
+            oids = np.ascontiguousarray(np.concatenate(opts) if opts else np.zeros(0, np.uint32))
+            olens = np.ascontiguousarray(np.array([x.size for x in opts], np.uint32))
+            self.keep += [head, state, oids, olens]
+            P = C.POINTER(C.c_uint32)
+            self.arr[i] = J1TokenizedRequest(head.ctypes.data_as(P), head.size, oids.ctypes.data_as(P),
+                                             olens.ctypes.data_as(P), len(opts), state.ctypes.data_as(P),
+                                             state.size, int(r.qtype))
+
+
+def encode_sequence(req: TokenizedRequest, opts: EncoderOptions):
+    """Encoder::sequence (src/encode.rs:138-195) on ids -> (Encoded, truncated)."""
+    o = opts.c()
+    rq = _Requests([req])
+    cap = max(int(o.max_length), 1)
+    ids = np.zeros(cap, np.uint32)
+    mk = np.zeros(max(len(req.options), 1), np.uint32)
+    n, tr = C.c_size_t(), C.c_int32()
+    check(lib().j1_encode_sequence(C.byref(o), rq.arr, ids.ctypes.data_as(C.POINTER(C.c_uint32)), cap, C.byref(n),
+                                   mk.ctypes.data_as(C.POINTER(C.c_uint32)), C.byref(tr)))
+    return Encoded(ids[:n.value].copy(), mk[:len(req.options)].copy(), int(req.qtype)), bool(tr.value)
+
+
+def _engine_logits_tokenized(self, rows: Sequence[TokenizedRequest], enc: EncoderOptions) -> List[List[float]]:
+    """Engine::logits (src/engine.rs:236-243) on tokenized requests."""
+    if len(rows) == 0:
+        return []
+    rq = _Requests(rows)
+    o = enc.c()
+    out = np.zeros(sum(len(r.options) for r in rows), np.float32)
+    check(lib().j1_engine_logits_tokenized(self._h, C.byref(o), len(rows), rq.arr,
+                                           out.ctypes.data_as(C.POINTER(C.c_float))))
+    res, k = [], 0
+    for r in rows:
+        res.append(list(map(float, out[k:k + len(r.options)])))
+        k += len(r.options)
+    return res
+
+
+Engine.logits_tokenized = _engine_logits_tokenized
+
+
+@dataclass
+class RouteResult:
+    """RouteResult (src/router.rs:15-26)."""
+    index: int
+    candidates: List[int]
+    probabilities: List[float]
+    rounds: int
+    model_rows: int
+    cache_hits: int
+    hierarchical: bool
+    probability_scope: str
+
+
+class Router:
+    """Router (src/router.rs) over an Engine, or over `scorer(rows) -> logits` where rows are
+    Encoded (ids, markers, qtype) and logits one list of floats per row (e.g. a test double)."""
+
+    def __init__(self, engine: Optional[Engine] = None, encoder: Optional[EncoderOptions] = None, scorer=None,
+                 width=20, survivors=2, batch_size=16, cache_size=0, max_options=4096):
+        if encoder is None:
+            raise J1Error(INVALID_ARG, "encoder options (special token ids) are required")
+        ro = J1RouterOptions()
+        lib().j1_router_options_default(C.byref(ro))
+        ro.width, ro.survivors, ro.batch_size = int(width), int(survivors), int(batch_size)
+        ro.cache_size, ro.max_options = int(cache_size), int(max_options)
+        eo = encoder.c()
+        h = C.c_void_p()
+        self._engine, self._cb = engine, None
+        if engine is not None:
+            check(lib().j1_router_create(engine._h, C.byref(eo), C.byref(ro), C.byref(h)))
+        elif scorer is not None:
+            def cb(user, n, ids, lens, markers, nmark, qtypes, out):
+                try:
+                    ln = np.ctypeslib.as_array(lens, (n,)).copy()
+                    nm = np.ctypeslib.as_array(nmark, (n,)).copy()
+                    ii = np.ctypeslib.as_array(ids, (int(ln.sum()),)) if ln.sum() else np.zeros(0, np.uint32)
+                    mm = np.ctypeslib.as_array(markers, (int(nm.sum()),)) if nm.sum() else np.zeros(0, np.uint32)
+                    qq = np.ctypeslib.as_array(qtypes, (n,))
+                    rows, t, k = [], 0, 0
+                    for r in range(n):
+                        rows.append(Encoded(ii[t:t + ln[r]].copy(), mm[k:k + nm[r]].copy(), int(qq[r])))
+                        t += int(ln[r])
+                        k += int(nm[r])
+                    z = scorer(rows)
+                    flat = np.concatenate([np.asarray(x, np.float32) for x in z]) if len(z) else np.zeros(0, np.float32)
+                    if flat.size != int(nm.sum()):
+                        return 2
+                    dst = np.ctypeslib.as_array(out, (flat.size,)) if flat.size else None
+                    if dst is not None:
+                        dst[:] = flat
+                    return 0
+                except Exception:
+                    return 1
+            self._cb = SCORER_FN(cb)
+            check(lib().j1_router_create_with_scorer(self._cb, None, C.byref(eo), C.byref(ro), C.byref(h)))
+        else:
+            raise J1Error(INVALID_ARG, "Router needs an engine or a scorer")
+        self._h = h
+        self.width, self.survivors, self.batch_size = int(width), int(survivors), int(batch_size)
+        self.cache_size, self.max_options = int(cache_size), int(max_options)
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().j1_router_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def clear_cache(self):
+        lib().j1_router_clear_cache(self._h)
+
+    def route_many(self, rows: Sequence[TokenizedRequest]) -> List[RouteResult]:
+        """Router::route_many: batch independent groups across requests; request order kept."""
+        rq = _Requests(rows)
+        res = (J1RouteResult * max(len(rows), 1))()
+        mr, ch = C.c_uint64(), C.c_uint64()
+        check(lib().j1_router_route_many(self._h, len(rows), rq.arr, res, C.byref(mr), C.byref(ch)))
+        out = []
+        for i in range(len(rows)):
+            r = res[i]
+            n = int(r.n_candidates)
+            hier = bool(r.hierarchical)
+            out.append(RouteResult(int(r.index), [int(r.candidates[k]) for k in range(n)],
+                                   [float(r.probabilities[k]) for k in range(n)], int(r.rounds), int(mr.value),
+                                   int(ch.value), hier, "final_candidates" if hier else "all_options"))
+        return out
+
+    def route(self, row: TokenizedRequest) -> RouteResult:
+        return self.route_many([row])[0]
 
 
 # ------------------------------------------------------------------ kernel-level ops (torch tensors)

@@ -1,0 +1,81 @@
+"""Tokenized requests and the router over the CUDA engine (B200).
+
+* Engine::logits on tokenized requests (j1_engine_logits_tokenized) gives exactly the
+  logits of j1_engine_logits_encoded on the rows the reference encoder builds
+  (oracle/router_ref.py restating src/encode.rs:138-195).
+* The router over the engine (j1_router_create) routes exactly like the restated
+  Router::route_many (src/router.rs:143-210) whose model is the same engine called
+  batch_size rows at a time, as the reference does: the library scores a round's jobs in
+  one call, which gives the same logits because a row's forward does not depend on the
+  other rows of its batch.
+"""
+import numpy as np
+import pytest
+
+import julia1 as j1
+from julia1 import synthetic
+from oracle import router_ref as R
+
+pytestmark = pytest.mark.gpu
+
+CLS, SEP, MASK = 1, 2, 4
+ENC = j1.EncoderOptions(cls_id=CLS, sep_id=SEP, mask_id=MASK, max_length=512, head_length=256)
+REF_ENC = R.EncOpts(CLS, SEP, MASK, 512, 256)
+
+
+def rand_request(rng, n_opt, head=(8, 24), opt=(4, 14), state=(50, 400), qtype=0):
+    tok = lambda n: rng.integers(5, 50000, size=int(n)).tolist()  # noqa: E731
+    return j1.TokenizedRequest(tok(rng.integers(*head)), [tok(rng.integers(*opt)) for _ in range(n_opt)],
+                               tok(rng.integers(*state)), qtype)
+
+
+def to_ref(r):
+    return R.Req(list(map(int, r.head)), [list(map(int, x)) for x in r.options], list(map(int, r.state)),
+                 int(r.qtype))
+
+
+@pytest.fixture(scope="module")
+def engine(torch_cuda):
+    ck = synthetic.cached_checkpoint(seed=0, perturb=True)
+    e = j1.Engine.load(ck, j1.EngineOptions(device="cuda", batch_size=64, max_batch_tokens=65536, max_length=512))
+    yield e
+    e.close()
+
+
+def test_logits_tokenized_equal_encoded(engine):
+    rng = np.random.default_rng(21)
+    rows = [rand_request(rng, int(rng.integers(2, 21)), qtype=int(rng.integers(0, 2))) for _ in range(40)]
+    rows.append(rand_request(rng, 2, qtype=2))
+    got = engine.logits_tokenized(rows, ENC)
+    enc = []
+    for r in rows:
+        ids, mk, _ = R.encode_sequence(REF_ENC, to_ref(r))
+        enc.append(j1.Encoded(np.array(ids, np.uint32), np.array(mk, np.uint32), int(r.qtype)))
+    want = engine.logits_encoded(enc)
+    assert got == want  # bitwise
+    with pytest.raises(j1.J1Error, match="JSONL line 1: options must contain 2–20"):
+        engine.logits_tokenized([rand_request(rng, 21)], ENC)
+
+
+def test_router_over_engine_matches_reference(engine):
+    rng = np.random.default_rng(22)
+    rows = [rand_request(rng, int(n)) for n in rng.choice([2, 7, 20, 21, 45, 100], size=24)]
+    rows.append(rows[5])
+
+    def model(reqs):  # the reference's Engine::logits on one chunk of batch_size jobs
+        enc = []
+        for q in reqs:
+            ids, mk, _ = R.encode_sequence(REF_ENC, q)
+            enc.append(j1.Encoded(np.array(ids, np.uint32), np.array(mk, np.uint32), int(q.qtype)))
+        return engine.logits_encoded(enc)
+
+    want, want_rows, want_hits = R.Router(model, width=20, survivors=2, batch_size=16).route_many(
+        [to_ref(r) for r in rows])
+    router = j1.Router(engine=engine, encoder=ENC, width=20, survivors=2, batch_size=16)
+    got = router.route_many(rows)
+    router.close()
+    for g, w in zip(got, want):
+        assert (g.index, g.candidates, g.rounds, g.hierarchical) == (w.index, w.candidates, w.rounds, w.hierarchical)
+        np.testing.assert_allclose(g.probabilities, w.probabilities, rtol=0, atol=1e-12)
+        assert (g.model_rows, g.cache_hits) == (want_rows, want_hits)
+    assert any(g.hierarchical for g in got) and any(not g.hierarchical for g in got)
