@@ -222,7 +222,8 @@ typedef struct j1_router j1_router;
 typedef struct j1_router_options {
   int32_t width;       /* 2..20, default 20 */
   int32_t survivors;   /* 1..width-1, default 2 */
-  int32_t batch_size;  /* accepted for the reference's signature; a round's jobs go to the engine together */
+  int32_t batch_size;  /* model rows per engine call, default 16 (the logits do not depend on it; raise it,
+                          e.g. to 4096, to let the engine cut full micro-batches) */
   int32_t cache_size;  /* 0 = no cache */
   int32_t max_options; /* default 4096 */
 } j1_router_options;
@@ -244,6 +245,11 @@ typedef int (*j1_scorer_fn)(void* user, size_t n_rows, const uint32_t* ids, cons
                             float* logits_out);
 
 J1_API void j1_router_options_default(j1_router_options* out);
+/* display_probabilities (src/request.rs:150-161): model-card rounding of probabilities. */
+J1_API void j1_display_probabilities(const double* values, size_t n, double* out);
+/* Router::confident_winner (src/router.rs:127-136): 1 when the group's local softmax keeps
+ * only `best`. */
+J1_API int32_t j1_router_confident_winner(const float* scores, size_t n, size_t best);
 /* Router::new over an engine (the engine must outlive the router). */
 J1_API j1_status j1_router_create(j1_engine* engine, const j1_encoder_options* enc, const j1_router_options* opts,
                                   j1_router** out);

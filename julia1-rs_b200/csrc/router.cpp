@@ -266,10 +266,9 @@ std::string job_key(const Job& j) {
 }
 
 // Router::score (src/router.rs:91-124): cache hits, de-duplication inside the call, then
-// one model row per distinct job. All distinct jobs of a round go to the engine in one
-// call (the reference sends them batch_size at a time): the forward of a row does not
-// depend on the other rows of its batch, so the logits are the same, and the engine's
-// own micro-batching fills the devices.
+// one model row per distinct job, batch_size rows per engine call. The logits do not
+// depend on batch_size (a row's forward does not depend on the other rows of its batch);
+// a large batch_size lets the engine cut full micro-batches for the devices.
 j1_status score(j1_router* R, const std::vector<Job>& jobs, std::vector<std::vector<float>>& values,
                 size_t& used, size_t& hits) {
   values.assign(jobs.size(), {});
@@ -296,23 +295,28 @@ j1_status score(j1_router* R, const std::vector<Job>& jobs, std::vector<std::vec
       missing.emplace_back(std::move(key), std::vector<size_t>{i});
     }
   }
-  EncodedRows rows;
-  for (const auto& ms : missing) {
-    const j1_tokenized_request v = jobs[ms.second[0]].view();
-    if (j1_status s = validate_request(v)) return s;
-    if (j1_status s = rows.add(R->enc, v)) return s;
-  }
-  std::vector<float> flat;
-  if (j1_status s = R->logits(rows, flat)) return s;
-  size_t o = 0;
-  for (size_t q = 0; q < missing.size(); ++q) {
-    const size_t n = rows.nmark[q];
-    std::vector<float> sc(flat.begin() + o, flat.begin() + o + n);
-    o += n;
-    for (float v : sc)
-      if (!std::isfinite(v)) return set_error(J1_ERR_NONFINITE, "Engine logits must be finite and match option count");
-    for (size_t i : missing[q].second) values[i] = sc;
-    R->cache_put(missing[q].first, sc);
+  const size_t chunk = static_cast<size_t>(R->opts.batch_size);
+  for (size_t c0 = 0; c0 < missing.size(); c0 += chunk) {
+    const size_t c1 = std::min(missing.size(), c0 + chunk);
+    EncodedRows rows;
+    for (size_t q = c0; q < c1; ++q) {
+      const j1_tokenized_request v = jobs[missing[q].second[0]].view();
+      if (j1_status s = validate_request(v)) return s;
+      if (j1_status s = rows.add(R->enc, v)) return s;
+    }
+    std::vector<float> flat;
+    if (j1_status s = R->logits(rows, flat)) return s;
+    size_t o = 0;
+    for (size_t q = c0; q < c1; ++q) {
+      const size_t n = rows.nmark[q - c0];
+      std::vector<float> sc(flat.begin() + o, flat.begin() + o + n);
+      o += n;
+      for (float v : sc)
+        if (!std::isfinite(v))
+          return set_error(J1_ERR_NONFINITE, "Engine logits must be finite and match option count");
+      for (size_t i : missing[q].second) values[i] = sc;
+      R->cache_put(missing[q].first, sc);
+    }
   }
   used = missing.size();
   return J1_OK;
@@ -407,6 +411,17 @@ j1_status j1_engine_logits_tokenized(j1_engine* engine, const j1_encoder_options
     if (j1_status s = enc.add(e, rows[i])) return s;
   return j1_engine_logits_encoded(engine, enc.n, enc.ids.data(), enc.lens.data(), enc.markers.data(),
                                   enc.nmark.data(), enc.qtypes.data(), logits_out);
+}
+
+void j1_display_probabilities(const double* values, size_t n, double* out) {
+  if (!values || !out) return;
+  const std::vector<double> p = display_probabilities(std::vector<double>(values, values + n));
+  std::copy(p.begin(), p.end(), out);
+}
+
+int32_t j1_router_confident_winner(const float* scores, size_t n, size_t best) {
+  if (!scores || best >= n) return 0;
+  return confident_winner(std::vector<float>(scores, scores + n), best) ? 1 : 0;
 }
 
 void j1_router_options_default(j1_router_options* o) {

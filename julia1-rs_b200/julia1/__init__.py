@@ -33,7 +33,7 @@ EXPORTS = [
     "j1_model_profile", "j1_model_profile_read", "j1_profile_family_name", "j1_plan_batches",
     "j1_engine_max_length", "j1_encoder_options_default", "j1_encode_sequence", "j1_engine_logits_tokenized",
     "j1_router_options_default", "j1_router_create", "j1_router_create_with_scorer", "j1_router_destroy",
-    "j1_router_clear_cache", "j1_router_route_many",
+    "j1_router_clear_cache", "j1_router_route_many", "j1_display_probabilities", "j1_router_confident_winner",
 ]
 PROF_FAMILIES = 12
 
@@ -162,6 +162,10 @@ def lib():
                                    C.POINTER(C.c_void_p)]
     L.j1_router_create_with_scorer.argtypes = [SCORER_FN, C.c_void_p, C.POINTER(J1EncoderOptions),
                                                C.POINTER(J1RouterOptions), C.POINTER(C.c_void_p)]
+    L.j1_display_probabilities.argtypes = [C.POINTER(C.c_double), C.c_size_t, C.POINTER(C.c_double)]
+    L.j1_display_probabilities.restype = None
+    L.j1_router_confident_winner.argtypes = [f32p, C.c_size_t, C.c_size_t]
+    L.j1_router_confident_winner.restype = C.c_int32
     L.j1_router_destroy.argtypes = [C.c_void_p]
     L.j1_router_destroy.restype = None
     L.j1_router_clear_cache.argtypes = [C.c_void_p]
@@ -547,6 +551,15 @@ def _engine_logits_tokenized(self, rows: Sequence[TokenizedRequest], enc: Encode
 Engine.logits_tokenized = _engine_logits_tokenized
 
 
+def display_probabilities(values: Sequence[float]) -> List[float]:
+    """display_probabilities (src/request.rs:150-161)."""
+    v = np.ascontiguousarray(np.asarray(values, np.float64))
+    out = np.zeros(v.size, np.float64)
+    lib().j1_display_probabilities(v.ctypes.data_as(C.POINTER(C.c_double)), v.size,
+                                   out.ctypes.data_as(C.POINTER(C.c_double)))
+    return out.tolist()
+
+
 @dataclass
 class RouteResult:
     """RouteResult (src/router.rs:15-26)."""
@@ -621,6 +634,12 @@ class Router:
 
     def clear_cache(self):
         lib().j1_router_clear_cache(self._h)
+
+    @staticmethod
+    def confident_winner(scores: Sequence[float], best: int) -> bool:
+        """Router::confident_winner (src/router.rs:127-136)."""
+        s = np.ascontiguousarray(np.asarray(scores, np.float32))
+        return bool(lib().j1_router_confident_winner(s.ctypes.data_as(C.POINTER(C.c_float)), s.size, int(best)))
 
     def route_many(self, rows: Sequence[TokenizedRequest]) -> List[RouteResult]:
         """Router::route_many: batch independent groups across requests; request order kept."""

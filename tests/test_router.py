@@ -226,3 +226,98 @@ def test_router_refusals():
     nan = j1.Router(encoder=enc, scorer=lambda rows: [[math.nan] * len(r.markers) for r in rows])
     with pytest.raises(j1.J1Error, match="finite"):
         nan.route_many([rand_request(rng, 3)])
+
+
+# ------------------------------------------------------------------ known answers of the reference's tests
+# tests/api.rs:139-215: the "Numeric" engine scores an option by its numeric label; here
+# option i is the single token LABEL0 + i and the scorer reads it back after each marker.
+LABEL0 = 1000
+
+
+def numeric_request(n, qtype=0):
+    return j1.TokenizedRequest([11, 12, 13], [[LABEL0 + i] for i in range(n)], [21, 22], qtype)
+
+
+class Numeric:
+    def __init__(self, scale):
+        self.scale, self.calls = scale, []
+
+    def lib(self, rows):  # encoded rows (library scorer callback)
+        self.calls.append([len(r.markers) for r in rows])
+        return [[np.float32(self.scale * float(int(r.ids[m + 1]) - LABEL0)) for m in r.markers] for r in rows]
+
+    def ref(self, reqs):  # requests (oracle router)
+        self.calls.append([len(q.options) for q in reqs])
+        return [[float(np.float32(self.scale * float(o[0] - LABEL0))) for o in q.options] for q in reqs]
+
+
+def both(scale, **kw):
+    a, b = Numeric(scale), Numeric(scale)
+    return (j1.Router(encoder=j1.EncoderOptions(**ENC), scorer=a.lib, **kw), a), (R.Router(b.ref, **kw), b)
+
+
+def test_reference_router_direct_and_hierarchical():
+    (lr, la), (rr, ra) = both(1.0, width=20, survivors=2, batch_size=3, cache_size=0, max_options=4096)
+    sizes = [2, 20, 21, 77, 4096]
+    got = lr.route_many([numeric_request(n) for n in sizes])
+    want, _, _ = rr.route_many([to_ref(numeric_request(n)) for n in sizes])
+    for res in (got, want):
+        assert [r.index for r in res] == [1, 19, 20, 76, 4095]
+        for r in res:
+            assert abs(sum(r.probabilities) - 1.0) < 1e-9 and r.index in r.candidates
+    assert got[0].probability_scope == "all_options" and got[4].probability_scope == "final_candidates"
+    for calls in (la.calls, ra.calls):  # every engine call holds at most batch_size rows of 2..20 options
+        assert all(len(c) <= 3 for c in calls) and all(2 <= n <= 20 for c in calls for n in c)
+    assert la.calls == ra.calls
+    assert lr.route_many([]) == []
+
+
+def test_reference_router_confident_group_shortcut():
+    for cw in (j1.Router.confident_winner, R.confident_winner):
+        assert cw([0.0, 4.0, -3.0], 1)
+        assert not cw([0.0, 3.0, -3.0], 1)
+    (lr, _), (rr, _) = both(10.0)
+    r = lr.route(numeric_request(2001))
+    assert (r.index, r.rounds, r.model_rows) == (2000, 3, 106)
+    w, rows, _ = rr.route_many([to_ref(numeric_request(2001))])
+    assert (w[0].index, w[0].rounds, rows) == (2000, 3, 106)
+
+
+def test_reference_router_cache_and_dedup():
+    (lr, _), (rr, _) = both(1.0, width=20, survivors=2, batch_size=16, cache_size=1, max_options=4096)
+    got = lr.route_many([numeric_request(5), numeric_request(5)])
+    assert (got[0].model_rows, got[0].cache_hits) == (1, 1)
+    assert lr.route(numeric_request(5)).model_rows == 0
+    lr.clear_cache()
+    assert lr.route(numeric_request(5)).model_rows == 1
+    lr.route(numeric_request(6))
+    assert lr.route(numeric_request(5)).model_rows == 1
+    # the restated router, same sequence
+    assert rr.route_many([to_ref(numeric_request(5))] * 2)[1:] == (1, 1)
+    assert rr.route_many([to_ref(numeric_request(5))])[1] == 0
+    rr.clear_cache()
+    assert rr.route_many([to_ref(numeric_request(5))])[1] == 1
+    rr.route_many([to_ref(numeric_request(6))])
+    assert rr.route_many([to_ref(numeric_request(5))])[1] == 1
+
+
+def test_reference_router_rejects_invalid_and_bad_engines():
+    (lr, _), (rr, _) = both(1.0)
+    for row in (numeric_request(1), numeric_request(30, qtype=1), numeric_request(3, qtype=2)):
+        with pytest.raises(j1.J1Error):
+            lr.route(row)
+        with pytest.raises(R.RefError):
+            rr.route_many([to_ref(row)])
+    fixed = j1.Router(encoder=j1.EncoderOptions(**ENC), scorer=lambda rows: [[0.0]] * len(rows))
+    with pytest.raises(j1.J1Error):
+        fixed.route(numeric_request(4))
+    assert R.argmax([3, 3, -1]) == 0
+
+
+def test_reference_display_probabilities():
+    for dp in (j1.display_probabilities, R.display_probabilities):
+        assert dp([0.955, 0.044, 0.001]) == [1.0, 0.0, 0.0]
+        assert dp([0.951, 0.049]) != [1.0, 0.0]
+        r = dp([0.6, 0.395, 0.005])
+        assert r[2] == 0.0 and abs(sum(r) - 1.0) < 1e-12 and abs(r[0] / r[1] - 0.6 / 0.395) < 1e-12
+        assert dp([]) == []

@@ -4,10 +4,10 @@
   logits of j1_engine_logits_encoded on the rows the reference encoder builds
   (oracle/router_ref.py restating src/encode.rs:138-195).
 * The router over the engine (j1_router_create) routes exactly like the restated
-  Router::route_many (src/router.rs:143-210) whose model is the same engine called
-  batch_size rows at a time, as the reference does: the library scores a round's jobs in
-  one call, which gives the same logits because a row's forward does not depend on the
-  other rows of its batch.
+  Router::route_many (src/router.rs:143-210) whose model is the same engine called 16
+  rows at a time (the reference's default batch_size), with the library router at
+  batch_size 16 and at 4096 (a whole round per engine call): a row's forward does not
+  depend on the other rows of its batch, so the logits and the routes are the same.
 """
 import numpy as np
 import pytest
@@ -71,11 +71,13 @@ def test_router_over_engine_matches_reference(engine):
 
     want, want_rows, want_hits = R.Router(model, width=20, survivors=2, batch_size=16).route_many(
         [to_ref(r) for r in rows])
-    router = j1.Router(engine=engine, encoder=ENC, width=20, survivors=2, batch_size=16)
-    got = router.route_many(rows)
-    router.close()
-    for g, w in zip(got, want):
-        assert (g.index, g.candidates, g.rounds, g.hierarchical) == (w.index, w.candidates, w.rounds, w.hierarchical)
-        np.testing.assert_allclose(g.probabilities, w.probabilities, rtol=0, atol=1e-12)
-        assert (g.model_rows, g.cache_hits) == (want_rows, want_hits)
-    assert any(g.hierarchical for g in got) and any(not g.hierarchical for g in got)
+    for bs in (16, 4096):
+        router = j1.Router(engine=engine, encoder=ENC, width=20, survivors=2, batch_size=bs)
+        got = router.route_many(rows)
+        router.close()
+        for g, w in zip(got, want):
+            assert (g.index, g.candidates, g.rounds, g.hierarchical) == \
+                (w.index, w.candidates, w.rounds, w.hierarchical)
+            np.testing.assert_allclose(g.probabilities, w.probabilities, rtol=0, atol=1e-12)
+            assert (g.model_rows, g.cache_hits) == (want_rows, want_hits)
+        assert any(g.hierarchical for g in got) and any(not g.hierarchical for g in got)
