@@ -263,6 +263,49 @@ J1_API void j1_router_clear_cache(j1_router* router);
 J1_API j1_status j1_router_route_many(j1_router* router, size_t n, const j1_tokenized_request* rows,
                                       j1_route_result* results, uint64_t* model_rows, uint64_t* cache_hits);
 
+/* ------------------------------------------------------------ text -> token ids
+ * The checkpoint's tokenizer.json (byte-level BPE, the HF `tokenizers` 0.22.2 format the
+ * reference loads with Tokenizer::from_bytes, src/encode.rs:55-101): added tokens, NFC
+ * normalizer, ByteLevel pre-tokenizer with the GPT-2 split, BPE merges. j1_tokenizer_encode
+ * returns the ids of Tokenizer::encode_fast(text, false) (src/encode.rs:114-129). Other
+ * normalizers / pre-tokenizers / models are refused at load (J1_ERR_UNSUPPORTED). */
+typedef struct j1_tokenizer j1_tokenizer;
+J1_API j1_status j1_tokenizer_load(const char* tokenizer_json_path, j1_tokenizer** out);
+J1_API j1_status j1_tokenizer_from_json(const char* json, size_t len, j1_tokenizer** out);
+J1_API void j1_tokenizer_destroy(j1_tokenizer* tok);
+/* Tokenizer::token_to_id; -1 when absent. */
+J1_API int64_t j1_tokenizer_token_to_id(const j1_tokenizer* tok, const char* token);
+/* UTF-8 text -> ids (cap entries; *n_ids is set even when cap is too small). */
+J1_API j1_status j1_tokenizer_encode(const j1_tokenizer* tok, const char* text, size_t len, uint32_t* ids, size_t cap,
+                                     size_t* n_ids);
+/* n texts on `threads` host threads; ids_out[i] must hold the ids of text i: call once with
+ * ids_out[i] = NULL to learn n_ids[i] (and the total), then with buffers. */
+J1_API j1_status j1_tokenizer_encode_batch(const j1_tokenizer* tok, size_t n, const char* const* texts,
+                                           const size_t* lens, int32_t threads, uint32_t** ids_out, size_t* n_ids,
+                                           size_t* total);
+
+/* Encoder (src/encode.rs:25-195) on text: Encoder::load(dir, max_length, head_length, strict,
+ * token_cache, encoding_cache) reads tokenizer.json and tokenizer_config.json (mask/cls/sep/pad
+ * tokens); encode builds one row from the rendered state, the question, the options and the
+ * qtype, with the reference's text forms, mask-token cleaning, strict refusals and LRU caches. */
+typedef struct j1_text_encoder j1_text_encoder;
+J1_API j1_status j1_text_encoder_load(const char* ckpt_dir, int32_t max_length, int32_t head_length, int32_t strict,
+                                      int64_t token_cache, int64_t encoding_cache, j1_text_encoder** out);
+J1_API void j1_text_encoder_destroy(j1_text_encoder* enc);
+J1_API void j1_text_encoder_clear_cache(j1_text_encoder* enc);
+/* The special ids and budgets in use (for j1_encode_sequence / j1_router_create). */
+J1_API j1_status j1_text_encoder_options(const j1_text_encoder* enc, j1_encoder_options* out);
+/* Encoder::tokenize: the token-fragment cache in front of the tokenizer. */
+J1_API j1_status j1_text_encoder_tokenize(j1_text_encoder* enc, const char* text, size_t len, uint32_t* ids,
+                                          size_t cap, size_t* n_ids);
+/* Encoder::encode: state (rendered; state_is_json only keys the cache like the reference),
+ * question, options[n_options] (UTF-8, NUL-terminated), qtype -> ids (cap >= max_length),
+ * markers[n_options], truncated. */
+J1_API j1_status j1_text_encoder_encode(j1_text_encoder* enc, const char* state, int32_t state_is_json,
+                                        const char* question, const char* const* options, size_t n_options,
+                                        uint8_t qtype, uint32_t* ids, size_t cap, size_t* ids_len, uint32_t* markers,
+                                        int32_t* truncated);
+
 /* ------------------------------------------------------------ kernel-level ops
  * On caller device memory (e.g. torch tensors); `stream` is a cudaStream_t or NULL.
  * With sync != 0 the call waits for completion and reports device-side timeouts. */

@@ -1,0 +1,922 @@
+// Text -> token ids for the checkpoint's tokenizer.json, and the text-level Encoder.
+//
+// The reference tokenizes with the HF `tokenizers` crate 0.22.2 (Cargo.lock), calling
+// `Tokenizer::encode_fast(text, false)` (src/encode.rs:114-129) on ModernBERT's byte-level
+// BPE tokenizer. This file restates the published algorithm of that pipeline for the
+// configurations that tokenizer.json family uses, and refuses anything else at load time:
+//   * added tokens (tokenizer.json "added_tokens"): leftmost-longest matches, first of the
+//     tokens with normalized=false on the raw text, then of the normalized=true tokens
+//     (matched in normalized form) on each remaining piece after normalisation; lstrip /
+//     rstrip widen a match over adjacent white space, single_word drops a match touching
+//     a word character; matched pieces map straight to their ids;
+//   * normalizer: none or NFC (Unicode canonical decomposition, canonical ordering,
+//     canonical composition; tables in unicode_tables.h);
+//   * pre_tokenizer ByteLevel: optional leading space per piece, the GPT-2 split
+//     's|'t|'re|'ve|'m|'ll|'d| ?\p{L}+| ?\p{N}+| ?[^\s\p{L}\p{N}]+|\s+(?!\S)|\s+, then
+//     every byte mapped to its printable stand-in (the GPT-2 byte <-> unicode table);
+//   * model BPE: merges applied lowest rank first (leftmost among equals), optional
+//     ignore_merges, no unk token, no dropout, no sub-word prefix/suffix.
+// On top of it, Encoder (src/encode.rs:25-137): tokenizer_config.json special tokens,
+// LRU caches of token fragments and of whole request encodings, the text forms of a
+// request, and Encoder::sequence (j1_encode_sequence).
+#include <algorithm>
+#include <atomic>
+#include <cstring>
+#include <fstream>
+#include <list>
+#include <memory>
+#include <mutex>
+#include <sstream>
+#include <string>
+#include <thread>
+#include <unordered_map>
+#include <vector>
+
+#include "json.h"
+#include "model.h"
+#include "unicode_tables.h"
+
+using namespace j1rt;
+
+namespace {
+
+// ------------------------------------------------------------------ unicode
+template <size_t N>
+bool in_ranges(const uint32_t (&r)[N][2], uint32_t cp) {
+  size_t lo = 0, hi = N;
+  while (lo < hi) {
+    const size_t mid = (lo + hi) / 2;
+    if (cp < r[mid][0])
+      hi = mid;
+    else if (cp > r[mid][1])
+      lo = mid + 1;
+    else
+      return true;
+  }
+  return false;
+}
+bool is_letter(uint32_t c) {
+  if (c < 0x80) return (c | 0x20) >= 'a' && (c | 0x20) <= 'z';
+  return in_ranges(ucd::kLetter, c);
+}
+bool is_number(uint32_t c) {
+  if (c < 0x80) return c >= '0' && c <= '9';
+  return in_ranges(ucd::kNumber, c);
+}
+bool is_space(uint32_t c) {
+  if (c < 0x80) return c == ' ' || (c >= 0x9 && c <= 0xD);
+  return in_ranges(ucd::kWhiteSpace, c);
+}
+
+void utf8_decode(const std::string& s, std::vector<uint32_t>& cps, std::vector<uint32_t>* offs = nullptr) {
+  cps.clear();
+  if (offs) offs->clear();
+  const unsigned char* p = reinterpret_cast<const unsigned char*>(s.data());
+  const size_t n = s.size();
+  for (size_t i = 0; i < n;) {
+    uint32_t c = p[i];
+    size_t len = 1;
+    if (c >= 0xF0 && i + 3 < n) {
+      c = ((c & 0x07) << 18) | ((p[i + 1] & 0x3F) << 12) | ((p[i + 2] & 0x3F) << 6) | (p[i + 3] & 0x3F);
+      len = 4;
+    } else if (c >= 0xE0 && i + 2 < n) {
+      c = ((c & 0x0F) << 12) | ((p[i + 1] & 0x3F) << 6) | (p[i + 2] & 0x3F);
+      len = 3;
+    } else if (c >= 0xC0 && i + 1 < n) {
+      c = ((c & 0x1F) << 6) | (p[i + 1] & 0x3F);
+      len = 2;
+    }
+    if (offs) offs->push_back(static_cast<uint32_t>(i));
+    cps.push_back(c);
+    i += len;
+  }
+  if (offs) offs->push_back(static_cast<uint32_t>(n));
+}
+
+void utf8_append(std::string& s, uint32_t c) {
+  if (c < 0x80) {
+    s += static_cast<char>(c);
+  } else if (c < 0x800) {
+    s += static_cast<char>(0xC0 | (c >> 6));
+    s += static_cast<char>(0x80 | (c & 0x3F));
+  } else if (c < 0x10000) {
+    s += static_cast<char>(0xE0 | (c >> 12));
+    s += static_cast<char>(0x80 | ((c >> 6) & 0x3F));
+    s += static_cast<char>(0x80 | (c & 0x3F));
+  } else {
+    s += static_cast<char>(0xF0 | (c >> 18));
+    s += static_cast<char>(0x80 | ((c >> 12) & 0x3F));
+    s += static_cast<char>(0x80 | ((c >> 6) & 0x3F));
+    s += static_cast<char>(0x80 | (c & 0x3F));
+  }
+}
+
+bool valid_utf8(const std::string& s) {
+  const unsigned char* p = reinterpret_cast<const unsigned char*>(s.data());
+  const size_t n = s.size();
+  for (size_t i = 0; i < n;) {
+    const unsigned c = p[i];
+    size_t len = c < 0x80 ? 1 : (c >> 5) == 6 ? 2 : (c >> 4) == 14 ? 3 : (c >> 3) == 30 ? 4 : 0;
+    if (len == 0 || i + len > n) return false;
+    for (size_t k = 1; k < len; ++k)
+      if ((p[i + k] & 0xC0) != 0x80) return false;
+    i += len;
+  }
+  return true;
+}
+
+// Unicode canonical normalisation form C (UAX #15), for the NFC normalizer.
+struct Nfc {
+  std::unordered_map<uint32_t, uint8_t> ccc;
+  std::unordered_map<uint32_t, std::pair<uint32_t, uint32_t>> decomp;
+  std::unordered_map<uint64_t, uint32_t> comp;
+  Nfc() {
+    for (const auto& e : ucd::kCombining) ccc[e[0]] = static_cast<uint8_t>(e[1]);
+    for (const auto& e : ucd::kDecomposition) decomp[e[0]] = {e[1], e[2]};
+    for (const auto& e : ucd::kComposition) comp[(static_cast<uint64_t>(e[0]) << 32) | e[1]] = e[2];
+  }
+  static constexpr uint32_t SBase = 0xAC00, LBase = 0x1100, VBase = 0x1161, TBase = 0x11A7;
+  static constexpr uint32_t LCount = 19, VCount = 21, TCount = 28, NCount = VCount * TCount, SCount = LCount * NCount;
+  int cc(uint32_t c) const {
+    if (c < 0x300) return 0;
+    auto it = ccc.find(c);
+    return it == ccc.end() ? 0 : it->second;
+  }
+  void decompose(uint32_t c, std::vector<uint32_t>& out) const {
+    if (c >= SBase && c < SBase + SCount) {
+      const uint32_t s = c - SBase;
+      out.push_back(LBase + s / NCount);
+      out.push_back(VBase + (s % NCount) / TCount);
+      if (s % TCount) out.push_back(TBase + s % TCount);
+      return;
+    }
+    auto it = decomp.find(c);
+    if (it == decomp.end()) {
+      out.push_back(c);
+      return;
+    }
+    decompose(it->second.first, out);
+    if (it->second.second) decompose(it->second.second, out);
+  }
+  uint32_t compose(uint32_t a, uint32_t b) const {
+    if (a >= LBase && a < LBase + LCount && b >= VBase && b < VBase + VCount)
+      return SBase + ((a - LBase) * VCount + (b - VBase)) * TCount;
+    if (a >= SBase && a < SBase + SCount && (a - SBase) % TCount == 0 && b > TBase && b < TBase + TCount)
+      return a + (b - TBase);
+    auto it = comp.find((static_cast<uint64_t>(a) << 32) | b);
+    return it == comp.end() ? 0 : it->second;
+  }
+  void normalize(std::string& s) const {
+    bool simple = true;
+    for (unsigned char ch : s)
+      if (ch >= 0xCC) {  // the lead bytes of every code point >= U+0300
+        simple = false;
+        break;
+      }
+    if (simple) return;  // below U+0300 every character is its own NFC
+    std::vector<uint32_t> cps, d;
+    utf8_decode(s, cps);
+    d.reserve(cps.size() + 8);
+    for (uint32_t c : cps) decompose(c, d);
+    // canonical ordering: stable sort of each run of non-starters by combining class
+    for (size_t i = 0; i < d.size();) {
+      if (cc(d[i]) == 0) {
+        ++i;
+        continue;
+      }
+      size_t j = i;
+      while (j < d.size() && cc(d[j]) != 0) ++j;
+      std::stable_sort(d.begin() + i, d.begin() + j, [&](uint32_t x, uint32_t y) { return cc(x) < cc(y); });
+      i = j;
+    }
+    // canonical composition
+    std::vector<uint32_t> out;
+    out.reserve(d.size());
+    long starter = -1;
+    int last_cc = -1;  // class of the last character kept after the starter; -1: none
+    for (uint32_t c : d) {
+      const int k = cc(c);
+      if (starter >= 0 && (last_cc == -1 || (last_cc != 0 && last_cc < k))) {
+        const uint32_t m = compose(out[starter], c);
+        if (m) {
+          out[starter] = m;
+          continue;
+        }
+      }
+      if (k == 0) {
+        starter = static_cast<long>(out.size());
+        last_cc = -1;
+      } else {
+        last_cc = k;
+      }
+      out.push_back(c);
+    }
+    s.clear();
+    for (uint32_t c : out) utf8_append(s, c);
+  }
+};
+
+const Nfc& nfc_tables() {
+  static const Nfc t;
+  return t;
+}
+
+// ------------------------------------------------------------------ LRU cache (lru::LruCache semantics)
+template <typename V>
+class Lru {
+ public:
+  explicit Lru(size_t cap) : cap_(cap) {}
+  bool get(const std::string& k, V& v) {
+    if (cap_ == 0) return false;
+    std::lock_guard<std::mutex> lk(mu_);
+    auto it = map_.find(k);
+    if (it == map_.end()) return false;
+    items_.splice(items_.begin(), items_, it->second);
+    v = it->second->second;
+    return true;
+  }
+  void put(const std::string& k, const V& v) {
+    if (cap_ == 0) return;
+    std::lock_guard<std::mutex> lk(mu_);
+    auto it = map_.find(k);
+    if (it != map_.end()) {
+      it->second->second = v;
+      items_.splice(items_.begin(), items_, it->second);
+      return;
+    }
+    if (items_.size() >= cap_) {
+      map_.erase(items_.back().first);
+      items_.pop_back();
+    }
+    items_.emplace_front(k, v);
+    map_[k] = items_.begin();
+  }
+  void clear() {
+    std::lock_guard<std::mutex> lk(mu_);
+    items_.clear();
+    map_.clear();
+  }
+
+ private:
+  size_t cap_;
+  std::mutex mu_;
+  std::list<std::pair<std::string, V>> items_;
+  std::unordered_map<std::string, typename std::list<std::pair<std::string, V>>::iterator> map_;
+};
+
+}  // namespace
+
+// ------------------------------------------------------------------ tokenizer
+namespace {
+std::atomic<uint64_t> g_tokenizer_generation{1};
+}
+
+struct j1_tokenizer {
+  const uint64_t generation = g_tokenizer_generation++;  // keys the per-thread BPE caches
+  struct Added {
+    std::string content, pattern;  // pattern: content, normalised for normalized tokens
+    uint32_t id;
+    bool single_word, lstrip, rstrip, normalized;
+  };
+  std::unordered_map<std::string, uint32_t> vocab;
+  std::unordered_map<uint64_t, std::pair<uint32_t, uint32_t>> merges;  // (a, b) -> (rank, merged id)
+  std::vector<Added> added;
+  std::vector<size_t> raw_by_byte[256], norm_by_byte[256];  // added tokens by first byte of their pattern
+  bool nfc = false, prefix_space = false, use_regex = true, ignore_merges = false, has_pre = false;
+  uint32_t byte_id[256];
+  bool byte_ok[256];
+  std::string byte_char[256];  // GPT-2 byte -> printable stand-in, UTF-8
+
+  // ---- added tokens
+  // One pass of leftmost-longest matching over `text` with the tokens of `by_byte`.
+  // Returns pieces: (token index or -1, byte range).
+  void split_added(const std::string& text, const std::vector<size_t> (&by_byte)[256],
+                   std::vector<std::pair<long, std::pair<size_t, size_t>>>& out) const {
+    out.clear();
+    size_t start_offset = 0;
+    const size_t n = text.size();
+    for (size_t pos = 0; pos < n;) {
+      const auto& cand = by_byte[static_cast<unsigned char>(text[pos])];
+      long best = -1;
+      size_t best_len = 0;
+      for (size_t a : cand) {
+        const std::string& pt = added[a].pattern;
+        if (pt.size() > best_len && pt.size() <= n - pos && std::memcmp(text.data() + pos, pt.data(), pt.size()) == 0) {
+          best = static_cast<long>(a);
+          best_len = pt.size();
+        }
+      }
+      if (best < 0) {
+        ++pos;
+        continue;
+      }
+      size_t start = pos, stop = pos + best_len;
+      pos = stop;  // the matcher resumes after this match even when it is dropped below
+      const Added& t = added[static_cast<size_t>(best)];
+      if (t.single_word) {
+        const bool start_space = start == 0 || !ends_with_word(text, start);
+        const bool stop_space = stop == n || !starts_with_word(text, stop);
+        if (!start_space || !stop_space) continue;
+      }
+      if (t.lstrip) start = std::max(space_leftmost_at_end(text, start), start_offset);
+      if (t.rstrip) stop += space_rightmost_at_start(text, stop);
+      if (start_offset < start) out.push_back({-1, {start_offset, start}});
+      out.push_back({best, {start, stop}});
+      start_offset = stop;
+    }
+    if (start_offset < n) out.push_back({-1, {start_offset, n}});
+  }
+  // regex \w (word characters for single_word tokens)
+  static bool word_char(uint32_t c) {
+    if (c < 0x80) return c == '_' || (c >= '0' && c <= '9') || ((c | 0x20) >= 'a' && (c | 0x20) <= 'z');
+    return in_ranges(ucd::kWord, c);
+  }
+  static uint32_t last_cp(const std::string& s, size_t end) {
+    size_t i = end;
+    while (i > 0 && (static_cast<unsigned char>(s[i - 1]) & 0xC0) == 0x80) --i;
+    if (i > 0) --i;
+    std::vector<uint32_t> c;
+    utf8_decode(s.substr(i, end - i), c);
+    return c.empty() ? 0 : c.back();
+  }
+  static uint32_t first_cp(const std::string& s, size_t start, size_t* len) {
+    const unsigned char c = static_cast<unsigned char>(s[start]);
+    const size_t l = c < 0x80 ? 1 : (c >> 5) == 6 ? 2 : (c >> 4) == 14 ? 3 : 4;
+    std::vector<uint32_t> cp;
+    utf8_decode(s.substr(start, std::min(l, s.size() - start)), cp);
+    if (len) *len = l;
+    return cp.empty() ? 0 : cp[0];
+  }
+  static bool ends_with_word(const std::string& s, size_t end) { return end > 0 && word_char(last_cp(s, end)); }
+  static bool starts_with_word(const std::string& s, size_t start) {
+    return start < s.size() && word_char(first_cp(s, start, nullptr));
+  }
+  // start of the white space that ends s[0, end)
+  static size_t space_leftmost_at_end(const std::string& s, size_t end) {
+    size_t i = end;
+    while (i > 0) {
+      size_t j = i;
+      while (j > 0 && (static_cast<unsigned char>(s[j - 1]) & 0xC0) == 0x80) --j;
+      --j;
+      size_t l = 0;
+      if (!is_space(first_cp(s, j, &l))) break;
+      i = j;
+    }
+    return i;
+  }
+  // bytes of white space at the start of s[start, ...)
+  static size_t space_rightmost_at_start(const std::string& s, size_t start) {
+    size_t i = start;
+    while (i < s.size()) {
+      size_t l = 0;
+      if (!is_space(first_cp(s, i, &l))) break;
+      i += l;
+    }
+    return i - start;
+  }
+
+  // ---- ByteLevel pre-tokenizer: the GPT-2 split of one piece (code point ranges)
+  static void gpt2_split(const std::vector<uint32_t>& c, std::vector<std::pair<size_t, size_t>>& out) {
+    out.clear();
+    const size_t n = c.size();
+    size_t i = 0;
+    auto run = [&](size_t j, auto pred) {
+      while (j < n && pred(c[j])) ++j;
+      return j;
+    };
+    auto other = [](uint32_t x) { return !is_space(x) && !is_letter(x) && !is_number(x); };
+    while (i < n) {
+      const uint32_t x = c[i];
+      if (x == '\'' && i + 1 < n) {  // 's 't 're 've 'm 'll 'd
+        const uint32_t a = c[i + 1], b = i + 2 < n ? c[i + 2] : 0;
+        size_t len = 0;
+        if (a == 's' || a == 't' || a == 'm' || a == 'd')
+          len = 2;
+        else if ((a == 'r' && b == 'e') || (a == 'v' && b == 'e') || (a == 'l' && b == 'l'))
+          len = 3;
+        if (len) {
+          out.push_back({i, i + len});
+          i += len;
+          continue;
+        }
+      }
+      const size_t k = (x == ' ' && i + 1 < n) ? i + 1 : i;  // optional leading space
+      if (is_letter(c[k]) && (k == i || x == ' ')) {
+        const size_t j = run(k, is_letter);
+        out.push_back({i, j});
+        i = j;
+        continue;
+      }
+      if (is_number(c[k]) && (k == i || x == ' ')) {
+        const size_t j = run(k, is_number);
+        out.push_back({i, j});
+        i = j;
+        continue;
+      }
+      if (other(c[k]) && (k == i || x == ' ')) {
+        const size_t j = run(k, other);
+        out.push_back({i, j});
+        i = j;
+        continue;
+      }
+      // white space: \s+(?!\S) keeps the last space for the next token, else \s+
+      const size_t j = run(i, is_space);
+      if (j == n || j - i == 1) {
+        out.push_back({i, j});
+        i = j;
+      } else {
+        out.push_back({i, j - 1});
+        i = j - 1;
+      }
+    }
+  }
+
+  // ---- BPE on one pre-token (its UTF-8 bytes)
+  void bpe(const std::string& piece, std::vector<uint32_t>& ids) const {
+    if (ignore_merges) {
+      std::string mapped;
+      for (unsigned char b : piece) mapped += byte_char[b];
+      auto it = vocab.find(mapped);
+      if (it != vocab.end()) {
+        ids.push_back(it->second);
+        return;
+      }
+    }
+    // BPE results of whole pieces, per thread (no locking); a cache belongs to one tokenizer
+    thread_local std::unordered_map<std::string, std::vector<uint32_t>> word_cache;
+    thread_local uint64_t cache_owner = 0;
+    if (cache_owner != generation) {
+      word_cache.clear();
+      cache_owner = generation;
+    }
+    {
+      auto it = word_cache.find(piece);
+      if (it != word_cache.end()) {
+        ids.insert(ids.end(), it->second.begin(), it->second.end());
+        return;
+      }
+    }
+    std::vector<uint32_t> sym;
+    sym.reserve(piece.size());
+    for (unsigned char b : piece)
+      if (byte_ok[b]) sym.push_back(byte_id[b]);  // a byte missing from the vocab is dropped (no unk token)
+    while (sym.size() > 1) {
+      uint32_t best_rank = UINT32_MAX, best_id = 0;
+      size_t best_pos = 0;
+      for (size_t i = 0; i + 1 < sym.size(); ++i) {
+        auto it = merges.find((static_cast<uint64_t>(sym[i]) << 32) | sym[i + 1]);
+        if (it != merges.end() && it->second.first < best_rank) {
+          best_rank = it->second.first;
+          best_id = it->second.second;
+          best_pos = i;
+        }
+      }
+      if (best_rank == UINT32_MAX) break;
+      sym[best_pos] = best_id;
+      sym.erase(sym.begin() + static_cast<std::ptrdiff_t>(best_pos) + 1);
+    }
+    ids.insert(ids.end(), sym.begin(), sym.end());
+    if (word_cache.size() > 100000) word_cache.clear();
+    word_cache.emplace(piece, std::move(sym));
+  }
+
+  // pre-tokenize + BPE one normalised piece (no added tokens inside)
+  void encode_piece(std::string text, std::vector<uint32_t>& ids) const {
+    if (text.empty()) return;
+    if (prefix_space && text[0] != ' ') text.insert(text.begin(), ' ');
+    if (!use_regex) {
+      bpe(text, ids);
+      return;
+    }
+    std::vector<uint32_t> cps, offs;
+    utf8_decode(text, cps, &offs);
+    std::vector<std::pair<size_t, size_t>> parts;
+    gpt2_split(cps, parts);
+    for (const auto& pr : parts) bpe(text.substr(offs[pr.first], offs[pr.second] - offs[pr.first]), ids);
+  }
+
+  // Tokenizer::encode_fast(text, add_special_tokens = false)
+  void encode(const std::string& text, std::vector<uint32_t>& ids) const {
+    ids.clear();
+    std::vector<std::pair<long, std::pair<size_t, size_t>>> raw, nrm;
+    split_added(text, raw_by_byte, raw);
+    for (const auto& r : raw) {
+      if (r.first >= 0) {
+        ids.push_back(added[static_cast<size_t>(r.first)].id);
+        continue;
+      }
+      std::string piece = text.substr(r.second.first, r.second.second - r.second.first);
+      if (nfc) nfc_tables().normalize(piece);
+      split_added(piece, norm_by_byte, nrm);
+      for (const auto& q : nrm) {
+        if (q.first >= 0)
+          ids.push_back(added[static_cast<size_t>(q.first)].id);
+        else
+          encode_piece(piece.substr(q.second.first, q.second.second - q.second.first), ids);
+      }
+    }
+  }
+
+  bool token_to_id(const std::string& t, uint32_t& id) const {
+    for (const auto& a : added)
+      if (a.content == t) {
+        id = a.id;
+        return true;
+      }
+    auto it = vocab.find(t);
+    if (it == vocab.end()) return false;
+    id = it->second;
+    return true;
+  }
+};
+
+namespace {
+
+j1_status load_tokenizer(const std::string& text, std::unique_ptr<j1_tokenizer>& out) {
+  Json j;
+  std::string err;
+  if (!parse_json(text, j, err)) return set_error(J1_ERR_INVALID_ARG, "tokenizer.json: " + err);
+  auto T = std::make_unique<j1_tokenizer>();
+  const Json* model = j.get("model");
+  if (!model || !model->get("type") || model->get("type")->str != "BPE")
+    return set_error(J1_ERR_UNSUPPORTED, "tokenizer.json: only BPE models are supported");
+  auto flag = [](const Json* o, const char* k) {
+    const Json* v = o ? o->get(k) : nullptr;
+    return v && v->kind == Json::Bool && v->b;
+  };
+  auto nonempty = [](const Json* o, const char* k) {
+    const Json* v = o ? o->get(k) : nullptr;
+    return v && v->kind == Json::String && !v->str.empty();
+  };
+  if (flag(model, "byte_fallback") || nonempty(model, "continuing_subword_prefix") ||
+      nonempty(model, "end_of_word_suffix") || (model->get("dropout") && model->get("dropout")->kind != Json::Null) ||
+      (model->get("unk_token") && model->get("unk_token")->kind != Json::Null))
+    return set_error(J1_ERR_UNSUPPORTED,
+                     "tokenizer.json: BPE with byte_fallback, unk_token, dropout or sub-word affixes is not supported");
+  T->ignore_merges = flag(model, "ignore_merges");
+  const Json* vocab = model->get("vocab");
+  const Json* merges = model->get("merges");
+  if (!vocab || vocab->kind != Json::Object || !merges || merges->kind != Json::Array)
+    return set_error(J1_ERR_INVALID_ARG, "tokenizer.json: model.vocab / model.merges missing");
+  T->vocab.reserve(vocab->obj.size() * 2);
+  for (const auto& kv : vocab->obj) T->vocab[kv.first] = static_cast<uint32_t>(kv.second.num);
+  uint32_t rank = 0;
+  for (const Json& m : merges->arr) {
+    std::string a, b;
+    if (m.kind == Json::String) {
+      const size_t sp = m.str.find(' ');
+      if (sp == std::string::npos) return set_error(J1_ERR_INVALID_ARG, "tokenizer.json: bad merge " + m.str);
+      a = m.str.substr(0, sp);
+      b = m.str.substr(sp + 1);
+    } else if (m.kind == Json::Array && m.arr.size() == 2) {
+      a = m.arr[0].str;
+      b = m.arr[1].str;
+    } else {
+      return set_error(J1_ERR_INVALID_ARG, "tokenizer.json: bad merge entry");
+    }
+    auto ia = T->vocab.find(a), ib = T->vocab.find(b), ic = T->vocab.find(a + b);
+    if (ia == T->vocab.end() || ib == T->vocab.end() || ic == T->vocab.end())
+      return set_error(J1_ERR_INVALID_ARG, "tokenizer.json: merge of tokens outside the vocabulary: " + a + " " + b);
+    // a pair listed twice keeps its last rank (the reference collects the list into a map)
+    T->merges[(static_cast<uint64_t>(ia->second) << 32) | ib->second] = {rank, ic->second};
+    ++rank;
+  }
+  // normalizer
+  const Json* norm = j.get("normalizer");
+  if (norm && norm->kind != Json::Null) {
+    const Json* t = norm->get("type");
+    if (!t || t->str != "NFC") return set_error(J1_ERR_UNSUPPORTED, "tokenizer.json: only the NFC normalizer is supported");
+    T->nfc = true;
+  }
+  // pre-tokenizer
+  const Json* pre = j.get("pre_tokenizer");
+  if (!pre || pre->kind == Json::Null || !pre->get("type") || pre->get("type")->str != "ByteLevel")
+    return set_error(J1_ERR_UNSUPPORTED, "tokenizer.json: only the ByteLevel pre-tokenizer is supported");
+  T->prefix_space = flag(pre, "add_prefix_space");
+  T->use_regex = !pre->get("use_regex") || flag(pre, "use_regex");
+  // GPT-2 byte <-> printable character table
+  {
+    std::vector<int> bs;
+    for (int b = '!'; b <= '~'; ++b) bs.push_back(b);
+    for (int b = 0xA1; b <= 0xAC; ++b) bs.push_back(b);
+    for (int b = 0xAE; b <= 0xFF; ++b) bs.push_back(b);
+    std::vector<uint32_t> cs(bs.begin(), bs.end());
+    uint32_t extra = 0;
+    for (int b = 0; b < 256; ++b)
+      if (std::find(bs.begin(), bs.end(), b) == bs.end()) {
+        bs.push_back(b);
+        cs.push_back(256 + extra++);
+      }
+    for (size_t i = 0; i < bs.size(); ++i) {
+      std::string ch;
+      utf8_append(ch, cs[i]);
+      T->byte_char[bs[i]] = ch;
+    }
+    for (int b = 0; b < 256; ++b) {
+      auto it = T->vocab.find(T->byte_char[b]);
+      T->byte_ok[b] = it != T->vocab.end();
+      T->byte_id[b] = T->byte_ok[b] ? it->second : 0;
+    }
+  }
+  // added tokens
+  const Json* added = j.get("added_tokens");
+  if (added && added->kind == Json::Array) {
+    for (const Json& a : added->arr) {
+      j1_tokenizer::Added t;
+      const Json* c = a.get("content");
+      const Json* id = a.get("id");
+      if (!c || !id) return set_error(J1_ERR_INVALID_ARG, "tokenizer.json: added token without content/id");
+      t.content = c->str;
+      t.id = static_cast<uint32_t>(id->num);
+      t.single_word = flag(&a, "single_word");
+      t.lstrip = flag(&a, "lstrip");
+      t.rstrip = flag(&a, "rstrip");
+      t.normalized = flag(&a, "normalized");
+      t.pattern = t.content;
+      if (t.normalized && T->nfc) nfc_tables().normalize(t.pattern);
+      if (t.pattern.empty()) continue;
+      T->added.push_back(t);
+    }
+  }
+  for (size_t i = 0; i < T->added.size(); ++i) {
+    const unsigned char b0 = static_cast<unsigned char>(T->added[i].pattern[0]);
+    (T->added[i].normalized ? T->norm_by_byte : T->raw_by_byte)[b0].push_back(i);
+  }
+  out = std::move(T);
+  return J1_OK;
+}
+
+bool read_file(const std::string& path, std::string& out) {
+  std::ifstream f(path, std::ios::binary);
+  if (!f) return false;
+  std::ostringstream ss;
+  ss << f.rdbuf();
+  out = ss.str();
+  return true;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ text encoder
+struct j1_text_encoder {
+  std::unique_ptr<j1_tokenizer> tok;
+  std::string mask_token;
+  j1_encoder_options opts{};
+  std::unique_ptr<Lru<std::vector<uint32_t>>> tokens;
+  struct Enc {
+    std::vector<uint32_t> ids, markers;
+    int32_t truncated;
+  };
+  std::unique_ptr<Lru<Enc>> encodings;
+
+  // Encoder::tokenize (src/encode.rs:114-129), with the token-fragment cache
+  void tokenize(const std::string& text, std::vector<uint32_t>& ids) {
+    if (tokens->get(text, ids)) return;
+    tok->encode(text, ids);
+    tokens->put(text, ids);
+  }
+};
+
+namespace {
+
+std::string replace_all(const std::string& s, const std::string& from, const std::string& to) {
+  if (from.empty()) return s;
+  std::string out;
+  size_t i = 0;
+  for (;;) {
+    const size_t j = s.find(from, i);
+    if (j == std::string::npos) break;
+    out.append(s, i, j - i);
+    out += to;
+    i = j + from.size();
+  }
+  out.append(s, i, std::string::npos);
+  return out;
+}
+
+const char* qtype_name(uint8_t q) { return q == 0 ? "choice" : q == 1 ? "score" : "noul"; }
+
+}  // namespace
+
+extern "C" {
+
+j1_status j1_tokenizer_load(const char* path, j1_tokenizer** out) {
+  if (!path || !out) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+  *out = nullptr;
+  std::string text;
+  if (!read_file(path, text)) return set_error(J1_ERR_IO, std::string("cannot read ") + path);
+  std::unique_ptr<j1_tokenizer> t;
+  if (j1_status s = load_tokenizer(text, t)) return s;
+  *out = t.release();
+  return J1_OK;
+}
+
+j1_status j1_tokenizer_from_json(const char* json, size_t len, j1_tokenizer** out) {
+  if (!json || !out) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+  *out = nullptr;
+  std::unique_ptr<j1_tokenizer> t;
+  if (j1_status s = load_tokenizer(std::string(json, len), t)) return s;
+  *out = t.release();
+  return J1_OK;
+}
+
+void j1_tokenizer_destroy(j1_tokenizer* t) { delete t; }
+
+int64_t j1_tokenizer_token_to_id(const j1_tokenizer* t, const char* token) {
+  uint32_t id = 0;
+  if (!t || !token || !t->token_to_id(token, id)) return -1;
+  return id;
+}
+
+j1_status j1_tokenizer_encode(const j1_tokenizer* t, const char* text, size_t len, uint32_t* ids, size_t cap,
+                              size_t* n_ids) {
+  if (!t || (!text && len) || !n_ids) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+  const std::string s(text ? text : "", len);
+  if (!valid_utf8(s)) return set_error(J1_ERR_INVALID_ARG, "text is not valid UTF-8");
+  std::vector<uint32_t> v;
+  t->encode(s, v);
+  *n_ids = v.size();
+  if (v.size() > cap || (!ids && !v.empty()))
+    return set_error(J1_ERR_INVALID_ARG, "ids buffer too small (" + std::to_string(v.size()) + " needed)");
+  if (!v.empty()) std::memcpy(ids, v.data(), v.size() * 4);
+  return J1_OK;
+}
+
+j1_status j1_tokenizer_encode_batch(const j1_tokenizer* t, size_t n, const char* const* texts, const size_t* lens,
+                                    int32_t threads, uint32_t** ids_out, size_t* n_ids, size_t* total) {
+  if (!t || (n && (!texts || !lens || !ids_out || !n_ids))) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+  std::vector<std::vector<uint32_t>> res(n);
+  std::atomic<size_t> next{0};
+  std::atomic<int> bad{-1};
+  auto work = [&]() {
+    for (size_t i = next++; i < n; i = next++) {
+      const std::string s(texts[i] ? texts[i] : "", lens[i]);
+      if (!valid_utf8(s)) {
+        bad = static_cast<int>(i);
+        continue;
+      }
+      t->encode(s, res[i]);
+    }
+  };
+  const int nt = std::max(1, std::min<int>(threads > 0 ? threads : 1, static_cast<int>(std::max<size_t>(n, 1))));
+  if (nt == 1) {
+    work();
+  } else {
+    std::vector<std::thread> pool;
+    for (int k = 0; k < nt; ++k) pool.emplace_back(work);
+    for (auto& th : pool) th.join();
+  }
+  if (bad >= 0) return set_error(J1_ERR_INVALID_ARG, "text " + std::to_string(bad) + " is not valid UTF-8");
+  size_t sum = 0;
+  for (size_t i = 0; i < n; ++i) {
+    n_ids[i] = res[i].size();
+    sum += res[i].size();
+  }
+  if (total) *total = sum;
+  for (size_t i = 0; i < n; ++i)
+    if (ids_out[i] && !res[i].empty()) std::memcpy(ids_out[i], res[i].data(), res[i].size() * 4);
+  return J1_OK;
+}
+
+j1_status j1_text_encoder_load(const char* dir, int32_t max_length, int32_t head_length, int32_t strict,
+                               int64_t token_cache, int64_t encoding_cache, j1_text_encoder** out) {
+  if (!dir || !out) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+  *out = nullptr;
+  const std::string root(dir);
+  std::string tj, cj;
+  if (!read_file(root + "/tokenizer.json", tj)) return set_error(J1_ERR_IO, "cannot read " + root + "/tokenizer.json");
+  if (!read_file(root + "/tokenizer_config.json", cj))
+    return set_error(J1_ERR_IO, "cannot read " + root + "/tokenizer_config.json");
+  // Encoder::from_parts (src/encode.rs:55-101)
+  if (static_cast<int64_t>(head_length) + 4 >= max_length)
+    return set_error(J1_ERR_INVALID_ARG, "max_length must leave room beyond the question head");
+  auto E = std::make_unique<j1_text_encoder>();
+  if (j1_status s = load_tokenizer(tj, E->tok)) return s;
+  Json cfg;
+  std::string err;
+  if (!parse_json(cj, cfg, err)) return set_error(J1_ERR_INVALID_ARG, "tokenizer_config.json: " + err);
+  auto special = [&](const char* key, std::string& name, uint32_t& id) -> j1_status {
+    const Json* v = cfg.get(key);
+    if (!v || v->kind != Json::String) return set_error(J1_ERR_INVALID_ARG, std::string("tokenizer lacks ") + key);
+    name = v->str;
+    if (!E->tok->token_to_id(name, id))
+      return set_error(J1_ERR_INVALID_ARG, std::string("unknown ") + key + " " + name);
+    return J1_OK;
+  };
+  std::string unused;
+  j1_encoder_options& o = E->opts;
+  if (j1_status s = special("mask_token", E->mask_token, o.mask_id)) return s;
+  if (j1_status s = special("cls_token", unused, o.cls_id)) return s;
+  if (j1_status s = special("sep_token", unused, o.sep_id)) return s;
+  uint32_t pad = 0;
+  if (j1_status s = special("pad_token", unused, pad)) return s;
+  o.max_length = max_length;
+  o.head_length = head_length;
+  o.strict = strict ? 1 : 0;
+  E->tokens = std::make_unique<Lru<std::vector<uint32_t>>>(token_cache > 0 ? static_cast<size_t>(token_cache) : 0);
+  E->encodings = std::make_unique<Lru<j1_text_encoder::Enc>>(encoding_cache > 0 ? static_cast<size_t>(encoding_cache)
+                                                                                 : 0);
+  *out = E.release();
+  return J1_OK;
+}
+
+void j1_text_encoder_destroy(j1_text_encoder* e) { delete e; }
+
+void j1_text_encoder_clear_cache(j1_text_encoder* e) {
+  if (!e) return;
+  e->tokens->clear();
+  e->encodings->clear();
+}
+
+j1_status j1_text_encoder_options(const j1_text_encoder* e, j1_encoder_options* out) {
+  if (!e || !out) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+  *out = e->opts;
+  return J1_OK;
+}
+
+j1_status j1_text_encoder_tokenize(j1_text_encoder* e, const char* text, size_t len, uint32_t* ids, size_t cap,
+                                   size_t* n_ids) {
+  if (!e || (!text && len) || !n_ids) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+  const std::string s(text ? text : "", len);
+  if (!valid_utf8(s)) return set_error(J1_ERR_INVALID_ARG, "text is not valid UTF-8");
+  std::vector<uint32_t> v;
+  e->tokenize(s, v);
+  *n_ids = v.size();
+  if (v.size() > cap || (!ids && !v.empty())) return set_error(J1_ERR_INVALID_ARG, "ids buffer too small");
+  if (!v.empty()) std::memcpy(ids, v.data(), v.size() * 4);
+  return J1_OK;
+}
+
+j1_status j1_text_encoder_encode(j1_text_encoder* e, const char* state, int32_t state_is_json, const char* question,
+                                 const char* const* options, size_t n_options, uint8_t qtype, uint32_t* ids,
+                                 size_t cap, size_t* ids_len, uint32_t* markers, int32_t* truncated) {
+  if (!e || !state || !question || (n_options && !options) || !ids_len)
+    return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+  if (qtype > 2) return set_error(J1_ERR_INVALID_ARG, "qtype must be 0 (choice), 1 (score) or 2 (noul)");
+  std::vector<std::string> opts(n_options);
+  for (size_t k = 0; k < n_options; ++k) {
+    if (!options[k]) return set_error(J1_ERR_INVALID_ARG, "NULL option");
+    opts[k] = options[k];
+  }
+  const std::string st(state), q(question);
+  for (const std::string* s : {&st, &q})
+    if (!valid_utf8(*s)) return set_error(J1_ERR_INVALID_ARG, "text is not valid UTF-8");
+  for (const auto& s : opts)
+    if (!valid_utf8(s)) return set_error(J1_ERR_INVALID_ARG, "text is not valid UTF-8");
+  // Encoder::encode (src/encode.rs:131-154): whole-request cache keyed on its text
+  std::string key;
+  if (true) {
+    key.reserve(st.size() + q.size() + 64);
+    auto put = [&key](const std::string& s) {
+      const uint64_t n = s.size();
+      key.append(reinterpret_cast<const char*>(&n), 8);
+      key += s;
+    };
+    put(st);
+    put(q);
+    for (const auto& s : opts) put(s);
+    key += static_cast<char>(qtype);
+    key += state_is_json ? 'j' : 't';
+  }
+  j1_text_encoder::Enc enc;
+  if (!e->encodings->get(key, enc)) {
+    // Encoder::sequence (src/encode.rs:138-195), text part
+    const std::string& mask = e->mask_token;
+    if (e->opts.strict) {
+      bool has = st.find(mask) != std::string::npos || q.find(mask) != std::string::npos;
+      for (const auto& s : opts) has = has || s.find(mask) != std::string::npos;
+      if (has) return set_error(J1_ERR_INVALID_ARG, "Reserved model marker in request");
+    }
+    auto clean = [&mask](const std::string& s) { return replace_all(s, mask, " "); };
+    std::vector<uint32_t> head, state_ids;
+    e->tokenize(std::string(qtype_name(qtype)) + " question: " + clean(q), head);
+    std::vector<uint32_t> opt_ids, opt_lens;
+    for (const auto& s : opts) {
+      std::vector<uint32_t> v;
+      e->tokenize(" " + clean(s), v);
+      opt_ids.insert(opt_ids.end(), v.begin(), v.end());
+      opt_lens.push_back(static_cast<uint32_t>(v.size()));
+    }
+    e->tokenize(clean(st), state_ids);
+    j1_tokenized_request r{head.data(), head.size(), opt_ids.data(), opt_lens.data(), n_options,
+                           state_ids.data(), state_ids.size(), qtype};
+    enc.ids.assign(static_cast<size_t>(e->opts.max_length), 0);
+    enc.markers.assign(std::max<size_t>(n_options, 1), 0);
+    size_t n = 0;
+    if (j1_status s = j1_encode_sequence(&e->opts, &r, enc.ids.data(), enc.ids.size(), &n, enc.markers.data(),
+                                         &enc.truncated))
+      return s;
+    enc.ids.resize(n);
+    enc.markers.resize(n_options);
+    e->encodings->put(key, enc);
+  }
+  *ids_len = enc.ids.size();
+  if (enc.ids.size() > cap || !ids || (!markers && n_options))
+    return set_error(J1_ERR_INVALID_ARG, "output arrays too small (ids_cap >= max_length, markers >= n_options)");
+  std::memcpy(ids, enc.ids.data(), enc.ids.size() * 4);
+  if (n_options) std::memcpy(markers, enc.markers.data(), n_options * 4);
+  if (truncated) *truncated = enc.truncated;
+  return J1_OK;
+}
+
+}  // extern "C"

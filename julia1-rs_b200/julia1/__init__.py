@@ -34,6 +34,9 @@ EXPORTS = [
     "j1_engine_max_length", "j1_encoder_options_default", "j1_encode_sequence", "j1_engine_logits_tokenized",
     "j1_router_options_default", "j1_router_create", "j1_router_create_with_scorer", "j1_router_destroy",
     "j1_router_clear_cache", "j1_router_route_many", "j1_display_probabilities", "j1_router_confident_winner",
+    "j1_tokenizer_load", "j1_tokenizer_from_json", "j1_tokenizer_destroy", "j1_tokenizer_token_to_id",
+    "j1_tokenizer_encode", "j1_tokenizer_encode_batch", "j1_text_encoder_load", "j1_text_encoder_destroy",
+    "j1_text_encoder_clear_cache", "j1_text_encoder_options", "j1_text_encoder_tokenize", "j1_text_encoder_encode",
 ]
 PROF_FAMILIES = 12
 
@@ -172,6 +175,27 @@ def lib():
     L.j1_router_clear_cache.restype = None
     L.j1_router_route_many.argtypes = [C.c_void_p, C.c_size_t, C.POINTER(J1TokenizedRequest),
                                        C.POINTER(J1RouteResult), C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]
+    L.j1_tokenizer_load.argtypes = [C.c_char_p, C.POINTER(C.c_void_p)]
+    L.j1_tokenizer_from_json.argtypes = [C.c_char_p, C.c_size_t, C.POINTER(C.c_void_p)]
+    L.j1_tokenizer_destroy.argtypes = [C.c_void_p]
+    L.j1_tokenizer_destroy.restype = None
+    L.j1_tokenizer_token_to_id.argtypes = [C.c_void_p, C.c_char_p]
+    L.j1_tokenizer_token_to_id.restype = C.c_int64
+    L.j1_tokenizer_encode.argtypes = [C.c_void_p, C.c_char_p, C.c_size_t, u32p, C.c_size_t, C.POINTER(C.c_size_t)]
+    L.j1_tokenizer_encode_batch.argtypes = [C.c_void_p, C.c_size_t, C.POINTER(C.c_char_p), C.POINTER(C.c_size_t),
+                                            C.c_int32, C.POINTER(u32p), C.POINTER(C.c_size_t), C.POINTER(C.c_size_t)]
+    L.j1_text_encoder_load.argtypes = [C.c_char_p, C.c_int32, C.c_int32, C.c_int32, C.c_int64, C.c_int64,
+                                       C.POINTER(C.c_void_p)]
+    L.j1_text_encoder_destroy.argtypes = [C.c_void_p]
+    L.j1_text_encoder_destroy.restype = None
+    L.j1_text_encoder_clear_cache.argtypes = [C.c_void_p]
+    L.j1_text_encoder_clear_cache.restype = None
+    L.j1_text_encoder_options.argtypes = [C.c_void_p, C.POINTER(J1EncoderOptions)]
+    L.j1_text_encoder_tokenize.argtypes = [C.c_void_p, C.c_char_p, C.c_size_t, u32p, C.c_size_t,
+                                           C.POINTER(C.c_size_t)]
+    L.j1_text_encoder_encode.argtypes = [C.c_void_p, C.c_char_p, C.c_int32, C.c_char_p, C.POINTER(C.c_char_p),
+                                         C.c_size_t, C.c_uint8, u32p, C.c_size_t, C.POINTER(C.c_size_t), u32p,
+                                         C.POINTER(C.c_int32)]
     L.j1_op_gemm.argtypes = [C.POINTER(J1GemmArgs), C.c_void_p, C.c_int]
     L.j1_op_attention.argtypes = [C.c_void_p, C.c_int64, C.c_int32, u32p, u32p, C.c_size_t, C.c_int32, C.c_void_p,
                                   C.c_void_p, C.c_int]
@@ -182,7 +206,9 @@ def lib():
                "j1_engine_logits_encoded", "j1_op_gemm", "j1_op_attention", "j1_op_attention_noalloc",
                "j1_op_geglu_interleave", "j1_model_profile", "j1_model_profile_read", "j1_encode_sequence",
                "j1_engine_logits_tokenized", "j1_router_create", "j1_router_create_with_scorer",
-               "j1_router_route_many"):
+               "j1_router_route_many", "j1_tokenizer_load", "j1_tokenizer_from_json", "j1_tokenizer_encode",
+               "j1_tokenizer_encode_batch", "j1_text_encoder_load", "j1_text_encoder_options",
+               "j1_text_encoder_tokenize", "j1_text_encoder_encode"):
         getattr(L, fn).restype = C.c_int
     _lib = L
     return L
@@ -659,6 +685,129 @@ class Router:
 
     def route(self, row: TokenizedRequest) -> RouteResult:
         return self.route_many([row])[0]
+
+
+# ------------------------------------------------------------------ text -> ids
+QTYPES = {"choice": 0, "score": 1, "noul": 2}
+
+
+class Tokenizer:
+    """The checkpoint's tokenizer.json (byte-level BPE, HF `tokenizers` 0.22.2 format) in libj1:
+    encode(text) == Tokenizer::encode_fast(text, false).ids (src/encode.rs:114-129)."""
+
+    def __init__(self, handle):
+        self._h = handle
+
+    @staticmethod
+    def from_file(path: str) -> "Tokenizer":
+        h = C.c_void_p()
+        check(lib().j1_tokenizer_load(path.encode(), C.byref(h)))
+        return Tokenizer(h)
+
+    @staticmethod
+    def from_str(text: str) -> "Tokenizer":
+        b = text.encode()
+        h = C.c_void_p()
+        check(lib().j1_tokenizer_from_json(b, len(b), C.byref(h)))
+        return Tokenizer(h)
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().j1_tokenizer_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def token_to_id(self, token: str) -> Optional[int]:
+        v = lib().j1_tokenizer_token_to_id(self._h, token.encode())
+        return None if v < 0 else int(v)
+
+    def encode(self, text: str) -> List[int]:
+        b = text.encode()
+        cap = 4 * len(b) + 16
+        out = np.zeros(cap, np.uint32)
+        n = C.c_size_t()
+        check(lib().j1_tokenizer_encode(self._h, b, len(b), out.ctypes.data_as(C.POINTER(C.c_uint32)), cap,
+                                        C.byref(n)))
+        return out[:n.value].tolist()
+
+    def encode_batch(self, texts: Sequence[str], threads: int = 1) -> List[List[int]]:
+        bs = [t.encode() for t in texts]
+        n = len(bs)
+        if n == 0:
+            return []
+        arr = (C.c_char_p * n)(*bs)
+        lens = (C.c_size_t * n)(*[len(b) for b in bs])
+        nids = (C.c_size_t * n)()
+        total = C.c_size_t()
+        null = (C.POINTER(C.c_uint32) * n)()
+        check(lib().j1_tokenizer_encode_batch(self._h, n, arr, lens, int(threads), null, nids, C.byref(total)))
+        bufs = [np.zeros(max(int(nids[i]), 1), np.uint32) for i in range(n)]
+        ptrs = (C.POINTER(C.c_uint32) * n)(*[b.ctypes.data_as(C.POINTER(C.c_uint32)) for b in bufs])
+        check(lib().j1_tokenizer_encode_batch(self._h, n, arr, lens, int(threads), ptrs, nids, C.byref(total)))
+        return [bufs[i][:int(nids[i])].tolist() for i in range(n)]
+
+
+class TextEncoder:
+    """encode::Encoder (src/encode.rs:25-195) over the checkpoint's tokenizer: special tokens
+    from tokenizer_config.json, LRU caches, the request's text forms and Encoder::sequence."""
+
+    def __init__(self, handle):
+        self._h = handle
+
+    @staticmethod
+    def load(ckpt_dir: str, max_length: int, head_length: int = 256, strict: bool = False,
+             token_cache: int = 8192, encoding_cache: int = 2048) -> "TextEncoder":
+        h = C.c_void_p()
+        check(lib().j1_text_encoder_load(ckpt_dir.encode(), int(max_length), int(head_length), int(bool(strict)),
+                                         int(token_cache), int(encoding_cache), C.byref(h)))
+        return TextEncoder(h)
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().j1_text_encoder_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def clear_cache(self):
+        lib().j1_text_encoder_clear_cache(self._h)
+
+    def options(self) -> EncoderOptions:
+        o = J1EncoderOptions()
+        check(lib().j1_text_encoder_options(self._h, C.byref(o)))
+        return EncoderOptions(int(o.cls_id), int(o.sep_id), int(o.mask_id), int(o.max_length), int(o.head_length),
+                              bool(o.strict))
+
+    def tokenize(self, text: str) -> List[int]:
+        b = text.encode()
+        cap = 4 * len(b) + 16
+        out = np.zeros(cap, np.uint32)
+        n = C.c_size_t()
+        check(lib().j1_text_encoder_tokenize(self._h, b, len(b), out.ctypes.data_as(C.POINTER(C.c_uint32)), cap,
+                                             C.byref(n)))
+        return out[:n.value].tolist()
+
+    def encode(self, state: str, question: str, options: Sequence[str], qtype=0, state_is_json=False):
+        """Encoder::encode on a request (state already rendered) -> (Encoded, truncated)."""
+        q = QTYPES[qtype] if isinstance(qtype, str) else int(qtype)
+        o = self.options()
+        ids = np.zeros(o.max_length, np.uint32)
+        mk = np.zeros(max(len(options), 1), np.uint32)
+        opts = (C.c_char_p * max(len(options), 1))(*[x.encode() for x in options])
+        n, tr = C.c_size_t(), C.c_int32()
+        check(lib().j1_text_encoder_encode(self._h, state.encode(), int(bool(state_is_json)), question.encode(), opts,
+                                           len(options), q, ids.ctypes.data_as(C.POINTER(C.c_uint32)), ids.size,
+                                           C.byref(n), mk.ctypes.data_as(C.POINTER(C.c_uint32)), C.byref(tr)))
+        return Encoded(ids[:n.value].copy(), mk[:len(options)].copy(), q), bool(tr.value)
 
 
 # ------------------------------------------------------------------ kernel-level ops (torch tensors)

@@ -242,3 +242,22 @@ class Router:
                     chosen.sort()
                     candidates[i].extend(chosen)
         return results, model_rows, hits
+
+
+QNAMES = {0: "choice", 1: "score", 2: "noul"}
+
+
+def encode_text(tokenize, mask_token: str, o: EncOpts, state: str, question: str, options, qtype: int = 0):
+    """Encoder::sequence with its text part (encode.rs:138-150): strict refusal of the mask
+    token's text, mask text replaced by a space, the head / option / state text forms,
+    tokenized by `tokenize` (the checkpoint tokenizer), then the layout on ids."""
+    if o.strict and any(mask_token in t for t in [state, question] + list(options)):
+        raise RefError("Reserved model marker in request")
+
+    def clean(t):
+        return t.replace(mask_token, " ")
+
+    head = tokenize("%s question: %s" % (QNAMES[qtype], clean(question)))
+    opts = [tokenize(" " + clean(x)) for x in options]
+    state_ids = tokenize(clean(state))
+    return encode_sequence(o, Req(list(head), [list(x) for x in opts], list(state_ids), qtype))

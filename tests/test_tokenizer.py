@@ -1,0 +1,149 @@
+"""Text -> token ids (no GPU needed).
+
+* libj1's tokenizer reproduces the reference's tokenizer library (HF `tokenizers` 0.22.2,
+  pinned in the reference's Cargo.lock; Tokenizer::encode_fast(text, false),
+  src/encode.rs:114-129) on the committed golden encodings of two byte-level BPE
+  tokenizers (tests/golden/make_tokenizer_golden.py made them with that library), and,
+  where the library is importable, on freshly generated random text.
+* Batch encoding on several threads equals encoding one text at a time.
+* Configurations outside the supported family are refused at load time.
+* The text Encoder (src/encode.rs:25-195) builds the same rows as the restated
+  Encoder::sequence (oracle/router_ref.py) over the same tokenizer, with the strict-mode
+  refusal of the mask token's text and its caches.
+"""
+import json
+import os
+import random
+
+import pytest
+
+import julia1 as j1
+from conftest import ROOT
+from oracle import router_ref as R
+
+GOLDEN = os.path.join(ROOT, "tests", "golden")
+KINDS = ["nfc", "prefix"]
+
+
+def load(kind):
+    return j1.Tokenizer.from_file(os.path.join(GOLDEN, "tokenizer_%s.json" % kind))
+
+
+@pytest.mark.parametrize("kind", KINDS)
+def test_golden_encodings(kind):
+    tok = load(kind)
+    data = json.load(open(os.path.join(GOLDEN, "tokenizer_%s_cases.json" % kind), encoding="utf-8"))
+    assert data["generator"].startswith("tokenizers 0.22")
+    for text, ids in data["cases"]:
+        assert tok.encode(text) == ids, repr(text)
+
+
+def random_text(rng):
+    blocks = [(0x20, 0x7E)] * 6 + [(0xA0, 0x17F), (0x300, 0x36F), (0x370, 0x3FF), (0x400, 0x4FF), (0x590, 0x6FF),
+                                   (0x900, 0x97F), (0x1100, 0x11FF), (0x2000, 0x206F), (0x3000, 0x30FF),
+                                   (0x4E00, 0x4E80), (0xAC00, 0xAC40), (0xFF00, 0xFF5E), (0x1F300, 0x1F64F)]
+    extras = ["[MASK]", " [MASK] ", "[CLS]", "|||IP_ADDRESS|||", "<br>", "lol", " lol ", "'s", "'LL", "\n", "\t",
+              "   ", "\r\n", "é", "각", "Å", " ", "　"]
+    out = []
+    for _ in range(rng.randint(0, 30)):
+        if rng.random() < 0.2:
+            out.append(rng.choice(extras))
+        else:
+            a, b = rng.choice(blocks)
+            out.append(chr(rng.randint(a, b)))
+    return "".join(out)
+
+
+@pytest.mark.parametrize("kind", KINDS)
+def test_random_text_matches_tokenizers_library(kind):
+    tokenizers = pytest.importorskip("tokenizers")
+    path = os.path.join(GOLDEN, "tokenizer_%s.json" % kind)
+    ref = tokenizers.Tokenizer.from_file(path)
+    tok = load(kind)
+    rng = random.Random(1234 + len(kind))
+    texts = [random_text(rng) for _ in range(3000)]
+    for t in texts:
+        t = t.encode("utf-8", "surrogatepass").decode("utf-8", "ignore")
+        assert tok.encode(t) == ref.encode(t, add_special_tokens=False).ids, repr(t)
+
+
+def test_batch_threads_and_lookup():
+    tok = load("nfc")
+    data = json.load(open(os.path.join(GOLDEN, "tokenizer_nfc_cases.json"), encoding="utf-8"))
+    texts = [t for t, _ in data["cases"]]
+    one = [tok.encode(t) for t in texts]
+    assert tok.encode_batch(texts, threads=1) == one
+    assert tok.encode_batch(texts, threads=4) == one
+    assert tok.encode_batch([]) == []
+    assert tok.token_to_id("[MASK]") == 977 and tok.token_to_id("no such token") is None
+    assert tok.token_to_id("the") is not None
+
+
+def test_refusals(tmp_path):
+    base = json.load(open(os.path.join(GOLDEN, "tokenizer_nfc.json"), encoding="utf-8"))
+    for patch, msg in [(("normalizer", {"type": "Lowercase"}), "only the NFC normalizer"),
+                       (("pre_tokenizer", {"type": "Whitespace"}), "only the ByteLevel pre-tokenizer"),
+                       (("model", {"type": "WordPiece", "vocab": {}}), "only BPE models")]:
+        d = dict(base)
+        d[patch[0]] = patch[1]
+        with pytest.raises(j1.J1Error, match=msg):
+            j1.Tokenizer.from_str(json.dumps(d))
+    d = json.loads(json.dumps(base))
+    d["model"]["unk_token"] = "[UNK]"
+    with pytest.raises(j1.J1Error, match="unk_token"):
+        j1.Tokenizer.from_str(json.dumps(d))
+    with pytest.raises(j1.J1Error, match="cannot read"):
+        j1.Tokenizer.from_file(str(tmp_path / "missing.json"))
+    tok = load("nfc")
+    L = j1.lib()
+    import ctypes as C
+    n = C.c_size_t()
+    buf = (C.c_uint32 * 16)()
+    assert L.j1_tokenizer_encode(tok._h, b"\xff\xfe", 2, buf, 16, C.byref(n)) == j1.INVALID_ARG
+
+
+# ------------------------------------------------------------------ text encoder
+@pytest.fixture(scope="module")
+def enc_dir(tmp_path_factory):
+    d = tmp_path_factory.mktemp("enc")
+    with open(os.path.join(GOLDEN, "tokenizer_nfc.json"), encoding="utf-8") as f:
+        (d / "tokenizer.json").write_text(f.read(), encoding="utf-8")
+    (d / "tokenizer_config.json").write_text(json.dumps(
+        {"mask_token": "[MASK]", "cls_token": "[CLS]", "sep_token": "[SEP]", "pad_token": "[PAD]"}))
+    return str(d)
+
+
+def test_text_encoder_matches_reference(enc_dir):
+    tok = load("nfc")
+    rng = random.Random(5)
+    words = ["win", "lose", "draw", "attack the left flank", "café au lait", "naïve", "日本語", "don't", "[MASK] x",
+             "Ελλάδα", "été", "12 345", "lol"]
+    for strict in (False, True):
+        enc = j1.TextEncoder.load(enc_dir, max_length=128, head_length=48, strict=strict)
+        o = enc.options()
+        assert (o.cls_id, o.sep_id, o.mask_id) == (974, 975, 977)
+        ro = R.EncOpts(o.cls_id, o.sep_id, o.mask_id, 128, 48, strict)
+        n_ok = n_err = 0
+        for _ in range(300):
+            k = 1 if strict else 3  # smaller requests in strict mode, which refuses large ones
+            opts = [" ".join(rng.choice(words) for _ in range(rng.randint(1, k + 1))) for _ in range(rng.randint(2, 3 * k))]
+            question = " ".join(rng.choice(words) for _ in range(rng.randint(1, 4 * k)))
+            state = " ".join(rng.choice(words) for _ in range(rng.randint(0, 20 * k)))
+            qtype = rng.choice([0, 0, 1])
+            try:
+                want = R.encode_text(tok.encode, "[MASK]", ro, state, question, opts, qtype)
+            except R.RefError as e:
+                with pytest.raises(j1.J1Error, match=str(e).split(";")[0]):
+                    enc.encode(state, question, opts, qtype)
+                n_err += 1
+                continue
+            got, tr = enc.encode(state, question, opts, qtype)
+            assert (got.ids.tolist(), got.markers.tolist(), tr) == (want[0], want[1], want[2])
+            n_ok += 1
+            again, _ = enc.encode(state, question, opts, qtype)  # from the encoding cache
+            assert again.ids.tolist() == want[0]
+        assert n_ok > 50 and (n_err > 20 or not strict)
+        enc.clear_cache()
+        assert enc.tokenize("the game") == tok.encode("the game")
+    with pytest.raises(j1.J1Error, match="max_length must leave room"):
+        j1.TextEncoder.load(enc_dir, max_length=40, head_length=48)
