@@ -306,6 +306,15 @@ J1_API j1_status j1_text_encoder_encode(j1_text_encoder* enc, const char* state,
                                         uint8_t qtype, uint32_t* ids, size_t cap, size_t* ids_len, uint32_t* markers,
                                         int32_t* truncated);
 
+/* The tokens of a request's pieces with the text rules of Encoder::sequence (mask text
+ * refused in strict mode, else replaced by a space; head "<qtype> question: <question>",
+ * each " <option>", the state): ids = head | option 0 | ... | option n-1 | state, with
+ * piece_lens[n_options + 2] = their lengths — a j1_tokenized_request for the router or
+ * j1_engine_logits_tokenized. With ids or piece_lens NULL only *total is set. */
+J1_API j1_status j1_text_encoder_request_tokens(j1_text_encoder* enc, const char* state, const char* question,
+                                                const char* const* options, size_t n_options, uint8_t qtype,
+                                                uint32_t* ids, size_t cap, size_t* total, uint32_t* piece_lens);
+
 /* ------------------------------------------------------------ kernel-level ops
  * On caller device memory (e.g. torch tensors); `stream` is a cudaStream_t or NULL.
  * With sync != 0 the call waits for completion and reports device-side timeouts. */

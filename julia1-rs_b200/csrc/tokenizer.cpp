@@ -696,6 +696,51 @@ std::string replace_all(const std::string& s, const std::string& from, const std
 
 const char* qtype_name(uint8_t q) { return q == 0 ? "choice" : q == 1 ? "score" : "noul"; }
 
+// The text part of Encoder::sequence (src/encode.rs:138-150, 180): strict refusal of the mask
+// token's text, the text replaced by a space otherwise, and the tokens of the head
+// "<qtype> question: <question>", of each " <option>" and of the state.
+j1_status request_tokens(j1_text_encoder* e, const std::string& st, const std::string& q,
+                         const std::vector<std::string>& opts, uint8_t qtype, std::vector<uint32_t>& head,
+                         std::vector<uint32_t>& opt_ids, std::vector<uint32_t>& opt_lens,
+                         std::vector<uint32_t>& state_ids) {
+  const std::string& mask = e->mask_token;
+  if (e->opts.strict) {
+    bool has = st.find(mask) != std::string::npos || q.find(mask) != std::string::npos;
+    for (const auto& s : opts) has = has || s.find(mask) != std::string::npos;
+    if (has) return set_error(J1_ERR_INVALID_ARG, "Reserved model marker in request");
+  }
+  auto clean = [&mask](const std::string& s) { return replace_all(s, mask, " "); };
+  e->tokenize(std::string(qtype_name(qtype)) + " question: " + clean(q), head);
+  opt_ids.clear();
+  opt_lens.clear();
+  for (const auto& s : opts) {
+    std::vector<uint32_t> v;
+    e->tokenize(" " + clean(s), v);
+    opt_ids.insert(opt_ids.end(), v.begin(), v.end());
+    opt_lens.push_back(static_cast<uint32_t>(v.size()));
+  }
+  e->tokenize(clean(st), state_ids);
+  return J1_OK;
+}
+
+j1_status read_request(const char* state, const char* question, const char* const* options, size_t n_options,
+                       uint8_t qtype, std::string& st, std::string& q, std::vector<std::string>& opts) {
+  if (!state || !question || (n_options && !options)) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+  if (qtype > 2) return set_error(J1_ERR_INVALID_ARG, "qtype must be 0 (choice), 1 (score) or 2 (noul)");
+  opts.assign(n_options, std::string());
+  for (size_t k = 0; k < n_options; ++k) {
+    if (!options[k]) return set_error(J1_ERR_INVALID_ARG, "NULL option");
+    opts[k] = options[k];
+  }
+  st = state;
+  q = question;
+  for (const std::string* s : {&st, &q})
+    if (!valid_utf8(*s)) return set_error(J1_ERR_INVALID_ARG, "text is not valid UTF-8");
+  for (const auto& s : opts)
+    if (!valid_utf8(s)) return set_error(J1_ERR_INVALID_ARG, "text is not valid UTF-8");
+  return J1_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -850,19 +895,10 @@ j1_status j1_text_encoder_tokenize(j1_text_encoder* e, const char* text, size_t 
 j1_status j1_text_encoder_encode(j1_text_encoder* e, const char* state, int32_t state_is_json, const char* question,
                                  const char* const* options, size_t n_options, uint8_t qtype, uint32_t* ids,
                                  size_t cap, size_t* ids_len, uint32_t* markers, int32_t* truncated) {
-  if (!e || !state || !question || (n_options && !options) || !ids_len)
-    return set_error(J1_ERR_INVALID_ARG, "NULL argument");
-  if (qtype > 2) return set_error(J1_ERR_INVALID_ARG, "qtype must be 0 (choice), 1 (score) or 2 (noul)");
-  std::vector<std::string> opts(n_options);
-  for (size_t k = 0; k < n_options; ++k) {
-    if (!options[k]) return set_error(J1_ERR_INVALID_ARG, "NULL option");
-    opts[k] = options[k];
-  }
-  const std::string st(state), q(question);
-  for (const std::string* s : {&st, &q})
-    if (!valid_utf8(*s)) return set_error(J1_ERR_INVALID_ARG, "text is not valid UTF-8");
-  for (const auto& s : opts)
-    if (!valid_utf8(s)) return set_error(J1_ERR_INVALID_ARG, "text is not valid UTF-8");
+  if (!e || !ids_len) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+  std::string st, q;
+  std::vector<std::string> opts;
+  if (j1_status s = read_request(state, question, options, n_options, qtype, st, q, opts)) return s;
   // Encoder::encode (src/encode.rs:131-154): whole-request cache keyed on its text
   std::string key;
   if (true) {
@@ -880,24 +916,8 @@ j1_status j1_text_encoder_encode(j1_text_encoder* e, const char* state, int32_t 
   }
   j1_text_encoder::Enc enc;
   if (!e->encodings->get(key, enc)) {
-    // Encoder::sequence (src/encode.rs:138-195), text part
-    const std::string& mask = e->mask_token;
-    if (e->opts.strict) {
-      bool has = st.find(mask) != std::string::npos || q.find(mask) != std::string::npos;
-      for (const auto& s : opts) has = has || s.find(mask) != std::string::npos;
-      if (has) return set_error(J1_ERR_INVALID_ARG, "Reserved model marker in request");
-    }
-    auto clean = [&mask](const std::string& s) { return replace_all(s, mask, " "); };
-    std::vector<uint32_t> head, state_ids;
-    e->tokenize(std::string(qtype_name(qtype)) + " question: " + clean(q), head);
-    std::vector<uint32_t> opt_ids, opt_lens;
-    for (const auto& s : opts) {
-      std::vector<uint32_t> v;
-      e->tokenize(" " + clean(s), v);
-      opt_ids.insert(opt_ids.end(), v.begin(), v.end());
-      opt_lens.push_back(static_cast<uint32_t>(v.size()));
-    }
-    e->tokenize(clean(st), state_ids);
+    std::vector<uint32_t> head, opt_ids, opt_lens, state_ids;
+    if (j1_status s = request_tokens(e, st, q, opts, qtype, head, opt_ids, opt_lens, state_ids)) return s;
     j1_tokenized_request r{head.data(), head.size(), opt_ids.data(), opt_lens.data(), n_options,
                            state_ids.data(), state_ids.size(), qtype};
     enc.ids.assign(static_cast<size_t>(e->opts.max_length), 0);
@@ -916,6 +936,27 @@ j1_status j1_text_encoder_encode(j1_text_encoder* e, const char* state, int32_t 
   std::memcpy(ids, enc.ids.data(), enc.ids.size() * 4);
   if (n_options) std::memcpy(markers, enc.markers.data(), n_options * 4);
   if (truncated) *truncated = enc.truncated;
+  return J1_OK;
+}
+
+j1_status j1_text_encoder_request_tokens(j1_text_encoder* e, const char* state, const char* question,
+                                         const char* const* options, size_t n_options, uint8_t qtype, uint32_t* ids,
+                                         size_t cap, size_t* total, uint32_t* piece_lens) {
+  if (!e || !total) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+  std::string st, q;
+  std::vector<std::string> opts;
+  if (j1_status s = read_request(state, question, options, n_options, qtype, st, q, opts)) return s;
+  std::vector<uint32_t> head, opt_ids, opt_lens, state_ids;
+  if (j1_status s = request_tokens(e, st, q, opts, qtype, head, opt_ids, opt_lens, state_ids)) return s;
+  *total = head.size() + opt_ids.size() + state_ids.size();
+  if (!ids || !piece_lens) return J1_OK;  // size query
+  if (*total > cap) return set_error(J1_ERR_INVALID_ARG, "ids buffer too small");
+  std::memcpy(ids, head.data(), head.size() * 4);
+  std::memcpy(ids + head.size(), opt_ids.data(), opt_ids.size() * 4);
+  std::memcpy(ids + head.size() + opt_ids.size(), state_ids.data(), state_ids.size() * 4);
+  piece_lens[0] = static_cast<uint32_t>(head.size());
+  for (size_t k = 0; k < n_options; ++k) piece_lens[1 + k] = opt_lens[k];
+  piece_lens[1 + n_options] = static_cast<uint32_t>(state_ids.size());
   return J1_OK;
 }
 

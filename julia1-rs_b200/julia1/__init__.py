@@ -37,6 +37,7 @@ EXPORTS = [
     "j1_tokenizer_load", "j1_tokenizer_from_json", "j1_tokenizer_destroy", "j1_tokenizer_token_to_id",
     "j1_tokenizer_encode", "j1_tokenizer_encode_batch", "j1_text_encoder_load", "j1_text_encoder_destroy",
     "j1_text_encoder_clear_cache", "j1_text_encoder_options", "j1_text_encoder_tokenize", "j1_text_encoder_encode",
+    "j1_text_encoder_request_tokens",
 ]
 PROF_FAMILIES = 12
 
@@ -196,6 +197,9 @@ def lib():
     L.j1_text_encoder_encode.argtypes = [C.c_void_p, C.c_char_p, C.c_int32, C.c_char_p, C.POINTER(C.c_char_p),
                                          C.c_size_t, C.c_uint8, u32p, C.c_size_t, C.POINTER(C.c_size_t), u32p,
                                          C.POINTER(C.c_int32)]
+    L.j1_text_encoder_request_tokens.argtypes = [C.c_void_p, C.c_char_p, C.c_char_p, C.POINTER(C.c_char_p),
+                                                 C.c_size_t, C.c_uint8, u32p, C.c_size_t, C.POINTER(C.c_size_t), u32p]
+    L.j1_text_encoder_request_tokens.restype = C.c_int
     L.j1_op_gemm.argtypes = [C.POINTER(J1GemmArgs), C.c_void_p, C.c_int]
     L.j1_op_attention.argtypes = [C.c_void_p, C.c_int64, C.c_int32, u32p, u32p, C.c_size_t, C.c_int32, C.c_void_p,
                                   C.c_void_p, C.c_int]
@@ -577,6 +581,22 @@ def _engine_logits_tokenized(self, rows: Sequence[TokenizedRequest], enc: Encode
 Engine.logits_tokenized = _engine_logits_tokenized
 
 
+def _check_text(rows: Sequence["Request"], line_prefix: bool):
+    for i, r in enumerate(rows):
+        if any(len(o) == 0 for o in r.options):
+            raise J1Error(INVALID_ARG, ("JSONL line %d: options must contain 2–20 nonempty rendered descriptions"
+                                        % (i + 1)) if line_prefix else "Options must be nonempty strings")
+
+
+def _engine_logits(self, rows: Sequence["Request"], text_encoder: "TextEncoder") -> List[List[float]]:
+    """Engine::logits (src/engine.rs:236-243) on text requests through the text encoder."""
+    _check_text(rows, True)
+    return self.logits_tokenized([text_encoder.tokenize_request(r) for r in rows], text_encoder.options())
+
+
+Engine.logits = _engine_logits
+
+
 def display_probabilities(values: Sequence[float]) -> List[float]:
     """display_probabilities (src/request.rs:150-161)."""
     v = np.ascontiguousarray(np.asarray(values, np.float64))
@@ -604,7 +624,11 @@ class Router:
     Encoded (ids, markers, qtype) and logits one list of floats per row (e.g. a test double)."""
 
     def __init__(self, engine: Optional[Engine] = None, encoder: Optional[EncoderOptions] = None, scorer=None,
-                 width=20, survivors=2, batch_size=16, cache_size=0, max_options=4096):
+                 width=20, survivors=2, batch_size=16, cache_size=0, max_options=4096,
+                 text_encoder: Optional["TextEncoder"] = None):
+        self._text = text_encoder
+        if encoder is None and text_encoder is not None:
+            encoder = text_encoder.options()
         if encoder is None:
             raise J1Error(INVALID_ARG, "encoder options (special token ids) are required")
         ro = J1RouterOptions()
@@ -667,8 +691,14 @@ class Router:
         s = np.ascontiguousarray(np.asarray(scores, np.float32))
         return bool(lib().j1_router_confident_winner(s.ctypes.data_as(C.POINTER(C.c_float)), s.size, int(best)))
 
-    def route_many(self, rows: Sequence[TokenizedRequest]) -> List[RouteResult]:
-        """Router::route_many: batch independent groups across requests; request order kept."""
+    def route_many(self, rows: Sequence) -> List[RouteResult]:
+        """Router::route_many: batch independent groups across requests; request order kept.
+        Rows are TokenizedRequest, or Request (text) when the router has a text_encoder."""
+        if any(isinstance(r, Request) for r in rows):
+            if self._text is None:
+                raise J1Error(INVALID_ARG, "text requests need Router(text_encoder=...)")
+            _check_text([r for r in rows if isinstance(r, Request)], False)
+            rows = [self._text.tokenize_request(r) if isinstance(r, Request) else r for r in rows]
         rq = _Requests(rows)
         res = (J1RouteResult * max(len(rows), 1))()
         mr, ch = C.c_uint64(), C.c_uint64()
@@ -752,6 +782,19 @@ class Tokenizer:
         return [bufs[i][:int(nids[i])].tolist() for i in range(n)]
 
 
+@dataclass
+class Request:
+    """request::Request (src/request.rs:77-82): the state is passed rendered (State::render)."""
+    state: str
+    question: str
+    options: Sequence[str]
+    qtype: object = "choice"  # "choice" | "score" | "noul" or 0 | 1 | 2
+    state_is_json: bool = False
+
+    def qtype_id(self) -> int:
+        return QTYPES[self.qtype] if isinstance(self.qtype, str) else int(self.qtype)
+
+
 class TextEncoder:
     """encode::Encoder (src/encode.rs:25-195) over the checkpoint's tokenizer: special tokens
     from tokenizer_config.json, LRU caches, the request's text forms and Encoder::sequence."""
@@ -795,6 +838,23 @@ class TextEncoder:
         check(lib().j1_text_encoder_tokenize(self._h, b, len(b), out.ctypes.data_as(C.POINTER(C.c_uint32)), cap,
                                              C.byref(n)))
         return out[:n.value].tolist()
+
+    def tokenize_request(self, r: "Request") -> TokenizedRequest:
+        """The request's head, option and state tokens under Encoder::sequence's text rules."""
+        q = r.qtype_id()
+        opts = (C.c_char_p * max(len(r.options), 1))(*[x.encode() for x in r.options])
+        total = C.c_size_t()
+        L = lib()
+        check(L.j1_text_encoder_request_tokens(self._h, r.state.encode(), r.question.encode(), opts, len(r.options),
+                                               q, None, 0, C.byref(total), None))
+        ids = np.zeros(max(total.value, 1), np.uint32)
+        lens = np.zeros(len(r.options) + 2, np.uint32)
+        check(L.j1_text_encoder_request_tokens(self._h, r.state.encode(), r.question.encode(), opts, len(r.options),
+                                               q, ids.ctypes.data_as(C.POINTER(C.c_uint32)), ids.size,
+                                               C.byref(total), lens.ctypes.data_as(C.POINTER(C.c_uint32))))
+        cut = np.concatenate([[0], np.cumsum(lens)]).astype(int)
+        pieces = [ids[cut[i]:cut[i + 1]].tolist() for i in range(len(lens))]
+        return TokenizedRequest(pieces[0], pieces[1:-1], pieces[-1], q)
 
     def encode(self, state: str, question: str, options: Sequence[str], qtype=0, state_is_json=False):
         """Encoder::encode on a request (state already rendered) -> (Encoded, truncated)."""

@@ -81,3 +81,26 @@ def test_router_over_engine_matches_reference(engine):
             np.testing.assert_allclose(g.probabilities, w.probabilities, rtol=0, atol=1e-12)
             assert (g.model_rows, g.cache_hits) == (want_rows, want_hits)
         assert any(g.hierarchical for g in got) and any(not g.hierarchical for g in got)
+
+
+def test_engine_logits_on_text(engine, tmp_path):
+    """Engine::logits on text requests (text encoder + tokenized path) equals logits_encoded
+    on the rows the text encoder builds (Encoder::encode), bitwise."""
+    import json
+    import os
+    golden = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+    with open(os.path.join(golden, "tokenizer_nfc.json"), encoding="utf-8") as f:
+        (tmp_path / "tokenizer.json").write_text(f.read(), encoding="utf-8")
+    (tmp_path / "tokenizer_config.json").write_text(json.dumps(
+        {"mask_token": "[MASK]", "cls_token": "[CLS]", "sep_token": "[SEP]", "pad_token": "[PAD]"}))
+    tenc = j1.TextEncoder.load(str(tmp_path), max_length=512)
+    rng = np.random.default_rng(4)
+    words = ["north", "south", "gold", "wood", "attack", "defend", "trade", "café", "Ελλάδα", "日本語", "[MASK]"]
+    reqs = [j1.Request(" ".join(rng.choice(words, size=int(rng.integers(10, 200)))), "which move?",
+                       [" ".join(rng.choice(words, size=int(rng.integers(1, 4)))) for _ in range(int(n))],
+                       qtype=("score" if i % 3 == 1 else "choice"))
+            for i, n in enumerate(rng.integers(2, 21, size=30))]
+    got = engine.logits(reqs, tenc)
+    rows = [tenc.encode(r.state, r.question, r.options, r.qtype)[0] for r in reqs]
+    assert got == engine.logits_encoded(rows)
+    assert all(len(g) == len(r.options) for g, r in zip(got, reqs))

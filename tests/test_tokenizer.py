@@ -147,3 +147,32 @@ def test_text_encoder_matches_reference(enc_dir):
         assert enc.tokenize("the game") == tok.encode("the game")
     with pytest.raises(j1.J1Error, match="max_length must leave room"):
         j1.TextEncoder.load(enc_dir, max_length=40, head_length=48)
+
+
+def test_text_requests_through_router(enc_dir):
+    """Text requests: TextEncoder.tokenize_request + the router give the routes of the
+    restated reference over the same tokenizer (scorer double: logits from the row ids)."""
+    from test_router import lib_scorer, ref_scorer  # noqa: E402
+    tok = load("nfc")
+    enc = j1.TextEncoder.load(enc_dir, max_length=256, head_length=96)
+    o = enc.options()
+    rng = random.Random(9)
+    words = ["north", "south", "gold", "wood", "attack", "defend", "trade", "café", "Ελλάδα", "[MASK]", "lol"]
+    reqs = [j1.Request(" ".join(rng.choice(words) for _ in range(30)), "what next?",
+                       [" ".join(rng.choice(words) for _ in range(rng.randint(1, 3))) for _ in range(n)])
+            for n in (2, 5, 20, 21, 45)]
+    router = j1.Router(text_encoder=enc, scorer=lib_scorer)
+    got = router.route_many(reqs)
+    ro = R.EncOpts(o.cls_id, o.sep_id, o.mask_id, 256, 96)
+    ref = R.Router(ref_scorer(ro))
+
+    def ref_req(r):
+        clean = lambda t: t.replace("[MASK]", " ")  # noqa: E731
+        return R.Req(tok.encode("choice question: " + clean(r.question)), [tok.encode(" " + clean(x)) for x in r.options],
+                     tok.encode(clean(r.state)), 0)
+
+    want, _, _ = ref.route_many([ref_req(r) for r in reqs])
+    assert [g.index for g in got] == [w.index for w in want]
+    assert [g.candidates for g in got] == [w.candidates for w in want]
+    with pytest.raises(j1.J1Error, match="Options must be nonempty strings"):
+        router.route_many([j1.Request("s", "q", ["a", ""])])
