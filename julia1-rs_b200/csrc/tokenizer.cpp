@@ -111,6 +111,8 @@ void utf8_append(std::string& s, uint32_t c) {
   }
 }
 
+// Well-formed UTF-8 (RFC 3629): no overlong forms, no surrogates, nothing above U+10FFFF —
+// what a Rust &str, the reference's input type, can hold.
 bool valid_utf8(const std::string& s) {
   const unsigned char* p = reinterpret_cast<const unsigned char*>(s.data());
   const size_t n = s.size();
@@ -118,8 +120,13 @@ bool valid_utf8(const std::string& s) {
     const unsigned c = p[i];
     size_t len = c < 0x80 ? 1 : (c >> 5) == 6 ? 2 : (c >> 4) == 14 ? 3 : (c >> 3) == 30 ? 4 : 0;
     if (len == 0 || i + len > n) return false;
-    for (size_t k = 1; k < len; ++k)
+    uint32_t cp = len == 1 ? c : len == 2 ? (c & 0x1F) : len == 3 ? (c & 0x0F) : (c & 0x07);
+    for (size_t k = 1; k < len; ++k) {
       if ((p[i + k] & 0xC0) != 0x80) return false;
+      cp = (cp << 6) | (p[i + k] & 0x3F);
+    }
+    static const uint32_t kMin[5] = {0, 0, 0x80, 0x800, 0x10000};
+    if (cp < kMin[len] || cp > 0x10FFFF || (cp >= 0xD800 && cp <= 0xDFFF)) return false;
     i += len;
   }
   return true;

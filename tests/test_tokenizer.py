@@ -99,7 +99,9 @@ def test_refusals(tmp_path):
     import ctypes as C
     n = C.c_size_t()
     buf = (C.c_uint32 * 16)()
-    assert L.j1_tokenizer_encode(tok._h, b"\xff\xfe", 2, buf, 16, C.byref(n)) == j1.INVALID_ARG
+    for bad in (b"\xff\xfe", b"\xc0\xaf", b"\xed\xa0\x80", b"\xf4\x90\x80\x80", b"ab\xe2\x82"):
+        assert L.j1_tokenizer_encode(tok._h, bad, len(bad), buf, 16, C.byref(n)) == j1.INVALID_ARG, bad
+    assert tok.encode("\U0010FFFF x") == tok.encode("\U0010FFFF x")
 
 
 # ------------------------------------------------------------------ text encoder
