@@ -141,7 +141,7 @@ __global__ void __launch_bounds__(192, 2)
   uint64_t* q_full = bars + 2 * NKV;  // [2] per Q buffer
   uint64_t* q_free = q_full + 2;      // [2] per Q buffer (one arrival per softmax warp)
   uint64_t* s_full = q_free + 2;      // [2] per S buffer: S(g) in TMEM
-  uint64_t* p_full = s_full + 2;      // [2] per P buffer: P(g) in TMEM and S(g) read (4 arrivals)
+  uint64_t* p_full = s_full + 2;      // [2] per S buffer: P(g) written over S(g) (4 arrivals)
   uint64_t* o_full = p_full + 2;      // [2] per O buffer: last P.V of an item done
   uint64_t* drain = o_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
