@@ -278,11 +278,13 @@ J1_API int64_t j1_tokenizer_token_to_id(const j1_tokenizer* tok, const char* tok
 /* UTF-8 text -> ids (cap entries; *n_ids is set even when cap is too small). */
 J1_API j1_status j1_tokenizer_encode(const j1_tokenizer* tok, const char* text, size_t len, uint32_t* ids, size_t cap,
                                      size_t* n_ids);
-/* n texts on `threads` host threads; ids_out[i] must hold the ids of text i: call once with
- * ids_out[i] = NULL to learn n_ids[i] (and the total), then with buffers. */
+/* n texts on `threads` host threads into one flat array: the ids of text i are
+ * ids[offsets[i] .. offsets[i + 1]) (offsets[n + 1]). A byte-level BPE emits at most one id
+ * per input byte plus one per piece for a prefix space, so cap = sum(lens) + n + 16 always
+ * suffices; when cap is too small offsets[n] still holds the size needed. */
 J1_API j1_status j1_tokenizer_encode_batch(const j1_tokenizer* tok, size_t n, const char* const* texts,
-                                           const size_t* lens, int32_t threads, uint32_t** ids_out, size_t* n_ids,
-                                           size_t* total);
+                                           const size_t* lens, int32_t threads, uint32_t* ids, size_t cap,
+                                           size_t* offsets);
 
 /* Encoder (src/encode.rs:25-195) on text: Encoder::load(dir, max_length, head_length, strict,
  * token_cache, encoding_cache) reads tokenizer.json and tokenizer_config.json (mask/cls/sep/pad

@@ -68,11 +68,10 @@ bool is_space(uint32_t c) {
   return in_ranges(ucd::kWhiteSpace, c);
 }
 
-void utf8_decode(const std::string& s, std::vector<uint32_t>& cps, std::vector<uint32_t>* offs = nullptr) {
+void utf8_decode(const char* text, size_t n, std::vector<uint32_t>& cps, std::vector<uint32_t>* offs = nullptr) {
   cps.clear();
   if (offs) offs->clear();
-  const unsigned char* p = reinterpret_cast<const unsigned char*>(s.data());
-  const size_t n = s.size();
+  const unsigned char* p = reinterpret_cast<const unsigned char*>(text);
   for (size_t i = 0; i < n;) {
     uint32_t c = p[i];
     size_t len = 1;
@@ -91,6 +90,10 @@ void utf8_decode(const std::string& s, std::vector<uint32_t>& cps, std::vector<u
     i += len;
   }
   if (offs) offs->push_back(static_cast<uint32_t>(n));
+}
+
+void utf8_decode(const std::string& s, std::vector<uint32_t>& cps, std::vector<uint32_t>* offs = nullptr) {
+  utf8_decode(s.data(), s.size(), cps, offs);
 }
 
 void utf8_append(std::string& s, uint32_t c) {
@@ -173,14 +176,14 @@ struct Nfc {
     auto it = comp.find((static_cast<uint64_t>(a) << 32) | b);
     return it == comp.end() ? 0 : it->second;
   }
+  // below U+0300 every character is its own NFC; 0xCC is the lowest lead byte above it
+  static bool simple(const char* p, size_t n) {
+    for (size_t i = 0; i < n; ++i)
+      if (static_cast<unsigned char>(p[i]) >= 0xCC) return false;
+    return true;
+  }
   void normalize(std::string& s) const {
-    bool simple = true;
-    for (unsigned char ch : s)
-      if (ch >= 0xCC) {  // the lead bytes of every code point >= U+0300
-        simple = false;
-        break;
-      }
-    if (simple) return;  // below U+0300 every character is its own NFC
+    if (simple(s.data(), s.size())) return;
     std::vector<uint32_t> cps, d;
     utf8_decode(s, cps);
     d.reserve(cps.size() + 8);
@@ -290,6 +293,7 @@ struct j1_tokenizer {
   std::vector<Added> added;
   std::vector<size_t> raw_by_byte[256], norm_by_byte[256];  // added tokens by first byte of their pattern
   bool nfc = false, prefix_space = false, use_regex = true, ignore_merges = false, has_pre = false;
+  bool has_norm_tokens = false;  // added tokens matched in normalised form exist
   uint32_t byte_id[256];
   bool byte_ok[256];
   std::string byte_char[256];  // GPT-2 byte -> printable stand-in, UTF-8
@@ -439,34 +443,58 @@ struct j1_tokenizer {
   }
 
   // ---- BPE on one pre-token (its UTF-8 bytes)
-  void bpe(const std::string& piece, std::vector<uint32_t>& ids) const {
+  // Per-thread cache of whole pre-tokens (no locking): entries keyed by a 64-bit hash of
+  // the bytes, which are kept and compared on a hit; a cache belongs to one tokenizer.
+  struct WordCache {
+    struct Entry {
+      uint32_t boff, blen, ioff, ilen;
+    };
+    uint64_t owner = 0;
+    std::unordered_map<uint64_t, Entry> map;
+    std::string bytes;
+    std::vector<uint32_t> ids;
+    void reset(uint64_t o) {
+      owner = o;
+      map.clear();
+      bytes.clear();
+      ids.clear();
+    }
+  };
+  static uint64_t hash_bytes(const char* p, size_t n) {
+    uint64_t h = 1469598103934665603ull;
+    for (size_t i = 0; i < n; ++i) {
+      h ^= static_cast<unsigned char>(p[i]);
+      h *= 1099511628211ull;
+    }
+    return h ^ (n * 0x9E3779B97F4A7C15ull);
+  }
+  void bpe(const char* p, size_t n, std::vector<uint32_t>& ids) const {
     if (ignore_merges) {
       std::string mapped;
-      for (unsigned char b : piece) mapped += byte_char[b];
+      for (size_t i = 0; i < n; ++i) mapped += byte_char[static_cast<unsigned char>(p[i])];
       auto it = vocab.find(mapped);
       if (it != vocab.end()) {
         ids.push_back(it->second);
         return;
       }
     }
-    // BPE results of whole pieces, per thread (no locking); a cache belongs to one tokenizer
-    thread_local std::unordered_map<std::string, std::vector<uint32_t>> word_cache;
-    thread_local uint64_t cache_owner = 0;
-    if (cache_owner != generation) {
-      word_cache.clear();
-      cache_owner = generation;
-    }
-    {
-      auto it = word_cache.find(piece);
-      if (it != word_cache.end()) {
-        ids.insert(ids.end(), it->second.begin(), it->second.end());
+    thread_local WordCache wc;
+    if (wc.owner != generation) wc.reset(generation);
+    const uint64_t h = hash_bytes(p, n);
+    auto hit = wc.map.find(h);
+    if (hit != wc.map.end()) {
+      const WordCache::Entry& e = hit->second;
+      if (e.blen == n && std::memcmp(wc.bytes.data() + e.boff, p, n) == 0) {
+        ids.insert(ids.end(), wc.ids.begin() + e.ioff, wc.ids.begin() + e.ioff + e.ilen);
         return;
       }
     }
-    std::vector<uint32_t> sym;
-    sym.reserve(piece.size());
-    for (unsigned char b : piece)
+    thread_local std::vector<uint32_t> sym;
+    sym.clear();
+    for (size_t i = 0; i < n; ++i) {
+      const unsigned char b = static_cast<unsigned char>(p[i]);
       if (byte_ok[b]) sym.push_back(byte_id[b]);  // a byte missing from the vocab is dropped (no unk token)
+    }
     while (sym.size() > 1) {
       uint32_t best_rank = UINT32_MAX, best_id = 0;
       size_t best_pos = 0;
@@ -483,23 +511,34 @@ struct j1_tokenizer {
       sym.erase(sym.begin() + static_cast<std::ptrdiff_t>(best_pos) + 1);
     }
     ids.insert(ids.end(), sym.begin(), sym.end());
-    if (word_cache.size() > 100000) word_cache.clear();
-    word_cache.emplace(piece, std::move(sym));
+    if (hit == wc.map.end()) {  // (a hash collision with another piece is left uncached)
+      if (wc.map.size() > 200000 || wc.bytes.size() > (64u << 20)) wc.reset(generation);
+      wc.map.emplace(h, WordCache::Entry{static_cast<uint32_t>(wc.bytes.size()), static_cast<uint32_t>(n),
+                                         static_cast<uint32_t>(wc.ids.size()), static_cast<uint32_t>(sym.size())});
+      wc.bytes.append(p, n);
+      wc.ids.insert(wc.ids.end(), sym.begin(), sym.end());
+    }
   }
 
   // pre-tokenize + BPE one normalised piece (no added tokens inside)
-  void encode_piece(std::string text, std::vector<uint32_t>& ids) const {
-    if (text.empty()) return;
-    if (prefix_space && text[0] != ' ') text.insert(text.begin(), ' ');
+  void encode_piece(const char* p, size_t n, std::vector<uint32_t>& ids) const {
+    if (n == 0) return;
+    thread_local std::string spaced;
+    if (prefix_space && p[0] != ' ') {
+      spaced.assign(1, ' ');
+      spaced.append(p, n);
+      p = spaced.data();
+      n = spaced.size();
+    }
     if (!use_regex) {
-      bpe(text, ids);
+      bpe(p, n, ids);
       return;
     }
-    std::vector<uint32_t> cps, offs;
-    utf8_decode(text, cps, &offs);
-    std::vector<std::pair<size_t, size_t>> parts;
+    thread_local std::vector<uint32_t> cps, offs;
+    thread_local std::vector<std::pair<size_t, size_t>> parts;
+    utf8_decode(p, n, cps, &offs);
     gpt2_split(cps, parts);
-    for (const auto& pr : parts) bpe(text.substr(offs[pr.first], offs[pr.second] - offs[pr.first]), ids);
+    for (const auto& pr : parts) bpe(p + offs[pr.first], offs[pr.second] - offs[pr.first], ids);
   }
 
   // Tokenizer::encode_fast(text, add_special_tokens = false)
@@ -512,14 +551,20 @@ struct j1_tokenizer {
         ids.push_back(added[static_cast<size_t>(r.first)].id);
         continue;
       }
-      std::string piece = text.substr(r.second.first, r.second.second - r.second.first);
+      const char* p = text.data() + r.second.first;
+      const size_t n = r.second.second - r.second.first;
+      if ((!nfc || Nfc::simple(p, n)) && !has_norm_tokens) {  // nothing to normalise or match: no copy
+        encode_piece(p, n, ids);
+        continue;
+      }
+      std::string piece(p, n);
       if (nfc) nfc_tables().normalize(piece);
       split_added(piece, norm_by_byte, nrm);
       for (const auto& q : nrm) {
         if (q.first >= 0)
           ids.push_back(added[static_cast<size_t>(q.first)].id);
         else
-          encode_piece(piece.substr(q.second.first, q.second.second - q.second.first), ids);
+          encode_piece(piece.data() + q.second.first, q.second.second - q.second.first, ids);
       }
     }
   }
@@ -648,6 +693,7 @@ j1_status load_tokenizer(const std::string& text, std::unique_ptr<j1_tokenizer>&
   for (size_t i = 0; i < T->added.size(); ++i) {
     const unsigned char b0 = static_cast<unsigned char>(T->added[i].pattern[0]);
     (T->added[i].normalized ? T->norm_by_byte : T->raw_by_byte)[b0].push_back(i);
+    T->has_norm_tokens = T->has_norm_tokens || T->added[i].normalized;
   }
   out = std::move(T);
   return J1_OK;
@@ -795,16 +841,16 @@ j1_status j1_tokenizer_encode(const j1_tokenizer* t, const char* text, size_t le
 }
 
 j1_status j1_tokenizer_encode_batch(const j1_tokenizer* t, size_t n, const char* const* texts, const size_t* lens,
-                                    int32_t threads, uint32_t** ids_out, size_t* n_ids, size_t* total) {
-  if (!t || (n && (!texts || !lens || !ids_out || !n_ids))) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+                                    int32_t threads, uint32_t* ids, size_t cap, size_t* offsets) {
+  if (!t || !offsets || (n && (!texts || !lens))) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
   std::vector<std::vector<uint32_t>> res(n);
   std::atomic<size_t> next{0};
-  std::atomic<int> bad{-1};
+  std::atomic<long> bad{-1};
   auto work = [&]() {
     for (size_t i = next++; i < n; i = next++) {
       const std::string s(texts[i] ? texts[i] : "", lens[i]);
       if (!valid_utf8(s)) {
-        bad = static_cast<int>(i);
+        bad = static_cast<long>(i);
         continue;
       }
       t->encode(s, res[i]);
@@ -819,14 +865,12 @@ j1_status j1_tokenizer_encode_batch(const j1_tokenizer* t, size_t n, const char*
     for (auto& th : pool) th.join();
   }
   if (bad >= 0) return set_error(J1_ERR_INVALID_ARG, "text " + std::to_string(bad) + " is not valid UTF-8");
-  size_t sum = 0;
-  for (size_t i = 0; i < n; ++i) {
-    n_ids[i] = res[i].size();
-    sum += res[i].size();
-  }
-  if (total) *total = sum;
+  offsets[0] = 0;
+  for (size_t i = 0; i < n; ++i) offsets[i + 1] = offsets[i] + res[i].size();
+  if (offsets[n] > cap || (!ids && offsets[n]))
+    return set_error(J1_ERR_INVALID_ARG, "ids buffer too small (" + std::to_string(offsets[n]) + " needed)");
   for (size_t i = 0; i < n; ++i)
-    if (ids_out[i] && !res[i].empty()) std::memcpy(ids_out[i], res[i].data(), res[i].size() * 4);
+    if (!res[i].empty()) std::memcpy(ids + offsets[i], res[i].data(), res[i].size() * 4);
   return J1_OK;
 }
 

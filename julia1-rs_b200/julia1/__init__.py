@@ -184,7 +184,7 @@ def lib():
     L.j1_tokenizer_token_to_id.restype = C.c_int64
     L.j1_tokenizer_encode.argtypes = [C.c_void_p, C.c_char_p, C.c_size_t, u32p, C.c_size_t, C.POINTER(C.c_size_t)]
     L.j1_tokenizer_encode_batch.argtypes = [C.c_void_p, C.c_size_t, C.POINTER(C.c_char_p), C.POINTER(C.c_size_t),
-                                            C.c_int32, C.POINTER(u32p), C.POINTER(C.c_size_t), C.POINTER(C.c_size_t)]
+                                            C.c_int32, u32p, C.c_size_t, C.POINTER(C.c_size_t)]
     L.j1_text_encoder_load.argtypes = [C.c_char_p, C.c_int32, C.c_int32, C.c_int32, C.c_int64, C.c_int64,
                                        C.POINTER(C.c_void_p)]
     L.j1_text_encoder_destroy.argtypes = [C.c_void_p]
@@ -765,21 +765,24 @@ class Tokenizer:
                                         C.byref(n)))
         return out[:n.value].tolist()
 
-    def encode_batch(self, texts: Sequence[str], threads: int = 1) -> List[List[int]]:
+    def encode_batch(self, texts: Sequence[str], threads: int = 1, flat: bool = False):
+        """Encode several texts on `threads` host threads. Returns a list of id lists, or with
+        flat=True the (ids, offsets) arrays as the C ABI writes them."""
         bs = [t.encode() for t in texts]
         n = len(bs)
         if n == 0:
-            return []
+            return (np.zeros(0, np.uint32), np.zeros(1, np.uint64)) if flat else []
         arr = (C.c_char_p * n)(*bs)
         lens = (C.c_size_t * n)(*[len(b) for b in bs])
-        nids = (C.c_size_t * n)()
-        total = C.c_size_t()
-        null = (C.POINTER(C.c_uint32) * n)()
-        check(lib().j1_tokenizer_encode_batch(self._h, n, arr, lens, int(threads), null, nids, C.byref(total)))
-        bufs = [np.zeros(max(int(nids[i]), 1), np.uint32) for i in range(n)]
-        ptrs = (C.POINTER(C.c_uint32) * n)(*[b.ctypes.data_as(C.POINTER(C.c_uint32)) for b in bufs])
-        check(lib().j1_tokenizer_encode_batch(self._h, n, arr, lens, int(threads), ptrs, nids, C.byref(total)))
-        return [bufs[i][:int(nids[i])].tolist() for i in range(n)]
+        cap = sum(len(b) for b in bs) + n + 16
+        ids = np.zeros(cap, np.uint32)
+        offs = np.zeros(n + 1, np.uint64)
+        check(lib().j1_tokenizer_encode_batch(self._h, n, arr, lens, int(threads),
+                                              ids.ctypes.data_as(C.POINTER(C.c_uint32)), cap,
+                                              offs.ctypes.data_as(C.POINTER(C.c_size_t))))
+        if flat:
+            return ids[:int(offs[-1])], offs
+        return [ids[int(offs[i]):int(offs[i + 1])].tolist() for i in range(n)]
 
 
 @dataclass

