@@ -308,6 +308,27 @@ J1_API j1_status j1_text_encoder_encode(j1_text_encoder* enc, const char* state,
                                         uint8_t qtype, uint32_t* ids, size_t cap, size_t* ids_len, uint32_t* markers,
                                         int32_t* truncated);
 
+/* A text request (Request, src/request.rs:77-82; the state already rendered). */
+typedef struct j1_text_request {
+  const char* state;
+  int32_t state_is_json;
+  const char* question;
+  const char* const* options;
+  size_t n_options;
+  uint8_t qtype; /* 0 choice, 1 score, 2 noul */
+} j1_text_request;
+/* Engine::encode's parallel Encoder::encode (src/engine.rs:183-188) on `threads` host threads:
+ * row i's ids are ids[offsets[i] .. offsets[i + 1]) and its markers markers[moffsets[i] ..];
+ * cap = n * max_length and mcap = sum(n_options) always suffice; truncated[n] may be NULL.
+ * The first failing row is reported as "JSONL line <i + 1>: ...". */
+J1_API j1_status j1_text_encoder_encode_batch(j1_text_encoder* enc, size_t n, const j1_text_request* rows,
+                                              int32_t threads, uint32_t* ids, size_t cap, size_t* offsets,
+                                              uint32_t* markers, size_t mcap, size_t* moffsets, int32_t* truncated);
+/* Engine::logits (src/engine.rs:236-243) on text requests: Request::validate, the parallel
+ * encode above, logits_encoded. logits_out: sum(n_options) floats, row after row. */
+J1_API j1_status j1_engine_logits_text(j1_engine* engine, j1_text_encoder* enc, size_t n, const j1_text_request* rows,
+                                       int32_t threads, float* logits_out);
+
 /* The tokens of a request's pieces with the text rules of Encoder::sequence (mask text
  * refused in strict mode, else replaced by a space; head "<qtype> question: <question>",
  * each " <option>", the state): ids = head | option 0 | ... | option n-1 | state, with

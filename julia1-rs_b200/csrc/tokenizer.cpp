@@ -990,6 +990,102 @@ j1_status j1_text_encoder_encode(j1_text_encoder* e, const char* state, int32_t 
   return J1_OK;
 }
 
+j1_status j1_text_encoder_encode_batch(j1_text_encoder* e, size_t n, const j1_text_request* rows, int32_t threads,
+                                      uint32_t* ids, size_t cap, size_t* offsets, uint32_t* markers, size_t mcap,
+                                      size_t* moffsets, int32_t* truncated) {
+  if (!e || !offsets || !moffsets || (n && !rows)) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+  struct Out {
+    std::vector<uint32_t> ids, markers;
+    int32_t truncated = 0;
+    j1_status status = J1_OK;
+    std::string err;
+  };
+  std::vector<Out> res(n);
+  const size_t row_cap = static_cast<size_t>(std::max(e->opts.max_length, 1));
+  std::atomic<size_t> next{0};
+  auto work = [&]() {
+    for (size_t i = next++; i < n; i = next++) {
+      const j1_text_request& r = rows[i];
+      Out& o = res[i];
+      o.ids.resize(row_cap);
+      o.markers.resize(std::max<size_t>(r.n_options, 1));
+      size_t len = 0;
+      o.status = j1_text_encoder_encode(e, r.state, r.state_is_json, r.question, r.options, r.n_options, r.qtype,
+                                        o.ids.data(), o.ids.size(), &len, o.markers.data(), &o.truncated);
+      if (o.status) {
+        char buf[512];
+        j1_last_error(buf, sizeof(buf));  // the message is thread-local: keep it with the row
+        o.err = buf;
+        continue;
+      }
+      o.ids.resize(len);
+      o.markers.resize(r.n_options);
+    }
+  };
+  const int nt = std::max(1, std::min<int>(threads > 0 ? threads : 1, static_cast<int>(std::max<size_t>(n, 1))));
+  if (nt == 1) {
+    work();
+  } else {
+    std::vector<std::thread> pool;
+    for (int k = 0; k < nt; ++k) pool.emplace_back(work);
+    for (auto& th : pool) th.join();
+  }
+  for (size_t i = 0; i < n; ++i)  // the first failing row, as an in-order encode would report it
+    if (res[i].status) return set_error(res[i].status, "JSONL line " + std::to_string(i + 1) + ": " + res[i].err);
+  offsets[0] = moffsets[0] = 0;
+  for (size_t i = 0; i < n; ++i) {
+    offsets[i + 1] = offsets[i] + res[i].ids.size();
+    moffsets[i + 1] = moffsets[i] + res[i].markers.size();
+  }
+  if (offsets[n] > cap || moffsets[n] > mcap || (offsets[n] && !ids) || (moffsets[n] && !markers))
+    return set_error(J1_ERR_INVALID_ARG, "output arrays too small (" + std::to_string(offsets[n]) + " ids, " +
+                                             std::to_string(moffsets[n]) + " markers needed)");
+  for (size_t i = 0; i < n; ++i) {
+    if (!res[i].ids.empty()) std::memcpy(ids + offsets[i], res[i].ids.data(), res[i].ids.size() * 4);
+    if (!res[i].markers.empty()) std::memcpy(markers + moffsets[i], res[i].markers.data(), res[i].markers.size() * 4);
+    if (truncated) truncated[i] = res[i].truncated;
+  }
+  return J1_OK;
+}
+
+j1_status j1_engine_logits_text(j1_engine* engine, j1_text_encoder* e, size_t n, const j1_text_request* rows,
+                                int32_t threads, float* logits_out) {
+  if (!engine || !e) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+  if (n == 0) return J1_OK;
+  if (!rows || !logits_out) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+  // Request::validate for every row before any encoding (src/engine.rs:183-188)
+  for (size_t i = 0; i < n; ++i) {
+    const j1_text_request& r = rows[i];
+    bool empty = r.n_options && !r.options;
+    for (size_t k = 0; k < r.n_options && !empty; ++k) empty = !r.options[k] || !r.options[k][0];
+    if (r.n_options < 2 || r.n_options > 20 || empty)
+      return set_error(J1_ERR_INVALID_ARG, "JSONL line " + std::to_string(i + 1) +
+                                               ": options must contain 2–20 nonempty rendered descriptions");
+    if (r.qtype == 2 && r.n_options != 2)
+      return set_error(J1_ERR_INVALID_ARG,
+                       "JSONL line " + std::to_string(i + 1) + ": noul options must be ordered [false, true]");
+  }
+  if (e->opts.max_length > j1_engine_max_length(engine))
+    return set_error(J1_ERR_INVALID_ARG, "encoder max_length exceeds the engine's max_length");
+  const size_t cap = n * static_cast<size_t>(std::max(e->opts.max_length, 1));
+  size_t mcap = 0;
+  for (size_t i = 0; i < n; ++i) mcap += rows[i].n_options;
+  std::vector<uint32_t> ids(cap), markers(std::max<size_t>(mcap, 1));
+  std::vector<size_t> offs(n + 1), moffs(n + 1);
+  if (j1_status s = j1_text_encoder_encode_batch(e, n, rows, threads, ids.data(), cap, offs.data(), markers.data(),
+                                                 mcap, moffs.data(), nullptr))
+    return s;
+  std::vector<uint32_t> lens(n), nmark(n);
+  std::vector<uint8_t> qt(n);
+  for (size_t i = 0; i < n; ++i) {
+    lens[i] = static_cast<uint32_t>(offs[i + 1] - offs[i]);
+    nmark[i] = static_cast<uint32_t>(moffs[i + 1] - moffs[i]);
+    qt[i] = rows[i].qtype;
+  }
+  return j1_engine_logits_encoded(engine, n, ids.data(), lens.data(), markers.data(), nmark.data(), qt.data(),
+                                  logits_out);
+}
+
 j1_status j1_text_encoder_request_tokens(j1_text_encoder* e, const char* state, const char* question,
                                          const char* const* options, size_t n_options, uint8_t qtype, uint32_t* ids,
                                          size_t cap, size_t* total, uint32_t* piece_lens) {

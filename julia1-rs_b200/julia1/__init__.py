@@ -37,7 +37,7 @@ EXPORTS = [
     "j1_tokenizer_load", "j1_tokenizer_from_json", "j1_tokenizer_destroy", "j1_tokenizer_token_to_id",
     "j1_tokenizer_encode", "j1_tokenizer_encode_batch", "j1_text_encoder_load", "j1_text_encoder_destroy",
     "j1_text_encoder_clear_cache", "j1_text_encoder_options", "j1_text_encoder_tokenize", "j1_text_encoder_encode",
-    "j1_text_encoder_request_tokens",
+    "j1_text_encoder_request_tokens", "j1_text_encoder_encode_batch", "j1_engine_logits_text",
 ]
 PROF_FAMILIES = 12
 
@@ -96,6 +96,11 @@ class J1RouterOptions(C.Structure):
 class J1RouteResult(C.Structure):
     _fields_ = [("index", C.c_uint32), ("n_candidates", C.c_uint32), ("candidates", C.c_uint32 * 20),
                 ("probabilities", C.c_double * 20), ("rounds", C.c_uint32), ("hierarchical", C.c_int32)]
+
+
+class J1TextRequest(C.Structure):
+    _fields_ = [("state", C.c_char_p), ("state_is_json", C.c_int32), ("question", C.c_char_p),
+                ("options", C.POINTER(C.c_char_p)), ("n_options", C.c_size_t), ("qtype", C.c_uint8)]
 
 
 SCORER_FN = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_size_t, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32),
@@ -200,6 +205,13 @@ def lib():
     L.j1_text_encoder_request_tokens.argtypes = [C.c_void_p, C.c_char_p, C.c_char_p, C.POINTER(C.c_char_p),
                                                  C.c_size_t, C.c_uint8, u32p, C.c_size_t, C.POINTER(C.c_size_t), u32p]
     L.j1_text_encoder_request_tokens.restype = C.c_int
+    L.j1_text_encoder_encode_batch.argtypes = [C.c_void_p, C.c_size_t, C.POINTER(J1TextRequest), C.c_int32, u32p,
+                                               C.c_size_t, C.POINTER(C.c_size_t), u32p, C.c_size_t,
+                                               C.POINTER(C.c_size_t), C.POINTER(C.c_int32)]
+    L.j1_text_encoder_encode_batch.restype = C.c_int
+    L.j1_engine_logits_text.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, C.POINTER(J1TextRequest), C.c_int32,
+                                        f32p]
+    L.j1_engine_logits_text.restype = C.c_int
     L.j1_op_gemm.argtypes = [C.POINTER(J1GemmArgs), C.c_void_p, C.c_int]
     L.j1_op_attention.argtypes = [C.c_void_p, C.c_int64, C.c_int32, u32p, u32p, C.c_size_t, C.c_int32, C.c_void_p,
                                   C.c_void_p, C.c_int]
@@ -588,10 +600,20 @@ def _check_text(rows: Sequence["Request"], line_prefix: bool):
                                         % (i + 1)) if line_prefix else "Options must be nonempty strings")
 
 
-def _engine_logits(self, rows: Sequence["Request"], text_encoder: "TextEncoder") -> List[List[float]]:
-    """Engine::logits (src/engine.rs:236-243) on text requests through the text encoder."""
-    _check_text(rows, True)
-    return self.logits_tokenized([text_encoder.tokenize_request(r) for r in rows], text_encoder.options())
+def _engine_logits(self, rows: Sequence["Request"], text_encoder: "TextEncoder", threads: int = 0) -> List[List[float]]:
+    """Engine::logits (src/engine.rs:236-243) on text requests: validate, encode in parallel
+    on `threads` host threads (0 = all cores), logits_encoded."""
+    if len(rows) == 0:
+        return []
+    arr, keep = TextEncoder._text_rows(rows)
+    out = np.zeros(sum(len(r.options) for r in rows), np.float32)
+    check(lib().j1_engine_logits_text(self._h, text_encoder._h, len(rows), arr, int(threads or os.cpu_count() or 1),
+                                      out.ctypes.data_as(C.POINTER(C.c_float))))
+    res, k = [], 0
+    for r in rows:
+        res.append(list(map(float, out[k:k + len(r.options)])))
+        k += len(r.options)
+    return res
 
 
 Engine.logits = _engine_logits
@@ -841,6 +863,37 @@ class TextEncoder:
         check(lib().j1_text_encoder_tokenize(self._h, b, len(b), out.ctypes.data_as(C.POINTER(C.c_uint32)), cap,
                                              C.byref(n)))
         return out[:n.value].tolist()
+
+    @staticmethod
+    def _text_rows(rows: Sequence["Request"]):
+        keep = []
+        arr = (J1TextRequest * max(len(rows), 1))()
+        for i, r in enumerate(rows):
+            opts = (C.c_char_p * max(len(r.options), 1))(*[x.encode() for x in r.options])
+            st, q = r.state.encode(), r.question.encode()
+            keep += [opts, st, q]
+            arr[i] = J1TextRequest(st, int(bool(r.state_is_json)), q, opts, len(r.options), r.qtype_id())
+        return arr, keep
+
+    def encode_batch(self, rows: Sequence["Request"], threads: int = 1):
+        """Engine::encode's parallel Encoder::encode -> [(Encoded, truncated)] in row order."""
+        n = len(rows)
+        if n == 0:
+            return []
+        arr, keep = self._text_rows(rows)
+        o = self.options()
+        cap = n * o.max_length
+        mcap = max(sum(len(r.options) for r in rows), 1)
+        ids, mk = np.zeros(cap, np.uint32), np.zeros(mcap, np.uint32)
+        offs, moffs, tr = np.zeros(n + 1, np.uint64), np.zeros(n + 1, np.uint64), np.zeros(n, np.int32)
+        check(lib().j1_text_encoder_encode_batch(self._h, n, arr, int(threads),
+                                                 ids.ctypes.data_as(C.POINTER(C.c_uint32)), cap,
+                                                 offs.ctypes.data_as(C.POINTER(C.c_size_t)),
+                                                 mk.ctypes.data_as(C.POINTER(C.c_uint32)), mcap,
+                                                 moffs.ctypes.data_as(C.POINTER(C.c_size_t)),
+                                                 tr.ctypes.data_as(C.POINTER(C.c_int32))))
+        return [(Encoded(ids[int(offs[i]):int(offs[i + 1])].copy(), mk[int(moffs[i]):int(moffs[i + 1])].copy(),
+                         rows[i].qtype_id()), bool(tr[i])) for i in range(n)]
 
     def tokenize_request(self, r: "Request") -> TokenizedRequest:
         """The request's head, option and state tokens under Encoder::sequence's text rules."""

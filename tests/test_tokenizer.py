@@ -178,3 +178,23 @@ def test_text_requests_through_router(enc_dir):
     assert [g.candidates for g in got] == [w.candidates for w in want]
     with pytest.raises(j1.J1Error, match="Options must be nonempty strings"):
         router.route_many([j1.Request("s", "q", ["a", ""])])
+
+
+def test_text_encoder_batch_equals_single(enc_dir):
+    """Engine::encode's parallel encode: the batch on 4 threads gives each row's Encoder::encode."""
+    enc = j1.TextEncoder.load(enc_dir, max_length=128, head_length=48)
+    rng = random.Random(12)
+    words = ["win", "lose", "gold", "wood", "café", "Ελλάδα", "日本語", "[MASK]", "lol", "don't"]
+    rows = [j1.Request(" ".join(rng.choice(words) for _ in range(rng.randint(0, 80))),
+                       " ".join(rng.choice(words) for _ in range(rng.randint(1, 6))),
+                       [" ".join(rng.choice(words) for _ in range(rng.randint(1, 3))) for _ in range(rng.randint(2, 8))],
+                       qtype=rng.choice(["choice", "score"]))
+            for _ in range(200)]
+    got = enc.encode_batch(rows, threads=4)
+    enc.clear_cache()
+    for (e, tr), r in zip(got, rows):
+        want, wtr = enc.encode(r.state, r.question, r.options, r.qtype)
+        assert e.ids.tolist() == want.ids.tolist() and e.markers.tolist() == want.markers.tolist() and tr == wtr
+    strict = j1.TextEncoder.load(enc_dir, max_length=128, head_length=48, strict=True)
+    with pytest.raises(j1.J1Error, match="JSONL line 2: Reserved model marker in request"):
+        strict.encode_batch([j1.Request("s", "q", ["a", "b"]), j1.Request("s [MASK]", "q", ["a", "b"])], threads=2)
