@@ -480,6 +480,36 @@ class Engine:
             o += n
         return res
 
+    def logits_tokenized(self, rows: Sequence["TokenizedRequest"], enc: "EncoderOptions") -> List[List[float]]:
+        """Engine::logits (src/engine.rs:236-243) on tokenized requests."""
+        if len(rows) == 0:
+            return []
+        rq = _Requests(rows)
+        o = enc.c()
+        out = np.zeros(sum(len(r.options) for r in rows), np.float32)
+        check(lib().j1_engine_logits_tokenized(self._h, C.byref(o), len(rows), rq.arr,
+                                               out.ctypes.data_as(C.POINTER(C.c_float))))
+        res, k = [], 0
+        for r in rows:
+            res.append(list(map(float, out[k:k + len(r.options)])))
+            k += len(r.options)
+        return res
+
+    def logits(self, rows: Sequence["Request"], text_encoder: "TextEncoder", threads: int = 0) -> List[List[float]]:
+        """Engine::logits (src/engine.rs:236-243) on text requests: validate, encode in parallel
+        on `threads` host threads (0 = all cores), logits_encoded."""
+        if len(rows) == 0:
+            return []
+        arr, keep = TextEncoder._text_rows(rows)
+        out = np.zeros(sum(len(r.options) for r in rows), np.float32)
+        check(lib().j1_engine_logits_text(self._h, text_encoder._h, len(rows), arr, int(threads or os.cpu_count() or 1),
+                                          out.ctypes.data_as(C.POINTER(C.c_float))))
+        res, k = [], 0
+        for r in rows:
+            res.append(list(map(float, out[k:k + len(r.options)])))
+            k += len(r.options)
+        return res
+
     def predict_encoded(self, rows, probabilities=False):
         """Engine::predict semantics on encoded rows: argmax index (+ softmax probabilities)."""
         out = []
@@ -574,25 +604,6 @@ def encode_sequence(req: TokenizedRequest, opts: EncoderOptions):
     return Encoded(ids[:n.value].copy(), mk[:len(req.options)].copy(), int(req.qtype)), bool(tr.value)
 
 
-def _engine_logits_tokenized(self, rows: Sequence[TokenizedRequest], enc: EncoderOptions) -> List[List[float]]:
-    """Engine::logits (src/engine.rs:236-243) on tokenized requests."""
-    if len(rows) == 0:
-        return []
-    rq = _Requests(rows)
-    o = enc.c()
-    out = np.zeros(sum(len(r.options) for r in rows), np.float32)
-    check(lib().j1_engine_logits_tokenized(self._h, C.byref(o), len(rows), rq.arr,
-                                           out.ctypes.data_as(C.POINTER(C.c_float))))
-    res, k = [], 0
-    for r in rows:
-        res.append(list(map(float, out[k:k + len(r.options)])))
-        k += len(r.options)
-    return res
-
-
-Engine.logits_tokenized = _engine_logits_tokenized
-
-
 def _check_text(rows: Sequence["Request"], line_prefix: bool):
     for i, r in enumerate(rows):
         if any(len(o) == 0 for o in r.options):
@@ -600,23 +611,6 @@ def _check_text(rows: Sequence["Request"], line_prefix: bool):
                                         % (i + 1)) if line_prefix else "Options must be nonempty strings")
 
 
-def _engine_logits(self, rows: Sequence["Request"], text_encoder: "TextEncoder", threads: int = 0) -> List[List[float]]:
-    """Engine::logits (src/engine.rs:236-243) on text requests: validate, encode in parallel
-    on `threads` host threads (0 = all cores), logits_encoded."""
-    if len(rows) == 0:
-        return []
-    arr, keep = TextEncoder._text_rows(rows)
-    out = np.zeros(sum(len(r.options) for r in rows), np.float32)
-    check(lib().j1_engine_logits_text(self._h, text_encoder._h, len(rows), arr, int(threads or os.cpu_count() or 1),
-                                      out.ctypes.data_as(C.POINTER(C.c_float))))
-    res, k = [], 0
-    for r in rows:
-        res.append(list(map(float, out[k:k + len(r.options)])))
-        k += len(r.options)
-    return res
-
-
-Engine.logits = _engine_logits
 
 
 def display_probabilities(values: Sequence[float]) -> List[float]:
