@@ -300,7 +300,7 @@ J1_API j1_status j1_text_encoder_options(const j1_text_encoder* enc, j1_encoder_
 /* Encoder::tokenize: the token-fragment cache in front of the tokenizer. */
 J1_API j1_status j1_text_encoder_tokenize(j1_text_encoder* enc, const char* text, size_t len, uint32_t* ids,
                                           size_t cap, size_t* n_ids);
-/* Encoder::encode: state (rendered; state_is_json only keys the cache like the reference),
+/* Encoder::encode: state (JSON text rendered by j1_json_dumps when state_is_json, as State::render),
  * question, options[n_options] (UTF-8, NUL-terminated), qtype -> ids (cap >= max_length),
  * markers[n_options], truncated. */
 J1_API j1_status j1_text_encoder_encode(j1_text_encoder* enc, const char* state, int32_t state_is_json,
@@ -308,7 +308,15 @@ J1_API j1_status j1_text_encoder_encode(j1_text_encoder* enc, const char* state,
                                         uint8_t qtype, uint32_t* ids, size_t cap, size_t* ids_len, uint32_t* markers,
                                         int32_t* truncated);
 
-/* A text request (Request, src/request.rs:77-82; the state already rendered). */
+/* State::render of a JSON state (src/pyjson.rs): Python's json.dumps(value, ensure_ascii=False)
+ * byte for byte — ", " and ": " separators, key order kept, integer literals as written,
+ * other numbers as float.__repr__, the json module's escapes. *out_len is set even when cap
+ * is too small. */
+J1_API j1_status j1_json_dumps(const char* json, size_t len, char* out, size_t cap, size_t* out_len);
+
+/* A text request (Request, src/request.rs:77-82). With state_is_json the state is JSON text
+ * (an object or an array, Request::validate), rendered with j1_json_dumps before tokenizing
+ * (State::render); otherwise it is the state text itself. */
 typedef struct j1_text_request {
   const char* state;
   int32_t state_is_json;

@@ -15,7 +15,7 @@ struct Json {
   enum Kind { Null, Bool, Number, String, Array, Object } kind = Null;
   bool b = false;
   double num = 0.0;
-  std::string str;
+  std::string str;  // String: the text; Number: the literal as written
   std::vector<Json> arr;
   std::vector<std::pair<std::string, Json>> obj;  // insertion order kept
 
@@ -216,6 +216,7 @@ class JsonParser {
       out.kind = Json::Number;
       out.num = std::strtod(tok.c_str(), &e);
       if (!e || *e) return fail("bad number");
+      out.str = tok;  // the literal as written (integers beyond double precision, int vs float)
       return true;
     }
     return fail("unexpected character");

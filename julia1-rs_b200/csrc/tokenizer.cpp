@@ -21,6 +21,8 @@
 // request, and Encoder::sequence (j1_encode_sequence).
 #include <algorithm>
 #include <atomic>
+#include <charconv>
+#include <cmath>
 #include <cstring>
 #include <fstream>
 #include <list>
@@ -749,6 +751,127 @@ std::string replace_all(const std::string& s, const std::string& from, const std
 
 const char* qtype_name(uint8_t q) { return q == 0 ? "choice" : q == 1 ? "score" : "noul"; }
 
+// ------------------------------------------------------------------ State::render for JSON states
+// Python's json.dumps(value, ensure_ascii=False), byte for byte (src/pyjson.rs): ", " and
+// ": " separators, key order kept, integers as written, other numbers as float.__repr__,
+// the json module's escapes.
+
+// float.__repr__: the shortest digits that round-trip, fixed notation for decimal
+// exponents -4 < point <= 16, else d.ddde+XX.
+std::string float_repr(double v) {
+  if (std::isnan(v)) return "NaN";
+  if (std::isinf(v)) return v > 0 ? "Infinity" : "-Infinity";
+  if (v == 0.0) return std::signbit(v) ? "-0.0" : "0.0";
+  char buf[64];
+  const auto res = std::to_chars(buf, buf + sizeof(buf), std::fabs(v), std::chars_format::scientific);
+  const std::string sci(buf, res.ptr);
+  const size_t epos = sci.find('e');
+  std::string digits;
+  for (size_t i = 0; i < epos; ++i)
+    if (sci[i] != '.') digits += sci[i];
+  const int exponent = std::atoi(sci.c_str() + epos + 1);
+  const int point = exponent + 1;  // v = 0.DIGITS x 10^point
+  const int n = static_cast<int>(digits.size());
+  std::string out = v < 0 ? "-" : "";
+  if (-4 < point && point <= 16) {
+    if (point <= 0) {
+      out += "0.";
+      out.append(static_cast<size_t>(-point), '0');
+      out += digits;
+    } else if (point >= n) {
+      out += digits;
+      out.append(static_cast<size_t>(point - n), '0');
+      out += ".0";
+    } else {
+      out += digits.substr(0, static_cast<size_t>(point));
+      out += '.';
+      out += digits.substr(static_cast<size_t>(point));
+    }
+  } else {
+    out += digits.substr(0, 1);
+    if (n > 1) {
+      out += '.';
+      out += digits.substr(1);
+    }
+    const int e = point - 1;
+    char eb[16];
+    std::snprintf(eb, sizeof(eb), "e%c%02d", e < 0 ? '-' : '+', e < 0 ? -e : e);
+    out += eb;
+  }
+  return out;
+}
+
+void py_dumps_string(std::string& out, const std::string& s) {
+  out += '"';
+  for (unsigned char c : s) {
+    switch (c) {
+      case '"': out += "\\\""; break;
+      case '\\': out += "\\\\"; break;
+      case '\n': out += "\\n"; break;
+      case '\r': out += "\\r"; break;
+      case '\t': out += "\\t"; break;
+      case 0x08: out += "\\b"; break;
+      case 0x0C: out += "\\f"; break;
+      default:
+        if (c < 0x20) {
+          char b[8];
+          std::snprintf(b, sizeof(b), "\\u%04x", c);
+          out += b;
+        } else {
+          out += static_cast<char>(c);
+        }
+    }
+  }
+  out += '"';
+}
+
+void py_dumps(std::string& out, const Json& v) {
+  switch (v.kind) {
+    case Json::Null: out += "null"; break;
+    case Json::Bool: out += v.b ? "true" : "false"; break;
+    case Json::Number:
+      // the json module reads literals without '.', 'e' or 'E' as int, the rest as float
+      if (v.str.find_first_of(".eE") != std::string::npos)
+        out += float_repr(v.num);
+      else if (v.str == "-0")
+        out += '0';
+      else
+        out += v.str;
+      break;
+    case Json::String: py_dumps_string(out, v.str); break;
+    case Json::Array:
+      out += '[';
+      for (size_t i = 0; i < v.arr.size(); ++i) {
+        if (i) out += ", ";
+        py_dumps(out, v.arr[i]);
+      }
+      out += ']';
+      break;
+    case Json::Object:
+      out += '{';
+      for (size_t i = 0; i < v.obj.size(); ++i) {
+        if (i) out += ", ";
+        py_dumps_string(out, v.obj[i].first);
+        out += ": ";
+        py_dumps(out, v.obj[i].second);
+      }
+      out += '}';
+      break;
+  }
+}
+
+// State::render of a JSON state (Request::validate: an object or an array).
+j1_status render_json_state(const std::string& text, std::string& out) {
+  Json j;
+  std::string err;
+  if (!parse_json(text, j, err)) return set_error(J1_ERR_INVALID_ARG, "state is not valid JSON: " + err);
+  if (j.kind != Json::Object && j.kind != Json::Array)
+    return set_error(J1_ERR_INVALID_ARG, "state must be text/JSON and question must be text");
+  out.clear();
+  py_dumps(out, j);
+  return J1_OK;
+}
+
 // The text part of Encoder::sequence (src/encode.rs:138-150, 180): strict refusal of the mask
 // token's text, the text replaced by a space otherwise, and the tokens of the head
 // "<qtype> question: <question>", of each " <option>" and of the state.
@@ -967,8 +1090,14 @@ j1_status j1_text_encoder_encode(j1_text_encoder* e, const char* state, int32_t 
   }
   j1_text_encoder::Enc enc;
   if (!e->encodings->get(key, enc)) {
+    std::string rendered;
+    if (state_is_json) {  // State::render (src/request.rs:49-54)
+      if (j1_status s = render_json_state(st, rendered)) return s;
+    }
     std::vector<uint32_t> head, opt_ids, opt_lens, state_ids;
-    if (j1_status s = request_tokens(e, st, q, opts, qtype, head, opt_ids, opt_lens, state_ids)) return s;
+    if (j1_status s = request_tokens(e, state_is_json ? rendered : st, q, opts, qtype, head, opt_ids, opt_lens,
+                                     state_ids))
+      return s;
     j1_tokenized_request r{head.data(), head.size(), opt_ids.data(), opt_lens.data(), n_options,
                            state_ids.data(), state_ids.size(), qtype};
     enc.ids.assign(static_cast<size_t>(e->opts.max_length), 0);
@@ -987,6 +1116,20 @@ j1_status j1_text_encoder_encode(j1_text_encoder* e, const char* state, int32_t 
   std::memcpy(ids, enc.ids.data(), enc.ids.size() * 4);
   if (n_options) std::memcpy(markers, enc.markers.data(), n_options * 4);
   if (truncated) *truncated = enc.truncated;
+  return J1_OK;
+}
+
+j1_status j1_json_dumps(const char* json, size_t len, char* out, size_t cap, size_t* out_len) {
+  if ((!json && len) || !out_len) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+  Json j;
+  std::string err;
+  if (!parse_json(std::string(json ? json : "", len), j, err)) return set_error(J1_ERR_INVALID_ARG, "invalid JSON: " + err);
+  std::string s;
+  py_dumps(s, j);
+  *out_len = s.size();
+  if (s.size() > cap || (!out && !s.empty()))
+    return set_error(J1_ERR_INVALID_ARG, "output buffer too small (" + std::to_string(s.size()) + " bytes needed)");
+  if (!s.empty()) std::memcpy(out, s.data(), s.size());
   return J1_OK;
 }
 

@@ -37,7 +37,7 @@ EXPORTS = [
     "j1_tokenizer_load", "j1_tokenizer_from_json", "j1_tokenizer_destroy", "j1_tokenizer_token_to_id",
     "j1_tokenizer_encode", "j1_tokenizer_encode_batch", "j1_text_encoder_load", "j1_text_encoder_destroy",
     "j1_text_encoder_clear_cache", "j1_text_encoder_options", "j1_text_encoder_tokenize", "j1_text_encoder_encode",
-    "j1_text_encoder_request_tokens", "j1_text_encoder_encode_batch", "j1_engine_logits_text",
+    "j1_text_encoder_request_tokens", "j1_text_encoder_encode_batch", "j1_engine_logits_text", "j1_json_dumps",
 ]
 PROF_FAMILIES = 12
 
@@ -212,6 +212,8 @@ def lib():
     L.j1_engine_logits_text.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, C.POINTER(J1TextRequest), C.c_int32,
                                         f32p]
     L.j1_engine_logits_text.restype = C.c_int
+    L.j1_json_dumps.argtypes = [C.c_char_p, C.c_size_t, C.c_char_p, C.c_size_t, C.POINTER(C.c_size_t)]
+    L.j1_json_dumps.restype = C.c_int
     L.j1_op_gemm.argtypes = [C.POINTER(J1GemmArgs), C.c_void_p, C.c_int]
     L.j1_op_attention.argtypes = [C.c_void_p, C.c_int64, C.c_int32, u32p, u32p, C.c_size_t, C.c_int32, C.c_void_p,
                                   C.c_void_p, C.c_int]
@@ -801,9 +803,21 @@ class Tokenizer:
         return [ids[int(offs[i]):int(offs[i + 1])].tolist() for i in range(n)]
 
 
+def json_dumps(text: str) -> str:
+    """State::render of a JSON state (src/pyjson.rs): json.dumps(value, ensure_ascii=False)
+    of the JSON text, byte for byte."""
+    b = text.encode()
+    n = C.c_size_t()
+    lib().j1_json_dumps(b, len(b), None, 0, C.byref(n))
+    buf = C.create_string_buffer(n.value + 1)
+    check(lib().j1_json_dumps(b, len(b), buf, n.value + 1, C.byref(n)))
+    return buf.raw[:n.value].decode()
+
+
 @dataclass
 class Request:
-    """request::Request (src/request.rs:77-82): the state is passed rendered (State::render)."""
+    """request::Request (src/request.rs:77-82): `state` is the state text, or JSON text (an
+    object or an array) with state_is_json=True, rendered like State::render."""
     state: str
     question: str
     options: Sequence[str]
