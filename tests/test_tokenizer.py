@@ -198,3 +198,38 @@ def test_text_encoder_batch_equals_single(enc_dir):
     strict = j1.TextEncoder.load(enc_dir, max_length=128, head_length=48, strict=True)
     with pytest.raises(j1.J1Error, match="JSONL line 2: Reserved model marker in request"):
         strict.encode_batch([j1.Request("s", "q", ["a", "b"]), j1.Request("s [MASK]", "q", ["a", "b"])], threads=2)
+
+
+def test_tokenizer_and_encoder_shared_by_threads(enc_dir):
+    """One tokenizer / text encoder used from several host threads at once (per-thread BPE
+    caches, mutex-guarded LRU caches) gives the single-threaded results."""
+    import threading
+    tok = load("nfc")
+    enc = j1.TextEncoder.load(enc_dir, max_length=128, head_length=48)
+    data = json.load(open(os.path.join(GOLDEN, "tokenizer_nfc_cases.json"), encoding="utf-8"))
+    texts = [t for t, _ in data["cases"]]
+    want = [ids for _, ids in data["cases"]]
+    reqs = [j1.Request(t[:200], "which?", ["a b", "c d", "e"]) for t in texts[:100]]
+    want_rows = [enc.encode(r.state, r.question, r.options)[0].ids.tolist() for r in reqs]
+    enc.clear_cache()
+    errs = []
+
+    def work(k):
+        try:
+            order = list(range(len(texts)))
+            random.Random(k).shuffle(order)
+            for i in order:
+                assert tok.encode(texts[i]) == want[i]
+            rorder = list(range(len(reqs)))
+            random.Random(k + 100).shuffle(rorder)
+            for i in rorder:
+                assert enc.encode(reqs[i].state, reqs[i].question, reqs[i].options)[0].ids.tolist() == want_rows[i]
+        except Exception as e:  # noqa: BLE001
+            errs.append(e)
+
+    ts = [threading.Thread(target=work, args=(k,)) for k in range(6)]
+    for t in ts:
+        t.start()
+    for t in ts:
+        t.join()
+    assert not errs, errs[:1]
