@@ -346,6 +346,21 @@ J1_API j1_status j1_text_encoder_request_tokens(j1_text_encoder* enc, const char
                                                 const char* const* options, size_t n_options, uint8_t qtype,
                                                 uint32_t* ids, size_t cap, size_t* total, uint32_t* piece_lens);
 
+/* ------------------------------------------------------------ failure testing
+ * Host-side fault injection: the next `count` device allocations (J1_FAULT_ALLOC ->
+ * J1_ERR_OOM), kernel launches (J1_FAULT_LAUNCH -> J1_ERR_CUDA) or score readbacks
+ * (J1_FAULT_NAN -> J1_ERR_NONFINITE, Engine::forward's check, src/engine.rs:219-221) of the
+ * process fail; count 0 disarms. The environment variable J1_FAULT=alloc|launch|nan arms one
+ * at the first j1_model_create. Nothing is done to the GPU: an injected allocation or launch
+ * does not happen and injected nonfinite scores are written into the host copy. */
+enum { J1_FAULT_ALLOC = 1, J1_FAULT_LAUNCH = 2, J1_FAULT_NAN = 3 };
+J1_API void j1_inject_fault(int32_t kind, int32_t count);
+/* Device-side failure detection without a fault: one thread waits, with the library's
+ * bounded wait and a limit of limit_cycles (1e3..4e9), on an mbarrier nothing arrives at.
+ * Returns J1_ERR_DEVICE_TIMEOUT (site 99) when the timeout was detected and reported, as a
+ * forward's stuck wait would be; the context stays usable. */
+J1_API j1_status j1_selftest_device_timeout(int ordinal, int64_t limit_cycles);
+
 /* ------------------------------------------------------------ kernel-level ops
  * On caller device memory (e.g. torch tensors); `stream` is a cudaStream_t or NULL.
  * With sync != 0 the call waits for completion and reports device-side timeouts. */

@@ -106,6 +106,9 @@ int launch_gather_rows(const void* src, const int* idx, void* dst, int rows, int
 // dst = bf16(src) with an optional row permutation: dst row r <- src row perm(r) (GEGLU interleave).
 int launch_f32_to_bf16(const float* src, bf16* dst, long long rows, int cols, int geglu_inter, cudaStream_t stream);
 bool hidden_supported(int hidden);
+// Self-test of the bounded device waits: one thread waits (with a limit of `limit` cycles) on an
+// mbarrier nothing arrives at, records the timeout in *err and returns.
+int launch_wait_timeout_selftest(int* err, long long limit, cudaStream_t stream);
 
 // ------------------------------------------------------------------ TMA maps
 // 2D bf16 row-major [rows, cols] with row stride `ld` elements; 128B swizzle box (64 x box_rows).

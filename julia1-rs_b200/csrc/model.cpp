@@ -4,9 +4,14 @@
 
 #include <sys/stat.h>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include <algorithm>
+#include <atomic>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
+#include <limits>
 #include <memory>
 #include <unordered_map>
 
@@ -49,6 +54,20 @@ j1_status cuda_error(cudaError_t e, const char* what) {
 }
 
 size_t last_error_copy(char* buf, size_t cap) { return copy_out(t_last_error, buf, cap); }
+
+// Host-side fault injection (j1_inject_fault, or J1_FAULT=alloc|launch|nan at model
+// creation): the next `count` device allocations / kernel launches / score readbacks of
+// the process report a failure, so callers can test their error handling. Nothing is done
+// to the GPU: an injected allocation or launch simply does not happen, and injected
+// nonfinite scores are written into the host copy.
+std::atomic<int> g_fault[4];
+
+bool take_fault(int kind) {
+  int n = g_fault[kind].load();
+  while (n > 0)
+    if (g_fault[kind].compare_exchange_weak(n, n - 1)) return true;
+  return false;
+}
 
 }  // namespace j1rt
 
@@ -94,18 +113,24 @@ void prof_fold(j1_model* model) {
   model->prof_used = 0;
 }
 
+// One launch: an NVTX range named by its kernel family (profilers), optional per-family
+// CUDA-event timing (j1_model_profile), injected launch faults.
 #define J1_TRY_LAUNCH(fam, expr, what)                                                       \
   do {                                                                                       \
+    if (take_fault(J1_FAULT_LAUNCH)) return set_error(J1_ERR_CUDA, std::string(what) + ": injected launch failure"); \
     cudaEvent_t* ev_ = model->prof_on ? prof_slot(model, (fam)) : nullptr;                   \
+    nvtxRangePushA(j1_profile_family_name(fam));                                             \
     if (ev_) cudaEventRecord(ev_[0], model->stream);                                         \
     int rc_ = (expr);                                                                        \
-    if (rc_ != 0) return cuda_error(static_cast<cudaError_t>(rc_), what);                    \
     if (ev_) cudaEventRecord(ev_[1], model->stream);                                         \
+    nvtxRangePop();                                                                          \
+    if (rc_ != 0) return cuda_error(static_cast<cudaError_t>(rc_), what);                    \
     ++model->launches;                                                                       \
   } while (0)
 
 j1_status dalloc(j1_model* model, void** p, size_t bytes, std::vector<void*>& list) {
   *p = nullptr;
+  if (take_fault(J1_FAULT_ALLOC)) return set_error(J1_ERR_OOM, "cudaMalloc: out of device memory (injected)");
   cudaError_t e = cudaMalloc(p, bytes < 256 ? 256 : bytes);
   if (e != cudaSuccess) return cuda_error(e, "cudaMalloc");
   list.push_back(*p);
@@ -496,7 +521,8 @@ j1_status collect(j1_model* model, int slot, float* scores_out, size_t m) {
     return set_error(J1_ERR_DEVICE_TIMEOUT,
                      "device-side wait timed out (site " + std::to_string(code >> 16) + "); results discarded");
   }
-  const float* sc = model->scores_host[slot];
+  float* sc = model->scores_host[slot];
+  if (m && take_fault(J1_FAULT_NAN)) sc[0] = std::numeric_limits<float>::quiet_NaN();
   for (size_t i = 0; i < m; ++i)
     if (!std::isfinite(sc[i])) return set_error(J1_ERR_NONFINITE, "Inference returned nonfinite logits");
   if (m) std::memcpy(scores_out, sc, m * 4);
@@ -815,7 +841,40 @@ j1_status j1_config_load(const char* ckpt_dir, j1_config* out) {
   return J1_OK;
 }
 
+void j1_inject_fault(int32_t kind, int32_t count) {
+  if (kind >= J1_FAULT_ALLOC && kind <= J1_FAULT_NAN) g_fault[kind] = count > 0 ? count : 0;
+}
+
+j1_status j1_selftest_device_timeout(int ordinal, int64_t limit_cycles) {
+  int n = 0;
+  J1_TRY_CUDA(cudaGetDeviceCount(&n), "cudaGetDeviceCount");
+  if (ordinal < 0 || ordinal >= n) return set_error(J1_ERR_INVALID_ARG, "no such device");
+  if (limit_cycles < 1000 || limit_cycles > 4000000000LL)
+    return set_error(J1_ERR_INVALID_ARG, "limit_cycles must be in [1e3, 4e9]");
+  J1_TRY_CUDA(cudaSetDevice(ordinal), "cudaSetDevice");
+  int* err = nullptr;
+  J1_TRY_CUDA(cudaMalloc(&err, 4), "cudaMalloc");
+  int code = 0;
+  cudaError_t e = cudaMemset(err, 0, 4);
+  if (e == cudaSuccess) e = static_cast<cudaError_t>(launch_wait_timeout_selftest(err, limit_cycles, nullptr));
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaMemcpy(&code, err, 4, cudaMemcpyDeviceToHost);
+  cudaFree(err);
+  if (e != cudaSuccess) return cuda_error(e, "device timeout self-test");
+  if (code == 0) return set_error(J1_ERR_CUDA, "device timeout self-test: the wait did not time out");
+  return set_error(J1_ERR_DEVICE_TIMEOUT,
+                   "device-side wait timed out (site " + std::to_string(code >> 16) + "); self-test");
+}
+
 j1_status j1_model_create(const char* ckpt_dir, int ordinal, j1_model** out) {
+  // J1_FAULT=alloc|launch|nan arms one injected fault for the process (j1_inject_fault)
+  if (const char* f = std::getenv("J1_FAULT")) {
+    static std::atomic<bool> armed{false};
+    if (!armed.exchange(true)) {
+      const std::string k(f);
+      j1_inject_fault(k == "alloc" ? J1_FAULT_ALLOC : k == "launch" ? J1_FAULT_LAUNCH : k == "nan" ? J1_FAULT_NAN : 0, 1);
+    }
+  }
   j1_status s = create_model(ckpt_dir, ordinal, out);
   return s;
 }

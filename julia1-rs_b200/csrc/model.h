@@ -2,6 +2,7 @@
 #pragma once
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -14,6 +15,9 @@ namespace j1rt {
 
 j1_status set_error(j1_status s, const std::string& msg);
 j1_status cuda_error(cudaError_t e, const char* what);
+// j1_inject_fault state: remaining injected faults per kind (J1_FAULT_*).
+extern std::atomic<int> g_fault[4];
+bool take_fault(int kind);
 
 // Restores the calling thread's current device on scope exit.
 class DeviceGuard {

@@ -84,6 +84,25 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// mbar_wait with a run-time limit instead of J1_WAIT_CYCLES (the device timeout self-test).
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err,
+                                              int site, long long limit) {
+  const long long t0 = clock64();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_test(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if ((it & 255u) == 0 && err && *reinterpret_cast<volatile int*>(err) != 0) {
+      *abort_flag = 1;
+      return false;
+    }
+    if (clock64() - t0 > limit) {
+      *abort_flag = 1;
+      if (err) atomicCAS(err, 0, 1 | (site << 16));
+      return false;
+    }
+  }
+}
+
 // Generic-proxy smem writes -> visible to the async proxy (tensor core / TMA).
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

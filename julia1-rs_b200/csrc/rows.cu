@@ -194,4 +194,23 @@ int launch_f32_to_bf16(const float* src, bf16* dst, long long rows, int cols, in
   return static_cast<int>(cudaGetLastError());
 }
 
+namespace {
+__global__ void wait_timeout_selftest_kernel(int* err, long long limit) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait_for(&bar, 0, &abort_flag, err, 99, limit);  // nothing ever arrives
+}
+}  // namespace
+
+int launch_wait_timeout_selftest(int* err, long long limit, cudaStream_t stream) {
+  wait_timeout_selftest_kernel<<<1, 32, 0, stream>>>(err, limit);
+  return static_cast<int>(cudaGetLastError());
+}
+
 }  // namespace j1rt

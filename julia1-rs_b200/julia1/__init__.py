@@ -38,7 +38,9 @@ EXPORTS = [
     "j1_tokenizer_encode", "j1_tokenizer_encode_batch", "j1_text_encoder_load", "j1_text_encoder_destroy",
     "j1_text_encoder_clear_cache", "j1_text_encoder_options", "j1_text_encoder_tokenize", "j1_text_encoder_encode",
     "j1_text_encoder_request_tokens", "j1_text_encoder_encode_batch", "j1_engine_logits_text", "j1_json_dumps",
+    "j1_inject_fault", "j1_selftest_device_timeout",
 ]
+FAULT_ALLOC, FAULT_LAUNCH, FAULT_NAN = 1, 2, 3
 PROF_FAMILIES = 12
 
 EPI_BF16, EPI_QKV_ROPE, EPI_GEGLU, EPI_RESID_LN, EPI_RESID, EPI_SCORER = range(6)
@@ -214,6 +216,10 @@ def lib():
     L.j1_engine_logits_text.restype = C.c_int
     L.j1_json_dumps.argtypes = [C.c_char_p, C.c_size_t, C.c_char_p, C.c_size_t, C.POINTER(C.c_size_t)]
     L.j1_json_dumps.restype = C.c_int
+    L.j1_inject_fault.argtypes = [C.c_int32, C.c_int32]
+    L.j1_inject_fault.restype = None
+    L.j1_selftest_device_timeout.argtypes = [C.c_int, C.c_int64]
+    L.j1_selftest_device_timeout.restype = C.c_int
     L.j1_op_gemm.argtypes = [C.POINTER(J1GemmArgs), C.c_void_p, C.c_int]
     L.j1_op_attention.argtypes = [C.c_void_p, C.c_int64, C.c_int32, u32p, u32p, C.c_size_t, C.c_int32, C.c_void_p,
                                   C.c_void_p, C.c_int]
@@ -801,6 +807,18 @@ class Tokenizer:
         if flat:
             return ids[:int(offs[-1])], offs
         return [ids[int(offs[i]):int(offs[i + 1])].tolist() for i in range(n)]
+
+
+def inject_fault(kind: int, count: int = 1):
+    """Host-side fault injection (j1_inject_fault): the next `count` device allocations
+    (FAULT_ALLOC), kernel launches (FAULT_LAUNCH) or score readbacks (FAULT_NAN) fail."""
+    lib().j1_inject_fault(int(kind), int(count))
+
+
+def selftest_device_timeout(ordinal: int = 0, limit_cycles: int = 2_000_000) -> int:
+    """Bounded device wait on a barrier nothing arrives at; returns the status
+    (DEVICE_TIMEOUT when the timeout was detected and reported)."""
+    return int(lib().j1_selftest_device_timeout(int(ordinal), int(limit_cycles)))
 
 
 def json_dumps(text: str) -> str:
