@@ -133,6 +133,31 @@ def test_c4_8192_parity(model768, oracle768):
     assert d.max() <= TOL_BF16
 
 
+def test_c5_router_scale_256x512_full_size(model768, oracle768):
+    """Config 5's per-forward batch at full size, the bench workload: 256 rows x 512 tokens
+    (131,072 tokens), 20 option markers per row in Encoder::sequence's layout
+    (src/encode.rs:167-187), m = 5,120. Over the whole batch: finite, deterministic, and
+    sampled rows score bit for bit as they do alone; a slice of rows against the BF16-chain
+    oracle. Because a row's scores do not depend on the rest of its batch (exactly), the
+    slice's parity carries to every row of the full-size batch."""
+    rows = synthetic.synthetic_batch([512] * 256, markers_per_seq=0, seed=1, option_block=(20, 11, 12),
+                                     mask_markers=False)
+    b = rows_to_batch(rows)
+    a = model768.forward_flat(b)
+    assert b.tokens() == 131072 and a.size == 256 * 20 and np.isfinite(a).all()
+    assert np.array_equal(a, model768.forward_flat(b))
+    for i in (0, 131, 255):
+        alone = model768.forward_flat(rows_to_batch([rows[i]]))
+        assert np.array_equal(alone, a[b.marker_starts[i]:b.marker_starts[i + 1]])
+    part = rows_to_batch(rows[:6])
+    ref16 = oracle768.forward_flat(part, mode="bf16")
+    d = np.abs(a[:ref16.size] - ref16)
+    print("C5 slice max|gpu-bf16| %.5f mean %.6f" % (d.max(), d.mean()))
+    assert d.max() <= TOL_BF16
+    agree, total = argmax_agreement(a[:ref16.size], ref16, part.marker_starts, TOL_BF16)
+    assert agree == total
+
+
 def test_batching_invariance_exact(model768):
     """tests/checkpoint.rs:91-105 property; here the per-row math is independent of the batch: exact."""
     rows = synthetic.synthetic_batch([300, 17, 129, 512, 1000, 64], markers_per_seq=5, seed=107, mask_markers=False)

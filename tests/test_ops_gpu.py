@@ -117,6 +117,49 @@ def test_gemm_resid_ln(torch_cuda, M, H, K, bias, ln_bias):
     _close_bf16(xn, ref.to(torch.bfloat16).float())
 
 
+@pytest.mark.parametrize("M", [32768, 131072])
+def test_c2_gemm_sweep_full_size(torch_cuda, M):
+    """The GEMM-sweep configuration's large sizes (M = 32,768 and 131,072 rows, hidden 768):
+    every fused GEMM of an encoder layer against its fp32 restatement, with the tolerances
+    of the small-size tests above."""
+    torch = torch_cuda
+    H, I = 768, 1152
+    pos = torch.arange(M, device="cuda", dtype=torch.int32) % 512
+    cos, sin = _rope_tables(torch, 160000.0, 512)
+    A = _rand(torch, (M, H), 1.0, 40, torch.bfloat16)
+    # QKV 768 -> 2304 + RoPE on q and k
+    W = _rand(torch, (3 * H, H), 0.02, 41, torch.bfloat16)
+    out = torch.empty((M, 3 * H), device="cuda", dtype=torch.bfloat16)
+    j1.op_gemm(j1.EPI_QKV_ROPE, A, W, out=out, pos=pos, rope_cos=cos, rope_sin=sin, rope_cols=2 * H)
+    acc = A.float() @ W.float().t()
+    c, s_ = cos[pos.long()], sin[pos.long()]
+    qk = acc[:, :2 * H].reshape(M, 2 * H // 64, 64)
+    lo, hi = qk[..., :32], qk[..., 32:]
+    rot = torch.cat([lo * c[:, None] - hi * s_[:, None], hi * c[:, None] + lo * s_[:, None]], dim=-1)
+    _close_bf16(out, torch.cat([rot.reshape(M, 2 * H), acc[:, 2 * H:]], dim=1).to(torch.bfloat16).float())
+    del out, acc, qk, lo, hi, rot
+    # Wi 768 -> 2304 + GEGLU -> 1152
+    Wf = _rand(torch, (2 * I, H), 0.02, 42, torch.bfloat16).float()
+    Wi = torch.empty((2 * I, H), device="cuda", dtype=torch.bfloat16)
+    j1.op_geglu_interleave(Wf.contiguous(), Wi, I, H)
+    g = torch.empty((M, I), device="cuda", dtype=torch.bfloat16)
+    j1.op_gemm(j1.EPI_GEGLU, A, Wi, out=g)
+    acc = A.float() @ Wf.t()
+    _close_bf16(g, (torch.nn.functional.gelu(acc[:, :I]) * acc[:, I:]).to(torch.bfloat16).float(), atol=3e-3)
+    del acc
+    # Wo 768 -> 768 and Wo2 1152 -> 768, each + FP32 residual + LayerNorm
+    lw = 1.0 + _rand(torch, (H,), 0.1, 43, torch.float32)
+    for K, src, seed in [(H, A, 44), (I, g, 46)]:
+        W = _rand(torch, (H, K), 0.02, seed, torch.bfloat16)
+        x0 = _rand(torch, (M, H), 1.0, seed + 1, torch.float32)
+        x = x0.clone()
+        xn = torch.empty((M, H), device="cuda", dtype=torch.bfloat16)
+        j1.op_gemm(j1.EPI_RESID_LN, src, W, x=x, ln_w=lw, ln_eps=1e-5, xn=xn)
+        xr = x0 + src.float() @ W.float().t()
+        torch.testing.assert_close(x, xr, rtol=1e-5, atol=1e-4)
+        _close_bf16(xn, torch.nn.functional.layer_norm(xr, (H,), lw, None, 1e-5).to(torch.bfloat16).float())
+
+
 def test_gemm_resid_only(torch_cuda):
     torch = torch_cuda
     M, H, K = 777, 768, 1152
