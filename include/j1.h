@@ -36,7 +36,9 @@ typedef enum j1_status {
   J1_ERR_OOM = 4,               /* device or pinned allocation failed */
   J1_ERR_NONFINITE = 5,         /* "Inference returned nonfinite logits" (src/engine.rs:219-221) */
   J1_ERR_DEVICE_TIMEOUT = 6,    /* a bounded device-side wait gave up; context still usable */
-  J1_ERR_IO = 7                 /* checkpoint / config could not be read or parsed (src/config.rs, src/weights.rs) */
+  J1_ERR_IO = 7,                /* checkpoint / config could not be read or parsed (src/config.rs, src/weights.rs) */
+  J1_ERR_INTERNAL = 8           /* a host-side failure inside the library (e.g. a thread that could not start);
+                                   host memory exhaustion is J1_ERR_OOM. No C++ exception leaves the library. */
 } j1_status;
 
 typedef struct j1_model j1_model;   /* one device replica: CudaModel */
@@ -350,10 +352,13 @@ J1_API j1_status j1_text_encoder_request_tokens(j1_text_encoder* enc, const char
  * Host-side fault injection: the next `count` device allocations (J1_FAULT_ALLOC ->
  * J1_ERR_OOM), kernel launches (J1_FAULT_LAUNCH -> J1_ERR_CUDA) or score readbacks
  * (J1_FAULT_NAN -> J1_ERR_NONFINITE, Engine::forward's check, src/engine.rs:219-221) of the
- * process fail; count 0 disarms. The environment variable J1_FAULT=alloc|launch|nan arms one
- * at the first j1_model_create. Nothing is done to the GPU: an injected allocation or launch
- * does not happen and injected nonfinite scores are written into the host copy. */
-enum { J1_FAULT_ALLOC = 1, J1_FAULT_LAUNCH = 2, J1_FAULT_NAN = 3 };
+ * process fail; count 0 disarms. J1_FAULT_HOST makes the next entry points' bodies throw
+ * std::bad_alloc (-> J1_ERR_OOM) and J1_FAULT_WORKER the next host worker threads (tokenizer,
+ * text encoder, engine device pool) throw std::runtime_error (-> J1_ERR_INTERNAL): the paths a
+ * real host failure takes. The environment variable J1_FAULT=alloc|launch|nan|host|worker
+ * arms one at the first j1_model_create. Nothing is done to the GPU: an injected allocation
+ * or launch does not happen and injected nonfinite scores are written into the host copy. */
+enum { J1_FAULT_ALLOC = 1, J1_FAULT_LAUNCH = 2, J1_FAULT_NAN = 3, J1_FAULT_HOST = 4, J1_FAULT_WORKER = 5 };
 J1_API void j1_inject_fault(int32_t kind, int32_t count);
 /* Device-side failure detection without a fault: one thread waits, with the library's
  * bounded wait and a limit of limit_cycles (1e3..4e9), on an mbarrier nothing arrives at.

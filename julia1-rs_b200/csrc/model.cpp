@@ -13,6 +13,8 @@
 #include <cstring>
 #include <limits>
 #include <memory>
+#include <stdexcept>
+#include <thread>
 #include <unordered_map>
 
 namespace j1rt {
@@ -48,6 +50,40 @@ j1_status set_error(j1_status s, const std::string& msg) {
   return s;
 }
 
+j1_status set_error_noexcept(j1_status s, const char* fn, const char* what) noexcept {
+  try {
+    t_last_error = std::string(fn) + ": " + what;
+  } catch (...) {
+    t_last_error.clear();
+  }
+  return s;
+}
+
+void run_pool(int n, const std::function<void()>& work) {
+  std::exception_ptr first;
+  std::mutex mu;
+  auto safe = [&]() noexcept {
+    try {
+      if (take_fault(J1_FAULT_WORKER)) throw std::runtime_error("injected worker failure");
+      work();
+    } catch (...) {
+      std::lock_guard<std::mutex> lock(mu);
+      if (!first) first = std::current_exception();
+    }
+  };
+  std::vector<std::thread> pool;
+  for (int k = 1; k < n; ++k) {
+    try {
+      pool.emplace_back(safe);
+    } catch (...) {  // no thread (or no room to hold one): the started ones and this thread do the rest
+      break;
+    }
+  }
+  safe();
+  for (auto& th : pool) th.join();
+  if (first) std::rethrow_exception(first);
+}
+
 j1_status cuda_error(cudaError_t e, const char* what) {
   if (e == cudaErrorMemoryAllocation) return set_error(J1_ERR_OOM, std::string(what) + ": out of device memory");
   return set_error(J1_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
@@ -60,7 +96,7 @@ size_t last_error_copy(char* buf, size_t cap) { return copy_out(t_last_error, bu
 // the process report a failure, so callers can test their error handling. Nothing is done
 // to the GPU: an injected allocation or launch simply does not happen, and injected
 // nonfinite scores are written into the host copy.
-std::atomic<int> g_fault[4];
+std::atomic<int> g_fault[6];
 
 bool take_fault(int kind) {
   int n = g_fault[kind].load();
@@ -813,6 +849,7 @@ const char* j1_status_name(j1_status s) {
     case J1_ERR_NONFINITE: return "J1_ERR_NONFINITE";
     case J1_ERR_DEVICE_TIMEOUT: return "J1_ERR_DEVICE_TIMEOUT";
     case J1_ERR_IO: return "J1_ERR_IO";
+    case J1_ERR_INTERNAL: return "J1_ERR_INTERNAL";
   }
   return "J1_ERR_UNKNOWN";
 }
@@ -820,140 +857,168 @@ const char* j1_status_name(j1_status s) {
 const char* j1_version(void) { return "libj1 0.1.0 sm_100a"; }
 
 j1_status j1_config_load(const char* ckpt_dir, j1_config* out) {
-  if (!ckpt_dir || !out) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
-  ModelConfig c;
-  std::string err;
-  if (!config_load(ckpt_dir, c, err)) return set_error(J1_ERR_IO, err);
-  out->hidden = c.hidden;
-  out->heads = c.heads;
-  out->head_dim = c.head_dim;
-  out->intermediate = c.intermediate;
-  out->layers = c.layers;
-  out->half_window = c.half_window;
-  out->vocab = c.vocab;
-  out->max_positions = c.max_positions;
-  out->head_layers = c.head_layers;
-  out->head_heads = c.head_heads;
-  out->head_ff = c.head_ff;
-  out->norm_eps = c.norm_eps;
-  out->n_global = 0;
-  for (bool g : c.global) out->n_global += g ? 1 : 0;
-  return J1_OK;
+  return guard("j1_config_load", [&]() -> j1_status {
+    if (!ckpt_dir || !out) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+    ModelConfig c;
+    std::string err;
+    if (!config_load(ckpt_dir, c, err)) return set_error(J1_ERR_IO, err);
+    out->hidden = c.hidden;
+    out->heads = c.heads;
+    out->head_dim = c.head_dim;
+    out->intermediate = c.intermediate;
+    out->layers = c.layers;
+    out->half_window = c.half_window;
+    out->vocab = c.vocab;
+    out->max_positions = c.max_positions;
+    out->head_layers = c.head_layers;
+    out->head_heads = c.head_heads;
+    out->head_ff = c.head_ff;
+    out->norm_eps = c.norm_eps;
+    out->n_global = 0;
+    for (bool g : c.global) out->n_global += g ? 1 : 0;
+    return J1_OK;
+  });
 }
 
 void j1_inject_fault(int32_t kind, int32_t count) {
-  if (kind >= J1_FAULT_ALLOC && kind <= J1_FAULT_NAN) g_fault[kind] = count > 0 ? count : 0;
+  if (kind >= J1_FAULT_ALLOC && kind <= J1_FAULT_WORKER) g_fault[kind] = count > 0 ? count : 0;
 }
 
 j1_status j1_selftest_device_timeout(int ordinal, int64_t limit_cycles) {
-  int n = 0;
-  J1_TRY_CUDA(cudaGetDeviceCount(&n), "cudaGetDeviceCount");
-  if (ordinal < 0 || ordinal >= n) return set_error(J1_ERR_INVALID_ARG, "no such device");
-  if (limit_cycles < 1000 || limit_cycles > 4000000000LL)
-    return set_error(J1_ERR_INVALID_ARG, "limit_cycles must be in [1e3, 4e9]");
-  J1_TRY_CUDA(cudaSetDevice(ordinal), "cudaSetDevice");
-  int* err = nullptr;
-  J1_TRY_CUDA(cudaMalloc(&err, 4), "cudaMalloc");
-  int code = 0;
-  cudaError_t e = cudaMemset(err, 0, 4);
-  if (e == cudaSuccess) e = static_cast<cudaError_t>(launch_wait_timeout_selftest(err, limit_cycles, nullptr));
-  if (e == cudaSuccess) e = cudaDeviceSynchronize();
-  if (e == cudaSuccess) e = cudaMemcpy(&code, err, 4, cudaMemcpyDeviceToHost);
-  cudaFree(err);
-  if (e != cudaSuccess) return cuda_error(e, "device timeout self-test");
-  if (code == 0) return set_error(J1_ERR_CUDA, "device timeout self-test: the wait did not time out");
-  return set_error(J1_ERR_DEVICE_TIMEOUT,
-                   "device-side wait timed out (site " + std::to_string(code >> 16) + "); self-test");
+  return guard("j1_selftest_device_timeout", [&]() -> j1_status {
+    int n = 0;
+    J1_TRY_CUDA(cudaGetDeviceCount(&n), "cudaGetDeviceCount");
+    if (ordinal < 0 || ordinal >= n) return set_error(J1_ERR_INVALID_ARG, "no such device");
+    if (limit_cycles < 1000 || limit_cycles > 4000000000LL)
+      return set_error(J1_ERR_INVALID_ARG, "limit_cycles must be in [1e3, 4e9]");
+    J1_TRY_CUDA(cudaSetDevice(ordinal), "cudaSetDevice");
+    int* err = nullptr;
+    J1_TRY_CUDA(cudaMalloc(&err, 4), "cudaMalloc");
+    int code = 0;
+    cudaError_t e = cudaMemset(err, 0, 4);
+    if (e == cudaSuccess) e = static_cast<cudaError_t>(launch_wait_timeout_selftest(err, limit_cycles, nullptr));
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpy(&code, err, 4, cudaMemcpyDeviceToHost);
+    cudaFree(err);
+    if (e != cudaSuccess) return cuda_error(e, "device timeout self-test");
+    if (code == 0) return set_error(J1_ERR_CUDA, "device timeout self-test: the wait did not time out");
+    return set_error(J1_ERR_DEVICE_TIMEOUT,
+                     "device-side wait timed out (site " + std::to_string(code >> 16) + "); self-test");
+  });
 }
 
 j1_status j1_model_create(const char* ckpt_dir, int ordinal, j1_model** out) {
-  // J1_FAULT=alloc|launch|nan arms one injected fault for the process (j1_inject_fault)
-  if (const char* f = std::getenv("J1_FAULT")) {
-    static std::atomic<bool> armed{false};
-    if (!armed.exchange(true)) {
-      const std::string k(f);
-      j1_inject_fault(k == "alloc" ? J1_FAULT_ALLOC : k == "launch" ? J1_FAULT_LAUNCH : k == "nan" ? J1_FAULT_NAN : 0, 1);
+  return guard("j1_model_create", [&]() -> j1_status {
+    // J1_FAULT=alloc|launch|nan|host|worker arms one injected fault for the process (j1_inject_fault)
+    if (const char* f = std::getenv("J1_FAULT")) {
+      static std::atomic<bool> armed{false};
+      if (!armed.exchange(true)) {
+        const std::string k(f);
+        j1_inject_fault(k == "alloc"    ? J1_FAULT_ALLOC
+                        : k == "launch" ? J1_FAULT_LAUNCH
+                        : k == "nan"    ? J1_FAULT_NAN
+                        : k == "host"   ? J1_FAULT_HOST
+                        : k == "worker" ? J1_FAULT_WORKER
+                                        : 0,
+                        1);
+      }
     }
-  }
-  j1_status s = create_model(ckpt_dir, ordinal, out);
-  return s;
+    j1_status s = create_model(ckpt_dir, ordinal, out);
+    return s;
+  });
 }
 
 void j1_model_destroy(j1_model* model) { destroy_model(model); }
 
 size_t j1_model_name(const j1_model* model, char* buf, size_t cap) {
-  return copy_out(model ? model->name : std::string(), buf, cap);
+  if (!model) {
+    if (buf && cap) buf[0] = 0;
+    return 0;
+  }
+  return copy_out(model->name, buf, cap);
 }
 
 j1_status j1_model_config(const j1_model* model, j1_config* out) {
-  if (!model || !out) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
-  const ModelConfig& c = model->cfg;
-  out->hidden = c.hidden;
-  out->heads = c.heads;
-  out->head_dim = c.head_dim;
-  out->intermediate = c.intermediate;
-  out->layers = c.layers;
-  out->half_window = c.half_window;
-  out->vocab = c.vocab;
-  out->max_positions = c.max_positions;
-  out->head_layers = c.head_layers;
-  out->head_heads = c.head_heads;
-  out->head_ff = c.head_ff;
-  out->norm_eps = c.norm_eps;
-  out->n_global = 0;
-  for (bool g : c.global) out->n_global += g ? 1 : 0;
-  return J1_OK;
+  return guard("j1_model_config", [&]() -> j1_status {
+    if (!model || !out) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+    const ModelConfig& c = model->cfg;
+    out->hidden = c.hidden;
+    out->heads = c.heads;
+    out->head_dim = c.head_dim;
+    out->intermediate = c.intermediate;
+    out->layers = c.layers;
+    out->half_window = c.half_window;
+    out->vocab = c.vocab;
+    out->max_positions = c.max_positions;
+    out->head_layers = c.head_layers;
+    out->head_heads = c.head_heads;
+    out->head_ff = c.head_ff;
+    out->norm_eps = c.norm_eps;
+    out->n_global = 0;
+    for (bool g : c.global) out->n_global += g ? 1 : 0;
+    return J1_OK;
+  });
 }
 
 j1_status j1_model_stage(j1_model* model, const uint32_t* ids, size_t t, const uint32_t* starts,
                          const uint32_t* lens, const uint8_t* qtypes, size_t nseq, const uint32_t* marker_rows,
                          const uint32_t* marker_starts, size_t m) {
-  if (!model) return set_error(J1_ERR_INVALID_ARG, "NULL model");
-  std::lock_guard<std::mutex> lk(model->mu);
-  DeviceGuard guard(model->device);
-  BatchView b{ids, t, starts, lens, qtypes, nseq, marker_rows, marker_starts, m};
-  return stage_batch(model, b);
+  return guard("j1_model_stage", [&]() -> j1_status {
+    if (!model) return set_error(J1_ERR_INVALID_ARG, "NULL model");
+    std::lock_guard<std::mutex> lk(model->mu);
+    DeviceGuard guard(model->device);
+    BatchView b{ids, t, starts, lens, qtypes, nseq, marker_rows, marker_starts, m};
+    return stage_batch(model, b);
+  });
 }
 
 j1_status j1_model_launch(j1_model* model) {
-  if (!model) return set_error(J1_ERR_INVALID_ARG, "NULL model");
-  std::lock_guard<std::mutex> lk(model->mu);
-  DeviceGuard guard(model->device);
-  return launch_forward(model);
+  return guard("j1_model_launch", [&]() -> j1_status {
+    if (!model) return set_error(J1_ERR_INVALID_ARG, "NULL model");
+    std::lock_guard<std::mutex> lk(model->mu);
+    DeviceGuard guard(model->device);
+    return launch_forward(model);
+  });
 }
 
 j1_status j1_model_finish(j1_model* model, float* scores_out, size_t m) {
-  if (!model) return set_error(J1_ERR_INVALID_ARG, "NULL model");
-  std::lock_guard<std::mutex> lk(model->mu);
-  DeviceGuard guard(model->device);
-  return finish_forward(model, scores_out, m);
+  return guard("j1_model_finish", [&]() -> j1_status {
+    if (!model) return set_error(J1_ERR_INVALID_ARG, "NULL model");
+    std::lock_guard<std::mutex> lk(model->mu);
+    DeviceGuard guard(model->device);
+    return finish_forward(model, scores_out, m);
+  });
 }
 
 j1_status j1_model_forward(j1_model* model, const uint32_t* ids, size_t t, const uint32_t* starts,
                            const uint32_t* lens, const uint8_t* qtypes, size_t nseq, const uint32_t* marker_rows,
                            const uint32_t* marker_starts, size_t m, float* scores_out) {
-  if (!model) return set_error(J1_ERR_INVALID_ARG, "NULL model");
-  std::lock_guard<std::mutex> lk(model->mu);
-  DeviceGuard guard(model->device);
-  BatchView b{ids, t, starts, lens, qtypes, nseq, marker_rows, marker_starts, m};
-  j1_status s = stage_batch(model, b);
-  if (s) return s;
-  if ((s = launch_forward(model))) return s;
-  return finish_forward(model, scores_out, m);
+  return guard("j1_model_forward", [&]() -> j1_status {
+    if (!model) return set_error(J1_ERR_INVALID_ARG, "NULL model");
+    std::lock_guard<std::mutex> lk(model->mu);
+    DeviceGuard guard(model->device);
+    BatchView b{ids, t, starts, lens, qtypes, nseq, marker_rows, marker_starts, m};
+    j1_status s = stage_batch(model, b);
+    if (s) return s;
+    if ((s = launch_forward(model))) return s;
+    return finish_forward(model, scores_out, m);
+  });
 }
 
 j1_status j1_model_forward_many(j1_model* model, size_t nbatch, const j1_batch* batches, float* const* scores_out) {
-  if (!model) return set_error(J1_ERR_INVALID_ARG, "NULL model");
-  if (nbatch && (!batches || !scores_out)) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
-  std::lock_guard<std::mutex> lk(model->mu);
-  DeviceGuard guard(model->device);
-  std::vector<BatchView> v;
-  v.reserve(nbatch);
-  for (size_t k = 0; k < nbatch; ++k) {
-    const j1_batch& b = batches[k];
-    v.push_back(BatchView{b.ids, b.t, b.starts, b.lens, b.qtypes, b.nseq, b.marker_rows, b.marker_starts, b.m});
-  }
-  return forward_many(model, v, scores_out);
+  return guard("j1_model_forward_many", [&]() -> j1_status {
+    if (!model) return set_error(J1_ERR_INVALID_ARG, "NULL model");
+    if (nbatch && (!batches || !scores_out)) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+    std::lock_guard<std::mutex> lk(model->mu);
+    DeviceGuard guard(model->device);
+    std::vector<BatchView> v;
+    v.reserve(nbatch);
+    for (size_t k = 0; k < nbatch; ++k) {
+      const j1_batch& b = batches[k];
+      v.push_back(BatchView{b.ids, b.t, b.starts, b.lens, b.qtypes, b.nseq, b.marker_rows, b.marker_starts, b.m});
+    }
+    return forward_many(model, v, scores_out);
+  });
 }
 
 void* j1_model_stream(j1_model* model) { return model ? static_cast<void*>(model->stream) : nullptr; }
@@ -961,21 +1026,25 @@ void* j1_model_stream(j1_model* model) { return model ? static_cast<void*>(model
 int64_t j1_model_launch_count(const j1_model* model) { return model ? model->launches : 0; }
 
 j1_status j1_model_profile(j1_model* model, int enable) {
-  if (!model) return set_error(J1_ERR_INVALID_ARG, "NULL model");
-  std::lock_guard<std::mutex> lk(model->mu);
-  DeviceGuard guard(model->device);
-  J1_TRY_CUDA(cudaStreamSynchronize(model->stream), "profile");
-  prof_fold(model);
-  model->prof_on = enable != 0;
-  for (int i = 0; i < J1_PROF_FAMILIES; ++i) model->prof_ms[i] = 0.0, model->prof_cnt[i] = 0;
-  return J1_OK;
+  return guard("j1_model_profile", [&]() -> j1_status {
+    if (!model) return set_error(J1_ERR_INVALID_ARG, "NULL model");
+    std::lock_guard<std::mutex> lk(model->mu);
+    DeviceGuard guard(model->device);
+    J1_TRY_CUDA(cudaStreamSynchronize(model->stream), "profile");
+    prof_fold(model);
+    model->prof_on = enable != 0;
+    for (int i = 0; i < J1_PROF_FAMILIES; ++i) model->prof_ms[i] = 0.0, model->prof_cnt[i] = 0;
+    return J1_OK;
+  });
 }
 
 j1_status j1_model_profile_read(j1_model* model, double* ms, int64_t* launches) {
-  if (!model || !ms || !launches) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
-  std::lock_guard<std::mutex> lk(model->mu);
-  for (int i = 0; i < J1_PROF_FAMILIES; ++i) ms[i] = model->prof_ms[i], launches[i] = model->prof_cnt[i];
-  return J1_OK;
+  return guard("j1_model_profile_read", [&]() -> j1_status {
+    if (!model || !ms || !launches) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+    std::lock_guard<std::mutex> lk(model->mu);
+    for (int i = 0; i < J1_PROF_FAMILIES; ++i) ms[i] = model->prof_ms[i], launches[i] = model->prof_cnt[i];
+    return J1_OK;
+  });
 }
 
 const char* j1_profile_family_name(int family) {
@@ -983,116 +1052,122 @@ const char* j1_profile_family_name(int family) {
 }
 
 j1_status j1_op_gemm(const j1_gemm_args* a, void* stream, int sync) {
-  if (!a || !a->A || !a->W) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
-  const GemmEpi epi = static_cast<GemmEpi>(a->epilogue);
-  if (a->epilogue < 0 || a->epilogue > 5) return set_error(J1_ERR_INVALID_ARG, "unknown epilogue");
-  const int bn = (epi == EPI_GEGLU) ? 256 : gemm_bn_for(a->N);
-  if (const char* why = gemm_shape_error(epi, bn, a->M, a->N, a->K)) return set_error(J1_ERR_UNSUPPORTED, why);
-  const bool full_row = epi == EPI_RESID_LN || epi == EPI_RESID || epi == EPI_SCORER;
-  if (full_row && a->M > 0 && epi != EPI_SCORER && (a->ldx < a->N || a->ldx % 4 != 0))
-    return set_error(J1_ERR_INVALID_ARG, "ldx must be >= N and a multiple of 4");
-  if ((epi == EPI_BF16 || epi == EPI_QKV_ROPE || epi == EPI_GEGLU) && !a->out)
-    return set_error(J1_ERR_INVALID_ARG, "out is NULL");
-  if ((epi == EPI_RESID_LN || epi == EPI_RESID) && !a->x) return set_error(J1_ERR_INVALID_ARG, "x is NULL");
-  if (epi == EPI_RESID_LN && (!a->ln_w || !a->xn)) return set_error(J1_ERR_INVALID_ARG, "ln_w/xn is NULL");
-  if (epi == EPI_QKV_ROPE && (!a->pos || !a->rope_cos || !a->rope_sin))
-    return set_error(J1_ERR_INVALID_ARG, "RoPE tables are NULL");
-  if (epi == EPI_SCORER && (!a->bias || !a->w2 || !a->scores)) return set_error(J1_ERR_INVALID_ARG, "scorer args NULL");
-  OpState* os;
-  j1_status s = op_state(&os);
-  if (s) return s;
-  CUtensorMap tmA, tmW, tmX;
-  const char* why = nullptr;
-  if (!make_tmap_bf16(&tmA, a->A, a->M, a->K, a->K, 128, &why) ||
-      !make_tmap_bf16(&tmW, a->W, a->N, a->K, a->K, gemm_w_box_rows(bn), &why))
-    return set_error(J1_ERR_INVALID_ARG, std::string("tensor map: ") + (why ? why : ""));
-  const bool resid = epi == EPI_RESID_LN || epi == EPI_RESID;
-  if (resid && !make_tmap_f32_resid(&tmX, a->x, a->M, a->N, a->ldx, &why))
-    return set_error(J1_ERR_INVALID_ARG, std::string("tensor map: ") + (why ? why : ""));
-  const bool tile_out = epi == EPI_BF16 || epi == EPI_QKV_ROPE || epi == EPI_GEGLU;
-  const int out_cols = epi == EPI_GEGLU ? a->N / 2 : a->N;
-  if (tile_out && (a->ldo < out_cols || a->ldo % 8 != 0))
-    return set_error(J1_ERR_INVALID_ARG, "ldo must be >= the output width and a multiple of 8");
-  if (tile_out && !make_tmap_bf16(&tmX, a->out, a->M, out_cols, a->ldo, 128, &why))
-    return set_error(J1_ERR_INVALID_ARG, std::string("tensor map: ") + (why ? why : ""));
-  EpiParams p;
-  std::memset(&p, 0, sizeof(p));
-  p.M = a->M, p.N = a->N, p.K = a->K;
-  p.out = static_cast<bf16*>(a->out), p.ldo = a->ldo;
-  p.bias = a->bias, p.relu = a->relu;
-  p.x = a->x, p.ldx = a->ldx;
-  p.ln_w = a->ln_w, p.ln_b = a->ln_b, p.ln_eps = a->ln_eps;
-  p.xn = static_cast<bf16*>(a->xn), p.ldxn = a->ldxn;
-  p.pos = a->pos, p.rope_cos = a->rope_cos, p.rope_sin = a->rope_sin, p.rope_cols = a->rope_cols;
-  p.w2 = a->w2, p.b2 = a->b2, p.scores = a->scores;
-  p.err = os->err;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int grid = a->grid_limit > 0 ? a->grid_limit : os->num_sms;
-  int rc = launch_gemm(epi, bn, tmA, tmW, (resid || tile_out) ? &tmX : nullptr, p, grid, st);
-  if (rc) return cuda_error(static_cast<cudaError_t>(rc), "gemm launch");
-  return sync ? op_sync_check(os, st) : J1_OK;
+  return guard("j1_op_gemm", [&]() -> j1_status {
+    if (!a || !a->A || !a->W) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+    const GemmEpi epi = static_cast<GemmEpi>(a->epilogue);
+    if (a->epilogue < 0 || a->epilogue > 5) return set_error(J1_ERR_INVALID_ARG, "unknown epilogue");
+    const int bn = (epi == EPI_GEGLU) ? 256 : gemm_bn_for(a->N);
+    if (const char* why = gemm_shape_error(epi, bn, a->M, a->N, a->K)) return set_error(J1_ERR_UNSUPPORTED, why);
+    const bool full_row = epi == EPI_RESID_LN || epi == EPI_RESID || epi == EPI_SCORER;
+    if (full_row && a->M > 0 && epi != EPI_SCORER && (a->ldx < a->N || a->ldx % 4 != 0))
+      return set_error(J1_ERR_INVALID_ARG, "ldx must be >= N and a multiple of 4");
+    if ((epi == EPI_BF16 || epi == EPI_QKV_ROPE || epi == EPI_GEGLU) && !a->out)
+      return set_error(J1_ERR_INVALID_ARG, "out is NULL");
+    if ((epi == EPI_RESID_LN || epi == EPI_RESID) && !a->x) return set_error(J1_ERR_INVALID_ARG, "x is NULL");
+    if (epi == EPI_RESID_LN && (!a->ln_w || !a->xn)) return set_error(J1_ERR_INVALID_ARG, "ln_w/xn is NULL");
+    if (epi == EPI_QKV_ROPE && (!a->pos || !a->rope_cos || !a->rope_sin))
+      return set_error(J1_ERR_INVALID_ARG, "RoPE tables are NULL");
+    if (epi == EPI_SCORER && (!a->bias || !a->w2 || !a->scores)) return set_error(J1_ERR_INVALID_ARG, "scorer args NULL");
+    OpState* os;
+    j1_status s = op_state(&os);
+    if (s) return s;
+    CUtensorMap tmA, tmW, tmX;
+    const char* why = nullptr;
+    if (!make_tmap_bf16(&tmA, a->A, a->M, a->K, a->K, 128, &why) ||
+        !make_tmap_bf16(&tmW, a->W, a->N, a->K, a->K, gemm_w_box_rows(bn), &why))
+      return set_error(J1_ERR_INVALID_ARG, std::string("tensor map: ") + (why ? why : ""));
+    const bool resid = epi == EPI_RESID_LN || epi == EPI_RESID;
+    if (resid && !make_tmap_f32_resid(&tmX, a->x, a->M, a->N, a->ldx, &why))
+      return set_error(J1_ERR_INVALID_ARG, std::string("tensor map: ") + (why ? why : ""));
+    const bool tile_out = epi == EPI_BF16 || epi == EPI_QKV_ROPE || epi == EPI_GEGLU;
+    const int out_cols = epi == EPI_GEGLU ? a->N / 2 : a->N;
+    if (tile_out && (a->ldo < out_cols || a->ldo % 8 != 0))
+      return set_error(J1_ERR_INVALID_ARG, "ldo must be >= the output width and a multiple of 8");
+    if (tile_out && !make_tmap_bf16(&tmX, a->out, a->M, out_cols, a->ldo, 128, &why))
+      return set_error(J1_ERR_INVALID_ARG, std::string("tensor map: ") + (why ? why : ""));
+    EpiParams p;
+    std::memset(&p, 0, sizeof(p));
+    p.M = a->M, p.N = a->N, p.K = a->K;
+    p.out = static_cast<bf16*>(a->out), p.ldo = a->ldo;
+    p.bias = a->bias, p.relu = a->relu;
+    p.x = a->x, p.ldx = a->ldx;
+    p.ln_w = a->ln_w, p.ln_b = a->ln_b, p.ln_eps = a->ln_eps;
+    p.xn = static_cast<bf16*>(a->xn), p.ldxn = a->ldxn;
+    p.pos = a->pos, p.rope_cos = a->rope_cos, p.rope_sin = a->rope_sin, p.rope_cols = a->rope_cols;
+    p.w2 = a->w2, p.b2 = a->b2, p.scores = a->scores;
+    p.err = os->err;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int grid = a->grid_limit > 0 ? a->grid_limit : os->num_sms;
+    int rc = launch_gemm(epi, bn, tmA, tmW, (resid || tile_out) ? &tmX : nullptr, p, grid, st);
+    if (rc) return cuda_error(static_cast<cudaError_t>(rc), "gemm launch");
+    return sync ? op_sync_check(os, st) : J1_OK;
+  });
 }
 
 j1_status j1_op_attention(const void* qkv, int64_t t, int32_t hidden, const uint32_t* seq_starts,
                           const uint32_t* seq_lens, size_t nseq, int32_t window, void* ctx, void* stream, int sync) {
-  if (!qkv || !ctx || (nseq && (!seq_starts || !seq_lens))) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
-  if (hidden % 64 != 0 || hidden <= 0) return set_error(J1_ERR_UNSUPPORTED, "hidden must be a multiple of 64");
-  std::vector<AttnTile> tiles;
-  for (size_t s = 0; s < nseq; ++s) {
-    if (seq_lens[s] == 0 || static_cast<int64_t>(seq_starts[s]) + seq_lens[s] > t)
-      return set_error(J1_ERR_INVALID_ARG, "sequence outside the qkv buffer");
-    const uint32_t PQ = static_cast<uint32_t>(attention_pair_queries());
-    for (uint32_t q0 = 0; q0 < seq_lens[s]; q0 += PQ) {
-      AttnTile tl;
-      tl.q_row0 = static_cast<int>(seq_starts[s] + q0);
-      tl.nq = static_cast<int>(std::min<uint32_t>(PQ, seq_lens[s] - q0));
-      tl.kv_row0 = static_cast<int>(seq_starts[s]);
-      tl.kv_len = static_cast<int>(seq_lens[s]);
-      tl.q_pos0 = static_cast<int>(q0);
-      tl.pad0 = tl.pad1 = tl.pad2 = 0;
-      tiles.push_back(tl);
+  return guard("j1_op_attention", [&]() -> j1_status {
+    if (!qkv || !ctx || (nseq && (!seq_starts || !seq_lens))) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+    if (hidden % 64 != 0 || hidden <= 0) return set_error(J1_ERR_UNSUPPORTED, "hidden must be a multiple of 64");
+    std::vector<AttnTile> tiles;
+    for (size_t s = 0; s < nseq; ++s) {
+      if (seq_lens[s] == 0 || static_cast<int64_t>(seq_starts[s]) + seq_lens[s] > t)
+        return set_error(J1_ERR_INVALID_ARG, "sequence outside the qkv buffer");
+      const uint32_t PQ = static_cast<uint32_t>(attention_pair_queries());
+      for (uint32_t q0 = 0; q0 < seq_lens[s]; q0 += PQ) {
+        AttnTile tl;
+        tl.q_row0 = static_cast<int>(seq_starts[s] + q0);
+        tl.nq = static_cast<int>(std::min<uint32_t>(PQ, seq_lens[s] - q0));
+        tl.kv_row0 = static_cast<int>(seq_starts[s]);
+        tl.kv_len = static_cast<int>(seq_lens[s]);
+        tl.q_pos0 = static_cast<int>(q0);
+        tl.pad0 = tl.pad1 = tl.pad2 = 0;
+        tiles.push_back(tl);
+      }
     }
-  }
-  OpState* os;
-  j1_status s = op_state(&os);
-  if (s) return s;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (tiles.size() > os->tiles_cap) {
-    J1_TRY_CUDA(cudaDeviceSynchronize(), "op attention");
-    if (os->tiles) cudaFree(os->tiles);
-    os->tiles = nullptr;
-    void* p;
-    J1_TRY_CUDA(cudaMalloc(&p, tiles.size() * sizeof(AttnTile)), "cudaMalloc");
-    os->tiles = static_cast<AttnTile*>(p);
-    os->tiles_cap = tiles.size();
-  }
-  if (!tiles.empty())
-    J1_TRY_CUDA(cudaMemcpyAsync(os->tiles, tiles.data(), tiles.size() * sizeof(AttnTile), cudaMemcpyHostToDevice, st),
-                "tiles upload");
-  CUtensorMap tm;
-  const char* why = nullptr;
-  if (!make_tmap_bf16(&tm, qkv, static_cast<uint64_t>(t), 3 * static_cast<uint64_t>(hidden), 3 * hidden, 128, &why))
-    return set_error(J1_ERR_INVALID_ARG, std::string("tensor map: ") + (why ? why : ""));
-  CUtensorMap tmO, tmKV;
-  if (!make_tmap_bf16(&tmO, ctx, static_cast<uint64_t>(t), static_cast<uint64_t>(hidden), hidden, 32, &why) ||
-      !make_tmap_bf16(&tmKV, qkv, static_cast<uint64_t>(t), 3 * static_cast<uint64_t>(hidden), 3 * hidden,
-                      attention_kv_box_rows(), &why))
-    return set_error(J1_ERR_INVALID_ARG, std::string("tensor map: ") + (why ? why : ""));
-  int rc = launch_attention(tm, tmKV, &tmO, os->tiles, static_cast<int>(tiles.size()), hidden / 64, 0, hidden, 2 * hidden,
-                            static_cast<bf16*>(ctx), hidden, window, kScaleLog2, os->err, os->num_sms, st);
-  if (rc) return cuda_error(static_cast<cudaError_t>(rc), "attention launch");
-  if (sync || !tiles.empty()) return op_sync_check(os, st);  // tiles are host-owned: wait before returning
-  return J1_OK;
+    OpState* os;
+    j1_status s = op_state(&os);
+    if (s) return s;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (tiles.size() > os->tiles_cap) {
+      J1_TRY_CUDA(cudaDeviceSynchronize(), "op attention");
+      if (os->tiles) cudaFree(os->tiles);
+      os->tiles = nullptr;
+      void* p;
+      J1_TRY_CUDA(cudaMalloc(&p, tiles.size() * sizeof(AttnTile)), "cudaMalloc");
+      os->tiles = static_cast<AttnTile*>(p);
+      os->tiles_cap = tiles.size();
+    }
+    if (!tiles.empty())
+      J1_TRY_CUDA(cudaMemcpyAsync(os->tiles, tiles.data(), tiles.size() * sizeof(AttnTile), cudaMemcpyHostToDevice, st),
+                  "tiles upload");
+    CUtensorMap tm;
+    const char* why = nullptr;
+    if (!make_tmap_bf16(&tm, qkv, static_cast<uint64_t>(t), 3 * static_cast<uint64_t>(hidden), 3 * hidden, 128, &why))
+      return set_error(J1_ERR_INVALID_ARG, std::string("tensor map: ") + (why ? why : ""));
+    CUtensorMap tmO, tmKV;
+    if (!make_tmap_bf16(&tmO, ctx, static_cast<uint64_t>(t), static_cast<uint64_t>(hidden), hidden, 32, &why) ||
+        !make_tmap_bf16(&tmKV, qkv, static_cast<uint64_t>(t), 3 * static_cast<uint64_t>(hidden), 3 * hidden,
+                        attention_kv_box_rows(), &why))
+      return set_error(J1_ERR_INVALID_ARG, std::string("tensor map: ") + (why ? why : ""));
+    int rc = launch_attention(tm, tmKV, &tmO, os->tiles, static_cast<int>(tiles.size()), hidden / 64, 0, hidden, 2 * hidden,
+                              static_cast<bf16*>(ctx), hidden, window, kScaleLog2, os->err, os->num_sms, st);
+    if (rc) return cuda_error(static_cast<cudaError_t>(rc), "attention launch");
+    if (sync || !tiles.empty()) return op_sync_check(os, st);  // tiles are host-owned: wait before returning
+    return J1_OK;
+  });
 }
 
 j1_status j1_op_geglu_interleave(const float* src_dev, void* dst_dev, int32_t inter, int32_t k, void* stream) {
-  if (!src_dev || !dst_dev) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
-  if (inter % 128 != 0) return set_error(J1_ERR_UNSUPPORTED, "inter must be a multiple of 128");
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  int rc = launch_f32_to_bf16(src_dev, static_cast<bf16*>(dst_dev), 2LL * inter, k, inter, st);
-  if (rc) return cuda_error(static_cast<cudaError_t>(rc), "interleave");
-  J1_TRY_CUDA(cudaStreamSynchronize(st), "interleave");
-  return J1_OK;
+  return guard("j1_op_geglu_interleave", [&]() -> j1_status {
+    if (!src_dev || !dst_dev) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+    if (inter % 128 != 0) return set_error(J1_ERR_UNSUPPORTED, "inter must be a multiple of 128");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    int rc = launch_f32_to_bf16(src_dev, static_cast<bf16*>(dst_dev), 2LL * inter, k, inter, st);
+    if (rc) return cuda_error(static_cast<cudaError_t>(rc), "interleave");
+    J1_TRY_CUDA(cudaStreamSynchronize(st), "interleave");
+    return J1_OK;
+  });
 }
 
 }  // extern "C"

@@ -3,7 +3,10 @@
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <exception>
+#include <functional>
 #include <mutex>
+#include <new>
 #include <string>
 #include <vector>
 
@@ -14,10 +17,35 @@
 namespace j1rt {
 
 j1_status set_error(j1_status s, const std::string& msg);
+// set_error for exception handlers: builds "<fn>: <what>" and never throws.
+j1_status set_error_noexcept(j1_status s, const char* fn, const char* what) noexcept;
 j1_status cuda_error(cudaError_t e, const char* what);
 // j1_inject_fault state: remaining injected faults per kind (J1_FAULT_*).
-extern std::atomic<int> g_fault[4];
+extern std::atomic<int> g_fault[6];
 bool take_fault(int kind);
+
+// Every C entry point runs its body through guard(): a C++ exception (host memory
+// exhausted, a thread that could not start, ...) becomes a status and a message instead
+// of unwinding into the caller's frames, which a C, Rust or ctypes caller cannot survive.
+template <class F>
+j1_status guard(const char* fn, F&& body) noexcept {
+  try {
+    if (take_fault(J1_FAULT_HOST)) throw std::bad_alloc();
+    return body();
+  } catch (const std::bad_alloc&) {
+    return set_error_noexcept(J1_ERR_OOM, fn, "host memory exhausted");
+  } catch (const std::exception& e) {
+    return set_error_noexcept(J1_ERR_INTERNAL, fn, e.what());
+  } catch (...) {
+    return set_error_noexcept(J1_ERR_INTERNAL, fn, "unknown C++ exception");
+  }
+}
+
+// Runs work() on the calling thread and on up to n - 1 more threads. work() takes its
+// items from a shared counter, so any number of threads finishes all of them: a thread
+// that cannot be started is skipped. An exception inside work() on any thread is caught
+// there and rethrown here (the first one) once every started thread has been joined.
+void run_pool(int n, const std::function<void()>& work);
 
 // Restores the calling thread's current device on scope exit.
 class DeviceGuard {

@@ -11,6 +11,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <limits>
 #include <list>
 #include <memory>
 #include <mutex>
@@ -376,52 +377,66 @@ void j1_encoder_options_default(j1_encoder_options* o) {
 
 j1_status j1_encode_sequence(const j1_encoder_options* opts, const j1_tokenized_request* req, uint32_t* ids_out,
                              size_t ids_cap, size_t* ids_len, uint32_t* markers_out, int32_t* truncated) {
-  if (!req || !ids_len) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
-  if (j1_status s = check_encoder(opts)) return s;
-  std::vector<uint32_t> ids, mk;
-  bool trunc = false;
-  if (j1_status s = encode_row(*opts, *req, ids, mk, trunc)) return s;
-  if (ids.size() > ids_cap || !ids_out || (!markers_out && !mk.empty()))
-    return set_error(J1_ERR_INVALID_ARG, "output arrays too small (ids_cap >= max_length, markers >= n_options)");
-  std::memcpy(ids_out, ids.data(), ids.size() * 4);
-  if (!mk.empty()) std::memcpy(markers_out, mk.data(), mk.size() * 4);
-  *ids_len = ids.size();
-  if (truncated) *truncated = trunc ? 1 : 0;
-  return J1_OK;
+  return guard("j1_encode_sequence", [&]() -> j1_status {
+    if (!req || !ids_len) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+    if (j1_status s = check_encoder(opts)) return s;
+    std::vector<uint32_t> ids, mk;
+    bool trunc = false;
+    if (j1_status s = encode_row(*opts, *req, ids, mk, trunc)) return s;
+    if (ids.size() > ids_cap || !ids_out || (!markers_out && !mk.empty()))
+      return set_error(J1_ERR_INVALID_ARG, "output arrays too small (ids_cap >= max_length, markers >= n_options)");
+    std::memcpy(ids_out, ids.data(), ids.size() * 4);
+    if (!mk.empty()) std::memcpy(markers_out, mk.data(), mk.size() * 4);
+    *ids_len = ids.size();
+    if (truncated) *truncated = trunc ? 1 : 0;
+    return J1_OK;
+  });
 }
 
 j1_status j1_engine_logits_tokenized(j1_engine* engine, const j1_encoder_options* opts, size_t n_rows,
                                      const j1_tokenized_request* rows, float* logits_out) {
-  if (!engine || !opts) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
-  if (n_rows == 0) return J1_OK;
-  if (!rows || !logits_out) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
-  j1_encoder_options e = *opts;
-  if (e.max_length == 0) e.max_length = j1_engine_max_length(engine);
-  if (j1_status s = check_encoder(&e)) return s;
-  // Engine::encode (src/engine.rs:183-188): validate every row before encoding any
-  for (size_t i = 0; i < n_rows; ++i)
-    if (j1_status s = validate_request(rows[i]))
-      return set_error(s, "JSONL line " + std::to_string(i + 1) + ": " + [] {
-        char buf[256];
-        j1_last_error(buf, sizeof(buf));
-        return std::string(buf);
-      }());
-  EncodedRows enc;
-  for (size_t i = 0; i < n_rows; ++i)
-    if (j1_status s = enc.add(e, rows[i])) return s;
-  return j1_engine_logits_encoded(engine, enc.n, enc.ids.data(), enc.lens.data(), enc.markers.data(),
-                                  enc.nmark.data(), enc.qtypes.data(), logits_out);
+  return guard("j1_engine_logits_tokenized", [&]() -> j1_status {
+    if (!engine || !opts) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+    if (n_rows == 0) return J1_OK;
+    if (!rows || !logits_out) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+    j1_encoder_options e = *opts;
+    if (e.max_length == 0) e.max_length = j1_engine_max_length(engine);
+    if (j1_status s = check_encoder(&e)) return s;
+    // Engine::encode (src/engine.rs:183-188): validate every row before encoding any
+    for (size_t i = 0; i < n_rows; ++i)
+      if (j1_status s = validate_request(rows[i]))
+        return set_error(s, "JSONL line " + std::to_string(i + 1) + ": " + [] {
+          char buf[256];
+          j1_last_error(buf, sizeof(buf));
+          return std::string(buf);
+        }());
+    EncodedRows enc;
+    for (size_t i = 0; i < n_rows; ++i)
+      if (j1_status s = enc.add(e, rows[i])) return s;
+    return j1_engine_logits_encoded(engine, enc.n, enc.ids.data(), enc.lens.data(), enc.markers.data(),
+                                    enc.nmark.data(), enc.qtypes.data(), logits_out);
+  });
 }
 
 void j1_display_probabilities(const double* values, size_t n, double* out) {
   if (!values || !out) return;
-  const std::vector<double> p = display_probabilities(std::vector<double>(values, values + n));
-  std::copy(p.begin(), p.end(), out);
+  const j1_status s = guard("j1_display_probabilities", [&]() -> j1_status {
+    const std::vector<double> p = display_probabilities(std::vector<double>(values, values + n));
+    std::copy(p.begin(), p.end(), out);
+    return J1_OK;
+  });
+  if (s)  // host memory exhausted: no probabilities (the message is in j1_last_error)
+    for (size_t i = 0; i < n; ++i) out[i] = std::numeric_limits<double>::quiet_NaN();
 }
 
 int32_t j1_router_confident_winner(const float* scores, size_t n, size_t best) {
   if (!scores || best >= n) return 0;
-  return confident_winner(std::vector<float>(scores, scores + n), best) ? 1 : 0;
+  int32_t win = 0;
+  guard("j1_router_confident_winner", [&]() -> j1_status {
+    win = confident_winner(std::vector<float>(scores, scores + n), best) ? 1 : 0;
+    return J1_OK;
+  });
+  return win;
 }
 
 void j1_router_options_default(j1_router_options* o) {
@@ -436,14 +451,18 @@ void j1_router_options_default(j1_router_options* o) {
 
 j1_status j1_router_create(j1_engine* engine, const j1_encoder_options* enc, const j1_router_options* opts,
                            j1_router** out) {
-  if (!engine) return set_error(J1_ERR_INVALID_ARG, "NULL engine");
-  return make_router(engine, nullptr, nullptr, enc, opts, out);
+  return guard("j1_router_create", [&]() -> j1_status {
+    if (!engine) return set_error(J1_ERR_INVALID_ARG, "NULL engine");
+    return make_router(engine, nullptr, nullptr, enc, opts, out);
+  });
 }
 
 j1_status j1_router_create_with_scorer(j1_scorer_fn fn, void* user, const j1_encoder_options* enc,
                                        const j1_router_options* opts, j1_router** out) {
-  if (!fn) return set_error(J1_ERR_INVALID_ARG, "NULL scorer");
-  return make_router(nullptr, fn, user, enc, opts, out);
+  return guard("j1_router_create_with_scorer", [&]() -> j1_status {
+    if (!fn) return set_error(J1_ERR_INVALID_ARG, "NULL scorer");
+    return make_router(nullptr, fn, user, enc, opts, out);
+  });
 }
 
 void j1_router_destroy(j1_router* r) { delete r; }
@@ -458,110 +477,112 @@ void j1_router_clear_cache(j1_router* r) {
 // Router::route_many (src/router.rs:143-210).
 j1_status j1_router_route_many(j1_router* R, size_t n, const j1_tokenized_request* rows, j1_route_result* results,
                                uint64_t* model_rows, uint64_t* cache_hits) {
-  if (!R) return set_error(J1_ERR_INVALID_ARG, "NULL router");
-  if (n && (!rows || !results)) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
-  std::lock_guard<std::mutex> lk(R->lock);
-  for (size_t i = 0; i < n; ++i)
-    if (j1_status s = validate_route(R, rows[i])) return s;
-  const size_t width = static_cast<size_t>(R->opts.width);
-  // per row: offsets of each option's tokens
-  std::vector<std::vector<size_t>> opt_off(n);
-  for (size_t i = 0; i < n; ++i) {
-    opt_off[i].assign(rows[i].n_options + 1, 0);
-    for (size_t k = 0; k < rows[i].n_options; ++k) opt_off[i][k + 1] = opt_off[i][k] + rows[i].option_lens[k];
-  }
-  std::vector<std::vector<uint32_t>> candidates(n);
-  for (size_t i = 0; i < n; ++i)
-    for (size_t k = 0; k < rows[i].n_options; ++k) candidates[i].push_back(static_cast<uint32_t>(k));
-  std::vector<char> done(n, 0);
-  std::vector<uint32_t> rounds(n, 0);
-  size_t used_total = 0, hits_total = 0, remaining = n;
-  struct Slot {
-    size_t row;
-    std::vector<uint32_t> group;
-    bool last;
-  };
-  while (remaining > 0) {
-    std::vector<Job> jobs;
-    std::vector<Slot> layout;
+  return guard("j1_router_route_many", [&]() -> j1_status {
+    if (!R) return set_error(J1_ERR_INVALID_ARG, "NULL router");
+    if (n && (!rows || !results)) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+    std::lock_guard<std::mutex> lk(R->lock);
+    for (size_t i = 0; i < n; ++i)
+      if (j1_status s = validate_route(R, rows[i])) return s;
+    const size_t width = static_cast<size_t>(R->opts.width);
+    // per row: offsets of each option's tokens
+    std::vector<std::vector<size_t>> opt_off(n);
     for (size_t i = 0; i < n; ++i) {
-      if (done[i]) continue;
-      ++rounds[i];
-      std::vector<uint32_t> current;
-      current.swap(candidates[i]);
-      const bool last = current.size() <= width;
-      for (size_t g0 = 0; g0 < current.size(); g0 += width) {
-        const size_t g1 = std::min(current.size(), g0 + width);
-        if (g1 - g0 == 1) {
-          candidates[i].push_back(current[g0]);
-          continue;
+      opt_off[i].assign(rows[i].n_options + 1, 0);
+      for (size_t k = 0; k < rows[i].n_options; ++k) opt_off[i][k + 1] = opt_off[i][k] + rows[i].option_lens[k];
+    }
+    std::vector<std::vector<uint32_t>> candidates(n);
+    for (size_t i = 0; i < n; ++i)
+      for (size_t k = 0; k < rows[i].n_options; ++k) candidates[i].push_back(static_cast<uint32_t>(k));
+    std::vector<char> done(n, 0);
+    std::vector<uint32_t> rounds(n, 0);
+    size_t used_total = 0, hits_total = 0, remaining = n;
+    struct Slot {
+      size_t row;
+      std::vector<uint32_t> group;
+      bool last;
+    };
+    while (remaining > 0) {
+      std::vector<Job> jobs;
+      std::vector<Slot> layout;
+      for (size_t i = 0; i < n; ++i) {
+        if (done[i]) continue;
+        ++rounds[i];
+        std::vector<uint32_t> current;
+        current.swap(candidates[i]);
+        const bool last = current.size() <= width;
+        for (size_t g0 = 0; g0 < current.size(); g0 += width) {
+          const size_t g1 = std::min(current.size(), g0 + width);
+          if (g1 - g0 == 1) {
+            candidates[i].push_back(current[g0]);
+            continue;
+          }
+          Job j;
+          j.row = &rows[i];
+          std::vector<uint32_t> group(current.begin() + g0, current.begin() + g1);
+          for (uint32_t k : group) {
+            j.opt_lens.push_back(rows[i].option_lens[k]);
+            j.opt_ids.insert(j.opt_ids.end(), rows[i].option_ids + opt_off[i][k], rows[i].option_ids + opt_off[i][k + 1]);
+          }
+          jobs.push_back(std::move(j));
+          layout.push_back(Slot{i, std::move(group), last});
         }
-        Job j;
-        j.row = &rows[i];
-        std::vector<uint32_t> group(current.begin() + g0, current.begin() + g1);
-        for (uint32_t k : group) {
-          j.opt_lens.push_back(rows[i].option_lens[k]);
-          j.opt_ids.insert(j.opt_ids.end(), rows[i].option_ids + opt_off[i][k], rows[i].option_ids + opt_off[i][k + 1]);
+      }
+      std::vector<std::vector<float>> scored;
+      size_t used = 0, hits = 0;
+      if (j1_status s = score(R, jobs, scored, used, hits)) return s;
+      used_total += used;
+      hits_total += hits;
+      for (size_t q = 0; q < layout.size(); ++q) {
+        const Slot& sl = layout[q];
+        const std::vector<float>& sc = scored[q];
+        const size_t best = argmax(sc.data(), sc.size());
+        const size_t i = sl.row;
+        if (sl.last) {
+          double mx = -INFINITY;
+          for (float v : sc) mx = std::max(mx, static_cast<double>(v));
+          std::vector<double> w(sc.size());
+          double total = 0.0;
+          for (size_t k = 0; k < sc.size(); ++k) {
+            w[k] = std::exp(static_cast<double>(sc[k]) - mx);
+            total += w[k];
+          }
+          for (double& v : w) v /= total;
+          const std::vector<double> p = display_probabilities(w);
+          j1_route_result& res = results[i];
+          std::memset(&res, 0, sizeof(res));
+          res.index = sl.group[best];
+          res.n_candidates = static_cast<uint32_t>(sl.group.size());
+          for (size_t k = 0; k < sl.group.size(); ++k) {
+            res.candidates[k] = sl.group[k];
+            res.probabilities[k] = p[k];
+          }
+          res.rounds = rounds[i];
+          res.hierarchical = rows[i].n_options > width ? 1 : 0;
+          done[i] = 1;
+          --remaining;
+        } else if (confident_winner(sc, best)) {
+          candidates[i].push_back(sl.group[best]);
+        } else {
+          std::vector<size_t> rest(sl.group.size());
+          for (size_t k = 0; k < rest.size(); ++k) rest[k] = k;
+          std::vector<uint32_t> chosen;
+          const size_t keep = std::min(static_cast<size_t>(R->opts.survivors), sl.group.size());
+          for (size_t c = 0; c < keep; ++c) {
+            std::vector<float> local(rest.size());
+            for (size_t k = 0; k < rest.size(); ++k) local[k] = sc[rest[k]];
+            const size_t a = argmax(local.data(), local.size());
+            chosen.push_back(sl.group[rest[a]]);
+            rest.erase(rest.begin() + static_cast<std::ptrdiff_t>(a));
+          }
+          std::sort(chosen.begin(), chosen.end());
+          candidates[i].insert(candidates[i].end(), chosen.begin(), chosen.end());
         }
-        jobs.push_back(std::move(j));
-        layout.push_back(Slot{i, std::move(group), last});
       }
     }
-    std::vector<std::vector<float>> scored;
-    size_t used = 0, hits = 0;
-    if (j1_status s = score(R, jobs, scored, used, hits)) return s;
-    used_total += used;
-    hits_total += hits;
-    for (size_t q = 0; q < layout.size(); ++q) {
-      const Slot& sl = layout[q];
-      const std::vector<float>& sc = scored[q];
-      const size_t best = argmax(sc.data(), sc.size());
-      const size_t i = sl.row;
-      if (sl.last) {
-        double mx = -INFINITY;
-        for (float v : sc) mx = std::max(mx, static_cast<double>(v));
-        std::vector<double> w(sc.size());
-        double total = 0.0;
-        for (size_t k = 0; k < sc.size(); ++k) {
-          w[k] = std::exp(static_cast<double>(sc[k]) - mx);
-          total += w[k];
-        }
-        for (double& v : w) v /= total;
-        const std::vector<double> p = display_probabilities(w);
-        j1_route_result& res = results[i];
-        std::memset(&res, 0, sizeof(res));
-        res.index = sl.group[best];
-        res.n_candidates = static_cast<uint32_t>(sl.group.size());
-        for (size_t k = 0; k < sl.group.size(); ++k) {
-          res.candidates[k] = sl.group[k];
-          res.probabilities[k] = p[k];
-        }
-        res.rounds = rounds[i];
-        res.hierarchical = rows[i].n_options > width ? 1 : 0;
-        done[i] = 1;
-        --remaining;
-      } else if (confident_winner(sc, best)) {
-        candidates[i].push_back(sl.group[best]);
-      } else {
-        std::vector<size_t> rest(sl.group.size());
-        for (size_t k = 0; k < rest.size(); ++k) rest[k] = k;
-        std::vector<uint32_t> chosen;
-        const size_t keep = std::min(static_cast<size_t>(R->opts.survivors), sl.group.size());
-        for (size_t c = 0; c < keep; ++c) {
-          std::vector<float> local(rest.size());
-          for (size_t k = 0; k < rest.size(); ++k) local[k] = sc[rest[k]];
-          const size_t a = argmax(local.data(), local.size());
-          chosen.push_back(sl.group[rest[a]]);
-          rest.erase(rest.begin() + static_cast<std::ptrdiff_t>(a));
-        }
-        std::sort(chosen.begin(), chosen.end());
-        candidates[i].insert(candidates[i].end(), chosen.begin(), chosen.end());
-      }
-    }
-  }
-  if (model_rows) *model_rows = used_total;
-  if (cache_hits) *cache_hits = hits_total;
-  return J1_OK;
+    if (model_rows) *model_rows = used_total;
+    if (cache_hits) *cache_hits = hits_total;
+    return J1_OK;
+  });
 }
 
 }  // extern "C"

@@ -922,121 +922,129 @@ j1_status read_request(const char* state, const char* question, const char* cons
 extern "C" {
 
 j1_status j1_tokenizer_load(const char* path, j1_tokenizer** out) {
-  if (!path || !out) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
-  *out = nullptr;
-  std::string text;
-  if (!read_file(path, text)) return set_error(J1_ERR_IO, std::string("cannot read ") + path);
-  std::unique_ptr<j1_tokenizer> t;
-  if (j1_status s = load_tokenizer(text, t)) return s;
-  *out = t.release();
-  return J1_OK;
+  return guard("j1_tokenizer_load", [&]() -> j1_status {
+    if (!path || !out) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+    *out = nullptr;
+    std::string text;
+    if (!read_file(path, text)) return set_error(J1_ERR_IO, std::string("cannot read ") + path);
+    std::unique_ptr<j1_tokenizer> t;
+    if (j1_status s = load_tokenizer(text, t)) return s;
+    *out = t.release();
+    return J1_OK;
+  });
 }
 
 j1_status j1_tokenizer_from_json(const char* json, size_t len, j1_tokenizer** out) {
-  if (!json || !out) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
-  *out = nullptr;
-  std::unique_ptr<j1_tokenizer> t;
-  if (j1_status s = load_tokenizer(std::string(json, len), t)) return s;
-  *out = t.release();
-  return J1_OK;
+  return guard("j1_tokenizer_from_json", [&]() -> j1_status {
+    if (!json || !out) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+    *out = nullptr;
+    std::unique_ptr<j1_tokenizer> t;
+    if (j1_status s = load_tokenizer(std::string(json, len), t)) return s;
+    *out = t.release();
+    return J1_OK;
+  });
 }
 
 void j1_tokenizer_destroy(j1_tokenizer* t) { delete t; }
 
 int64_t j1_tokenizer_token_to_id(const j1_tokenizer* t, const char* token) {
   uint32_t id = 0;
-  if (!t || !token || !t->token_to_id(token, id)) return -1;
-  return id;
+  int64_t out = -1;
+  guard("j1_tokenizer_token_to_id", [&]() -> j1_status {
+    if (t && token && t->token_to_id(token, id)) out = id;
+    return J1_OK;
+  });
+  return out;
 }
 
 j1_status j1_tokenizer_encode(const j1_tokenizer* t, const char* text, size_t len, uint32_t* ids, size_t cap,
                               size_t* n_ids) {
-  if (!t || (!text && len) || !n_ids) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
-  const std::string s(text ? text : "", len);
-  if (!valid_utf8(s)) return set_error(J1_ERR_INVALID_ARG, "text is not valid UTF-8");
-  std::vector<uint32_t> v;
-  t->encode(s, v);
-  *n_ids = v.size();
-  if (v.size() > cap || (!ids && !v.empty()))
-    return set_error(J1_ERR_INVALID_ARG, "ids buffer too small (" + std::to_string(v.size()) + " needed)");
-  if (!v.empty()) std::memcpy(ids, v.data(), v.size() * 4);
-  return J1_OK;
+  return guard("j1_tokenizer_encode", [&]() -> j1_status {
+    if (!t || (!text && len) || !n_ids) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+    const std::string s(text ? text : "", len);
+    if (!valid_utf8(s)) return set_error(J1_ERR_INVALID_ARG, "text is not valid UTF-8");
+    std::vector<uint32_t> v;
+    t->encode(s, v);
+    *n_ids = v.size();
+    if (v.size() > cap || (!ids && !v.empty()))
+      return set_error(J1_ERR_INVALID_ARG, "ids buffer too small (" + std::to_string(v.size()) + " needed)");
+    if (!v.empty()) std::memcpy(ids, v.data(), v.size() * 4);
+    return J1_OK;
+  });
 }
 
 j1_status j1_tokenizer_encode_batch(const j1_tokenizer* t, size_t n, const char* const* texts, const size_t* lens,
                                     int32_t threads, uint32_t* ids, size_t cap, size_t* offsets) {
-  if (!t || !offsets || (n && (!texts || !lens))) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
-  std::vector<std::vector<uint32_t>> res(n);
-  std::atomic<size_t> next{0};
-  std::atomic<long> bad{-1};
-  auto work = [&]() {
-    for (size_t i = next++; i < n; i = next++) {
-      const std::string s(texts[i] ? texts[i] : "", lens[i]);
-      if (!valid_utf8(s)) {
-        bad = static_cast<long>(i);
-        continue;
+  return guard("j1_tokenizer_encode_batch", [&]() -> j1_status {
+    if (!t || !offsets || (n && (!texts || !lens))) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+    std::vector<std::vector<uint32_t>> res(n);
+    std::atomic<size_t> next{0};
+    std::atomic<long> bad{-1};
+    auto work = [&]() {
+      for (size_t i = next++; i < n; i = next++) {
+        const std::string s(texts[i] ? texts[i] : "", lens[i]);
+        if (!valid_utf8(s)) {
+          bad = static_cast<long>(i);
+          continue;
+        }
+        t->encode(s, res[i]);
       }
-      t->encode(s, res[i]);
-    }
-  };
-  const int nt = std::max(1, std::min<int>(threads > 0 ? threads : 1, static_cast<int>(std::max<size_t>(n, 1))));
-  if (nt == 1) {
-    work();
-  } else {
-    std::vector<std::thread> pool;
-    for (int k = 0; k < nt; ++k) pool.emplace_back(work);
-    for (auto& th : pool) th.join();
-  }
-  if (bad >= 0) return set_error(J1_ERR_INVALID_ARG, "text " + std::to_string(bad) + " is not valid UTF-8");
-  offsets[0] = 0;
-  for (size_t i = 0; i < n; ++i) offsets[i + 1] = offsets[i] + res[i].size();
-  if (offsets[n] > cap || (!ids && offsets[n]))
-    return set_error(J1_ERR_INVALID_ARG, "ids buffer too small (" + std::to_string(offsets[n]) + " needed)");
-  for (size_t i = 0; i < n; ++i)
-    if (!res[i].empty()) std::memcpy(ids + offsets[i], res[i].data(), res[i].size() * 4);
-  return J1_OK;
+    };
+    const int nt = std::max(1, std::min<int>(threads > 0 ? threads : 1, static_cast<int>(std::max<size_t>(n, 1))));
+    run_pool(nt, work);
+    if (bad >= 0) return set_error(J1_ERR_INVALID_ARG, "text " + std::to_string(bad) + " is not valid UTF-8");
+    offsets[0] = 0;
+    for (size_t i = 0; i < n; ++i) offsets[i + 1] = offsets[i] + res[i].size();
+    if (offsets[n] > cap || (!ids && offsets[n]))
+      return set_error(J1_ERR_INVALID_ARG, "ids buffer too small (" + std::to_string(offsets[n]) + " needed)");
+    for (size_t i = 0; i < n; ++i)
+      if (!res[i].empty()) std::memcpy(ids + offsets[i], res[i].data(), res[i].size() * 4);
+    return J1_OK;
+  });
 }
 
 j1_status j1_text_encoder_load(const char* dir, int32_t max_length, int32_t head_length, int32_t strict,
                                int64_t token_cache, int64_t encoding_cache, j1_text_encoder** out) {
-  if (!dir || !out) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
-  *out = nullptr;
-  const std::string root(dir);
-  std::string tj, cj;
-  if (!read_file(root + "/tokenizer.json", tj)) return set_error(J1_ERR_IO, "cannot read " + root + "/tokenizer.json");
-  if (!read_file(root + "/tokenizer_config.json", cj))
-    return set_error(J1_ERR_IO, "cannot read " + root + "/tokenizer_config.json");
-  // Encoder::from_parts (src/encode.rs:55-101)
-  if (static_cast<int64_t>(head_length) + 4 >= max_length)
-    return set_error(J1_ERR_INVALID_ARG, "max_length must leave room beyond the question head");
-  auto E = std::make_unique<j1_text_encoder>();
-  if (j1_status s = load_tokenizer(tj, E->tok)) return s;
-  Json cfg;
-  std::string err;
-  if (!parse_json(cj, cfg, err)) return set_error(J1_ERR_INVALID_ARG, "tokenizer_config.json: " + err);
-  auto special = [&](const char* key, std::string& name, uint32_t& id) -> j1_status {
-    const Json* v = cfg.get(key);
-    if (!v || v->kind != Json::String) return set_error(J1_ERR_INVALID_ARG, std::string("tokenizer lacks ") + key);
-    name = v->str;
-    if (!E->tok->token_to_id(name, id))
-      return set_error(J1_ERR_INVALID_ARG, std::string("unknown ") + key + " " + name);
+  return guard("j1_text_encoder_load", [&]() -> j1_status {
+    if (!dir || !out) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+    *out = nullptr;
+    const std::string root(dir);
+    std::string tj, cj;
+    if (!read_file(root + "/tokenizer.json", tj)) return set_error(J1_ERR_IO, "cannot read " + root + "/tokenizer.json");
+    if (!read_file(root + "/tokenizer_config.json", cj))
+      return set_error(J1_ERR_IO, "cannot read " + root + "/tokenizer_config.json");
+    // Encoder::from_parts (src/encode.rs:55-101)
+    if (static_cast<int64_t>(head_length) + 4 >= max_length)
+      return set_error(J1_ERR_INVALID_ARG, "max_length must leave room beyond the question head");
+    auto E = std::make_unique<j1_text_encoder>();
+    if (j1_status s = load_tokenizer(tj, E->tok)) return s;
+    Json cfg;
+    std::string err;
+    if (!parse_json(cj, cfg, err)) return set_error(J1_ERR_INVALID_ARG, "tokenizer_config.json: " + err);
+    auto special = [&](const char* key, std::string& name, uint32_t& id) -> j1_status {
+      const Json* v = cfg.get(key);
+      if (!v || v->kind != Json::String) return set_error(J1_ERR_INVALID_ARG, std::string("tokenizer lacks ") + key);
+      name = v->str;
+      if (!E->tok->token_to_id(name, id))
+        return set_error(J1_ERR_INVALID_ARG, std::string("unknown ") + key + " " + name);
+      return J1_OK;
+    };
+    std::string unused;
+    j1_encoder_options& o = E->opts;
+    if (j1_status s = special("mask_token", E->mask_token, o.mask_id)) return s;
+    if (j1_status s = special("cls_token", unused, o.cls_id)) return s;
+    if (j1_status s = special("sep_token", unused, o.sep_id)) return s;
+    uint32_t pad = 0;
+    if (j1_status s = special("pad_token", unused, pad)) return s;
+    o.max_length = max_length;
+    o.head_length = head_length;
+    o.strict = strict ? 1 : 0;
+    E->tokens = std::make_unique<Lru<std::vector<uint32_t>>>(token_cache > 0 ? static_cast<size_t>(token_cache) : 0);
+    E->encodings = std::make_unique<Lru<j1_text_encoder::Enc>>(encoding_cache > 0 ? static_cast<size_t>(encoding_cache)
+                                                                                   : 0);
+    *out = E.release();
     return J1_OK;
-  };
-  std::string unused;
-  j1_encoder_options& o = E->opts;
-  if (j1_status s = special("mask_token", E->mask_token, o.mask_id)) return s;
-  if (j1_status s = special("cls_token", unused, o.cls_id)) return s;
-  if (j1_status s = special("sep_token", unused, o.sep_id)) return s;
-  uint32_t pad = 0;
-  if (j1_status s = special("pad_token", unused, pad)) return s;
-  o.max_length = max_length;
-  o.head_length = head_length;
-  o.strict = strict ? 1 : 0;
-  E->tokens = std::make_unique<Lru<std::vector<uint32_t>>>(token_cache > 0 ? static_cast<size_t>(token_cache) : 0);
-  E->encodings = std::make_unique<Lru<j1_text_encoder::Enc>>(encoding_cache > 0 ? static_cast<size_t>(encoding_cache)
-                                                                                 : 0);
-  *out = E.release();
-  return J1_OK;
+  });
 }
 
 void j1_text_encoder_destroy(j1_text_encoder* e) { delete e; }
@@ -1048,206 +1056,214 @@ void j1_text_encoder_clear_cache(j1_text_encoder* e) {
 }
 
 j1_status j1_text_encoder_options(const j1_text_encoder* e, j1_encoder_options* out) {
-  if (!e || !out) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
-  *out = e->opts;
-  return J1_OK;
+  return guard("j1_text_encoder_options", [&]() -> j1_status {
+    if (!e || !out) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+    *out = e->opts;
+    return J1_OK;
+  });
 }
 
 j1_status j1_text_encoder_tokenize(j1_text_encoder* e, const char* text, size_t len, uint32_t* ids, size_t cap,
                                    size_t* n_ids) {
-  if (!e || (!text && len) || !n_ids) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
-  const std::string s(text ? text : "", len);
-  if (!valid_utf8(s)) return set_error(J1_ERR_INVALID_ARG, "text is not valid UTF-8");
-  std::vector<uint32_t> v;
-  e->tokenize(s, v);
-  *n_ids = v.size();
-  if (v.size() > cap || (!ids && !v.empty())) return set_error(J1_ERR_INVALID_ARG, "ids buffer too small");
-  if (!v.empty()) std::memcpy(ids, v.data(), v.size() * 4);
-  return J1_OK;
+  return guard("j1_text_encoder_tokenize", [&]() -> j1_status {
+    if (!e || (!text && len) || !n_ids) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+    const std::string s(text ? text : "", len);
+    if (!valid_utf8(s)) return set_error(J1_ERR_INVALID_ARG, "text is not valid UTF-8");
+    std::vector<uint32_t> v;
+    e->tokenize(s, v);
+    *n_ids = v.size();
+    if (v.size() > cap || (!ids && !v.empty())) return set_error(J1_ERR_INVALID_ARG, "ids buffer too small");
+    if (!v.empty()) std::memcpy(ids, v.data(), v.size() * 4);
+    return J1_OK;
+  });
 }
 
 j1_status j1_text_encoder_encode(j1_text_encoder* e, const char* state, int32_t state_is_json, const char* question,
                                  const char* const* options, size_t n_options, uint8_t qtype, uint32_t* ids,
                                  size_t cap, size_t* ids_len, uint32_t* markers, int32_t* truncated) {
-  if (!e || !ids_len) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
-  std::string st, q;
-  std::vector<std::string> opts;
-  if (j1_status s = read_request(state, question, options, n_options, qtype, st, q, opts)) return s;
-  // Encoder::encode (src/encode.rs:131-154): whole-request cache keyed on its text
-  std::string key;
-  if (true) {
-    key.reserve(st.size() + q.size() + 64);
-    auto put = [&key](const std::string& s) {
-      const uint64_t n = s.size();
-      key.append(reinterpret_cast<const char*>(&n), 8);
-      key += s;
-    };
-    put(st);
-    put(q);
-    for (const auto& s : opts) put(s);
-    key += static_cast<char>(qtype);
-    key += state_is_json ? 'j' : 't';
-  }
-  j1_text_encoder::Enc enc;
-  if (!e->encodings->get(key, enc)) {
-    std::string rendered;
-    if (state_is_json) {  // State::render (src/request.rs:49-54)
-      if (j1_status s = render_json_state(st, rendered)) return s;
+  return guard("j1_text_encoder_encode", [&]() -> j1_status {
+    if (!e || !ids_len) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+    std::string st, q;
+    std::vector<std::string> opts;
+    if (j1_status s = read_request(state, question, options, n_options, qtype, st, q, opts)) return s;
+    // Encoder::encode (src/encode.rs:131-154): whole-request cache keyed on its text
+    std::string key;
+    if (true) {
+      key.reserve(st.size() + q.size() + 64);
+      auto put = [&key](const std::string& s) {
+        const uint64_t n = s.size();
+        key.append(reinterpret_cast<const char*>(&n), 8);
+        key += s;
+      };
+      put(st);
+      put(q);
+      for (const auto& s : opts) put(s);
+      key += static_cast<char>(qtype);
+      key += state_is_json ? 'j' : 't';
     }
-    std::vector<uint32_t> head, opt_ids, opt_lens, state_ids;
-    if (j1_status s = request_tokens(e, state_is_json ? rendered : st, q, opts, qtype, head, opt_ids, opt_lens,
-                                     state_ids))
-      return s;
-    j1_tokenized_request r{head.data(), head.size(), opt_ids.data(), opt_lens.data(), n_options,
-                           state_ids.data(), state_ids.size(), qtype};
-    enc.ids.assign(static_cast<size_t>(e->opts.max_length), 0);
-    enc.markers.assign(std::max<size_t>(n_options, 1), 0);
-    size_t n = 0;
-    if (j1_status s = j1_encode_sequence(&e->opts, &r, enc.ids.data(), enc.ids.size(), &n, enc.markers.data(),
-                                         &enc.truncated))
-      return s;
-    enc.ids.resize(n);
-    enc.markers.resize(n_options);
-    e->encodings->put(key, enc);
-  }
-  *ids_len = enc.ids.size();
-  if (enc.ids.size() > cap || !ids || (!markers && n_options))
-    return set_error(J1_ERR_INVALID_ARG, "output arrays too small (ids_cap >= max_length, markers >= n_options)");
-  std::memcpy(ids, enc.ids.data(), enc.ids.size() * 4);
-  if (n_options) std::memcpy(markers, enc.markers.data(), n_options * 4);
-  if (truncated) *truncated = enc.truncated;
-  return J1_OK;
+    j1_text_encoder::Enc enc;
+    if (!e->encodings->get(key, enc)) {
+      std::string rendered;
+      if (state_is_json) {  // State::render (src/request.rs:49-54)
+        if (j1_status s = render_json_state(st, rendered)) return s;
+      }
+      std::vector<uint32_t> head, opt_ids, opt_lens, state_ids;
+      if (j1_status s = request_tokens(e, state_is_json ? rendered : st, q, opts, qtype, head, opt_ids, opt_lens,
+                                       state_ids))
+        return s;
+      j1_tokenized_request r{head.data(), head.size(), opt_ids.data(), opt_lens.data(), n_options,
+                             state_ids.data(), state_ids.size(), qtype};
+      enc.ids.assign(static_cast<size_t>(e->opts.max_length), 0);
+      enc.markers.assign(std::max<size_t>(n_options, 1), 0);
+      size_t n = 0;
+      if (j1_status s = j1_encode_sequence(&e->opts, &r, enc.ids.data(), enc.ids.size(), &n, enc.markers.data(),
+                                           &enc.truncated))
+        return s;
+      enc.ids.resize(n);
+      enc.markers.resize(n_options);
+      e->encodings->put(key, enc);
+    }
+    *ids_len = enc.ids.size();
+    if (enc.ids.size() > cap || !ids || (!markers && n_options))
+      return set_error(J1_ERR_INVALID_ARG, "output arrays too small (ids_cap >= max_length, markers >= n_options)");
+    std::memcpy(ids, enc.ids.data(), enc.ids.size() * 4);
+    if (n_options) std::memcpy(markers, enc.markers.data(), n_options * 4);
+    if (truncated) *truncated = enc.truncated;
+    return J1_OK;
+  });
 }
 
 j1_status j1_json_dumps(const char* json, size_t len, char* out, size_t cap, size_t* out_len) {
-  if ((!json && len) || !out_len) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
-  Json j;
-  std::string err;
-  if (!parse_json(std::string(json ? json : "", len), j, err)) return set_error(J1_ERR_INVALID_ARG, "invalid JSON: " + err);
-  std::string s;
-  py_dumps(s, j);
-  *out_len = s.size();
-  if (s.size() > cap || (!out && !s.empty()))
-    return set_error(J1_ERR_INVALID_ARG, "output buffer too small (" + std::to_string(s.size()) + " bytes needed)");
-  if (!s.empty()) std::memcpy(out, s.data(), s.size());
-  return J1_OK;
+  return guard("j1_json_dumps", [&]() -> j1_status {
+    if ((!json && len) || !out_len) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+    Json j;
+    std::string err;
+    if (!parse_json(std::string(json ? json : "", len), j, err)) return set_error(J1_ERR_INVALID_ARG, "invalid JSON: " + err);
+    std::string s;
+    py_dumps(s, j);
+    *out_len = s.size();
+    if (s.size() > cap || (!out && !s.empty()))
+      return set_error(J1_ERR_INVALID_ARG, "output buffer too small (" + std::to_string(s.size()) + " bytes needed)");
+    if (!s.empty()) std::memcpy(out, s.data(), s.size());
+    return J1_OK;
+  });
 }
 
 j1_status j1_text_encoder_encode_batch(j1_text_encoder* e, size_t n, const j1_text_request* rows, int32_t threads,
                                       uint32_t* ids, size_t cap, size_t* offsets, uint32_t* markers, size_t mcap,
                                       size_t* moffsets, int32_t* truncated) {
-  if (!e || !offsets || !moffsets || (n && !rows)) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
-  struct Out {
-    std::vector<uint32_t> ids, markers;
-    int32_t truncated = 0;
-    j1_status status = J1_OK;
-    std::string err;
-  };
-  std::vector<Out> res(n);
-  const size_t row_cap = static_cast<size_t>(std::max(e->opts.max_length, 1));
-  std::atomic<size_t> next{0};
-  auto work = [&]() {
-    for (size_t i = next++; i < n; i = next++) {
-      const j1_text_request& r = rows[i];
-      Out& o = res[i];
-      o.ids.resize(row_cap);
-      o.markers.resize(std::max<size_t>(r.n_options, 1));
-      size_t len = 0;
-      o.status = j1_text_encoder_encode(e, r.state, r.state_is_json, r.question, r.options, r.n_options, r.qtype,
-                                        o.ids.data(), o.ids.size(), &len, o.markers.data(), &o.truncated);
-      if (o.status) {
-        char buf[512];
-        j1_last_error(buf, sizeof(buf));  // the message is thread-local: keep it with the row
-        o.err = buf;
-        continue;
+  return guard("j1_text_encoder_encode_batch", [&]() -> j1_status {
+    if (!e || !offsets || !moffsets || (n && !rows)) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+    struct Out {
+      std::vector<uint32_t> ids, markers;
+      int32_t truncated = 0;
+      j1_status status = J1_OK;
+      std::string err;
+    };
+    std::vector<Out> res(n);
+    const size_t row_cap = static_cast<size_t>(std::max(e->opts.max_length, 1));
+    std::atomic<size_t> next{0};
+    auto work = [&]() {
+      for (size_t i = next++; i < n; i = next++) {
+        const j1_text_request& r = rows[i];
+        Out& o = res[i];
+        o.ids.resize(row_cap);
+        o.markers.resize(std::max<size_t>(r.n_options, 1));
+        size_t len = 0;
+        o.status = j1_text_encoder_encode(e, r.state, r.state_is_json, r.question, r.options, r.n_options, r.qtype,
+                                          o.ids.data(), o.ids.size(), &len, o.markers.data(), &o.truncated);
+        if (o.status) {
+          char buf[512];
+          j1_last_error(buf, sizeof(buf));  // the message is thread-local: keep it with the row
+          o.err = buf;
+          continue;
+        }
+        o.ids.resize(len);
+        o.markers.resize(r.n_options);
       }
-      o.ids.resize(len);
-      o.markers.resize(r.n_options);
+    };
+    const int nt = std::max(1, std::min<int>(threads > 0 ? threads : 1, static_cast<int>(std::max<size_t>(n, 1))));
+    run_pool(nt, work);
+    for (size_t i = 0; i < n; ++i)  // the first failing row, as an in-order encode would report it
+      if (res[i].status) return set_error(res[i].status, "JSONL line " + std::to_string(i + 1) + ": " + res[i].err);
+    offsets[0] = moffsets[0] = 0;
+    for (size_t i = 0; i < n; ++i) {
+      offsets[i + 1] = offsets[i] + res[i].ids.size();
+      moffsets[i + 1] = moffsets[i] + res[i].markers.size();
     }
-  };
-  const int nt = std::max(1, std::min<int>(threads > 0 ? threads : 1, static_cast<int>(std::max<size_t>(n, 1))));
-  if (nt == 1) {
-    work();
-  } else {
-    std::vector<std::thread> pool;
-    for (int k = 0; k < nt; ++k) pool.emplace_back(work);
-    for (auto& th : pool) th.join();
-  }
-  for (size_t i = 0; i < n; ++i)  // the first failing row, as an in-order encode would report it
-    if (res[i].status) return set_error(res[i].status, "JSONL line " + std::to_string(i + 1) + ": " + res[i].err);
-  offsets[0] = moffsets[0] = 0;
-  for (size_t i = 0; i < n; ++i) {
-    offsets[i + 1] = offsets[i] + res[i].ids.size();
-    moffsets[i + 1] = moffsets[i] + res[i].markers.size();
-  }
-  if (offsets[n] > cap || moffsets[n] > mcap || (offsets[n] && !ids) || (moffsets[n] && !markers))
-    return set_error(J1_ERR_INVALID_ARG, "output arrays too small (" + std::to_string(offsets[n]) + " ids, " +
-                                             std::to_string(moffsets[n]) + " markers needed)");
-  for (size_t i = 0; i < n; ++i) {
-    if (!res[i].ids.empty()) std::memcpy(ids + offsets[i], res[i].ids.data(), res[i].ids.size() * 4);
-    if (!res[i].markers.empty()) std::memcpy(markers + moffsets[i], res[i].markers.data(), res[i].markers.size() * 4);
-    if (truncated) truncated[i] = res[i].truncated;
-  }
-  return J1_OK;
+    if (offsets[n] > cap || moffsets[n] > mcap || (offsets[n] && !ids) || (moffsets[n] && !markers))
+      return set_error(J1_ERR_INVALID_ARG, "output arrays too small (" + std::to_string(offsets[n]) + " ids, " +
+                                               std::to_string(moffsets[n]) + " markers needed)");
+    for (size_t i = 0; i < n; ++i) {
+      if (!res[i].ids.empty()) std::memcpy(ids + offsets[i], res[i].ids.data(), res[i].ids.size() * 4);
+      if (!res[i].markers.empty()) std::memcpy(markers + moffsets[i], res[i].markers.data(), res[i].markers.size() * 4);
+      if (truncated) truncated[i] = res[i].truncated;
+    }
+    return J1_OK;
+  });
 }
 
 j1_status j1_engine_logits_text(j1_engine* engine, j1_text_encoder* e, size_t n, const j1_text_request* rows,
                                 int32_t threads, float* logits_out) {
-  if (!engine || !e) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
-  if (n == 0) return J1_OK;
-  if (!rows || !logits_out) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
-  // Request::validate for every row before any encoding (src/engine.rs:183-188)
-  for (size_t i = 0; i < n; ++i) {
-    const j1_text_request& r = rows[i];
-    bool empty = r.n_options && !r.options;
-    for (size_t k = 0; k < r.n_options && !empty; ++k) empty = !r.options[k] || !r.options[k][0];
-    if (r.n_options < 2 || r.n_options > 20 || empty)
-      return set_error(J1_ERR_INVALID_ARG, "JSONL line " + std::to_string(i + 1) +
-                                               ": options must contain 2–20 nonempty rendered descriptions");
-    if (r.qtype == 2 && r.n_options != 2)
-      return set_error(J1_ERR_INVALID_ARG,
-                       "JSONL line " + std::to_string(i + 1) + ": noul options must be ordered [false, true]");
-  }
-  if (e->opts.max_length > j1_engine_max_length(engine))
-    return set_error(J1_ERR_INVALID_ARG, "encoder max_length exceeds the engine's max_length");
-  const size_t cap = n * static_cast<size_t>(std::max(e->opts.max_length, 1));
-  size_t mcap = 0;
-  for (size_t i = 0; i < n; ++i) mcap += rows[i].n_options;
-  std::vector<uint32_t> ids(cap), markers(std::max<size_t>(mcap, 1));
-  std::vector<size_t> offs(n + 1), moffs(n + 1);
-  if (j1_status s = j1_text_encoder_encode_batch(e, n, rows, threads, ids.data(), cap, offs.data(), markers.data(),
-                                                 mcap, moffs.data(), nullptr))
-    return s;
-  std::vector<uint32_t> lens(n), nmark(n);
-  std::vector<uint8_t> qt(n);
-  for (size_t i = 0; i < n; ++i) {
-    lens[i] = static_cast<uint32_t>(offs[i + 1] - offs[i]);
-    nmark[i] = static_cast<uint32_t>(moffs[i + 1] - moffs[i]);
-    qt[i] = rows[i].qtype;
-  }
-  return j1_engine_logits_encoded(engine, n, ids.data(), lens.data(), markers.data(), nmark.data(), qt.data(),
-                                  logits_out);
+  return guard("j1_engine_logits_text", [&]() -> j1_status {
+    if (!engine || !e) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+    if (n == 0) return J1_OK;
+    if (!rows || !logits_out) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+    // Request::validate for every row before any encoding (src/engine.rs:183-188)
+    for (size_t i = 0; i < n; ++i) {
+      const j1_text_request& r = rows[i];
+      bool empty = r.n_options && !r.options;
+      for (size_t k = 0; k < r.n_options && !empty; ++k) empty = !r.options[k] || !r.options[k][0];
+      if (r.n_options < 2 || r.n_options > 20 || empty)
+        return set_error(J1_ERR_INVALID_ARG, "JSONL line " + std::to_string(i + 1) +
+                                                 ": options must contain 2–20 nonempty rendered descriptions");
+      if (r.qtype == 2 && r.n_options != 2)
+        return set_error(J1_ERR_INVALID_ARG,
+                         "JSONL line " + std::to_string(i + 1) + ": noul options must be ordered [false, true]");
+    }
+    if (e->opts.max_length > j1_engine_max_length(engine))
+      return set_error(J1_ERR_INVALID_ARG, "encoder max_length exceeds the engine's max_length");
+    const size_t cap = n * static_cast<size_t>(std::max(e->opts.max_length, 1));
+    size_t mcap = 0;
+    for (size_t i = 0; i < n; ++i) mcap += rows[i].n_options;
+    std::vector<uint32_t> ids(cap), markers(std::max<size_t>(mcap, 1));
+    std::vector<size_t> offs(n + 1), moffs(n + 1);
+    if (j1_status s = j1_text_encoder_encode_batch(e, n, rows, threads, ids.data(), cap, offs.data(), markers.data(),
+                                                   mcap, moffs.data(), nullptr))
+      return s;
+    std::vector<uint32_t> lens(n), nmark(n);
+    std::vector<uint8_t> qt(n);
+    for (size_t i = 0; i < n; ++i) {
+      lens[i] = static_cast<uint32_t>(offs[i + 1] - offs[i]);
+      nmark[i] = static_cast<uint32_t>(moffs[i + 1] - moffs[i]);
+      qt[i] = rows[i].qtype;
+    }
+    return j1_engine_logits_encoded(engine, n, ids.data(), lens.data(), markers.data(), nmark.data(), qt.data(),
+                                    logits_out);
+  });
 }
 
 j1_status j1_text_encoder_request_tokens(j1_text_encoder* e, const char* state, const char* question,
                                          const char* const* options, size_t n_options, uint8_t qtype, uint32_t* ids,
                                          size_t cap, size_t* total, uint32_t* piece_lens) {
-  if (!e || !total) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
-  std::string st, q;
-  std::vector<std::string> opts;
-  if (j1_status s = read_request(state, question, options, n_options, qtype, st, q, opts)) return s;
-  std::vector<uint32_t> head, opt_ids, opt_lens, state_ids;
-  if (j1_status s = request_tokens(e, st, q, opts, qtype, head, opt_ids, opt_lens, state_ids)) return s;
-  *total = head.size() + opt_ids.size() + state_ids.size();
-  if (!ids || !piece_lens) return J1_OK;  // size query
-  if (*total > cap) return set_error(J1_ERR_INVALID_ARG, "ids buffer too small");
-  std::memcpy(ids, head.data(), head.size() * 4);
-  std::memcpy(ids + head.size(), opt_ids.data(), opt_ids.size() * 4);
-  std::memcpy(ids + head.size() + opt_ids.size(), state_ids.data(), state_ids.size() * 4);
-  piece_lens[0] = static_cast<uint32_t>(head.size());
-  for (size_t k = 0; k < n_options; ++k) piece_lens[1 + k] = opt_lens[k];
-  piece_lens[1 + n_options] = static_cast<uint32_t>(state_ids.size());
-  return J1_OK;
+  return guard("j1_text_encoder_request_tokens", [&]() -> j1_status {
+    if (!e || !total) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+    std::string st, q;
+    std::vector<std::string> opts;
+    if (j1_status s = read_request(state, question, options, n_options, qtype, st, q, opts)) return s;
+    std::vector<uint32_t> head, opt_ids, opt_lens, state_ids;
+    if (j1_status s = request_tokens(e, st, q, opts, qtype, head, opt_ids, opt_lens, state_ids)) return s;
+    *total = head.size() + opt_ids.size() + state_ids.size();
+    if (!ids || !piece_lens) return J1_OK;  // size query
+    if (*total > cap) return set_error(J1_ERR_INVALID_ARG, "ids buffer too small");
+    std::memcpy(ids, head.data(), head.size() * 4);
+    std::memcpy(ids + head.size(), opt_ids.data(), opt_ids.size() * 4);
+    std::memcpy(ids + head.size() + opt_ids.size(), state_ids.data(), state_ids.size() * 4);
+    piece_lens[0] = static_cast<uint32_t>(head.size());
+    for (size_t k = 0; k < n_options; ++k) piece_lens[1 + k] = opt_lens[k];
+    piece_lens[1 + n_options] = static_cast<uint32_t>(state_ids.size());
+    return J1_OK;
+  });
 }
 
 }  // extern "C"

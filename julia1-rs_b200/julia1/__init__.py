@@ -17,9 +17,9 @@ import numpy as np
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(os.path.dirname(_HERE), "lib", "libj1.so")
 
-OK, INVALID_ARG, UNSUPPORTED, CUDA, OOM, NONFINITE, DEVICE_TIMEOUT, IO = range(8)
+OK, INVALID_ARG, UNSUPPORTED, CUDA, OOM, NONFINITE, DEVICE_TIMEOUT, IO, INTERNAL = range(9)
 STATUS_NAMES = ["J1_OK", "J1_ERR_INVALID_ARG", "J1_ERR_UNSUPPORTED", "J1_ERR_CUDA", "J1_ERR_OOM",
-                "J1_ERR_NONFINITE", "J1_ERR_DEVICE_TIMEOUT", "J1_ERR_IO"]
+                "J1_ERR_NONFINITE", "J1_ERR_DEVICE_TIMEOUT", "J1_ERR_IO", "J1_ERR_INTERNAL"]
 
 # Every symbol include/j1.h declares (checked by tests against the built library).
 EXPORTS = [
@@ -40,7 +40,7 @@ EXPORTS = [
     "j1_text_encoder_request_tokens", "j1_text_encoder_encode_batch", "j1_engine_logits_text", "j1_json_dumps",
     "j1_inject_fault", "j1_selftest_device_timeout",
 ]
-FAULT_ALLOC, FAULT_LAUNCH, FAULT_NAN = 1, 2, 3
+FAULT_ALLOC, FAULT_LAUNCH, FAULT_NAN, FAULT_HOST, FAULT_WORKER = 1, 2, 3, 4, 5
 PROF_FAMILIES = 12
 
 EPI_BF16, EPI_QKV_ROPE, EPI_GEGLU, EPI_RESID_LN, EPI_RESID, EPI_SCORER = range(6)
@@ -811,7 +811,9 @@ class Tokenizer:
 
 def inject_fault(kind: int, count: int = 1):
     """Host-side fault injection (j1_inject_fault): the next `count` device allocations
-    (FAULT_ALLOC), kernel launches (FAULT_LAUNCH) or score readbacks (FAULT_NAN) fail."""
+    (FAULT_ALLOC), kernel launches (FAULT_LAUNCH) or score readbacks (FAULT_NAN) fail; with
+    FAULT_HOST the next entry points throw std::bad_alloc inside the library (-> OOM), with
+    FAULT_WORKER the next host worker threads throw (-> INTERNAL)."""
     lib().j1_inject_fault(int(kind), int(count))
 
 

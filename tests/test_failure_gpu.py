@@ -1,7 +1,7 @@
 """Failure detection without a GPU fault (B200). Every failure is made on the host or by a
 bounded device wait that runs out, never by faulting or hanging the GPU:
-* injected allocation / launch failures and nonfinite scores (j1_inject_fault) come back as
-  J1_ERR_OOM / J1_ERR_CUDA / J1_ERR_NONFINITE ("Inference returned nonfinite logits",
+* injected allocation / launch failures, nonfinite scores and a failing host worker thread
+  (j1_inject_fault) come back as J1_ERR_OOM / J1_ERR_CUDA / J1_ERR_NONFINITE / J1_ERR_INTERNAL ("Inference returned nonfinite logits",
   src/engine.rs:219-221) through the model, the engine and the router, and the same handle
   then computes the right logits again;
 * a device wait on a barrier nothing arrives at times out after its limit, is reported as
@@ -60,6 +60,11 @@ def test_injected_faults_through_engine_and_router(torch_cuda, ckpt):
     j1.inject_fault(j1.FAULT_LAUNCH, 1)
     with pytest.raises(j1.J1Error, match="injected launch failure"):
         eng.logits_encoded(rows)
+    assert eng.logits_encoded(rows) == want
+    j1.inject_fault(j1.FAULT_WORKER, 1)  # the engine's device worker throws on the host
+    with pytest.raises(j1.J1Error, match="injected worker failure") as e:
+        eng.logits_encoded(rows)
+    assert e.value.status == j1.INTERNAL
     assert eng.logits_encoded(rows) == want
     enc = j1.EncoderOptions(cls_id=1, sep_id=2, mask_id=4, max_length=512)
     router = j1.Router(engine=eng, encoder=enc)
