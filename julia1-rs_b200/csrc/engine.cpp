@@ -91,6 +91,11 @@ void plan(size_t n_rows, const uint32_t* row_lens, size_t batch_size, size_t max
 
 }  // namespace
 
+size_t j1rt::engine_pipeline_rows(const j1_engine* e) {
+  const size_t b = e->opts.batch_size > 0 ? static_cast<size_t>(e->opts.batch_size) : 16;
+  return std::max<size_t>(256, 4 * b * std::max<size_t>(e->models.size(), 1));
+}
+
 extern "C" {
 
 void j1_engine_options_default(j1_engine_options* o) {

@@ -47,6 +47,10 @@ j1_status guard(const char* fn, F&& body) noexcept {
 // there and rethrown here (the first one) once every started thread has been joined.
 void run_pool(int n, const std::function<void()>& work);
 
+// Rows per chunk when j1_engine_logits_text overlaps text encoding with the forward: four
+// of the engine's micro-batches per device (at least 256 rows).
+size_t engine_pipeline_rows(const j1_engine* e);
+
 // Restores the calling thread's current device on scope exit.
 class DeviceGuard {
  public:

@@ -1149,59 +1149,124 @@ j1_status j1_json_dumps(const char* json, size_t len, char* out, size_t cap, siz
   });
 }
 
+namespace {
+
+// Engine::encode's parallel Encoder::encode over rows[0, n); a failing row is reported as
+// "JSONL line <line0 + its index + 1>" (the first failing one, as an in-order encode would).
+j1_status encode_rows(j1_text_encoder* e, size_t n, const j1_text_request* rows, int32_t threads, size_t line0,
+                      uint32_t* ids, size_t cap, size_t* offsets, uint32_t* markers, size_t mcap, size_t* moffsets,
+                      int32_t* truncated) {
+  if (!e || !offsets || !moffsets || (n && !rows)) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
+  struct Out {
+    std::vector<uint32_t> ids, markers;
+    int32_t truncated = 0;
+    j1_status status = J1_OK;
+    std::string err;
+  };
+  std::vector<Out> res(n);
+  const size_t row_cap = static_cast<size_t>(std::max(e->opts.max_length, 1));
+  std::atomic<size_t> next{0};
+  auto work = [&]() {
+    for (size_t i = next++; i < n; i = next++) {
+      const j1_text_request& r = rows[i];
+      Out& o = res[i];
+      o.ids.resize(row_cap);
+      o.markers.resize(std::max<size_t>(r.n_options, 1));
+      size_t len = 0;
+      o.status = j1_text_encoder_encode(e, r.state, r.state_is_json, r.question, r.options, r.n_options, r.qtype,
+                                        o.ids.data(), o.ids.size(), &len, o.markers.data(), &o.truncated);
+      if (o.status) {
+        char buf[512];
+        j1_last_error(buf, sizeof(buf));  // the message is thread-local: keep it with the row
+        o.err = buf;
+        continue;
+      }
+      o.ids.resize(len);
+      o.markers.resize(r.n_options);
+    }
+  };
+  const int nt = std::max(1, std::min<int>(threads > 0 ? threads : 1, static_cast<int>(std::max<size_t>(n, 1))));
+  run_pool(nt, work);
+  for (size_t i = 0; i < n; ++i)  // the first failing row, as an in-order encode would report it
+    if (res[i].status) return set_error(res[i].status, "JSONL line " + std::to_string(line0 + i + 1) + ": " + res[i].err);
+  offsets[0] = moffsets[0] = 0;
+  for (size_t i = 0; i < n; ++i) {
+    offsets[i + 1] = offsets[i] + res[i].ids.size();
+    moffsets[i + 1] = moffsets[i] + res[i].markers.size();
+  }
+  if (offsets[n] > cap || moffsets[n] > mcap || (offsets[n] && !ids) || (moffsets[n] && !markers))
+    return set_error(J1_ERR_INVALID_ARG, "output arrays too small (" + std::to_string(offsets[n]) + " ids, " +
+                                             std::to_string(moffsets[n]) + " markers needed)");
+  for (size_t i = 0; i < n; ++i) {
+    if (!res[i].ids.empty()) std::memcpy(ids + offsets[i], res[i].ids.data(), res[i].ids.size() * 4);
+    if (!res[i].markers.empty()) std::memcpy(markers + moffsets[i], res[i].markers.data(), res[i].markers.size() * 4);
+    if (truncated) truncated[i] = res[i].truncated;
+  }
+  return J1_OK;
+}
+
+}  // namespace
+
 j1_status j1_text_encoder_encode_batch(j1_text_encoder* e, size_t n, const j1_text_request* rows, int32_t threads,
                                       uint32_t* ids, size_t cap, size_t* offsets, uint32_t* markers, size_t mcap,
                                       size_t* moffsets, int32_t* truncated) {
   return guard("j1_text_encoder_encode_batch", [&]() -> j1_status {
-    if (!e || !offsets || !moffsets || (n && !rows)) return set_error(J1_ERR_INVALID_ARG, "NULL argument");
-    struct Out {
-      std::vector<uint32_t> ids, markers;
-      int32_t truncated = 0;
-      j1_status status = J1_OK;
-      std::string err;
-    };
-    std::vector<Out> res(n);
-    const size_t row_cap = static_cast<size_t>(std::max(e->opts.max_length, 1));
-    std::atomic<size_t> next{0};
-    auto work = [&]() {
-      for (size_t i = next++; i < n; i = next++) {
-        const j1_text_request& r = rows[i];
-        Out& o = res[i];
-        o.ids.resize(row_cap);
-        o.markers.resize(std::max<size_t>(r.n_options, 1));
-        size_t len = 0;
-        o.status = j1_text_encoder_encode(e, r.state, r.state_is_json, r.question, r.options, r.n_options, r.qtype,
-                                          o.ids.data(), o.ids.size(), &len, o.markers.data(), &o.truncated);
-        if (o.status) {
-          char buf[512];
-          j1_last_error(buf, sizeof(buf));  // the message is thread-local: keep it with the row
-          o.err = buf;
-          continue;
-        }
-        o.ids.resize(len);
-        o.markers.resize(r.n_options);
-      }
-    };
-    const int nt = std::max(1, std::min<int>(threads > 0 ? threads : 1, static_cast<int>(std::max<size_t>(n, 1))));
-    run_pool(nt, work);
-    for (size_t i = 0; i < n; ++i)  // the first failing row, as an in-order encode would report it
-      if (res[i].status) return set_error(res[i].status, "JSONL line " + std::to_string(i + 1) + ": " + res[i].err);
-    offsets[0] = moffsets[0] = 0;
-    for (size_t i = 0; i < n; ++i) {
-      offsets[i + 1] = offsets[i] + res[i].ids.size();
-      moffsets[i + 1] = moffsets[i] + res[i].markers.size();
-    }
-    if (offsets[n] > cap || moffsets[n] > mcap || (offsets[n] && !ids) || (moffsets[n] && !markers))
-      return set_error(J1_ERR_INVALID_ARG, "output arrays too small (" + std::to_string(offsets[n]) + " ids, " +
-                                               std::to_string(moffsets[n]) + " markers needed)");
-    for (size_t i = 0; i < n; ++i) {
-      if (!res[i].ids.empty()) std::memcpy(ids + offsets[i], res[i].ids.data(), res[i].ids.size() * 4);
-      if (!res[i].markers.empty()) std::memcpy(markers + moffsets[i], res[i].markers.data(), res[i].markers.size() * 4);
-      if (truncated) truncated[i] = res[i].truncated;
-    }
-    return J1_OK;
+    return encode_rows(e, n, rows, threads, 0, ids, cap, offsets, markers, mcap, moffsets, truncated);
   });
 }
+
+namespace {
+
+// The calling thread's last error message, for handing it to another thread.
+std::string last_error_text() {
+  const size_t n = j1_last_error(nullptr, 0);
+  std::string m(n + 1, '\0');
+  j1_last_error(&m[0], m.size());
+  m.resize(n);
+  return m;
+}
+
+// One chunk of rows [r0, r1) of a j1_engine_logits_text call, encoded for the engine.
+struct TextChunk {
+  size_t r0 = 0, r1 = 0;
+  std::vector<uint32_t> ids, markers, lens, nmark;
+  std::vector<uint8_t> qt;
+  std::vector<size_t> offs, moffs;
+  j1_status st = J1_OK;
+  std::string err;
+};
+
+void encode_chunk(j1_text_encoder* e, const j1_text_request* rows, const std::vector<size_t>& mstart,
+                  int32_t threads, TextChunk& c) noexcept {
+  try {
+    const size_t m = c.r1 - c.r0;
+    const size_t L = static_cast<size_t>(std::max(e->opts.max_length, 1));
+    c.ids.resize(m * L);
+    c.markers.resize(std::max<size_t>(mstart[c.r1] - mstart[c.r0], 1));
+    c.offs.resize(m + 1);
+    c.moffs.resize(m + 1);
+    c.st = encode_rows(e, m, rows + c.r0, threads, c.r0, c.ids.data(), c.ids.size(), c.offs.data(),
+                       c.markers.data(), c.markers.size(), c.moffs.data(), nullptr);
+    if (c.st) {
+      c.err = last_error_text();
+      return;
+    }
+    c.lens.resize(m);
+    c.nmark.resize(m);
+    c.qt.resize(m);
+    for (size_t i = 0; i < m; ++i) {
+      c.lens[i] = static_cast<uint32_t>(c.offs[i + 1] - c.offs[i]);
+      c.nmark[i] = static_cast<uint32_t>(c.moffs[i + 1] - c.moffs[i]);
+      c.qt[i] = rows[c.r0 + i].qtype;
+    }
+  } catch (const std::bad_alloc&) {
+    c.st = J1_ERR_OOM;  // the caller words the message
+  } catch (...) {
+    c.st = J1_ERR_INTERNAL;
+  }
+}
+
+}  // namespace
 
 j1_status j1_engine_logits_text(j1_engine* engine, j1_text_encoder* e, size_t n, const j1_text_request* rows,
                                 int32_t threads, float* logits_out) {
@@ -1223,23 +1288,51 @@ j1_status j1_engine_logits_text(j1_engine* engine, j1_text_encoder* e, size_t n,
     }
     if (e->opts.max_length > j1_engine_max_length(engine))
       return set_error(J1_ERR_INVALID_ARG, "encoder max_length exceeds the engine's max_length");
-    const size_t cap = n * static_cast<size_t>(std::max(e->opts.max_length, 1));
-    size_t mcap = 0;
-    for (size_t i = 0; i < n; ++i) mcap += rows[i].n_options;
-    std::vector<uint32_t> ids(cap), markers(std::max<size_t>(mcap, 1));
-    std::vector<size_t> offs(n + 1), moffs(n + 1);
-    if (j1_status s = j1_text_encoder_encode_batch(e, n, rows, threads, ids.data(), cap, offs.data(), markers.data(),
-                                                   mcap, moffs.data(), nullptr))
-      return s;
-    std::vector<uint32_t> lens(n), nmark(n);
-    std::vector<uint8_t> qt(n);
-    for (size_t i = 0; i < n; ++i) {
-      lens[i] = static_cast<uint32_t>(offs[i + 1] - offs[i]);
-      nmark[i] = static_cast<uint32_t>(moffs[i + 1] - moffs[i]);
-      qt[i] = rows[i].qtype;
+    // Engine::logits (src/engine.rs:236-243) encodes every row, then scores them all. Here the
+    // rows go in chunks of a few engine micro-batches and a helper thread encodes chunk k + 1
+    // while this thread scores chunk k. A row's logits do not depend on the rows batched
+    // with it, so the results are the same bits; an encoding error (the first failing row)
+    // still takes precedence over a forward error, as in encode-then-score order.
+    std::vector<size_t> mstart(n + 1, 0);
+    for (size_t i = 0; i < n; ++i) mstart[i + 1] = mstart[i] + rows[i].n_options;
+    const size_t R = std::max<size_t>(1, engine_pipeline_rows(engine));
+    auto failed = [](const TextChunk& c) {
+      return set_error(c.st, !c.err.empty() ? c.err
+                             : c.st == J1_ERR_OOM ? "j1_engine_logits_text: host memory exhausted"
+                                                  : "j1_engine_logits_text: encoding failed");
+    };
+    TextChunk cur, next;
+    cur.r1 = std::min(n, std::max<size_t>(R / 4, 1));  // a short first chunk: less encoding left unhidden
+    encode_chunk(e, rows, mstart, threads, cur);
+    j1_status fwd = J1_OK;
+    std::string fwd_msg;
+    while (true) {
+      if (cur.st) return failed(cur);
+      const bool more = cur.r1 < n;
+      std::thread helper;
+      if (more) {
+        next = TextChunk();
+        next.r0 = cur.r1;
+        next.r1 = std::min(n, next.r0 + R);
+        try {
+          helper = std::thread([&] { encode_chunk(e, rows, mstart, threads, next); });
+        } catch (...) {  // no helper thread: encode the next chunk after this one's forward
+        }
+      }
+      if (!fwd) {
+        fwd = j1_engine_logits_encoded(engine, cur.r1 - cur.r0, cur.ids.data(), cur.lens.data(), cur.markers.data(),
+                                       cur.nmark.data(), cur.qt.data(), logits_out + mstart[cur.r0]);
+        if (fwd) fwd_msg = last_error_text();
+      }
+      if (helper.joinable())
+        helper.join();
+      else if (more)
+        encode_chunk(e, rows, mstart, threads, next);
+      if (!more) break;
+      cur = std::move(next);
     }
-    return j1_engine_logits_encoded(engine, n, ids.data(), lens.data(), markers.data(), nmark.data(), qt.data(),
-                                    logits_out);
+    if (fwd) return set_error(fwd, fwd_msg);
+    return J1_OK;
   });
 }
 

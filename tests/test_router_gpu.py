@@ -104,3 +104,34 @@ def test_engine_logits_on_text(engine, tmp_path):
     rows = [tenc.encode(r.state, r.question, r.options, r.qtype)[0] for r in reqs]
     assert got == engine.logits_encoded(rows)
     assert all(len(g) == len(r.options) for g, r in zip(got, reqs))
+
+
+def test_engine_logits_on_text_pipelined_chunks(engine, tmp_path):
+    """With more rows than one pipeline chunk (four engine micro-batches: 256 rows here),
+    text encoding of chunk k + 1 overlaps the forward of chunk k; the logits equal the
+    encode-everything-then-score result bitwise, and an encoding error in a later chunk is
+    reported with its own line number (Engine::encode's order) before any forward error."""
+    import json
+    import os
+    golden = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+    with open(os.path.join(golden, "tokenizer_nfc.json"), encoding="utf-8") as f:
+        (tmp_path / "tokenizer.json").write_text(f.read(), encoding="utf-8")
+    (tmp_path / "tokenizer_config.json").write_text(json.dumps(
+        {"mask_token": "[MASK]", "cls_token": "[CLS]", "sep_token": "[SEP]", "pad_token": "[PAD]"}))
+    rng = np.random.default_rng(9)
+    words = ["north", "south", "gold", "wood", "attack", "defend", "trade", "café", "Ελλάδα", "日本語"]
+    reqs = [j1.Request(" ".join(rng.choice(words, size=int(rng.integers(5, 400)))), "which move %d?" % i,
+                       [" ".join(rng.choice(words, size=int(rng.integers(1, 4)))) for _ in range(int(n))],
+                       qtype=("score" if i % 3 == 1 else "choice"))
+            for i, n in enumerate(rng.integers(2, 21, size=700))]
+    tenc = j1.TextEncoder.load(str(tmp_path), max_length=512)
+    got = engine.logits(reqs, tenc)
+    encoded = [e for e, _ in tenc.encode_batch(reqs, threads=4)]
+    assert got == engine.logits_encoded(encoded)
+    strict = j1.TextEncoder.load(str(tmp_path), max_length=512, strict=True)
+    bad = [j1.Request(" ".join(rng.choice(words, size=int(rng.integers(5, 30)))), "which move?",
+                      [str(rng.choice(words)) for _ in range(int(rng.integers(2, 6)))]) for _ in range(700)]
+    assert len(engine.logits(bad, strict)) == 700  # small rows: strict mode accepts all of them
+    bad[600] = j1.Request("a state with [MASK] in it", "which?", ["left", "right"])
+    with pytest.raises(j1.J1Error, match="JSONL line 601: Reserved model marker in request"):
+        engine.logits(bad, strict)
