@@ -234,46 +234,83 @@ const Nfc& nfc_tables() {
 }
 
 // ------------------------------------------------------------------ LRU cache (lru::LruCache semantics)
+// Shared by the threads of a text encoder: get promotes the entry, put of a new key evicts
+// the least recently used one when full. Values are shared (the reference keeps Arc values).
+// Keys are hashed, and new entries built, outside the lock; inside it there is only a bucket
+// lookup with one key comparison, a list splice and a shared_ptr copy, and evicted entries
+// are freed after it, so threads encoding large requests rarely wait on one another.
 template <typename V>
 class Lru {
  public:
+  using Ptr = std::shared_ptr<const V>;
   explicit Lru(size_t cap) : cap_(cap) {}
-  bool get(const std::string& k, V& v) {
-    if (cap_ == 0) return false;
+  Ptr get(const std::string& k) {
+    if (cap_ == 0) return nullptr;
+    const uint64_t h = hash(k);
     std::lock_guard<std::mutex> lk(mu_);
-    auto it = map_.find(k);
-    if (it == map_.end()) return false;
-    items_.splice(items_.begin(), items_, it->second);
-    v = it->second->second;
-    return true;
+    const auto it = find(h, k);
+    if (it == items_.end()) return nullptr;
+    items_.splice(items_.begin(), items_, it);
+    return it->value;
   }
-  void put(const std::string& k, const V& v) {
+  void put(const std::string& k, Ptr v) {
     if (cap_ == 0) return;
+    const uint64_t h = hash(k);
+    std::list<Node> node;  // the entry and its index slot are allocated before locking
+    node.push_back(Node{h, k, std::move(v)});
+    Index slot;
+    slot.emplace(h, node.begin());
+    auto handle = slot.extract(slot.begin());
+    std::list<Node> evicted;  // declared before the lock: freed after it is released
     std::lock_guard<std::mutex> lk(mu_);
-    auto it = map_.find(k);
-    if (it != map_.end()) {
-      it->second->second = v;
-      items_.splice(items_.begin(), items_, it->second);
+    const auto it = find(h, k);
+    if (it != items_.end()) {
+      std::swap(it->value, node.front().value);
+      items_.splice(items_.begin(), items_, it);
       return;
     }
     if (items_.size() >= cap_) {
-      map_.erase(items_.back().first);
-      items_.pop_back();
+      const auto last = std::prev(items_.end());
+      unindex(last);
+      evicted.splice(evicted.begin(), items_, last);
     }
-    items_.emplace_front(k, v);
-    map_[k] = items_.begin();
+    items_.splice(items_.begin(), node, node.begin());
+    handle.mapped() = items_.begin();
+    index_.insert(std::move(handle));
   }
   void clear() {
+    std::list<Node> items;
+    Index index;
     std::lock_guard<std::mutex> lk(mu_);
-    items_.clear();
-    map_.clear();
+    items.swap(items_);
+    index.swap(index_);
   }
 
  private:
+  struct Node {
+    uint64_t hash;
+    std::string key;
+    Ptr value;
+  };
+  using It = typename std::list<Node>::iterator;
+  using Index = std::unordered_multimap<uint64_t, It>;
+  static uint64_t hash(const std::string& k) { return std::hash<std::string>()(k); }
+  It find(uint64_t h, const std::string& k) {
+    for (auto [b, e] = index_.equal_range(h); b != e; ++b)
+      if (b->second->key == k) return b->second;
+    return items_.end();
+  }
+  void unindex(It it) {
+    for (auto [b, e] = index_.equal_range(it->hash); b != e; ++b)
+      if (b->second == it) {
+        index_.erase(b);
+        return;
+      }
+  }
   size_t cap_;
   std::mutex mu_;
-  std::list<std::pair<std::string, V>> items_;
-  std::unordered_map<std::string, typename std::list<std::pair<std::string, V>>::iterator> map_;
+  std::list<Node> items_;
+  Index index_;
 };
 
 }  // namespace
@@ -726,9 +763,12 @@ struct j1_text_encoder {
 
   // Encoder::tokenize (src/encode.rs:114-129), with the token-fragment cache
   void tokenize(const std::string& text, std::vector<uint32_t>& ids) {
-    if (tokens->get(text, ids)) return;
+    if (const auto hit = tokens->get(text)) {
+      ids = *hit;
+      return;
+    }
     tok->encode(text, ids);
-    tokens->put(text, ids);
+    tokens->put(text, std::make_shared<const std::vector<uint32_t>>(ids));
   }
 };
 
@@ -1101,8 +1141,9 @@ j1_status j1_text_encoder_encode(j1_text_encoder* e, const char* state, int32_t 
       key += static_cast<char>(qtype);
       key += state_is_json ? 'j' : 't';
     }
-    j1_text_encoder::Enc enc;
-    if (!e->encodings->get(key, enc)) {
+    std::shared_ptr<const j1_text_encoder::Enc> hit = e->encodings->get(key);
+    if (!hit) {
+      j1_text_encoder::Enc enc;
       std::string rendered;
       if (state_is_json) {  // State::render (src/request.rs:49-54)
         if (j1_status s = render_json_state(st, rendered)) return s;
@@ -1121,8 +1162,10 @@ j1_status j1_text_encoder_encode(j1_text_encoder* e, const char* state, int32_t 
         return s;
       enc.ids.resize(n);
       enc.markers.resize(n_options);
-      e->encodings->put(key, enc);
+      hit = std::make_shared<const j1_text_encoder::Enc>(std::move(enc));
+      e->encodings->put(key, hit);
     }
+    const j1_text_encoder::Enc& enc = *hit;
     *ids_len = enc.ids.size();
     if (enc.ids.size() > cap || !ids || (!markers && n_options))
       return set_error(J1_ERR_INVALID_ARG, "output arrays too small (ids_cap >= max_length, markers >= n_options)");

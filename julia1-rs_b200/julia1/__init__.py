@@ -105,6 +105,25 @@ class J1TextRequest(C.Structure):
                 ("options", C.POINTER(C.c_char_p)), ("n_options", C.c_size_t), ("qtype", C.c_uint8)]
 
 
+_TEXT_DT = np.dtype({"names": ["state", "state_is_json", "question", "options", "n_options", "qtype"],
+                     "formats": [np.uint64, np.int32, np.uint64, np.uint64, np.uint64, np.uint8],
+                     "offsets": [J1TextRequest.state.offset, J1TextRequest.state_is_json.offset,
+                                 J1TextRequest.question.offset, J1TextRequest.options.offset,
+                                 J1TextRequest.n_options.offset, J1TextRequest.qtype.offset],
+                     "itemsize": C.sizeof(J1TextRequest)})  # j1_text_request, for whole batches at once
+
+
+def _cstrings(bs):
+    """Byte strings as C strings without one ctypes object each: one NUL-separated buffer
+    (kept alive by the returned array) and the address of each string."""
+    mem = np.frombuffer(b"\0".join(bs) + b"\0", np.uint8)
+    lens = np.fromiter(map(len, bs), np.int64, len(bs))
+    starts = np.zeros(len(bs), np.int64)
+    if len(bs) > 1:
+        np.cumsum(lens[:-1] + 1, out=starts[1:])
+    return mem, np.uint64(mem.ctypes.data) + starts.astype(np.uint64), lens
+
+
 SCORER_FN = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_size_t, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32),
                         C.POINTER(C.c_uint32), C.POINTER(C.c_uint32), C.POINTER(C.c_uint8), C.POINTER(C.c_float))
 
@@ -796,9 +815,11 @@ class Tokenizer:
         n = len(bs)
         if n == 0:
             return (np.zeros(0, np.uint32), np.zeros(1, np.uint64)) if flat else []
-        arr = (C.c_char_p * n)(*bs)
-        lens = (C.c_size_t * n)(*[len(b) for b in bs])
-        cap = sum(len(b) for b in bs) + n + 16
+        mem, addr, blen = _cstrings(bs)
+        addr, blen = np.ascontiguousarray(addr), np.ascontiguousarray(blen.astype(np.uint64))
+        arr = addr.ctypes.data_as(C.POINTER(C.c_char_p))
+        lens = blen.ctypes.data_as(C.POINTER(C.c_size_t))
+        cap = int(blen.sum()) + n + 16
         ids = np.zeros(cap, np.uint32)
         offs = np.zeros(n + 1, np.uint64)
         check(lib().j1_tokenizer_encode_batch(self._h, n, arr, lens, int(threads),
@@ -894,14 +915,25 @@ class TextEncoder:
 
     @staticmethod
     def _text_rows(rows: Sequence["Request"]):
-        keep = []
-        arr = (J1TextRequest * max(len(rows), 1))()
-        for i, r in enumerate(rows):
-            opts = (C.c_char_p * max(len(r.options), 1))(*[x.encode() for x in r.options])
-            st, q = r.state.encode(), r.question.encode()
-            keep += [opts, st, q]
-            arr[i] = J1TextRequest(st, int(bool(r.state_is_json)), q, opts, len(r.options), r.qtype_id())
-        return arr, keep
+        """The rows as a j1_text_request array (and what keeps its strings alive), built with
+        numpy in a few passes rather than one ctypes object per string."""
+        n = len(rows)
+        nopt = np.fromiter((len(r.options) for r in rows), np.int64, n)
+        strings = [r.state.encode() for r in rows] + [r.question.encode() for r in rows] + \
+            [x.encode() for r in rows for x in r.options]
+        mem, addr, _ = _cstrings(strings)
+        optp = np.ascontiguousarray(addr[2 * n:]) if len(strings) > 2 * n else np.zeros(1, np.uint64)
+        first = np.zeros(n, np.int64)
+        if n > 1:
+            np.cumsum(nopt[:-1], out=first[1:])
+        rec = np.zeros(max(n, 1), _TEXT_DT)
+        rec["state"][:n] = addr[:n]
+        rec["question"][:n] = addr[n:2 * n]
+        rec["options"][:n] = np.uint64(optp.ctypes.data) + (first * 8).astype(np.uint64)
+        rec["n_options"][:n] = nopt
+        rec["state_is_json"][:n] = np.fromiter((bool(r.state_is_json) for r in rows), np.int32, n)
+        rec["qtype"][:n] = np.fromiter((r.qtype_id() for r in rows), np.uint8, n)
+        return rec.ctypes.data_as(C.POINTER(J1TextRequest)), (mem, optp, rec)
 
     def encode_batch(self, rows: Sequence["Request"], threads: int = 1):
         """Engine::encode's parallel Encoder::encode -> [(Encoded, truncated)] in row order."""
