@@ -580,6 +580,15 @@ struct j1_tokenizer {
     for (const auto& pr : parts) bpe(p + offs[pr.first], offs[pr.second] - offs[pr.first], ids);
   }
 
+  // True when some byte of [p, p + n) begins the pattern of a normalised added token; only
+  // then can matching on the normalised piece (equal to the piece when it is NFC-stable)
+  // find one.
+  bool may_start_norm_token(const char* p, size_t n) const {
+    for (size_t i = 0; i < n; ++i)
+      if (!norm_by_byte[static_cast<unsigned char>(p[i])].empty()) return true;
+    return false;
+  }
+
   // Tokenizer::encode_fast(text, add_special_tokens = false)
   void encode(const std::string& text, std::vector<uint32_t>& ids) const {
     ids.clear();
@@ -592,7 +601,8 @@ struct j1_tokenizer {
       }
       const char* p = text.data() + r.second.first;
       const size_t n = r.second.second - r.second.first;
-      if ((!nfc || Nfc::simple(p, n)) && !has_norm_tokens) {  // nothing to normalise or match: no copy
+      // nothing to normalise, and no normalised added token can start in the piece: no copy
+      if ((!nfc || Nfc::simple(p, n)) && (!has_norm_tokens || !may_start_norm_token(p, n))) {
         encode_piece(p, n, ids);
         continue;
       }

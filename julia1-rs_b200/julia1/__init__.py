@@ -507,6 +507,18 @@ class Engine:
             o += n
         return res
 
+    def logits_flat(self, batch: "EncodedBatch") -> np.ndarray:
+        """Engine::logits_encoded on an EncodedBatch (flat arrays, as TextEncoder.encode_batch
+        returns with flat=True): all rows' option logits, row after row, as one float32 array."""
+        n = int(batch.lens.size)
+        out = np.zeros(int(batch.nmark.sum()), np.float32)
+        if n == 0:
+            return out
+        keep = [_u32(batch.ids), _u32(batch.lens), _u32(batch.markers), _u32(batch.nmark), _u8(batch.qtypes)]
+        check(lib().j1_engine_logits_encoded(self._h, n, keep[0][1], keep[1][1], keep[2][1], keep[3][1], keep[4][1],
+                                             out.ctypes.data_as(C.POINTER(C.c_float))))
+        return out
+
     def logits_tokenized(self, rows: Sequence["TokenizedRequest"], enc: "EncoderOptions") -> List[List[float]]:
         """Engine::logits (src/engine.rs:236-243) on tokenized requests."""
         if len(rows) == 0:
@@ -522,15 +534,19 @@ class Engine:
             k += len(r.options)
         return res
 
-    def logits(self, rows: Sequence["Request"], text_encoder: "TextEncoder", threads: int = 0) -> List[List[float]]:
-        """Engine::logits (src/engine.rs:236-243) on text requests: validate, encode in parallel
-        on `threads` host threads (0 = all cores), logits_encoded."""
-        if len(rows) == 0:
-            return []
-        arr, keep = TextEncoder._text_rows(rows)
-        out = np.zeros(sum(len(r.options) for r in rows), np.float32)
-        check(lib().j1_engine_logits_text(self._h, text_encoder._h, len(rows), arr, int(threads or os.cpu_count() or 1),
+    def logits(self, rows, text_encoder: "TextEncoder", threads: int = 0, flat: bool = False):
+        """Engine::logits (src/engine.rs:236-243) on text requests (a list of Request, or a
+        TextBatch): validate, encode in parallel on `threads` host threads (0 = all cores),
+        logits_encoded. Per-row lists, or with flat=True one float32 array."""
+        tb = rows if isinstance(rows, TextBatch) else TextBatch(rows)
+        rows = tb.rows
+        out = np.zeros(int(tb.n_options.sum()), np.float32)
+        if tb.n == 0:
+            return out if flat else []
+        check(lib().j1_engine_logits_text(self._h, text_encoder._h, tb.n, tb.arr, int(threads or os.cpu_count() or 1),
                                           out.ctypes.data_as(C.POINTER(C.c_float))))
+        if flat:
+            return out
         res, k = [], 0
         for r in rows:
             res.append(list(map(float, out[k:k + len(r.options)])))
@@ -869,6 +885,42 @@ class Request:
         return QTYPES[self.qtype] if isinstance(self.qtype, str) else int(self.qtype)
 
 
+class TextBatch:
+    """Text requests marshalled once for the C ABI (a j1_text_request array and the strings it
+    points to), for calling several entry points on the same rows without rebuilding it."""
+
+    def __init__(self, rows: Sequence["Request"]):
+        self.rows = list(rows)
+        self.n = len(self.rows)
+        self.arr, self._keep = TextEncoder._text_rows(self.rows)
+        rec = self._keep[2]
+        self.n_options = rec["n_options"][:self.n].astype(np.int64)
+        self.qtypes = rec["qtype"][:self.n].copy()
+
+
+@dataclass
+class EncodedBatch:
+    """Encoded rows as flat arrays: ids of all rows back to back with their lengths, marker
+    positions (within each row) with their counts per row, question types, truncation flags."""
+    ids: np.ndarray
+    lens: np.ndarray
+    markers: np.ndarray
+    nmark: np.ndarray
+    qtypes: np.ndarray
+    truncated: np.ndarray
+
+    @staticmethod
+    def empty() -> "EncodedBatch":
+        z = np.zeros(0, np.uint32)
+        return EncodedBatch(z, z, z, z, np.zeros(0, np.uint8), np.zeros(0, bool))
+
+    def rows(self) -> List[Encoded]:
+        i0 = np.concatenate([[0], np.cumsum(self.lens)]).astype(np.int64)
+        m0 = np.concatenate([[0], np.cumsum(self.nmark)]).astype(np.int64)
+        return [Encoded(self.ids[i0[k]:i0[k + 1]].copy(), self.markers[m0[k]:m0[k + 1]].copy(), int(self.qtypes[k]))
+                for k in range(self.lens.size)]
+
+
 class TextEncoder:
     """encode::Encoder (src/encode.rs:25-195) over the checkpoint's tokenizer: special tokens
     from tokenizer_config.json, LRU caches, the request's text forms and Encoder::sequence."""
@@ -935,15 +987,16 @@ class TextEncoder:
         rec["qtype"][:n] = np.fromiter((r.qtype_id() for r in rows), np.uint8, n)
         return rec.ctypes.data_as(C.POINTER(J1TextRequest)), (mem, optp, rec)
 
-    def encode_batch(self, rows: Sequence["Request"], threads: int = 1):
-        """Engine::encode's parallel Encoder::encode -> [(Encoded, truncated)] in row order."""
-        n = len(rows)
+    def encode_batch(self, rows, threads: int = 1, flat: bool = False):
+        """Engine::encode's parallel Encoder::encode on a list of Request (or a TextBatch)
+        -> [(Encoded, truncated)] in row order, or with flat=True one EncodedBatch."""
+        tb = rows if isinstance(rows, TextBatch) else TextBatch(rows)
+        rows, n, arr = tb.rows, tb.n, tb.arr
         if n == 0:
-            return []
-        arr, keep = self._text_rows(rows)
+            return EncodedBatch.empty() if flat else []
         o = self.options()
         cap = n * o.max_length
-        mcap = max(sum(len(r.options) for r in rows), 1)
+        mcap = max(int(tb.n_options.sum()), 1)
         ids, mk = np.zeros(cap, np.uint32), np.zeros(mcap, np.uint32)
         offs, moffs, tr = np.zeros(n + 1, np.uint64), np.zeros(n + 1, np.uint64), np.zeros(n, np.int32)
         check(lib().j1_text_encoder_encode_batch(self._h, n, arr, int(threads),
@@ -952,6 +1005,9 @@ class TextEncoder:
                                                  mk.ctypes.data_as(C.POINTER(C.c_uint32)), mcap,
                                                  moffs.ctypes.data_as(C.POINTER(C.c_size_t)),
                                                  tr.ctypes.data_as(C.POINTER(C.c_int32))))
+        if flat:
+            return EncodedBatch(ids[:int(offs[-1])], np.diff(offs).astype(np.uint32), mk[:int(moffs[-1])],
+                                np.diff(moffs).astype(np.uint32), tb.qtypes.copy(), tr.astype(bool))
         return [(Encoded(ids[int(offs[i]):int(offs[i + 1])].copy(), mk[int(moffs[i]):int(moffs[i + 1])].copy(),
                          rows[i].qtype_id()), bool(tr[i])) for i in range(n)]
 

@@ -10,6 +10,10 @@ A third timing is the whole text path as one call (Engine::logits, src/engine.rs
 here j1_engine_logits_text, which encodes the next chunk of rows while the engine scores
 the current one), also with cleared caches.
 
+The rows are marshalled for the C ABI once (a TextBatch) and results are kept as flat
+arrays, so the timings are the library's (the reference's are of Rust calls); building
+per-row Python objects would add a serial cost of the Python binding to every number.
+
 Inputs are synthetic: the reference reads a public dataset of typed rows, which is not
 used here. Each row has a game-state text of about `--words` words, a question and 2 to
 20 short options, mixing ASCII and other scripts; the tokenizer is a checkpoint
@@ -69,31 +73,31 @@ def main():
     try:
         enc = j1.TextEncoder.load(tdir, max_length=512, head_length=256)
         ck = synthetic.cached_checkpoint(seed=0, perturb=True)
-        rows = make_rows(a.rows, a.words, 11)
+        rows = j1.TextBatch(make_rows(a.rows, a.words, 11))
         for bs in [int(x) for x in a.batch_size.split(",")]:
             eng = j1.Engine.load(ck, j1.EngineOptions(device="cuda", batch_size=bs, max_batch_tokens=131072,
                                                       max_length=512))
-            encoded = [e for e, _ in enc.encode_batch(rows, threads=a.threads)]
-            eng.logits_encoded(encoded)  # untimed pass, as the reference's first engine.logits
-            tokens = sum(int(e.ids.size) for e in encoded)
+            encoded = enc.encode_batch(rows, threads=a.threads, flat=True)
+            eng.logits_flat(encoded)  # untimed pass, as the reference's first engine.logits
+            tokens = int(encoded.ids.size)
             reps = []
             for _ in range(a.reps):
                 enc.clear_cache()
                 t0 = time.perf_counter()
-                encoded = [e for e, _ in enc.encode_batch(rows, threads=a.threads)]
+                encoded = enc.encode_batch(rows, threads=a.threads, flat=True)
                 te = time.perf_counter() - t0
                 t0 = time.perf_counter()
-                eng.logits_encoded(encoded)
+                eng.logits_flat(encoded)
                 tf = time.perf_counter() - t0
                 enc.clear_cache()
                 t0 = time.perf_counter()
-                eng.logits(rows, enc, threads=a.threads)
+                eng.logits(rows, enc, threads=a.threads, flat=True)
                 tl = time.perf_counter() - t0
                 print("batch %d: encode %.1f ms, forward %.1f ms, text -> logits in one call %.1f ms"
                       % (bs, te * 1e3, tf * 1e3, tl * 1e3), flush=True)
                 reps.append((te, tf, tl))
             te, tf, tl = (min(r[k] for r in reps) for k in range(3))
-            print(json.dumps({"tool": "split_timing", "rows": a.rows, "tokens": tokens, "batch_size": bs,
+            print(json.dumps({"tool": "split_timing", "rows": rows.n, "tokens": tokens, "batch_size": bs,
                               "host_threads": a.threads, "encode_ms": round(te * 1e3, 2),
                               "forward_ms": round(tf * 1e3, 2), "encode_tokens_per_s": round(tokens / te),
                               "forward_tokens_per_s": round(tokens / tf),

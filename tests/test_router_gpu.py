@@ -128,6 +128,10 @@ def test_engine_logits_on_text_pipelined_chunks(engine, tmp_path):
     got = engine.logits(reqs, tenc)
     encoded = [e for e, _ in tenc.encode_batch(reqs, threads=4)]
     assert got == engine.logits_encoded(encoded)
+    tb = j1.TextBatch(reqs)  # the flat paths: same bits
+    flat = engine.logits(tb, tenc, flat=True)
+    assert flat.tolist() == [v for row in got for v in row]
+    assert np.array_equal(engine.logits_flat(tenc.encode_batch(tb, threads=4, flat=True)), flat)
     strict = j1.TextEncoder.load(str(tmp_path), max_length=512, strict=True)
     bad = [j1.Request(" ".join(rng.choice(words, size=int(rng.integers(5, 30)))), "which move?",
                       [str(rng.choice(words)) for _ in range(int(rng.integers(2, 6)))]) for _ in range(700)]

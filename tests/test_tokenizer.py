@@ -233,3 +233,21 @@ def test_tokenizer_and_encoder_shared_by_threads(enc_dir):
     for t in ts:
         t.join()
     assert not errs, errs[:1]
+
+
+def test_text_encoder_flat_batch_equals_rows(enc_dir):
+    """TextBatch + encode_batch(flat=True) gives the per-row results as flat arrays."""
+    enc = j1.TextEncoder.load(enc_dir, max_length=128, head_length=48)
+    rng = random.Random(12)
+    words = ["win", "lose", "draw", "café", "日本語", "[MASK]", "don't", "12 345"]
+    rows = [j1.Request(" ".join(rng.choice(words) for _ in range(rng.randint(0, 60))), "which %d?" % i,
+                       [" ".join(rng.choice(words) for _ in range(rng.randint(1, 3))) for _ in range(rng.randint(2, 20))],
+                       rng.choice(["choice", "score"])) for i in range(97)]
+    want = enc.encode_batch(rows, threads=3)
+    tb = j1.TextBatch(rows)
+    flat = enc.encode_batch(tb, threads=3, flat=True)
+    got = flat.rows()
+    assert [(e.ids.tolist(), e.markers.tolist(), e.qtype) for e, _ in want] == \
+        [(e.ids.tolist(), e.markers.tolist(), e.qtype) for e in got]
+    assert flat.truncated.tolist() == [t for _, t in want]
+    assert enc.encode_batch([], flat=True).ids.size == 0
