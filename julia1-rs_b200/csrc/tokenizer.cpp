@@ -32,6 +32,7 @@
 #include <string>
 #include <thread>
 #include <unordered_map>
+#include <unordered_set>
 #include <vector>
 
 #include "json.h"
@@ -142,10 +143,16 @@ struct Nfc {
   std::unordered_map<uint32_t, uint8_t> ccc;
   std::unordered_map<uint32_t, std::pair<uint32_t, uint32_t>> decomp;
   std::unordered_map<uint64_t, uint32_t> comp;
-  Nfc() {
+  std::unordered_set<uint32_t> seconds;  // code points some composition takes as its second part
+  // per code point: 0 not yet known, 1 NFC_QC = Yes, 2 otherwise (filled on first use)
+  std::unique_ptr<std::atomic<uint8_t>[]> qc;
+  Nfc() : qc(new std::atomic<uint8_t>[0x110000]()) {
     for (const auto& e : ucd::kCombining) ccc[e[0]] = static_cast<uint8_t>(e[1]);
     for (const auto& e : ucd::kDecomposition) decomp[e[0]] = {e[1], e[2]};
-    for (const auto& e : ucd::kComposition) comp[(static_cast<uint64_t>(e[0]) << 32) | e[1]] = e[2];
+    for (const auto& e : ucd::kComposition) {
+      comp[(static_cast<uint64_t>(e[0]) << 32) | e[1]] = e[2];
+      seconds.insert(e[1]);
+    }
   }
   static constexpr uint32_t SBase = 0xAC00, LBase = 0x1100, VBase = 0x1161, TBase = 0x11A7;
   static constexpr uint32_t LCount = 19, VCount = 21, TCount = 28, NCount = VCount * TCount, SCount = LCount * NCount;
@@ -178,14 +185,51 @@ struct Nfc {
     auto it = comp.find((static_cast<uint64_t>(a) << 32) | b);
     return it == comp.end() ? 0 : it->second;
   }
-  // below U+0300 every character is its own NFC; 0xCC is the lowest lead byte above it
-  static bool simple(const char* p, size_t n) {
-    for (size_t i = 0; i < n; ++i)
-      if (static_cast<unsigned char>(p[i]) >= 0xCC) return false;
+  // UAX #15 quick check of one code point, NFC_QC = Yes: a starter that no composition
+  // takes as its second part (Hangul medial and final jamo included) and that NFC maps to
+  // itself. Below U+0300 every character qualifies.
+  bool qc_yes(uint32_t c) const {
+    if (c < 0x300) return true;
+    uint8_t v = qc[c].load(std::memory_order_relaxed);
+    if (v == 0) {
+      const bool hangul_vt = (c >= VBase && c < VBase + VCount) || (c > TBase && c < TBase + TCount);
+      bool yes = cc(c) == 0 && !hangul_vt && !seconds.count(c);
+      if (yes) {
+        std::string one, t;
+        utf8_append(one, c);
+        t = one;
+        normalize_full(t);
+        yes = t == one;
+      }
+      v = yes ? 1 : 2;
+      qc[c].store(v, std::memory_order_relaxed);
+    }
+    return v == 1;
+  }
+  // True when the (valid UTF-8) text is in NFC by the quick check: every code point is
+  // NFC_QC = Yes, so no character can change or combine with a neighbour.
+  bool quick_yes(const char* p, size_t n) const {
+    const unsigned char* u = reinterpret_cast<const unsigned char*>(p);
+    for (size_t i = 0; i < n;) {
+      const unsigned b = u[i];
+      if (b < 0xCC) {  // ASCII, or a 2-byte lead below U+0300 (then its continuation byte)
+        i += b < 0x80 ? 1 : 2;
+        continue;
+      }
+      const size_t len = (b >> 5) == 6 ? 2 : (b >> 4) == 14 ? 3 : 4;
+      if (i + len > n) return false;
+      uint32_t c = len == 2 ? (b & 0x1F) : len == 3 ? (b & 0x0F) : (b & 0x07);
+      for (size_t k = 1; k < len; ++k) c = (c << 6) | (u[i + k] & 0x3F);
+      if (c > 0x10FFFF || !qc_yes(c)) return false;
+      i += len;
+    }
     return true;
   }
   void normalize(std::string& s) const {
-    if (simple(s.data(), s.size())) return;
+    if (quick_yes(s.data(), s.size())) return;
+    normalize_full(s);
+  }
+  void normalize_full(std::string& s) const {
     std::vector<uint32_t> cps, d;
     utf8_decode(s, cps);
     d.reserve(cps.size() + 8);
@@ -602,7 +646,7 @@ struct j1_tokenizer {
       const char* p = text.data() + r.second.first;
       const size_t n = r.second.second - r.second.first;
       // nothing to normalise, and no normalised added token can start in the piece: no copy
-      if ((!nfc || Nfc::simple(p, n)) && (!has_norm_tokens || !may_start_norm_token(p, n))) {
+      if ((!nfc || nfc_tables().quick_yes(p, n)) && (!has_norm_tokens || !may_start_norm_token(p, n))) {
         encode_piece(p, n, ids);
         continue;
       }

@@ -9,6 +9,13 @@ NFC normalisation:
   * canonical decompositions, canonical combining classes and the primary composites
     (pairs whose canonical composition is not excluded: NFC of the composite is itself).
 
+The normalisation tables are pinned to the NFC of the reference's tokenizer library (HF
+`tokenizers`, the version the reference's Cargo.lock pins) when its Python binding is
+importable: that library's tables are of an older Unicode version, and it treats characters
+assigned after it as starters without a decomposition. Each code point whose normalisation
+differs between this unicodedata and the library (probed alone and next to combining marks)
+is left out of the three tables, which makes libj1 treat it the same way.
+
 Usage: python julia1-rs_b200/gen_unicode_tables.py   (rewrites csrc/unicode_tables.h)
 """
 import os
@@ -60,6 +67,31 @@ def canonical_decomposition(cp):
     return [int(x, 16) for x in d.split()]
 
 
+def library_unknown():
+    """Code points whose NFC/NFD differs between this unicodedata and the tokenizer
+    library's normalizers, or (set(), None) when the library is not importable."""
+    try:
+        import tokenizers
+        from tokenizers import normalizers
+    except ImportError:
+        return set(), None
+    nfc, nfd = normalizers.NFC(), normalizers.NFD()
+    out = set()
+    for cp in range(MAXCP):
+        if 0xD800 <= cp <= 0xDFFF:
+            continue
+        ch = chr(cp)
+        d = unicodedata.decomposition(ch)
+        if not unicodedata.combining(ch) and not (d and not d.startswith("<")):
+            continue
+        for s in (ch, "\u0345" + ch, "a" + ch + "\u0301", ch + "\u0301"):
+            if nfd.normalize_str(s) != unicodedata.normalize("NFD", s) or \
+                    nfc.normalize_str(s) != unicodedata.normalize("NFC", s):
+                out.add(cp)
+                break
+    return out, tokenizers.__version__
+
+
 def emit_ranges(name, rs):
     lines = ["constexpr uint32_t %s[][2] = {" % name]
     row = []
@@ -91,8 +123,15 @@ def main():
             if len(d) == 2 and unicodedata.normalize("NFC", chr(cp)) == chr(cp):
                 comp.append((d[0], d[1], cp))
     comp.sort()
+    unknown, lib_version = library_unknown()
+    ccc = [x for x in ccc if x[0] not in unknown]
+    decomp = [x for x in decomp if x[0] not in unknown]
+    comp = [x for x in comp if not unknown.intersection(x)]
+    pin = ("// Normalisation tables pinned to the NFC of HF tokenizers %s: %d code points newer than its"
+           " Unicode tables are left out of them." % (lib_version, len(unknown))) if lib_version else \
+        "// Normalisation tables not pinned (the tokenizer library was not importable)."
     L = ["// Generated by julia1-rs_b200/gen_unicode_tables.py from Python %s unicodedata (Unicode %s)."
-         % (sys.version.split()[0], unicodedata.unidata_version),
+         % (sys.version.split()[0], unicodedata.unidata_version), pin,
          "// Do not edit by hand.", "#pragma once", "#include <cstdint>", "", "namespace j1rt {", "namespace ucd {", "",
          "constexpr const char* kUnicodeVersion = \"%s\";" % unicodedata.unidata_version, ""]
     L += emit_ranges("kLetter", letters) + [""]

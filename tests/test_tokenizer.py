@@ -251,3 +251,29 @@ def test_text_encoder_flat_batch_equals_rows(enc_dir):
         [(e.ids.tolist(), e.markers.tolist(), e.qtype) for e in got]
     assert flat.truncated.tolist() == [t for _, t in want]
     assert enc.encode_batch([], flat=True).ids.size == 0
+
+
+def test_nfc_quick_check_every_bmp_code_point():
+    """The NFC normaliser skips texts whose code points all pass the UAX #15 quick check
+    (NFC_QC = Yes), and its tables follow the library's Unicode version. For every BMP code
+    point and every other one with a combining class or a canonical decomposition, alone,
+    after a letter, after a Hangul leading consonant and before a combining mark, the ids
+    equal the reference's tokenizer library's."""
+    tokenizers = pytest.importorskip("tokenizers")
+    path = os.path.join(GOLDEN, "tokenizer_nfc.json")
+    ref = tokenizers.Tokenizer.from_file(path)
+    tok = load("nfc")
+    import unicodedata
+    cps = [c for c in range(0x80, 0x10000) if not 0xD800 <= c <= 0xDFFF]
+    # beyond the BMP: every code point with a combining class or a canonical decomposition
+    cps += [c for c in range(0x10000, 0x110000) if unicodedata.combining(chr(c)) or
+            (unicodedata.decomposition(chr(c)) and not unicodedata.decomposition(chr(c)).startswith("<"))]
+    texts = []
+    for c in cps:
+        ch = chr(c)
+        texts += [ch, "e" + ch, ch + "́", "ᄀ" + ch]
+    want = [e.ids for e in ref.encode_batch(texts, add_special_tokens=False)]
+    got = tok.encode_batch(texts, threads=4)
+    bad = [(hex(ord(t[-1]) if len(t) > 1 and t[0] in "eᄀ" else ord(t[0])), t) for t, g, w in zip(texts, got, want)
+           if g != w]
+    assert not bad, bad[:10]
