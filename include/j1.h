@@ -355,10 +355,12 @@ J1_API j1_status j1_text_encoder_request_tokens(j1_text_encoder* enc, const char
  * process fail; count 0 disarms. J1_FAULT_HOST makes the next entry points' bodies throw
  * std::bad_alloc (-> J1_ERR_OOM) and J1_FAULT_WORKER the next host worker threads (tokenizer,
  * text encoder, engine device pool) throw std::runtime_error (-> J1_ERR_INTERNAL): the paths a
- * real host failure takes. The environment variable J1_FAULT=alloc|launch|nan|host|worker
+ * real host failure takes. J1_FAULT_THREAD makes the next attempts to start a host worker
+ * thread fail; the call then finishes its work on the threads it has (no error). The environment variable J1_FAULT=alloc|launch|nan|host|worker
  * arms one at the first j1_model_create. Nothing is done to the GPU: an injected allocation
  * or launch does not happen and injected nonfinite scores are written into the host copy. */
-enum { J1_FAULT_ALLOC = 1, J1_FAULT_LAUNCH = 2, J1_FAULT_NAN = 3, J1_FAULT_HOST = 4, J1_FAULT_WORKER = 5 };
+enum { J1_FAULT_ALLOC = 1, J1_FAULT_LAUNCH = 2, J1_FAULT_NAN = 3, J1_FAULT_HOST = 4, J1_FAULT_WORKER = 5,
+       J1_FAULT_THREAD = 6 };
 J1_API void j1_inject_fault(int32_t kind, int32_t count);
 /* Device-side failure detection without a fault: one thread waits, with the library's
  * bounded wait and a limit of limit_cycles (1e3..4e9), on an mbarrier nothing arrives at.

@@ -14,6 +14,7 @@
 #include <limits>
 #include <memory>
 #include <stdexcept>
+#include <system_error>
 #include <thread>
 #include <unordered_map>
 
@@ -74,6 +75,7 @@ void run_pool(int n, const std::function<void()>& work) {
   std::vector<std::thread> pool;
   for (int k = 1; k < n; ++k) {
     try {
+      if (take_fault(J1_FAULT_THREAD)) throw std::system_error(std::make_error_code(std::errc::resource_unavailable_try_again));
       pool.emplace_back(safe);
     } catch (...) {  // no thread (or no room to hold one): the started ones and this thread do the rest
       break;
@@ -96,7 +98,7 @@ size_t last_error_copy(char* buf, size_t cap) { return copy_out(t_last_error, bu
 // the process report a failure, so callers can test their error handling. Nothing is done
 // to the GPU: an injected allocation or launch simply does not happen, and injected
 // nonfinite scores are written into the host copy.
-std::atomic<int> g_fault[6];
+std::atomic<int> g_fault[7];
 
 bool take_fault(int kind) {
   int n = g_fault[kind].load();
@@ -881,7 +883,7 @@ j1_status j1_config_load(const char* ckpt_dir, j1_config* out) {
 }
 
 void j1_inject_fault(int32_t kind, int32_t count) {
-  if (kind >= J1_FAULT_ALLOC && kind <= J1_FAULT_WORKER) g_fault[kind] = count > 0 ? count : 0;
+  if (kind >= J1_FAULT_ALLOC && kind <= J1_FAULT_THREAD) g_fault[kind] = count > 0 ? count : 0;
 }
 
 j1_status j1_selftest_device_timeout(int ordinal, int64_t limit_cycles) {

@@ -22,7 +22,7 @@ GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 @pytest.fixture(autouse=True)
 def disarm():
     yield
-    for k in (j1.FAULT_HOST, j1.FAULT_WORKER):
+    for k in (j1.FAULT_HOST, j1.FAULT_WORKER, j1.FAULT_THREAD):
         j1.inject_fault(k, 0)
 
 
@@ -123,3 +123,17 @@ def test_concurrent_calls_with_faults_armed(tok):
     assert "wrong" not in outcomes
     assert set(outcomes) <= {"ok", j1.OOM, j1.INTERNAL}
     assert outcomes.count(j1.OOM) == 40 and outcomes.count(j1.INTERNAL) >= 1
+
+
+def test_threads_that_cannot_start_are_done_without(tok, enc):
+    """When worker threads cannot be started, the pool finishes the work on the threads it
+    has (the calling thread at least): same results, no error."""
+    texts = ["text %d: café 日本語 — %d" % (i, i * 3) for i in range(200)]
+    want = tok.encode_batch(texts, threads=1)
+    j1.inject_fault(j1.FAULT_THREAD, 1000)
+    assert tok.encode_batch(texts, threads=8) == want
+    rows = [j1.Request("state %d" % i, "which?", ["a", "b %d" % i]) for i in range(50)]
+    got = enc.encode_batch(rows, threads=8)
+    j1.inject_fault(j1.FAULT_THREAD, 0)
+    ref = enc.encode_batch(rows, threads=1)
+    assert [(e.ids.tolist(), t) for e, t in got] == [(e.ids.tolist(), t) for e, t in ref]
