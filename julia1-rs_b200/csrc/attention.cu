@@ -147,6 +147,7 @@ __global__ void __launch_bounds__(192, 2)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
+  grid_dep_launch();
   const int warp = warp_id(), lane = lane_id();
   const int items = ntiles * heads;
   {  // exit before allocating anything when an earlier CTA of this launch gave up
@@ -179,6 +180,7 @@ __global__ void __launch_bounds__(192, 2)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  grid_dep_wait();  // the previous kernel's outputs (this kernel's inputs and outputs) are ready
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 5) {
@@ -492,9 +494,9 @@ int launch_attention(const CUtensorMap& tmQ, const CUtensorMap& tmKV, const CUte
   const int items = ntiles * heads;
   const int limit = 2 * grid_limit;  // two CTAs per SM
   const int grid = items < limit ? items : limit;
-  attn_tc_kernel<<<grid, 192, ATT_SMEM, stream>>>(tmQ, tmKV, tmO ? *tmO : tmQ, tmO ? 1 : 0, tiles, ntiles, heads,
-                                                   out, ldo, q_col0, k_col0, v_col0, window, scale_log2, err);
-  return static_cast<int>(cudaGetLastError());
+  return static_cast<int>(launch_kernel(attn_tc_kernel, dim3(grid), dim3(192), ATT_SMEM, stream, tmQ, tmKV,
+                                        tmO ? *tmO : tmQ, tmO ? 1 : 0, tiles, ntiles, heads, out, ldo, q_col0, k_col0,
+                                        v_col0, window, scale_log2, err));
 }
 
 }  // namespace j1rt

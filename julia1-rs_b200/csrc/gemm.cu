@@ -154,6 +154,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GemmCfg<BN, EPI>::TH
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(lnempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
+  grid_dep_launch();
   const int warp = warp_id(), lane = lane_id();
   const uint32_t rank = cluster_ctarank();  // 0: the CTA that issues the pair's MMAs
   const bool leader = rank == 0;
@@ -208,6 +209,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GemmCfg<BN, EPI>::TH
   tc_fence_before();
   cluster_sync();  // barriers of both CTAs initialised, TMEM allocated in both
   tc_fence_after();
+  grid_dep_wait();  // the previous kernel's outputs (this kernel's inputs and outputs) are ready
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
@@ -646,8 +648,8 @@ int launch_one(const CUtensorMap& tmA, const CUtensorMap& tmW, const CUtensorMap
   const int max_pairs = grid_limit / 2 > 0 ? grid_limit / 2 : 1;
   const int pairs = units < max_pairs ? units : max_pairs;
   if (pairs <= 0) return 0;
-  kern<<<2 * pairs, GemmCfg<BN, EPI>::THREADS, GemmCfg<BN, EPI>::SMEM, stream>>>(tmA, tmW, tmX, p);
-  return static_cast<int>(cudaGetLastError());
+  return static_cast<int>(
+      launch_kernel(kern, dim3(2 * pairs), dim3(GemmCfg<BN, EPI>::THREADS), GemmCfg<BN, EPI>::SMEM, stream, tmA, tmW, tmX, p));
 }
 
 template <int EPI>

@@ -6,10 +6,41 @@
 #include <stdint.h>
 
 #include <atomic>
+#include <cstdlib>
+#include <cstring>
+#include <utility>
 
 namespace j1rt {
 
 using bf16 = __nv_bfloat16;
+
+// Programmatic dependent launch for the forward's kernels: each is launched so that it may
+// begin (launch its CTAs and run its local set-up: barriers, TMEM, descriptor prefetch) while
+// the previous kernel of the stream drains, and waits (griddepcontrol.wait) before it reads or
+// writes any global data. J1_PDL=0 in the environment launches them the ordinary way.
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("J1_PDL");
+    return !(v && std::strcmp(v, "0") == 0);
+  }();
+  return on;
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                                 Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 // cudaFuncSetAttribute acts on the kernel as loaded in the current device's
 // context, so a process that drives several GPUs (the engine pool) must raise the

@@ -103,6 +103,13 @@ __device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, vo
   }
 }
 
+// Programmatic dependent launch. grid_dep_launch: the next kernel of the stream may start
+// launching its CTAs (it still waits in grid_dep_wait). grid_dep_wait: block until the
+// previous kernel of the stream has completed and its memory operations are visible; a no-op
+// when this kernel was not launched programmatically.
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // Generic-proxy smem writes -> visible to the async proxy (tensor core / TMA).
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

@@ -81,6 +81,8 @@ template <int H>
 __global__ void __launch_bounds__(256) embed_ln_kernel(const int* __restrict__ ids, const float* __restrict__ table,
                                                        const float* __restrict__ w, float* __restrict__ x,
                                                        bf16* __restrict__ xn, int rows, float eps) {
+  grid_dep_launch();
+  grid_dep_wait();
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= rows) return;
   Row<H> r;
@@ -97,6 +99,8 @@ __global__ void __launch_bounds__(256) final_norm_kernel(float* __restrict__ x, 
                                                          const int* __restrict__ qtype, const float* __restrict__ hw,
                                                          const float* __restrict__ hb, bf16* __restrict__ xn,
                                                          int rows, float eps) {
+  grid_dep_launch();
+  grid_dep_wait();
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= rows) return;
   Row<H> r;
@@ -111,6 +115,8 @@ __global__ void __launch_bounds__(256) final_norm_kernel(float* __restrict__ x, 
 
 __global__ void __launch_bounds__(256) gather_rows_kernel(const uint8_t* __restrict__ src, const int* __restrict__ idx,
                                                           uint8_t* __restrict__ dst, int rows, int row_bytes) {
+  grid_dep_launch();
+  grid_dep_wait();
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= rows) return;
   const uint4* s = reinterpret_cast<const uint4*>(src + static_cast<size_t>(idx[row]) * row_bytes);
@@ -138,14 +144,14 @@ __global__ void f32_to_bf16_kernel(const float* __restrict__ src, bf16* __restri
 template <int H>
 int embed_ln_h(const int* ids, const float* table, const float* w, float* x, bf16* xn, int rows, float eps,
                cudaStream_t st) {
-  embed_ln_kernel<H><<<(rows + 7) / 8, 256, 0, st>>>(ids, table, w, x, xn, rows, eps);
-  return static_cast<int>(cudaGetLastError());
+  return static_cast<int>(launch_kernel(embed_ln_kernel<H>, dim3((rows + 7) / 8), dim3(256), 0, st, ids, table, w, x,
+                                        xn, rows, eps));
 }
 template <int H>
 int final_norm_h(float* x, const float* fw, const float* te, const int* qt, const float* hw, const float* hb,
                  bf16* xn, int rows, float eps, cudaStream_t st) {
-  final_norm_kernel<H><<<(rows + 7) / 8, 256, 0, st>>>(x, fw, te, qt, hw, hb, xn, rows, eps);
-  return static_cast<int>(cudaGetLastError());
+  return static_cast<int>(launch_kernel(final_norm_kernel<H>, dim3((rows + 7) / 8), dim3(256), 0, st, x, fw, te, qt,
+                                        hw, hb, xn, rows, eps));
 }
 
 }  // namespace
@@ -180,9 +186,9 @@ int launch_final_norm(int hidden, float* x, const float* fw, const float* te, co
 
 int launch_gather_rows(const void* src, const int* idx, void* dst, int rows, int row_bytes, cudaStream_t st) {
   if (rows == 0) return 0;
-  gather_rows_kernel<<<(rows + 7) / 8, 256, 0, st>>>(static_cast<const uint8_t*>(src), idx,
-                                                      static_cast<uint8_t*>(dst), rows, row_bytes);
-  return static_cast<int>(cudaGetLastError());
+  return static_cast<int>(launch_kernel(gather_rows_kernel, dim3((rows + 7) / 8), dim3(256), 0, st,
+                                        static_cast<const uint8_t*>(src), idx, static_cast<uint8_t*>(dst), rows,
+                                        row_bytes));
 }
 
 int launch_f32_to_bf16(const float* src, bf16* dst, long long rows, int cols, int geglu_inter, cudaStream_t st) {
