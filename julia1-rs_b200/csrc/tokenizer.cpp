@@ -1416,15 +1416,19 @@ j1_status j1_engine_logits_text(j1_engine* engine, j1_text_encoder* e, size_t n,
         } catch (...) {  // no helper thread: encode the next chunk after this one's forward
         }
       }
-      if (!fwd) {
-        fwd = j1_engine_logits_encoded(engine, cur.r1 - cur.r0, cur.ids.data(), cur.lens.data(), cur.markers.data(),
-                                       cur.nmark.data(), cur.qt.data(), logits_out + mstart[cur.r0]);
-        if (fwd) fwd_msg = last_error_text();
+      // Nothing between the helper's start and its join may throw (a joinable std::thread
+      // must not be destroyed): the forward entry point returns a status, never throws.
+      const bool async = helper.joinable();
+      j1_status fs = J1_OK;
+      if (!fwd)
+        fs = j1_engine_logits_encoded(engine, cur.r1 - cur.r0, cur.ids.data(), cur.lens.data(), cur.markers.data(),
+                                      cur.nmark.data(), cur.qt.data(), logits_out + mstart[cur.r0]);
+      if (async) helper.join();
+      if (fs) {  // this thread's message, taken before any encoding on this thread replaces it
+        fwd = fs;
+        fwd_msg = last_error_text();
       }
-      if (helper.joinable())
-        helper.join();
-      else if (more)
-        encode_chunk(e, rows, mstart, threads, next);
+      if (!async && more) encode_chunk(e, rows, mstart, threads, next);
       if (!more) break;
       cur = std::move(next);
     }
