@@ -106,7 +106,7 @@ def emit_ranges(name, rs):
     return lines
 
 
-def main():
+def main(out=OUT):
     letters = ranges(lambda cp: cat(cp).startswith("L"))
     numbers = ranges(lambda cp: cat(cp).startswith("N"))
     words = ranges(is_word)
@@ -163,10 +163,10 @@ def main():
         L.append("    " + ", ".join("{0x%X, 0x%X, 0x%X}" % x for x in comp[i:i + 5]) + ",")
     L.append("};")
     L += ["", "}  // namespace ucd", "}  // namespace j1rt", ""]
-    with open(OUT, "w") as f:
+    with open(out, "w") as f:
         f.write("\n".join(L))
     print("wrote %s: %d letter ranges, %d number ranges, %d combining, %d decompositions, %d compositions"
-          % (OUT, len(letters), len(numbers), len(ccc), len(decomp), len(comp)))
+          % (out, len(letters), len(numbers), len(ccc), len(decomp), len(comp)))
 
 
 if __name__ == "__main__":

@@ -277,3 +277,25 @@ def test_nfc_quick_check_every_bmp_code_point():
     bad = [(hex(ord(t[-1]) if len(t) > 1 and t[0] in "eᄀ" else ord(t[0])), t) for t, g, w in zip(texts, got, want)
            if g != w]
     assert not bad, bad[:10]
+
+
+def test_unicode_tables_match_their_generator(tmp_path):
+    """csrc/unicode_tables.h is what gen_unicode_tables.py writes from this Python's
+    unicodedata, pinned to the tokenizer library's normalisation (skipped when the Unicode
+    version or the library differs from the ones the header was made with)."""
+    import importlib.util
+    import unicodedata
+    tokenizers = pytest.importorskip("tokenizers")
+    header = os.path.join(ROOT, "julia1-rs_b200", "csrc", "unicode_tables.h")
+    first = open(header, encoding="utf-8").read().split("\n")[:2]
+    if unicodedata.unidata_version not in first[0] or tokenizers.__version__ not in first[1]:
+        pytest.skip("header made with another Unicode version or tokenizer library")
+    spec = importlib.util.spec_from_file_location("gen_unicode_tables",
+                                                  os.path.join(ROOT, "julia1-rs_b200", "gen_unicode_tables.py"))
+    gen = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(gen)
+    out = tmp_path / "unicode_tables.h"
+    gen.main(str(out))
+    got = out.read_text(encoding="utf-8").split("\n")
+    want = open(header, encoding="utf-8").read().split("\n")
+    assert got[2:] == want[2:]  # line 1 names the Python version that ran the generator
