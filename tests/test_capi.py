@@ -208,3 +208,19 @@ def test_null_handles_are_rejected():
     assert L.j1_model_launch(None) == j1.INVALID_ARG
     assert L.j1_engine_logits_encoded(None, 0, None, None, None, None, None, None) == j1.INVALID_ARG
     assert "NULL" in j1.last_error()
+
+
+def test_python_constants_match_the_header():
+    """The Python mirror's status codes, status names and fault kinds are the header's enums."""
+    text = open(HEADER, encoding="utf-8").read()
+    values = {name: int(v) for name, v in re.findall(r"\b(J1_(?:OK|ERR_[A-Z_]+|FAULT_[A-Z_]+))\s*=\s*(\d+)", text)}
+    statuses = {k: v for k, v in values.items() if k == "J1_OK" or k.startswith("J1_ERR_")}
+    assert statuses, "no status enum found"
+    for name, v in statuses.items():
+        assert getattr(j1, "OK" if name == "J1_OK" else name[len("J1_ERR_"):]) == v, name
+        assert j1.STATUS_NAMES[v] == name
+    assert len(j1.STATUS_NAMES) == len(statuses)
+    faults = {k: v for k, v in values.items() if k.startswith("J1_FAULT_")}
+    assert faults
+    for name, v in faults.items():
+        assert getattr(j1, name[len("J1_"):]) == v, name
