@@ -73,7 +73,7 @@ J1_API void j1_model_destroy(j1_model* model);
 J1_API size_t j1_model_name(const j1_model* model, char* buf, size_t cap);
 J1_API j1_status j1_model_config(const j1_model* model, j1_config* out);
 
-/* CudaModel::forward over one packed batch (model::Batch, src/model.rs:225-269):
+/* CudaModel::forward over one packed batch (model::Batch, src/model.rs:113-157):
  *   ids[t]            token ids of all sequences, back to back
  *   starts/lens[nseq] packed start row and length of each sequence (starts[s] == sum(lens[<s]))
  *   qtypes[nseq]      question type (0..2) per sequence
@@ -356,11 +356,15 @@ J1_API j1_status j1_text_encoder_request_tokens(j1_text_encoder* enc, const char
  * std::bad_alloc (-> J1_ERR_OOM) and J1_FAULT_WORKER the next host worker threads (tokenizer,
  * text encoder, engine device pool) throw std::runtime_error (-> J1_ERR_INTERNAL): the paths a
  * real host failure takes. J1_FAULT_THREAD makes the next attempts to start a host worker
- * thread fail; the call then finishes its work on the threads it has (no error). The environment variable J1_FAULT=alloc|launch|nan|host|worker
- * arms one at the first j1_model_create. Nothing is done to the GPU: an injected allocation
- * or launch does not happen and injected nonfinite scores are written into the host copy. */
+ * thread fail; the call then finishes its work on the threads it has (no error).
+ * J1_FAULT_DEVICE_WAIT makes the next j1_op_attention_noalloc calls follow their attention
+ * kernel with one bounded device wait (about 1 ms) that times out and records its site
+ * (99) in the call's error word, as a timed-out wait of that kernel would. The environment
+ * variable J1_FAULT=alloc|launch|nan|host|worker arms one at the first j1_model_create.
+ * Nothing faults on the GPU: an injected allocation or launch does not happen, injected
+ * nonfinite scores are written into the host copy, and the injected wait is bounded. */
 enum { J1_FAULT_ALLOC = 1, J1_FAULT_LAUNCH = 2, J1_FAULT_NAN = 3, J1_FAULT_HOST = 4, J1_FAULT_WORKER = 5,
-       J1_FAULT_THREAD = 6 };
+       J1_FAULT_THREAD = 6, J1_FAULT_DEVICE_WAIT = 7 };
 J1_API void j1_inject_fault(int32_t kind, int32_t count);
 /* Device-side failure detection without a fault: one thread waits, with the library's
  * bounded wait and a limit of limit_cycles (1e3..4e9), on an mbarrier nothing arrives at.
@@ -419,13 +423,18 @@ J1_API j1_status j1_op_attention(const void* qkv, int64_t t, int32_t hidden, con
                           const uint32_t* seq_lens, size_t nseq, int32_t window, void* ctx, void* stream, int sync);
 
 /* j1_op_attention with no run-time allocation (no counterpart in the reference).
- * Same arguments, results and errors as j1_op_attention, but the tile list and the
- * error word live in a fixed device array of this library, so callers that cannot
- * allocate device memory (a pool that owns all free HBM; a loop that must not hit
- * cudaMalloc's device-wide synchronisation) can use it. At most 8192 query tiles
- * (sum of ceil(len / 128)) per call, else J1_ERR_INVALID_ARG. All calls on a device
- * share that array: calls on one stream are ordered, overlapping calls race. The
- * first call on each device does its set-up and should precede any stream capture. */
+ * Same arguments and results as j1_op_attention, but the tile list and the error words
+ * live in a fixed device array of this library, so callers that cannot allocate device
+ * memory (a pool that owns all free HBM; a loop that must not hit cudaMalloc's
+ * device-wide synchronisation) can use it. At most 8192 query tiles (sum of
+ * ceil(len / 128)) per call, else J1_ERR_INVALID_ARG. All calls on a device share that
+ * array: calls on one stream are ordered, calls that overlap on the GPU (streams with no
+ * ordering between them) race. CUDA places the array in device memory at the first call
+ * on each device, which also does the set-up: make it (nseq = 0 does only that) before a
+ * pool reserves the free memory and before any stream capture. Device-side timeouts: a
+ * call with sync = 0 returns before its kernel runs, so a timeout of its kernel is
+ * reported by the next call on that device made with sync = 1 (nseq = 0 with sync = 1
+ * only collects), as J1_ERR_DEVICE_TIMEOUT "... in an earlier call made with sync = 0". */
 J1_API j1_status j1_op_attention_noalloc(const void* qkv, int64_t t, int32_t hidden, const uint32_t* seq_starts,
                                          const uint32_t* seq_lens, size_t nseq, int32_t window, void* ctx,
                                          void* stream, int sync);

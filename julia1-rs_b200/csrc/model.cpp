@@ -98,7 +98,7 @@ size_t last_error_copy(char* buf, size_t cap) { return copy_out(t_last_error, bu
 // the process report a failure, so callers can test their error handling. Nothing is done
 // to the GPU: an injected allocation or launch simply does not happen, and injected
 // nonfinite scores are written into the host copy.
-std::atomic<int> g_fault[7];
+std::atomic<int> g_fault[8];
 
 bool take_fault(int kind) {
   int n = g_fault[kind].load();
@@ -883,7 +883,7 @@ j1_status j1_config_load(const char* ckpt_dir, j1_config* out) {
 }
 
 void j1_inject_fault(int32_t kind, int32_t count) {
-  if (kind >= J1_FAULT_ALLOC && kind <= J1_FAULT_THREAD) g_fault[kind] = count > 0 ? count : 0;
+  if (kind >= J1_FAULT_ALLOC && kind <= J1_FAULT_DEVICE_WAIT) g_fault[kind] = count > 0 ? count : 0;
 }
 
 j1_status j1_selftest_device_timeout(int ordinal, int64_t limit_cycles) {

@@ -21,7 +21,7 @@ j1_status set_error(j1_status s, const std::string& msg);
 j1_status set_error_noexcept(j1_status s, const char* fn, const char* what) noexcept;
 j1_status cuda_error(cudaError_t e, const char* what);
 // j1_inject_fault state: remaining injected faults per kind (J1_FAULT_*).
-extern std::atomic<int> g_fault[7];
+extern std::atomic<int> g_fault[8];
 bool take_fault(int kind);
 
 // Every C entry point runs its body through guard(): a C++ exception (host memory

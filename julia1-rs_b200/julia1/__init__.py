@@ -40,7 +40,7 @@ EXPORTS = [
     "j1_text_encoder_request_tokens", "j1_text_encoder_encode_batch", "j1_engine_logits_text", "j1_json_dumps",
     "j1_inject_fault", "j1_selftest_device_timeout",
 ]
-FAULT_ALLOC, FAULT_LAUNCH, FAULT_NAN, FAULT_HOST, FAULT_WORKER, FAULT_THREAD = 1, 2, 3, 4, 5, 6
+FAULT_ALLOC, FAULT_LAUNCH, FAULT_NAN, FAULT_HOST, FAULT_WORKER, FAULT_THREAD, FAULT_DEVICE_WAIT = 1, 2, 3, 4, 5, 6, 7
 PROF_FAMILIES = 12
 
 EPI_BF16, EPI_QKV_ROPE, EPI_GEGLU, EPI_RESID_LN, EPI_RESID, EPI_SCORER = range(6)
@@ -851,7 +851,9 @@ def inject_fault(kind: int, count: int = 1):
     (FAULT_ALLOC), kernel launches (FAULT_LAUNCH) or score readbacks (FAULT_NAN) fail; with
     FAULT_HOST the next entry points throw std::bad_alloc inside the library (-> OOM), with
     FAULT_WORKER the next host worker threads throw (-> INTERNAL); with FAULT_THREAD the next
-    worker threads fail to start (the call finishes on the threads it has)."""
+    worker threads fail to start (the call finishes on the threads it has); with
+    FAULT_DEVICE_WAIT the next op_attention_noalloc calls record a bounded device wait that
+    timed out in their error word."""
     lib().j1_inject_fault(int(kind), int(count))
 
 

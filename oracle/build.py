@@ -17,7 +17,10 @@ BUILD = os.path.join(HERE, "_build")
 REF = os.path.join(HERE, "_ref")
 LIB = os.path.join(BUILD, "libj1oracle.so")
 CUBIN = os.path.join(REF, "kernels.cubin")
-REFERENCE_KERNELS = os.path.join(os.environ.get("J1_REFERENCE_DIR", "/root/reference"), "src", "cuda", "kernels.cu")
+# The reference checkout: $J1_REFERENCE_DIR, else a directory named "reference" beside this
+# repository's root. Without one (the GPU box) the prebuilt cubin is used.
+REFERENCE_DIR = os.environ.get("J1_REFERENCE_DIR") or os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
+REFERENCE_KERNELS = os.path.join(REFERENCE_DIR, "src", "cuda", "kernels.cu")
 
 
 def build_oracle(force=False):

@@ -41,11 +41,40 @@ def test_gemm_peak_share():
     model_f = {f: {"flops": 1e12} for f in ("gemm_qkv_rope", "gemm_wo_resid_ln", "gemm_wi_geglu",
                                              "gemm_wo2_resid_ln")}
     timed = {f: (2.0, 2) for f in model_f}  # 2 launches in 2 ms per family -> 1 PF/s
-    g = bench.gemm_peak_share(timed, model_f, 1362.0)
+    g = bench.gemm_peak_share(timed, model_f, 1638.8)
     assert g["tflops"] == pytest.approx(1000.0)
-    assert g["frac_of_measured_sustained"] == pytest.approx(1000.0 / 1362.0, abs=1e-4)
+    assert g["frac_of_measured_burst"] == pytest.approx(1000.0 / 1638.8, abs=1e-4)
     assert g["frac_of_nominal"] == pytest.approx(1000.0 / 2250.0, abs=1e-4)
     assert bench.gemm_peak_share({}, model_f, 1362.0) is None
+
+
+def test_encoder_flops_of_ragged_lengths():
+    # one forward over several sequences is the sum of the per-sequence FLOPs
+    lens = [16, 200, 1024]
+    assert bench.encoder_flops(lens) == pytest.approx(sum(bench.encoder_flops([s]) for s in lens))
+    assert bench.encoder_flops([8192]) / 8192 == pytest.approx(427.45e6, rel=1e-3)
+
+
+def test_roofline_entry_fractions():
+    fm = {"flops": 4.0e11, "bytes": 1.0e9, "bound": "tensor"}
+    r = bench.roofline_entry("gemm_wi_geglu", fm, 0.4, 0.2, 6551.0, 1638.8, 1387.9, "measured")
+    assert r["achieved"] == pytest.approx(1000.0) and r["frac"] == pytest.approx(1000.0 / 1638.8, abs=1e-4)
+    assert r["frac_of_sustained"] == pytest.approx(1000.0 / 1387.9, abs=1e-4)
+    assert r["bound"] == "tensor" and r["unit"] == "TFLOP/s" and r["peak"] == 1638.8
+    fm = {"flops": 1.0, "bytes": 1.3e9, "bound": "hbm"}
+    r = bench.roofline_entry("gemm_wo2_resid_ln", fm, 0.26, 0.2, 6551.0, 1638.8, 1387.9, "measured")
+    assert r["achieved"] == pytest.approx(5000.0) and r["frac"] == pytest.approx(5000.0 / 6551.0, abs=1e-4)
+
+
+def test_job_split_covers_every_row_once():
+    """The strong-scaling job: 4096 rows in 16 micro-batches of 256, dealt to 1/2/4/8 ranks."""
+    from julia1.replicas import rank_share
+    lens = [bench.SEQ] * bench.JOB_ROWS
+    for world in (1, 2, 4, 8):
+        shares = [rank_share(lens, bench.BATCH_ROWS, bench.MAX_BATCH_TOKENS, r, world) for r in range(world)]
+        assert all(len(s) == 16 // world for s in shares)
+        rows = sorted(i for s in shares for b in s for i in b)
+        assert rows == list(range(bench.JOB_ROWS))
 
 
 def test_traffic_table_parses_committed_profile():
