@@ -20,7 +20,7 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-fvisibility=hidden", "-I", os.path.join(ROOT, "include")]
-SOURCES = ["gemm.cu", "attention.cu", "rows.cu", "attention_noalloc.cu", "checkpoint.cpp", "model.cpp", "engine.cpp", "router.cpp", "tokenizer.cpp"]
+SOURCES = ["gemm.cu", "gemm_resid.cu", "attention.cu", "rows.cu", "attention_noalloc.cu", "checkpoint.cpp", "model.cpp", "engine.cpp", "router.cpp", "tokenizer.cpp"]
 
 
 def _newest_header():

@@ -669,6 +669,15 @@ int launch_full_row(int H, const CUtensorMap& tmA, const CUtensorMap& tmW, const
 
 int gemm_bn_for(int n) { return (n % 256 == 0) ? 256 : 128; }
 
+// J1_RESID_KERNEL=pair selects the earlier CTA-pair residual kernel (A/B measurements).
+bool resid_cluster_kernel() {
+  static const bool on = [] {
+    const char* v = std::getenv("J1_RESID_KERNEL");
+    return !(v && std::strcmp(v, "pair") == 0);
+  }();
+  return on;
+}
+
 const char* gemm_shape_error(GemmEpi epi, int bn, int M, int N, int K) {
   if (M < 0 || N <= 0 || K <= 0) return "GEMM dimensions must be positive";
   if (bn != 128 && bn != 256) return "GEMM tile width must be 128 or 256";
@@ -681,9 +690,12 @@ const char* gemm_shape_error(GemmEpi epi, int bn, int M, int N, int K) {
 }
 
 int launch_gemm(GemmEpi epi, int bn, const CUtensorMap& tmA, const CUtensorMap& tmW, const CUtensorMap* tmX,
-                const EpiParams& p, int grid_limit, cudaStream_t stream) {
+                const EpiParams& p, int grid_limit, cudaStream_t stream, const CUtensorMap* tmXs,
+                const CUtensorMap* tmXN) {
   if (p.M == 0) return 0;
   if (!tmX && epi != EPI_SCORER) return static_cast<int>(cudaErrorInvalidValue);
+  if ((epi == EPI_RESID_LN || epi == EPI_RESID) && resid_cluster_kernel())
+    return launch_resid_gemm(epi == EPI_RESID_LN, tmA, tmW, *tmX, tmXs, tmXN, p, grid_limit, stream);
   const CUtensorMap& X = tmX ? *tmX : tmA;  // unused by the scorer epilogue
   switch (epi) {
     case EPI_BF16:
@@ -749,8 +761,8 @@ bool make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t 
 }
 
 bool make_tmap_f32_resid(CUtensorMap* map, const float* base, uint64_t rows, uint64_t cols, uint64_t ld,
-                         const char** why) {
-  return make_tmap(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, rows, cols, ld, 32, 128, why);
+                         const char** why, uint32_t box_rows) {
+  return make_tmap(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, rows, cols, ld, 32, box_rows, why);
 }
 
 }  // namespace j1rt

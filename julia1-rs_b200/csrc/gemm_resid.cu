@@ -1,0 +1,553 @@
+// Residual (+ LayerNorm) GEMM on row-split clusters: x += bf16(A . W^T) (+ bias), then
+// xn = bf16(LayerNorm(x; ln_w, ln_b, eps)) for the next projection.
+//
+// Replaces the reference's cuBLAS Wo / Wo2 / out_proj / linear2 GEMMs with BF16 output
+// (src/cuda/mod.rs:456,461,490-495) and the row kernel that consumed them, ln_bf16
+// (src/cuda/kernels.cu:97-109): the GEMM output is rounded to BF16 exactly where the
+// reference rounds it, added to the FP32 residual, the bias added after it, and the
+// normalised row rounded to BF16.
+//
+// A cluster of 2 NG CTAs owns 256 whole rows at a time (a unit). It is NG CTA pairs: pair j
+// computes columns [j BN, (j + 1) BN) of the unit's rows with tcgen05 .cta_group::2 (M = 256,
+// N = BN; each CTA loads its own 128 rows of A and half of the pair's BN rows of W, the even
+// CTA issues the MMAs), so each CTA holds the FP32 accumulator of its 128 rows x BN columns,
+// twice in TMEM: the main loop of the next unit runs while the epilogue of this one drains.
+// Per CTA:
+//   warp 0      TMA producer: A (128 x 64) and W (BN/2 x 64) boxes into a 3-stage ring
+//   warp 1      TMEM allocator; in the even CTA the single-thread tcgen05.mma issuer
+//   warp 2      x producer: TMA loads of 128 x 32 FP32 residual chunks into a ring
+//   warps 4..7  epilogue, one thread per row (TMEM lane = row):
+//     pass 1: per 32-column chunk, x += bf16(acc) (+ bias), written back into the
+//             chunk (TMA store) and into TMEM over the accumulator; chunk mean / M2
+//             merged into the row's running statistics (Chan)
+//     exchange: the row's (mean, M2) over its BN columns goes to the other NG - 1 CTAs
+//             that hold the same rows by st.async (DSMEM, completing bytes on the
+//             receiver's mbarrier); each merges the NG partials in pair order, so all
+//             of them hold the same mean and rstd for the row
+//     pass 2: the updated row is read back from TMEM, normalised, rounded to BF16 and
+//             staged in 32 x 64 boxes (128B swizzle) that leave by TMA store
+//   Each epilogue warp stores its own 32 rows of every chunk and box, so the four warps run
+//   without a common barrier.
+// Unlike a GEMM whose epilogue re-reads x from global memory, the row never leaves the
+// chip between its update and its normalisation: per row the kernel reads A and x once
+// and writes x and xn once.
+//
+// No TMA load in this file uses cluster multicast: every CTA loads its own A rows and its
+// own half of the W tile (the NG pairs of a cluster read the same A rows; the second and
+// later reads hit L2).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "kernels.h"
+#include "ptx.cuh"
+
+namespace j1rt {
+
+namespace {
+
+// Ring depths (compile-time): A/W stages and residual chunks in flight.
+#ifndef J1_RLN_STAGES
+#define J1_RLN_STAGES 3
+#endif
+#ifndef J1_RLN_NX
+#define J1_RLN_NX 5
+#endif
+
+constexpr int RBM = 128;                     // rows per CTA (256 per pair)
+constexpr int RBK = 64;                      // K per stage
+constexpr uint32_t RX_CHUNK = 128 * 32 * 4;  // one 128 x 32 FP32 residual chunk (16 KB)
+constexpr uint32_t RO_WBOX = 32 * 64 * 2;    // one warp's 32 x 64 BF16 xn box (4 KB)
+
+template <int NG, int BN>
+struct RlnCfg {
+  static constexpr int CS = 2 * NG;  // CTAs per cluster
+  static constexpr int STAGES = J1_RLN_STAGES;
+  static constexpr int NX = J1_RLN_NX;  // residual chunks in flight
+  static constexpr int THREADS = 256;
+  static constexpr uint32_t A_BYTES = RBM * RBK * 2;
+  static constexpr uint32_t W_BYTES = (BN / 2) * RBK * 2;
+  static constexpr uint32_t STAGE_BYTES = A_BYTES + W_BYTES;
+  static constexpr uint32_t O_BYTES = 4 * 2 * RO_WBOX;      // two xn boxes per epilogue warp
+  static constexpr uint32_t PAR_BYTES = 3 * BN * 4;         // ln_w, ln_b, bias of this CTA's columns
+  static constexpr uint32_t STAT_BYTES = 2 * NG * RBM * 8;  // [2 slots][NG pairs][128 rows] (mean, M2)
+  static constexpr uint32_t SMEM = STAGES * STAGE_BYTES + NX * RX_CHUNK + O_BYTES + PAR_BYTES + STAT_BYTES +
+                                   1024 /*align*/ + 256 /*barriers*/;
+  static constexpr uint32_t TMEM_COLS = 2 * BN;  // 256 or 512
+  static_assert(SMEM <= 232448, "shared memory budget");
+  static_assert(BN == 128 || BN == 256, "columns per pair");
+  static_assert(CS <= 8, "portable cluster size");
+};
+
+// st.async of two floats into the shared memory of a CTA of the cluster, completing 8
+// bytes on that CTA's mbarrier (both addresses are shared::cluster addresses).
+__device__ __forceinline__ void st_async_f2(uint32_t caddr, float a, float b, uint32_t mbar_caddr) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(caddr),
+               "f"(a), "f"(b), "r"(mbar_caddr)
+               : "memory");
+}
+
+// Rounds two FP32 values to BF16 (round to nearest even) and back.
+__device__ __forceinline__ void bf16_round2(float& a, float& b) {
+  const uint32_t u = pack_bf16x2(a, b);
+  a = __uint_as_float(u << 16);
+  b = __uint_as_float(u & 0xffff0000u);
+}
+
+template <int NG, int BN, bool LN>
+__global__ void __launch_bounds__(256, 1)
+    resid_ln_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
+                    const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmXs,
+                    const __grid_constant__ CUtensorMap tmXN, const EpiParams p) {
+  using C = RlnCfg<NG, BN>;
+  constexpr int CS = C::CS;
+  constexpr int NCH = BN / 32;   // residual chunks per unit
+  constexpr int NBOX = BN / 64;  // xn boxes per unit
+  constexpr int H = NG * BN;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sW = sA + C::STAGES * C::A_BYTES;
+  uint8_t* sX = sW + C::STAGES * C::W_BYTES;
+  uint8_t* sO = sX + C::NX * RX_CHUNK;                            // [warp][2] xn boxes
+  float* sPar = reinterpret_cast<float*>(sO + C::O_BYTES);         // [3][BN]: ln_w, ln_b, bias
+  float2* sStat = reinterpret_cast<float2*>(sO + C::O_BYTES + C::PAR_BYTES);  // [slot][pair][row]
+  uint64_t* full = reinterpret_cast<uint64_t*>(sO + C::O_BYTES + C::PAR_BYTES + C::STAT_BYTES);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* tfull = empty + C::STAGES;  // [2]
+  uint64_t* tempty = tfull + 2;         // [2] (the even CTA's: 4 arrivals from each CTA of the pair)
+  uint64_t* xfull = tempty + 2;         // [NX]
+  uint64_t* xempty = xfull + C::NX;     // [NX]
+  uint64_t* statbar = xempty + C::NX;   // [2] the other pairs' row statistics of a unit have arrived
+  uint64_t* drain = statbar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  grid_dep_launch();
+  const int warp = warp_id(), lane = lane_id();
+  const uint32_t rank = cluster_ctarank();
+  const uint32_t half = rank & 1u;          // rows [256 u + 128 half, +128) of a unit
+  const int pr = static_cast<int>(rank >> 1);  // column group: columns [pr BN, (pr + 1) BN)
+  const uint32_t lead = rank & ~1u;         // the even CTA of this pair (issues the MMAs)
+  const bool leader = half == 0;
+  const int cid = static_cast<int>(blockIdx.x) / CS, ncl = static_cast<int>(gridDim.x) / CS;
+  const int units = (p.M + 2 * RBM - 1) / (2 * RBM);
+  const int kblocks = p.K / RBK;
+  const int col0 = pr * BN;
+  {  // exit before allocating anything when an earlier CTA of this launch gave up; rank 0
+     // decides for the whole cluster (once every CTA of it has started) so that its CTAs
+     // stay together: a CTA that left could not receive its peers' statistics
+    __shared__ int s_abort;
+    cluster_sync();
+    if (rank == 0 && threadIdx.x == 0) {
+      const uint32_t a = device_aborted(p.err) ? 1u : 0u;
+      for (int r = 0; r < CS; ++r) st_shared_cluster_u32(mapa_shared(smem_u32(&s_abort), r), a);
+    }
+    cluster_sync();
+    if (s_abort) return;
+  }
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 8);   // one arrival per epilogue warp of both CTAs of the pair
+      mbar_init(&statbar[b], 1);  // the local expect_tx; the bytes come from the other pairs
+    }
+    for (int b = 0; b < C::NX; ++b) {
+      mbar_init(&xfull[b], 1);
+      mbar_init(&xempty[b], 4);  // one arrival per epilogue warp (its rows' store has read the slot)
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmW);
+    tma_prefetch_desc(&tmX);
+    tma_prefetch_desc(&tmXs);
+    if (LN) tma_prefetch_desc(&tmXN);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers of every CTA initialised, TMEM allocated in both CTAs of each pair
+  tc_fence_after();
+  grid_dep_wait();  // the previous kernel's outputs (this kernel's inputs and outputs) are ready
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ A / W producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int u = cid; u < units && ok; u += ncl) {
+        const int m0 = u * 2 * RBM + static_cast<int>(half) * RBM;
+        const int n0 = col0 + static_cast<int>(half) * (BN / 2);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait<true>(&empty[stage], phase ^ 1, abort_flag, p.err, 31)) {
+            ok = false;
+            break;
+          }
+          // both CTAs' boxes of this stage complete on the even CTA's barrier
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * C::STAGE_BYTES);
+          const uint32_t fb = mapa_shared(smem_u32(&full[stage]), lead);
+          tma_load_2d_pair(&tmA, fb, sA + stage * C::A_BYTES, kb * RBK, m0);
+          tma_load_2d_pair(&tmW, fb, sW + stage * C::W_BYTES, kb * RBK, n0);
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        // Unwinding: loads of this CTA may complete on the other CTA's barrier, so they
+        // cannot all be waited for here; give any copy in flight ample time to land
+        // before the CTA releases its shared memory (this path only follows a timeout).
+        const long long t0 = clock64();
+        while (clock64() - t0 < 2000000) __nanosleep(1000);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (even CTA)
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16(2 * RBM, BN, false, false);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      bool ok = true;
+      for (int u = cid; u < units && ok; u += ncl, ++acc) {
+        const int buf = acc & 1;
+        if (!mbar_wait<true>(&tempty[buf], ((acc >> 1) & 1) ^ 1, abort_flag, p.err, 32)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + buf * BN;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait<true>(&full[stage], phase, abort_flag, p.err, 33)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * C::A_BYTES);
+          const uint32_t b0 = smem_u32(sW + stage * C::W_BYTES);
+#pragma unroll
+          for (int k = 0; k < RBK / 16; ++k)
+            umma_bf16_pair(d, sdesc_sw128(a0 + k * 32, 16, 1024), sdesc_sw128(b0 + k * 32, 16, 1024), idesc,
+                           (kb | k) != 0);
+          umma_commit_pair(mapa_shared(smem_u32(&empty[stage]), lead));
+          umma_commit_pair(mapa_shared(smem_u32(&empty[stage]), lead + 1));
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(mapa_shared(smem_u32(&tfull[buf]), lead));
+        umma_commit_pair(mapa_shared(smem_u32(&tfull[buf]), lead + 1));
+      }
+      // every MMA of this thread has completed before TMEM is released (in both CTAs)
+      umma_commit_pair(mapa_shared(smem_u32(drain), lead));
+      volatile int no_abort = 0;
+      mbar_wait<true>(drain, 0, &no_abort, nullptr, 0);
+    }
+  } else if (warp == 2) {
+    // ------------------------------------------------------------ residual producer
+    if (lane == 0) {
+      uint32_t gx = 0;
+      uint32_t armed = 0, armed_par = 0;
+      bool ok = true;
+      for (int u = cid; u < units && ok; u += ncl) {
+        const int m0 = u * 2 * RBM + static_cast<int>(half) * RBM;
+        for (int c = 0; c < NCH; ++c, ++gx) {
+          const uint32_t b = gx % C::NX, ph = (gx / C::NX) & 1;
+          if (!mbar_wait<true>(&xempty[b], ph ^ 1, abort_flag, p.err, 34)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&xfull[b], RX_CHUNK);
+          tma_load_2d(&tmX, &xfull[b], sX + b * RX_CHUNK, col0 + c * 32, m0);
+          armed |= 1u << b;
+          armed_par = (armed_par & ~(1u << b)) | (ph << b);
+        }
+      }
+      if (!ok) {  // unwinding: every load already issued must land before smem is released
+        volatile int no_abort = 0;
+        for (int b = 0; b < C::NX; ++b)
+          if (armed & (1u << b)) mbar_wait<true>(&xfull[b], (armed_par >> b) & 1u, &no_abort, nullptr, 0);
+      }
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ epilogue (warps 4..7)
+    // Each warp owns 32 rows (its TMEM lane quarter) and works through the units on its own:
+    // it stores its rows of every residual chunk and every xn box itself (32-row TMA boxes),
+    // so no barrier couples the four warps. After an abort every wait returns at once and
+    // the loops run out without stores.
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int trow = q * 32 + lane;
+    {  // this CTA's columns of ln_w, ln_b and bias, once
+      const int et = threadIdx.x - 128;
+      for (int j = et; j < BN; j += 128) {
+        sPar[j] = LN ? p.ln_w[col0 + j] : 0.f;
+        sPar[BN + j] = (LN && p.ln_b) ? p.ln_b[col0 + j] : 0.f;
+        sPar[2 * BN + j] = p.bias ? p.bias[col0 + j] : 0.f;
+      }
+      named_bar_sync(1, 128);
+    }
+    const float4* parw = reinterpret_cast<const float4*>(sPar);
+    const float4* parb = reinterpret_cast<const float4*>(sPar + BN);
+    const float4* parc = reinterpret_cast<const float4*>(sPar + 2 * BN);
+    int acc = 0;
+    uint32_t gch = 0;  // residual chunks consumed so far
+    int xpend = -1;    // ring slot whose store (of this warp's rows) may still be reading smem
+    int ob = 0;        // this warp's xn box in use (of two)
+    for (int u = cid; u < units; u += ncl, ++acc) {
+      const int m0 = u * 2 * RBM + static_cast<int>(half) * RBM;
+      const int buf = acc & 1;
+      mbar_wait<true>(&tfull[buf], (acc >> 1) & 1, abort_flag, p.err, 35);
+      tc_fence_after();
+      const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
+      float w_mean = 0.f, w_m2 = 0.f, w_n = 0.f;
+      // ---------------- pass 1: residual update
+#pragma unroll 1
+      for (int c = 0; c < NCH; ++c, ++gch) {
+        const uint32_t b = gch % C::NX;
+        uint32_t r[32];
+        tmem_ld32(tb + c * 32, r);
+        tmem_ld_wait();
+        mbar_wait<true>(&xfull[b], (gch / C::NX) & 1, abort_flag, p.err, 36);
+        uint8_t* xrow = sX + b * RX_CHUNK + trow * 128;  // 16-byte unit i at (i ^ (row & 7)) * 16
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          float4* slot = reinterpret_cast<float4*>(xrow + ((static_cast<uint32_t>(i) ^ (trow & 7)) << 4));
+          float4 o = *slot;
+          float d0 = __uint_as_float(r[4 * i + 0]), d1 = __uint_as_float(r[4 * i + 1]);
+          float d2 = __uint_as_float(r[4 * i + 2]), d3 = __uint_as_float(r[4 * i + 3]);
+          bf16_round2(d0, d1);  // delta = bf16(A . W^T), as the reference's GEMM output
+          bf16_round2(d2, d3);
+          o.x += d0;
+          o.y += d1;
+          o.z += d2;
+          o.w += d3;
+          if (p.bias) {
+            const float4 bb = parc[c * 8 + i];
+            o.x += bb.x;
+            o.y += bb.y;
+            o.z += bb.z;
+            o.w += bb.w;
+          }
+          *slot = o;
+          v[4 * i + 0] = o.x;
+          v[4 * i + 1] = o.y;
+          v[4 * i + 2] = o.z;
+          v[4 * i + 3] = o.w;
+        }
+        if constexpr (LN) {
+          uint32_t vv[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) vv[j] = __float_as_uint(v[j]);
+          tmem_st32(tb + c * 32, vv);  // the updated row stays on chip for pass 2
+          // chunk mean / M2 (two-pass over registers), merged into the row's running state
+          float cs4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int j = 0; j < 32; ++j) cs4[j & 3] += v[j];
+          const float cm = ((cs4[0] + cs4[1]) + (cs4[2] + cs4[3])) * (1.f / 32.f);
+          float c24[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int j = 0; j < 32; ++j) c24[j & 3] += (v[j] - cm) * (v[j] - cm);
+          const float c2 = (c24[0] + c24[1]) + (c24[2] + c24[3]);
+          const float n_new = w_n + 32.f;
+          const float delta = cm - w_mean;
+          w_mean += delta * (32.f / n_new);
+          w_m2 += c2 + delta * delta * (w_n * 32.f / n_new);
+          w_n = n_new;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if (!*abort_flag) {
+            tma_store_2d(&tmXs, sX + b * RX_CHUNK + q * 32 * 128, col0 + c * 32, m0 + q * 32);
+            bulk_commit();
+          }
+          bulk_wait_read_1();  // this warp's previous chunk store has read its slot: release it
+          if (xpend >= 0) mbar_arrive(&xempty[xpend]);
+          xpend = static_cast<int>(b);
+        }
+        __syncwarp();
+      }
+      if (lane == 0) {  // the unit's last chunk: release its slot once the store has read it
+        bulk_wait_read_all();
+        if (xpend >= 0) mbar_arrive(&xempty[xpend]);
+        xpend = -1;
+      }
+      if constexpr (LN) {
+        tmem_st_wait();
+        // ---------------- row statistics over the pairs of the cluster
+        const int su = acc & 1;
+        float mean = w_mean, m2 = w_m2;
+        if constexpr (NG > 1) {
+          float2* mine = sStat + (su * NG + pr) * RBM + trow;
+          const uint32_t bar_local = smem_u32(&statbar[su]);
+          for (int j = 0; j < NG; ++j)
+            if (j != pr) {
+              const uint32_t dst = static_cast<uint32_t>(2 * j) + half;  // same rows, pair j
+              st_async_f2(mapa_shared(smem_u32(mine), dst), w_mean, w_m2, mapa_shared(bar_local, dst));
+            }
+          if (trow == 0) mbar_arrive_expect_tx(&statbar[su], (NG - 1) * RBM * 8);
+          mbar_wait<true>(&statbar[su], (acc >> 1) & 1, abort_flag, p.err, 37);
+          float pm[NG], pq[NG];
+#pragma unroll
+          for (int j = 0; j < NG; ++j) {
+            const float2 s2 = j == pr ? make_float2(w_mean, w_m2) : sStat[(su * NG + j) * RBM + trow];
+            pm[j] = s2.x;
+            pq[j] = s2.y;
+          }
+          float s = 0.f;
+#pragma unroll
+          for (int j = 0; j < NG; ++j) s += pm[j];
+          mean = s * (1.f / NG);
+          m2 = 0.f;
+#pragma unroll
+          for (int j = 0; j < NG; ++j) {
+            const float d = pm[j] - mean;
+            m2 += pq[j] + static_cast<float>(BN) * d * d;
+          }
+        }
+        const float rstd = rsqrtf(m2 * (1.f / static_cast<float>(H)) + p.ln_eps);
+        // ---------------- pass 2: normalise from TMEM, BF16 boxes of this warp's rows out by TMA
+#pragma unroll 1
+        for (int bx = 0; bx < NBOX; ++bx) {
+          uint8_t* box = sO + (q * 2 + ob) * RO_WBOX;
+          uint8_t* srow = box + lane * 128;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int c = 2 * bx + h;
+            uint32_t r[32];
+            tmem_ld32(tb + c * 32, r);
+            tmem_ld_wait();
+            float y[32];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const float4 g = parw[c * 8 + i], be = parb[c * 8 + i];
+              y[4 * i + 0] = (__uint_as_float(r[4 * i + 0]) - mean) * rstd * g.x + be.x;
+              y[4 * i + 1] = (__uint_as_float(r[4 * i + 1]) - mean) * rstd * g.y + be.y;
+              y[4 * i + 2] = (__uint_as_float(r[4 * i + 2]) - mean) * rstd * g.z + be.z;
+              y[4 * i + 3] = (__uint_as_float(r[4 * i + 3]) - mean) * rstd * g.w + be.w;
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              uint4 w;
+              w.x = pack_bf16x2(y[8 * i + 0], y[8 * i + 1]);
+              w.y = pack_bf16x2(y[8 * i + 2], y[8 * i + 3]);
+              w.z = pack_bf16x2(y[8 * i + 4], y[8 * i + 5]);
+              w.w = pack_bf16x2(y[8 * i + 6], y[8 * i + 7]);
+              *reinterpret_cast<uint4*>(srow + ((static_cast<uint32_t>(4 * h + i) ^ (lane & 7)) << 4)) = w;
+            }
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            if (!*abort_flag) {
+              tma_store_2d(&tmXN, box, col0 + bx * 64, m0 + q * 32);
+              bulk_commit();
+            }
+            bulk_wait_read_1();  // the other box's store has read it: it can be rewritten next
+          }
+          __syncwarp();
+          ob ^= 1;
+        }
+      }
+      // this warp has read its lanes of the buffer: release it to the pair's MMA
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&tempty[buf]), lead));
+    }
+    if (lane == 0) bulk_wait_all();  // every store complete: this kernel's x and xn are in memory
+  }
+
+  tc_fence_before();
+  // every role of every CTA is done (no st.async can still target this CTA's smem) and the
+  // MMAs have drained
+  cluster_sync();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+}
+
+template <int NG, int BN, bool LN>
+int launch_rln(const CUtensorMap& tmA, const CUtensorMap& tmW, const CUtensorMap& tmX, const CUtensorMap& tmXs,
+               const CUtensorMap& tmXN, const EpiParams& p, int grid_limit, cudaStream_t stream) {
+  using C = RlnCfg<NG, BN>;
+  static std::atomic<unsigned long long> configured{0};
+  static std::atomic<int> max_clusters[64];
+  auto kern = resid_ln_kernel<NG, BN, LN>;
+  cudaError_t e = set_smem_once(kern, C::SMEM, configured);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  int dev = 0;
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return static_cast<int>(e);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = C::CS;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.blockDim = dim3(C::THREADS);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  // clusters that fit on the device at once (clusters of more than two CTAs cannot always
+  // use every SM: a cluster lives inside one GPC)
+  int mc = (dev >= 0 && dev < 64) ? max_clusters[dev].load() : 0;
+  if (mc <= 0) {
+    cfg.gridDim = dim3(C::CS * 64);
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&mc, kern, &cfg) != cudaSuccess || mc <= 0) {
+      (void)cudaGetLastError();
+      int sms = 0;
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      mc = sms / C::CS;
+    }
+    if (dev >= 0 && dev < 64) max_clusters[dev].store(mc);
+  }
+  cfg.numAttrs = 2;
+  const int units = (p.M + 2 * RBM - 1) / (2 * RBM);
+  int ncl = units < mc ? units : mc;
+  const int by_limit = grid_limit / C::CS > 0 ? grid_limit / C::CS : 1;
+  if (by_limit < ncl) ncl = by_limit;
+  if (ncl <= 0) return 0;
+  cfg.gridDim = dim3(C::CS * ncl);
+  return static_cast<int>(cudaLaunchKernelEx(&cfg, kern, tmA, tmW, tmX, tmXs, tmXN, p));
+}
+
+template <bool LN>
+int launch_rln_h(const CUtensorMap& tmA, const CUtensorMap& tmW, const CUtensorMap& tmX, const CUtensorMap& tmXs,
+                 const CUtensorMap& tmXN, const EpiParams& p, int grid_limit, cudaStream_t stream) {
+  // pairs of BN = gemm_bn_for(H) columns; W boxes are BN/2 rows (gemm_w_box_rows)
+  switch (p.N) {
+    case 256: return launch_rln<1, 256, LN>(tmA, tmW, tmX, tmXs, tmXN, p, grid_limit, stream);
+    case 384: return launch_rln<3, 128, LN>(tmA, tmW, tmX, tmXs, tmXN, p, grid_limit, stream);
+    case 512: return launch_rln<2, 256, LN>(tmA, tmW, tmX, tmXs, tmXN, p, grid_limit, stream);
+    case 768: return launch_rln<3, 256, LN>(tmA, tmW, tmX, tmXs, tmXN, p, grid_limit, stream);
+    case 1024: return launch_rln<4, 256, LN>(tmA, tmW, tmX, tmXs, tmXN, p, grid_limit, stream);
+  }
+  return static_cast<int>(cudaErrorInvalidValue);
+}
+
+}  // namespace
+
+int launch_resid_gemm(bool ln, const CUtensorMap& tmA, const CUtensorMap& tmW, const CUtensorMap& tmX,
+                      const CUtensorMap* tmXs, const CUtensorMap* tmXN, const EpiParams& p, int grid_limit,
+                      cudaStream_t stream) {
+  if (p.M == 0) return 0;
+  if (!tmXs || (ln && !tmXN)) return static_cast<int>(cudaErrorInvalidValue);
+  return ln ? launch_rln_h<true>(tmA, tmW, tmX, *tmXs, *tmXN, p, grid_limit, stream)
+            : launch_rln_h<false>(tmA, tmW, tmX, *tmXs, *tmXs, p, grid_limit, stream);
+}
+
+}  // namespace j1rt

@@ -409,7 +409,11 @@ j1_status stage_batch(j1_model* model, const BatchView& b, int slot = 0, bool sy
             make_tmap_bf16(&model->tm_kv, model->qkv, t, 3 * H, 3 * H, attention_kv_box_rows(), &why) &&
             make_tmap_bf16(&model->tm_cm_o, model->cm, m, H, H, 32, &why) &&
             make_tmap_f32_resid(&model->tm_x, model->x, t, H, H, &why) &&
-            make_tmap_f32_resid(&model->tm_ym, model->ym, m, H, H, &why);
+            make_tmap_f32_resid(&model->tm_ym, model->ym, m, H, H, &why) &&
+            make_tmap_f32_resid(&model->tm_x_st, model->x, t, H, H, &why, 32) &&
+            make_tmap_f32_resid(&model->tm_ym_st, model->ym, m, H, H, &why, 32) &&
+            make_tmap_bf16(&model->tm_xn_st, model->xn, t, H, H, 32, &why) &&
+            make_tmap_bf16(&model->tm_ymb_st, model->ymb, m, H, H, 32, &why);
   if (!ok) return set_error(J1_ERR_CUDA, std::string("activation tensor map: ") + (why ? why : ""));
   model->staged = true;
   return J1_OK;
@@ -448,7 +452,7 @@ j1_status launch_forward(j1_model* model) {
     p.M = t, p.N = H, p.K = H;
     p.x = model->x, p.ldx = H;
     p.ln_w = ly.mlp_norm, p.ln_eps = c.norm_eps, p.xn = model->xn, p.ldxn = H;
-    J1_TRY_LAUNCH(F_WO, launch_gemm(EPI_RESID_LN, bn_full, model->tm_ctx, ly.tm_wo, &model->tm_x, p, nsm, st), "gemm wo");
+    J1_TRY_LAUNCH(F_WO, launch_gemm(EPI_RESID_LN, bn_full, model->tm_ctx, ly.tm_wo, &model->tm_x, p, nsm, st, &model->tm_x_st, &model->tm_xn_st), "gemm wo");
     p = base;
     p.M = t, p.N = 2 * I, p.K = H;
     p.out = model->g, p.ldo = I;
@@ -458,9 +462,9 @@ j1_status launch_forward(j1_model* model) {
     p.x = model->x, p.ldx = H;
     if (l + 1 < L) {
       p.ln_w = model->layers[l + 1].attn_norm, p.ln_eps = c.norm_eps, p.xn = model->xn, p.ldxn = H;
-      J1_TRY_LAUNCH(F_WO2, launch_gemm(EPI_RESID_LN, bn_full, model->tm_g, ly.tm_wo2, &model->tm_x, p, nsm, st), "gemm wo2");
+      J1_TRY_LAUNCH(F_WO2, launch_gemm(EPI_RESID_LN, bn_full, model->tm_g, ly.tm_wo2, &model->tm_x, p, nsm, st, &model->tm_x_st, &model->tm_xn_st), "gemm wo2");
     } else {
-      J1_TRY_LAUNCH(F_WO2, launch_gemm(EPI_RESID, bn_full, model->tm_g, ly.tm_wo2, &model->tm_x, p, nsm, st), "gemm wo2");
+      J1_TRY_LAUNCH(F_WO2, launch_gemm(EPI_RESID, bn_full, model->tm_g, ly.tm_wo2, &model->tm_x, p, nsm, st, &model->tm_x_st), "gemm wo2");
     }
   }
   const auto& h0 = model->head[0];
@@ -483,7 +487,7 @@ j1_status launch_forward(j1_model* model) {
       p.M = t, p.N = H, p.K = H, p.bias = hl.out_b;
       p.x = model->x, p.ldx = H, p.ln_w = hl.norm2_w, p.ln_b = hl.norm2_b, p.ln_eps = 1e-5f;
       p.xn = model->xn, p.ldxn = H;
-      J1_TRY_LAUNCH(F_HEAD_GEMM, launch_gemm(EPI_RESID_LN, bn_full, model->tm_ctx, hl.tm_out, &model->tm_x, p, nsm, st), "gemm out_proj");
+      J1_TRY_LAUNCH(F_HEAD_GEMM, launch_gemm(EPI_RESID_LN, bn_full, model->tm_ctx, hl.tm_out, &model->tm_x, p, nsm, st, &model->tm_x_st, &model->tm_xn_st), "gemm out_proj");
       p = base;
       p.M = t, p.N = FF, p.K = H, p.bias = hl.lin1_b, p.relu = 1;
       J1_TRY_LAUNCH(F_HEAD_GEMM, launch_gemm(EPI_BF16, bn_ff, model->tm_xn, hl.tm_lin1, &model->tm_h, p, nsm, st), "gemm linear1");
@@ -492,7 +496,7 @@ j1_status launch_forward(j1_model* model) {
       p.M = t, p.N = H, p.K = FF, p.bias = hl.lin2_b;
       p.x = model->x, p.ldx = H, p.ln_w = nx.norm1_w, p.ln_b = nx.norm1_b, p.ln_eps = 1e-5f;
       p.xn = model->xn, p.ldxn = H;
-      J1_TRY_LAUNCH(F_HEAD_GEMM, launch_gemm(EPI_RESID_LN, bn_full, model->tm_h, hl.tm_lin2, &model->tm_x, p, nsm, st), "gemm linear2");
+      J1_TRY_LAUNCH(F_HEAD_GEMM, launch_gemm(EPI_RESID_LN, bn_full, model->tm_h, hl.tm_lin2, &model->tm_x, p, nsm, st, &model->tm_x_st, &model->tm_xn_st), "gemm linear2");
     } else if (m > 0) {
       // Last head layer: only the option markers feed the scorer, so the queries, the
       // attention rows and everything after them are computed for the m marker rows
@@ -514,7 +518,7 @@ j1_status launch_forward(j1_model* model) {
       p.M = m, p.N = H, p.K = H, p.bias = hl.out_b;
       p.x = model->ym, p.ldx = H, p.ln_w = hl.norm2_w, p.ln_b = hl.norm2_b, p.ln_eps = 1e-5f;
       p.xn = model->ymb, p.ldxn = H;
-      J1_TRY_LAUNCH(F_HEAD_GEMM, launch_gemm(EPI_RESID_LN, bn_full, model->tm_cm, hl.tm_out, &model->tm_ym, p, nsm, st), "gemm out_proj");
+      J1_TRY_LAUNCH(F_HEAD_GEMM, launch_gemm(EPI_RESID_LN, bn_full, model->tm_cm, hl.tm_out, &model->tm_ym, p, nsm, st, &model->tm_ym_st, &model->tm_ymb_st), "gemm out_proj");
       p = base;
       p.M = m, p.N = FF, p.K = H, p.bias = hl.lin1_b, p.relu = 1;
       J1_TRY_LAUNCH(F_HEAD_GEMM, launch_gemm(EPI_BF16, bn_ff, model->tm_ymb, hl.tm_lin1, &model->tm_hm, p, nsm, st), "gemm linear1");
@@ -522,7 +526,7 @@ j1_status launch_forward(j1_model* model) {
       p.M = m, p.N = H, p.K = FF, p.bias = hl.lin2_b;
       p.x = model->ym, p.ldx = H, p.ln_w = model->s_norm_w, p.ln_b = model->s_norm_b, p.ln_eps = 1e-5f;
       p.xn = model->ymb, p.ldxn = H;
-      J1_TRY_LAUNCH(F_HEAD_GEMM, launch_gemm(EPI_RESID_LN, bn_full, model->tm_hm, hl.tm_lin2, &model->tm_ym, p, nsm, st), "gemm linear2");
+      J1_TRY_LAUNCH(F_HEAD_GEMM, launch_gemm(EPI_RESID_LN, bn_full, model->tm_hm, hl.tm_lin2, &model->tm_ym, p, nsm, st, &model->tm_ym_st, &model->tm_ymb_st), "gemm linear2");
     }
   }
   EpiParams p = base;
@@ -1087,6 +1091,13 @@ j1_status j1_op_gemm(const j1_gemm_args* a, void* stream, int sync) {
       return set_error(J1_ERR_INVALID_ARG, "ldo must be >= the output width and a multiple of 8");
     if (tile_out && !make_tmap_bf16(&tmX, a->out, a->M, out_cols, a->ldo, 128, &why))
       return set_error(J1_ERR_INVALID_ARG, std::string("tensor map: ") + (why ? why : ""));
+    CUtensorMap tmXN, tmXs;
+    if (epi == EPI_RESID_LN && (a->ldxn < a->N || a->ldxn % 8 != 0))
+      return set_error(J1_ERR_INVALID_ARG, "ldxn must be >= N and a multiple of 8");
+    if (epi == EPI_RESID_LN && !make_tmap_bf16(&tmXN, a->xn, a->M, a->N, a->ldxn, 32, &why))
+      return set_error(J1_ERR_INVALID_ARG, std::string("tensor map: ") + (why ? why : ""));
+    if (resid && !make_tmap_f32_resid(&tmXs, a->x, a->M, a->N, a->ldx, &why, 32))
+      return set_error(J1_ERR_INVALID_ARG, std::string("tensor map: ") + (why ? why : ""));
     EpiParams p;
     std::memset(&p, 0, sizeof(p));
     p.M = a->M, p.N = a->N, p.K = a->K;
@@ -1100,7 +1111,8 @@ j1_status j1_op_gemm(const j1_gemm_args* a, void* stream, int sync) {
     p.err = os->err;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const int grid = a->grid_limit > 0 ? a->grid_limit : os->num_sms;
-    int rc = launch_gemm(epi, bn, tmA, tmW, (resid || tile_out) ? &tmX : nullptr, p, grid, st);
+    int rc = launch_gemm(epi, bn, tmA, tmW, (resid || tile_out) ? &tmX : nullptr, p, grid, st,
+                         resid ? &tmXs : nullptr, epi == EPI_RESID_LN ? &tmXN : nullptr);
     if (rc) return cuda_error(static_cast<cudaError_t>(rc), "gemm launch");
     return sync ? op_sync_check(os, st) : J1_OK;
   });

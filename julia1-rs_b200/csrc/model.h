@@ -150,6 +150,8 @@ struct j1_model {
   CUtensorMap tm_ctx_o, tm_cm_o;  // attention outputs, 64 x 32 boxes (TMA stores of O)
   CUtensorMap tm_kv;              // qkv with K/V-block boxes for attention
   CUtensorMap tm_x, tm_ym;  // FP32 residual streams (tokens, markers)
+  CUtensorMap tm_x_st, tm_ym_st;    // the same with 32-row boxes (per-warp stores of the residual GEMMs)
+  CUtensorMap tm_xn_st, tm_ymb_st;  // LayerNorm outputs with 64 x 32 boxes (per-warp stores)
   int64_t launches = 0;
 
   // ---- optional per-launch CUDA-event timing by kernel family (j1_model_profile)
