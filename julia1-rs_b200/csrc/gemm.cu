@@ -4,19 +4,19 @@
 // and the row kernels that consumed their BF16 outputs:
 //   Wqkv                 -> EPI_QKV_ROPE (RoPE of src/cuda/kernels.cu:215-252 moved here)
 //   Wi + geglu           -> EPI_GEGLU    (kernels.cu:137-155)
-//   Wo / Wo2 + ln_bf16   -> EPI_RESID_LN (kernels.cu:97-109, residual added in FP32)
 //   head in_proj/lin1    -> EPI_BF16 with bias (+relu)  (kernels.cu:158-172)
 //   scorer W1 + scorer   -> EPI_SCORER   (kernels.cu:186-194)
+// (Wo / Wo2 with the residual and LayerNorm epilogues live in gemm_resid.cu.)
+// Where the reference rounds a GEMM output to BF16 before a row kernel reads it (the QKV
+// output before RoPE, both GEGLU halves), the epilogue rounds the FP32 accumulator at the
+// same point.
 //
-// Structure: persistent CTA pairs (clusters of two CTAs on two SMs), 224 threads per CTA;
+// Structure: persistent CTA pairs (clusters of two CTAs on two SMs), 192 threads per CTA;
 // the pair shares each 256-row tile through tcgen05 .cta_group::2 (see gemm_tc_kernel).
 //   warp 0      TMA producer: A (128 x 64) and W (BN x 64) boxes into a smem ring
 //   warp 1      TMEM allocator; in the even CTA also the single-thread tcgen05.mma issuer
 //               (M=256 over the pair, N=BN, K=16)
 //   warps 2..5  epilogue: tcgen05.ld of the FP32 accumulator (TMEM lane = row), fused math
-//   warp 6      residual producer (RESID*): TMA loads of x chunks into a smem ring
-//   warps 7..10 LayerNorm (RESID_LN only): normalise the previous unit's updated rows
-//               while warps 2..5 work on the next unit
 // The accumulator is double buffered in TMEM (2 x BN columns) so the epilogue of one
 // tile overlaps the main loop of the next.
 //
@@ -24,12 +24,8 @@
 // 128B-swizzled smem boxes (three in rotation) and leave by TMA store, so global
 // writes are whole lines instead of 16-byte pieces of 32 different rows.
 //
-// Full-row epilogues (RESID*, SCORER) own whole rows: one work unit is 128 rows x H
-// columns, computed as H/BN sub-tiles. The residual stream x (FP32) moves through
-// shared memory in 128 x 32 chunks (load by warp 6, in-place update, TMA store), with
-// NXB chunks in flight so that HBM latency is covered; per-row LayerNorm statistics
-// are merged chunk by chunk (Welford/Chan) and handed over in smem, and the LayerNorm
-// warps produce the normalized BF16 rows from the updated x with warp-coalesced loads.
+// The scorer epilogue owns whole rows: one work unit is 128 rows x H columns, computed as
+// H/BN sub-tiles.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -42,12 +38,9 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr uint32_t XCHUNK = 128 * 32 * 4;  // one 128-row x 32-column FP32 residual chunk
-constexpr uint32_t NXB = 4;                // residual chunks in flight per CTA (64 KB)
 constexpr uint32_t OBUF = 128 * 64 * 2;    // one 128-row x 64-column BF16 output box
 
-__host__ __device__ constexpr bool is_full_row(int epi) { return epi == EPI_RESID_LN || epi == EPI_RESID || epi == EPI_SCORER; }
-__host__ __device__ constexpr bool is_resid(int epi) { return epi == EPI_RESID_LN || epi == EPI_RESID; }
+__host__ __device__ constexpr bool is_full_row(int epi) { return epi == EPI_SCORER; }
 __host__ __device__ constexpr bool is_tile_out(int epi) {
   return epi == EPI_BF16 || epi == EPI_QKV_ROPE || epi == EPI_GEGLU;
 }
@@ -55,23 +48,17 @@ __host__ __device__ constexpr bool is_tile_out(int epi) {
 template <int BN, int EPI>
 struct GemmCfg {
   // per CTA of a pair: 128 rows of A and BN/2 rows of W per stage; the ring takes what is
-  // left of 227 KB after the x ring / output boxes
-  static constexpr int STAGES = (EPI == EPI_SCORER)   ? (BN == 256 ? 6 : 8)
-                                : (EPI == EPI_RESID_LN) ? (BN == 256 ? 4 : 6)
-                                : is_resid(EPI)       ? (BN == 256 ? 5 : 6)
-                                                      : (BN == 256 ? 5 : 7);
-  // RESID_LN adds four LayerNorm warps (7..10) that normalise the previous unit's rows
-  static constexpr int THREADS = (EPI == EPI_RESID_LN) ? 352 : 224;
-  static constexpr uint32_t STATS_BYTES = (EPI == EPI_RESID_LN) ? 2 * BM * 8 : 0;  // 2 slots x (mean, rstd)
+  // left of 227 KB after the output boxes
+  static constexpr int STAGES = (EPI == EPI_SCORER) ? (BN == 256 ? 6 : 8) : (BN == 256 ? 5 : 7);
+  static constexpr int THREADS = 192;
   static constexpr uint32_t A_BYTES = BM * BK * 2;
   static constexpr uint32_t B_BYTES = (BN / 2) * BK * 2;
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr uint32_t X_BYTES = is_resid(EPI) ? NXB * XCHUNK : 0;
   static constexpr uint32_t O_BYTES = is_tile_out(EPI) ? 3 * OBUF : 0;
   static constexpr uint32_t SMEM =
-      STAGES * STAGE_BYTES + X_BYTES + O_BYTES + STATS_BYTES + 1024 /*align*/ + 512 /*barriers*/;
+      STAGES * STAGE_BYTES + O_BYTES + 1024 /*align*/ + 256 /*barriers*/;
   static_assert(SMEM <= 232448, "shared memory budget");
-  static_assert(2 * STAGES + 4 + 1 + 2 * NXB + 4 <= 62, "barrier area");
+  static_assert((2 * STAGES + 5) * 8 + 8 <= 256, "barrier area");
 };
 
 __device__ __forceinline__ float gelu_erf(float v) { return 0.5f * v * (1.f + erff(v * 0.70710678118654752f)); }
@@ -120,7 +107,7 @@ __device__ __forceinline__ void put_row32(uint8_t* srow, int r, int unit0, const
   }
 }
 
-// BN: MMA tile width; NSUB: sub-tiles per full-row unit (full-row width H = NSUB * BN).
+// BN: MMA tile width; NSUB: sub-tiles per full-row (scorer) unit (H = NSUB * BN).
 // Launched as clusters of two CTAs (a pair). A pair computes 256-row tiles: each CTA
 // loads its own 128 rows of A and its own half (BN/2 rows) of the W tile into smem, the
 // even CTA issues tcgen05.mma.cta_group::2 (M = 256, N = BN) over both CTAs' operands,
@@ -132,26 +119,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GemmCfg<BN, EPI>::TH
                    const __grid_constant__ CUtensorMap tmX, const EpiParams p) {
   using C = GemmCfg<BN, EPI>;
   constexpr bool FULL_ROW = is_full_row(EPI);
-  constexpr bool RES = is_resid(EPI);
-  constexpr int H = NSUB * BN;       // full-row width
-  constexpr int NCH = H / 32;        // residual chunks per row
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + C::STAGES * C::A_BYTES;
-  uint8_t* sX = sB + C::STAGES * C::B_BYTES;  // NXB x XCHUNK (1024-aligned) when RES
-  uint8_t* sO = sX + C::X_BYTES;              // 3 x OBUF output boxes when tile-out
-  float2* stats = reinterpret_cast<float2*>(sO + C::O_BYTES);  // [2][128] (mean, rstd) when RESID_LN
-  uint64_t* full = reinterpret_cast<uint64_t*>(sO + C::O_BYTES + C::STATS_BYTES);
+  uint8_t* sO = sB + C::STAGES * C::B_BYTES;  // 3 x OBUF output boxes when tile-out
+  uint64_t* full = reinterpret_cast<uint64_t*>(sO + C::O_BYTES);
   uint64_t* empty = full + C::STAGES;
   uint64_t* tfull = empty + C::STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint64_t* xfull = drain + 1;     // NXB barriers
-  uint64_t* xempty = xfull + NXB;  // NXB barriers
-  uint64_t* lnfull = xempty + NXB;  // [2] a unit's row statistics are in `stats` (RESID_LN)
-  uint64_t* lnempty = lnfull + 2;   // [2] the LayerNorm warps are done with a stats slot
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(lnempty + 2);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   grid_dep_launch();
@@ -185,14 +163,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GemmCfg<BN, EPI>::TH
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], 8);  // one arrival per epilogue warp of both CTAs
     }
-    for (uint32_t b = 0; b < NXB; ++b) {
-      mbar_init(&xfull[b], 1);
-      mbar_init(&xempty[b], 1);
-    }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&lnfull[b], 1);
-      mbar_init(&lnempty[b], 4);
-    }
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -200,7 +170,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GemmCfg<BN, EPI>::TH
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmW);
-    if (RES || is_tile_out(EPI)) tma_prefetch_desc(&tmX);
+    if (is_tile_out(EPI)) tma_prefetch_desc(&tmX);
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, 2 * BN);
@@ -305,10 +275,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GemmCfg<BN, EPI>::TH
     const int trow = q * 32 + lane;
     const bool storer = (threadIdx.x == 64);  // issues the TMA stores of the epilogue
     int acc = 0;
-    uint32_t gch = 0;  // residual chunks consumed so far (ring slot = gch % NXB)
-    int xpend = -1;    // ring slot whose store may still be reading smem
     int ob = 0;        // output box in use (of three)
-    int nunit = 0;     // units done by this CTA
     // BF16 output: this thread's 64 values of row trow -> box `ob` (128B swizzle), then
     // one TMA store of the 128 x 64 box at (col, m0). Three boxes rotate: after issuing
     // a store the storer waits until only that store may still read smem, so the box
@@ -331,7 +298,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GemmCfg<BN, EPI>::TH
       const int m0 = mt * 2 * BM + static_cast<int>(rank) * BM;  // this CTA's 128 rows
       const int row = m0 + trow;
       const bool valid = row < p.M;
-      float w_n = 0.f, w_mean = 0.f, w_m2 = 0.f;  // Welford state of this row
       float score = 0.f;
       float4 rc[8], rsn[8];  // RoPE cos/sin of this row's position (QKV epilogue)
       if constexpr (EPI == EPI_QKV_ROPE) {
@@ -387,7 +353,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GemmCfg<BN, EPI>::TH
             const int col = n0 + g * 64;
             float a[32], b[32];
             if (col < p.rope_cols) {
-              // rotate-half on pairs of dimensions at once (packed FP32):
+              // qkv = bf16(acc) as the reference's GEMM writes it, then rotate-half on pairs
+              // of dimensions at once (packed FP32):
               //   a = x c - y s,  b = y c + x s   for x = q[d], y = q[d + 32]
 #pragma unroll
               for (int i = 0; i < 8; ++i) {
@@ -397,8 +364,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GemmCfg<BN, EPI>::TH
                   const uint64_t cc = k == 0 ? f2pack(rc[i].x, rc[i].y) : f2pack(rc[i].z, rc[i].w);
                   const uint64_t ss = k == 0 ? f2pack(rsn[i].x, rsn[i].y) : f2pack(rsn[i].z, rsn[i].w);
                   const uint64_t ns = k == 0 ? f2pack(-rsn[i].x, -rsn[i].y) : f2pack(-rsn[i].z, -rsn[i].w);
-                  const uint64_t x = f2pack(__uint_as_float(lo[j]), __uint_as_float(lo[j + 1]));
-                  const uint64_t y = f2pack(__uint_as_float(hi[j]), __uint_as_float(hi[j + 1]));
+                  float x0 = __uint_as_float(lo[j]), x1 = __uint_as_float(lo[j + 1]);
+                  float y0 = __uint_as_float(hi[j]), y1 = __uint_as_float(hi[j + 1]);
+                  bf16_round2(x0, x1);
+                  bf16_round2(y0, y1);
+                  const uint64_t x = f2pack(x0, x1), y = f2pack(y0, y1);
                   f2unpack(fma2(y, ns, mul2(x, cc)), a[j], a[j + 1]);
                   f2unpack(fma2(x, ss, mul2(y, cc)), b[j], b[j + 1]);
                 }
@@ -423,9 +393,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GemmCfg<BN, EPI>::TH
               tmem_ld32(tb + 128 + h * 64, rb);
               tmem_ld_wait();
 #pragma unroll
-              for (int j = 0; j < 32; j += 2)
-                geglu2(__uint_as_float(ra[j]), __uint_as_float(ra[j + 1]), __uint_as_float(rb[j]),
-                       __uint_as_float(rb[j + 1]), a[j], a[j + 1]);
+              for (int j = 0; j < 32; j += 2) {  // h = bf16(xn . Wi^T) as in the reference, then GEGLU
+                float h0 = __uint_as_float(ra[j]), h1 = __uint_as_float(ra[j + 1]);
+                float g0 = __uint_as_float(rb[j]), g1 = __uint_as_float(rb[j + 1]);
+                bf16_round2(h0, h1);
+                bf16_round2(g0, g1);
+                geglu2(h0, h1, g0, g1, a[j], a[j + 1]);
+              }
             }
             {
               uint32_t ra[32], rb[32];
@@ -433,73 +407,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GemmCfg<BN, EPI>::TH
               tmem_ld32(tb + 128 + h * 64 + 32, rb);
               tmem_ld_wait();
 #pragma unroll
-              for (int j = 0; j < 32; j += 2)
-                geglu2(__uint_as_float(ra[j]), __uint_as_float(ra[j + 1]), __uint_as_float(rb[j]),
-                       __uint_as_float(rb[j + 1]), b[j], b[j + 1]);
+              for (int j = 0; j < 32; j += 2) {
+                float h0 = __uint_as_float(ra[j]), h1 = __uint_as_float(ra[j + 1]);
+                float g0 = __uint_as_float(rb[j]), g1 = __uint_as_float(rb[j + 1]);
+                bf16_round2(h0, h1);
+                bf16_round2(g0, g1);
+                geglu2(h0, h1, g0, g1, b[j], b[j + 1]);
+              }
             }
             store_box(a, b, nu * 128 + h * 64, m0);
           }
-        } else if constexpr (RES) {
-#pragma unroll 1
-          for (int cc = 0; cc < BN / 32; ++cc) {
-            const int c = s * (BN / 32) + cc;  // chunk index within the row
-            const uint32_t b = gch % NXB;
-            uint32_t r[32];
-            tmem_ld32(tb + cc * 32, r);
-            tmem_ld_wait();
-            mbar_wait<true>(&xfull[b], (gch / NXB) & 1, abort_flag, p.err, 5);
-            // this row's 32 residual values, 128B-swizzled: 16-byte unit i sits at i ^ (row & 7)
-            uint8_t* xrow = sX + b * XCHUNK + trow * 128;
-            float v[32];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              float4* slot = reinterpret_cast<float4*>(xrow + ((static_cast<uint32_t>(i) ^ (trow & 7)) << 4));
-              float4 o = *slot;
-              const int col = c * 32 + 4 * i;
-              float4 bb = make_float4(0.f, 0.f, 0.f, 0.f);
-              if (p.bias) bb = *reinterpret_cast<const float4*>(p.bias + col);
-              o.x += __uint_as_float(r[4 * i + 0]) + bb.x;
-              o.y += __uint_as_float(r[4 * i + 1]) + bb.y;
-              o.z += __uint_as_float(r[4 * i + 2]) + bb.z;
-              o.w += __uint_as_float(r[4 * i + 3]) + bb.w;
-              *slot = o;
-              v[4 * i + 0] = o.x;
-              v[4 * i + 1] = o.y;
-              v[4 * i + 2] = o.z;
-              v[4 * i + 3] = o.w;
-            }
-            if constexpr (EPI == EPI_RESID_LN) {
-              // chunk mean / M2 (two-pass over registers), merged into the row's running state
-              float cs4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-              for (int j = 0; j < 32; ++j) cs4[j & 3] += v[j];
-              const float cm = ((cs4[0] + cs4[1]) + (cs4[2] + cs4[3])) * (1.f / 32.f);
-              float c24[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-              for (int j = 0; j < 32; ++j) c24[j & 3] += (v[j] - cm) * (v[j] - cm);
-              const float c2 = (c24[0] + c24[1]) + (c24[2] + c24[3]);
-              const float n_new = w_n + 32.f;
-              const float delta = cm - w_mean;
-              w_mean += delta * (32.f / n_new);
-              w_m2 += c2 + delta * delta * (w_n * 32.f / n_new);
-              w_n = n_new;
-            }
-            fence_proxy_async_smem();
-            named_bar_sync(1, 128);
-            if (storer && !*abort_flag) {
-              // the LayerNorm warps re-read the updated rows one unit later: ask L2 to keep them
-              if constexpr (EPI == EPI_RESID_LN)
-                tma_store_2d_hint(&tmX, sX + b * XCHUNK, c * 32, m0, l2_policy_evict_last());
-              else
-                tma_store_2d(&tmX, sX + b * XCHUNK, c * 32, m0);
-              bulk_commit();
-              bulk_wait_read_1();  // the previous chunk's store has read its slot: hand it back
-              if (xpend >= 0) mbar_arrive(&xempty[xpend]);
-              xpend = static_cast<int>(b);
-            }
-            ++gch;
-          }
-        } else if constexpr (EPI == EPI_SCORER) {
+                } else if constexpr (EPI == EPI_SCORER) {
 #pragma unroll 1
           for (int c = 0; c < BN / 32; ++c) {
             uint32_t r[32];
@@ -517,117 +435,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GemmCfg<BN, EPI>::TH
         if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&tempty[buf]), 0));
         ++acc;
       }
-      if constexpr (RES) {
-        // the updated rows must be in global memory before they are re-read (LayerNorm
-        // warps) or read by the next kernel
-        if (storer) {
-          bulk_wait_all();
-          fence_proxy_async_global();
-          if (xpend >= 0) mbar_arrive(&xempty[xpend]);
-          xpend = -1;
-        }
-      }
-      if constexpr (EPI == EPI_RESID_LN) {
-        // hand this unit's row statistics to the LayerNorm warps (slot = unit parity)
-        const int slot = nunit & 1;
-        if (nunit >= 2) mbar_wait<true>(&lnempty[slot], ((nunit - 2) >> 1) & 1, abort_flag, p.err, 7);
-        stats[slot * BM + trow] = make_float2(w_mean, rsqrtf(w_m2 * (1.f / static_cast<float>(H)) + p.ln_eps));
-        named_bar_sync(1, 128);  // every row's statistics written; the unit's x stores complete
-        if (storer) mbar_arrive(&lnfull[slot]);
-      } else if constexpr (RES) {
-        named_bar_sync(1, 128);
-      } else if constexpr (EPI == EPI_SCORER) {
+      if constexpr (EPI == EPI_SCORER) {
         if (valid) p.scores[row] = score + p.b2;
       }
-      ++nunit;
     }
     if (storer) bulk_wait_all();  // no store of ours may still read smem at exit
-  } else if (warp == 6) {
-    // ------------------------------------------------------------ residual producer (RESID*)
-    if constexpr (RES) {
-      if (lane == 0) {
-        uint32_t gx = 0;                    // chunks issued so far (ring slot = gx % NXB)
-        uint32_t armed = 0, armed_par = 0;  // per slot: armed bit and the parity it was armed with
-        bool ok = true;
-        for (int u = pair; u < units && ok; u += npairs) {
-          const int m0 = (u / n_per_m) * 2 * BM + static_cast<int>(rank) * BM;
-          for (int c = 0; c < NCH; ++c, ++gx) {
-            const uint32_t b = gx % NXB, ph = (gx / NXB) & 1;
-            if (!mbar_wait<true>(&xempty[b], ph ^ 1, abort_flag, p.err, 6)) {
-              ok = false;
-              break;
-            }
-            mbar_arrive_expect_tx(&xfull[b], XCHUNK);
-            tma_load_2d(&tmX, &xfull[b], sX + b * XCHUNK, c * 32, m0);
-            armed |= 1u << b;
-            armed_par = (armed_par & ~(1u << b)) | (ph << b);
-          }
-        }
-        if (!ok) {  // unwinding: every load already issued must land before smem is released
-          volatile int no_abort = 0;
-          for (uint32_t b = 0; b < NXB; ++b)
-            if (armed & (1u << b)) mbar_wait<true>(&xfull[b], (armed_par >> b) & 1u, &no_abort, nullptr, 0);
-        }
-      }
-    }
-  } else if (warp >= 7) {
-    // ------------------------------------------------------------ LayerNorm warps (RESID_LN)
-    // Warp 7 + k normalises rows 32k .. 32k+31 of each unit once warps 2..5 have stored
-    // the unit's updated x and its row statistics: coalesced loads of x (lane = 4
-    // consecutive columns per 128-column slice), RB rows in flight, BF16 xn out.
-    if constexpr (EPI == EPI_RESID_LN) {
-      const int k = warp - 7;
-      constexpr int NV = H / 128;
-      constexpr int RB = (NV <= 3) ? 8 : (NV <= 6 ? 4 : 2);
-      float4 gw[NV], gb[NV];
-#pragma unroll
-      for (int v = 0; v < NV; ++v) {
-        gw[v] = reinterpret_cast<const float4*>(p.ln_w)[v * 32 + lane];
-        gb[v] = p.ln_b ? reinterpret_cast<const float4*>(p.ln_b)[v * 32 + lane] : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-      const uint64_t pol_first = l2_policy_evict_first();  // last read of these rows here
-      int nunit = 0;
-      for (int u = pair; u < units; u += npairs, ++nunit) {
-        const int m0 = (u / n_per_m) * 2 * BM + static_cast<int>(rank) * BM;
-        const int slot = nunit & 1;
-        if (!__all_sync(0xffffffffu, mbar_wait<true>(&lnfull[slot], (nunit >> 1) & 1, abort_flag, p.err, 8))) break;
-        fence_proxy_async_global();
-        const float2 my = stats[slot * BM + k * 32 + lane];  // (mean, rstd) of row 32k + lane
-        const int wrow0 = m0 + k * 32;
-#pragma unroll 1
-        for (int rr = 0; rr < 32; rr += RB) {
-          float4 xv[RB][NV];
-#pragma unroll
-          for (int i = 0; i < RB; ++i) {
-            const int rw = wrow0 + rr + i;
-            if (rw < p.M) {
-              const float4* src = reinterpret_cast<const float4*>(p.x + static_cast<size_t>(rw) * p.ldx);
-#pragma unroll
-              for (int v = 0; v < NV; ++v) xv[i][v] = ld_cg_hint(src + v * 32 + lane, pol_first);
-            }
-          }
-#pragma unroll
-          for (int i = 0; i < RB; ++i) {
-            const int rw = wrow0 + rr + i;
-            const float mu = __shfl_sync(0xffffffffu, my.x, rr + i);
-            const float rs = __shfl_sync(0xffffffffu, my.y, rr + i);
-            if (rw < p.M) {
-              uint2* dst = reinterpret_cast<uint2*>(p.xn + static_cast<size_t>(rw) * p.ldxn);
-#pragma unroll
-              for (int v = 0; v < NV; ++v) {
-                const float4 a = xv[i][v], g = gw[v], bb = gb[v];
-                uint2 o;
-                o.x = pack_bf16x2((a.x - mu) * rs * g.x + bb.x, (a.y - mu) * rs * g.y + bb.y);
-                o.y = pack_bf16x2((a.z - mu) * rs * g.z + bb.z, (a.w - mu) * rs * g.w + bb.w);
-                dst[v * 32 + lane] = o;
-              }
-            }
-          }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&lnempty[slot]);
-      }
-    }
   }
 
   tc_fence_before();
@@ -669,22 +481,14 @@ int launch_full_row(int H, const CUtensorMap& tmA, const CUtensorMap& tmW, const
 
 int gemm_bn_for(int n) { return (n % 256 == 0) ? 256 : 128; }
 
-// J1_RESID_KERNEL=pair selects the earlier CTA-pair residual kernel (A/B measurements).
-bool resid_cluster_kernel() {
-  static const bool on = [] {
-    const char* v = std::getenv("J1_RESID_KERNEL");
-    return !(v && std::strcmp(v, "pair") == 0);
-  }();
-  return on;
-}
-
 const char* gemm_shape_error(GemmEpi epi, int bn, int M, int N, int K) {
   if (M < 0 || N <= 0 || K <= 0) return "GEMM dimensions must be positive";
   if (bn != 128 && bn != 256) return "GEMM tile width must be 128 or 256";
   if (K % BK != 0) return "GEMM K must be a multiple of 64";
   if (N % bn != 0) return "GEMM N must be a multiple of the tile width";
   if (epi == EPI_GEGLU && bn != 256) return "GEGLU epilogue needs 256-wide tiles";
-  if (is_full_row(epi) && !(N == 256 || N == 384 || N == 512 || N == 768 || N == 1024))
+  const bool full_row = epi == EPI_RESID_LN || epi == EPI_RESID || epi == EPI_SCORER;
+  if (full_row && !(N == 256 || N == 384 || N == 512 || N == 768 || N == 1024))
     return "full-row epilogues support N in {256, 384, 512, 768, 1024}";
   return nullptr;
 }
@@ -694,7 +498,7 @@ int launch_gemm(GemmEpi epi, int bn, const CUtensorMap& tmA, const CUtensorMap& 
                 const CUtensorMap* tmXN) {
   if (p.M == 0) return 0;
   if (!tmX && epi != EPI_SCORER) return static_cast<int>(cudaErrorInvalidValue);
-  if ((epi == EPI_RESID_LN || epi == EPI_RESID) && resid_cluster_kernel())
+  if (epi == EPI_RESID_LN || epi == EPI_RESID)
     return launch_resid_gemm(epi == EPI_RESID_LN, tmA, tmW, *tmX, tmXs, tmXN, p, grid_limit, stream);
   const CUtensorMap& X = tmX ? *tmX : tmA;  // unused by the scorer epilogue
   switch (epi) {
@@ -706,12 +510,10 @@ int launch_gemm(GemmEpi epi, int bn, const CUtensorMap& tmA, const CUtensorMap& 
                        : launch_one<128, EPI_QKV_ROPE, 1>(tmA, tmW, X, p, grid_limit, stream);
     case EPI_GEGLU:
       return launch_one<256, EPI_GEGLU, 1>(tmA, tmW, X, p, grid_limit, stream);
-    case EPI_RESID_LN:
-      return launch_full_row<EPI_RESID_LN>(p.N, tmA, tmW, X, p, grid_limit, stream);
-    case EPI_RESID:
-      return launch_full_row<EPI_RESID>(p.N, tmA, tmW, X, p, grid_limit, stream);
     case EPI_SCORER:
       return launch_full_row<EPI_SCORER>(p.N, tmA, tmW, X, p, grid_limit, stream);
+    default:
+      break;
   }
   return static_cast<int>(cudaErrorInvalidValue);
 }

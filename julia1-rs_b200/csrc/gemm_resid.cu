@@ -86,13 +86,6 @@ __device__ __forceinline__ void st_async_f2(uint32_t caddr, float a, float b, ui
                : "memory");
 }
 
-// Rounds two FP32 values to BF16 (round to nearest even) and back.
-__device__ __forceinline__ void bf16_round2(float& a, float& b) {
-  const uint32_t u = pack_bf16x2(a, b);
-  a = __uint_as_float(u << 16);
-  b = __uint_as_float(u & 0xffff0000u);
-}
-
 template <int NG, int BN, bool LN>
 __global__ void __launch_bounds__(256, 1)
     resid_ln_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,

@@ -64,8 +64,8 @@ inline cudaError_t set_smem_once(Kernel kern, int bytes, std::atomic<unsigned lo
 // pair loads half of the tile's W rows; see gemm_w_box_rows).
 enum GemmEpi : int {
   EPI_BF16 = 0,      // out = bf16(acc (+bias)) (relu when `relu`)
-  EPI_QKV_ROPE = 1,  // out = bf16(rope(acc)) on columns < rope_cols, bf16(acc) elsewhere
-  EPI_GEGLU = 2,     // W rows interleaved per 128: out[:, n/2 + j] = bf16(gelu(acc_a) * acc_b)
+  EPI_QKV_ROPE = 1,  // out = bf16(rope(bf16(acc))) on columns < rope_cols, bf16(acc) elsewhere
+  EPI_GEGLU = 2,     // W rows interleaved per 128: out[:, n/2 + j] = bf16(gelu(bf16(acc_a)) * bf16(acc_b))
   EPI_RESID_LN = 3,  // full row: x += bf16(acc) (+bias); xn = bf16(LN(x; ln_w, ln_b, eps))
   EPI_RESID = 4,     // full row: x += bf16(acc) (+bias)
   EPI_SCORER = 5,    // full row: scores[r] = sum_j gelu(acc + bias[j]) * w2[j] + b2
@@ -96,14 +96,13 @@ struct EpiParams {
 
 // Column width of one MMA tile for an N (or full-row width): 256 when N % 256 == 0, else 128.
 int gemm_bn_for(int n);
-// Whether EPI_RESID_LN / EPI_RESID run on the row-split cluster kernel (default).
-bool resid_cluster_kernel();
 // Rows of one W box for tile width bn (the two CTAs of a pair each load half of the tile).
 inline uint32_t gemm_w_box_rows(int bn) { return static_cast<uint32_t>(bn / 2); }
 // Returns 0 on success, or a cudaError_t value. tmX: the map of the epilogue's global tensor:
-// the FP32 residual map (make_tmap_f32_resid) over p.x for EPI_RESID_LN / EPI_RESID; the
-// BF16 output map over p.out (make_tmap_bf16, box 64 x 128, N columns -- N/2 for GEGLU --
-// and row stride p.ldo) for EPI_BF16 / EPI_QKV_ROPE / EPI_GEGLU; ignored by EPI_SCORER.
+// the FP32 residual map (make_tmap_f32_resid, 32 x 128 boxes) over p.x for EPI_RESID_LN /
+// EPI_RESID; the BF16 output map over p.out (make_tmap_bf16, box 64 x 128, N columns -- N/2
+// for GEGLU -- and row stride p.ldo) for EPI_BF16 / EPI_QKV_ROPE / EPI_GEGLU; ignored by
+// EPI_SCORER.
 // For EPI_RESID_LN / EPI_RESID also: tmXs, the FP32 residual map over p.x with 32-row boxes
 // (make_tmap_f32_resid(..., 32)) through which each epilogue warp stores its rows; and for
 // EPI_RESID_LN tmXN, the BF16 map over p.xn with 64 x 32 boxes (make_tmap_bf16, N columns,

@@ -404,7 +404,6 @@ j1_status stage_batch(j1_model* model, const BatchView& b, int slot = 0, bool sy
             make_tmap_bf16(&model->tm_ymb, model->ymb, m, H, H, 128, &why) &&
             make_tmap_bf16(&model->tm_hm, model->hm, m, FF, FF, 128, &why) &&
             make_tmap_bf16(&model->tm_qm, model->qm, m, H, H, 128, &why) &&
-            make_tmap_bf16(&model->tm_qkv_kv, model->qkv + H, t, 2 * H, 3 * H, 128, &why) &&
             make_tmap_bf16(&model->tm_ctx_o, model->ctx, t, H, H, 32, &why) &&
             make_tmap_bf16(&model->tm_kv, model->qkv, t, 3 * H, 3 * H, attention_kv_box_rows(), &why) &&
             make_tmap_bf16(&model->tm_cm_o, model->cm, m, H, H, 32, &why) &&
@@ -413,7 +412,8 @@ j1_status stage_batch(j1_model* model, const BatchView& b, int slot = 0, bool sy
             make_tmap_f32_resid(&model->tm_x_st, model->x, t, H, H, &why, 32) &&
             make_tmap_f32_resid(&model->tm_ym_st, model->ym, m, H, H, &why, 32) &&
             make_tmap_bf16(&model->tm_xn_st, model->xn, t, H, H, 32, &why) &&
-            make_tmap_bf16(&model->tm_ymb_st, model->ymb, m, H, H, 32, &why);
+            make_tmap_bf16(&model->tm_ymb_st, model->ymb, m, H, H, 32, &why) &&
+            make_tmap_bf16(&model->tm_qkv_kv, model->qkv + H, t, 2 * H, 3 * H, 128, &why);
   if (!ok) return set_error(J1_ERR_CUDA, std::string("activation tensor map: ") + (why ? why : ""));
   model->staged = true;
   return J1_OK;

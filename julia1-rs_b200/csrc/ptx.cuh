@@ -366,6 +366,12 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
 }
+// Rounds two FP32 values to BF16 (round to nearest even) and back, with one conversion.
+__device__ __forceinline__ void bf16_round2(float& a, float& b) {
+  const uint32_t u = pack_bf16x2(a, b);
+  a = __uint_as_float(u << 16);
+  b = __uint_as_float(u & 0xffff0000u);
+}
 // True when an earlier CTA of this forward already gave up; new CTAs then exit at once.
 __device__ __forceinline__ bool device_aborted(const int* err) {
   return err && *reinterpret_cast<const volatile int*>(err) != 0;

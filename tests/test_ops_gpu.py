@@ -74,6 +74,40 @@ def test_gemm_bias_relu(torch_cuda, relu):
     _close_bf16(out, ref.to(torch.bfloat16).float())
 
 
+def _close_bf16_flips(out, ref, scale, frac=2e-3):
+    """_close_bf16, except that an input rounded to BF16 before the fused math (as the
+    reference rounds its GEMM outputs) may round the other way when fp32 summation order
+    moves it across a rounding boundary: such elements (at most `frac`) may differ by up to
+    2^-6 of `scale`, the magnitude of the inputs they were computed from."""
+    diff = (out.float() - ref.float()).abs()
+    bad = diff > 2e-3 + 1.6e-2 * ref.float().abs()
+    assert (diff[bad] <= 2.0 ** -6 * scale[bad] + 2e-3).all(), diff.max().item()
+    assert bad.float().mean().item() <= frac, bad.float().mean().item()
+
+
+def _qkv_ref(torch, acc, cos, sin, pos, H):
+    """EPI_QKV_ROPE restated: qkv = bf16(acc) (the reference's GEMM output), q and k rotated
+    in fp32 (rotate-half on d, d + 32 within each head) and rounded again. Returns (ref, scale)."""
+    M = acc.shape[0]
+    r = acc.to(torch.bfloat16).float()
+    c, s_ = cos[pos.long()], sin[pos.long()]
+    qk = r[:, :2 * H].reshape(M, 2 * H // 64, 64)
+    lo, hi = qk[..., :32], qk[..., 32:]
+    rot = torch.cat([lo * c[:, None] - hi * s_[:, None], hi * c[:, None] + lo * s_[:, None]], dim=-1)
+    ref = torch.cat([rot.reshape(M, 2 * H), r[:, 2 * H:]], dim=1).to(torch.bfloat16).float()
+    mag = torch.maximum(lo.abs(), hi.abs())
+    scale = torch.cat([torch.cat([mag, mag], dim=-1).reshape(M, 2 * H), r[:, 2 * H:].abs()], dim=1)
+    return ref, scale
+
+
+def _geglu_ref(torch, acc, I):
+    """EPI_GEGLU restated: h = bf16(acc) (the reference's GEMM output), g = gelu(h_a) * h_b."""
+    h = acc.to(torch.bfloat16).float()
+    ref = (torch.nn.functional.gelu(h[:, :I]) * h[:, I:]).to(torch.bfloat16).float()
+    scale = (h[:, :I].abs() + 1.0) * h[:, I:].abs()
+    return ref, scale
+
+
 def _rope_tables(torch, theta, positions):
     # rope_table (src/config.rs:99-112): f32 inv_freq, f32 products
     inv = 1.0 / np.power(np.float32(theta), (np.arange(32, dtype=np.float32) * 2) / np.float32(64)).astype(np.float32)
@@ -93,12 +127,8 @@ def test_gemm_qkv_rope(torch_cuda, H, theta):
     out = torch.empty((M, 3 * H), device="cuda", dtype=torch.bfloat16)
     j1.op_gemm(j1.EPI_QKV_ROPE, A, W, out=out, pos=pos, rope_cos=cos, rope_sin=sin, rope_cols=2 * H)
     acc = A.float() @ W.float().t()
-    c, s = cos[pos.long()], sin[pos.long()]
-    qk = acc[:, :2 * H].reshape(M, 2 * H // 64, 64)
-    lo, hi = qk[..., :32], qk[..., 32:]
-    rot = torch.cat([lo * c[:, None] - hi * s[:, None], hi * c[:, None] + lo * s[:, None]], dim=-1)
-    ref = torch.cat([rot.reshape(M, 2 * H), acc[:, 2 * H:]], dim=1)
-    _close_bf16(out, ref.to(torch.bfloat16).float())
+    ref, scale = _qkv_ref(torch, acc, cos, sin, pos, H)
+    _close_bf16_flips(out, ref, scale)
 
 
 @pytest.mark.parametrize("M,I,K", [(500, 1152, 768), (64, 1152, 384), (4096, 1152, 768)])
@@ -111,8 +141,8 @@ def test_gemm_geglu(torch_cuda, M, I, K):
     out = torch.empty((M, I), device="cuda", dtype=torch.bfloat16)
     j1.op_gemm(j1.EPI_GEGLU, A, Wi, out=out)
     acc = A.float() @ Wf.t()
-    ref = torch.nn.functional.gelu(acc[:, :I]) * acc[:, I:]
-    _close_bf16(out, ref.to(torch.bfloat16).float(), atol=3e-3)
+    ref, scale = _geglu_ref(torch, acc, I)
+    _close_bf16_flips(out, ref, scale)
 
 
 @pytest.mark.parametrize("M,H,K,bias,ln_bias", [(300, 768, 768, False, False), (1000, 768, 1152, True, True),
@@ -148,12 +178,9 @@ def test_c2_gemm_sweep_full_size(torch_cuda, M):
     out = torch.empty((M, 3 * H), device="cuda", dtype=torch.bfloat16)
     j1.op_gemm(j1.EPI_QKV_ROPE, A, W, out=out, pos=pos, rope_cos=cos, rope_sin=sin, rope_cols=2 * H)
     acc = A.float() @ W.float().t()
-    c, s_ = cos[pos.long()], sin[pos.long()]
-    qk = acc[:, :2 * H].reshape(M, 2 * H // 64, 64)
-    lo, hi = qk[..., :32], qk[..., 32:]
-    rot = torch.cat([lo * c[:, None] - hi * s_[:, None], hi * c[:, None] + lo * s_[:, None]], dim=-1)
-    _close_bf16(out, torch.cat([rot.reshape(M, 2 * H), acc[:, 2 * H:]], dim=1).to(torch.bfloat16).float())
-    del out, acc, qk, lo, hi, rot
+    ref, scale = _qkv_ref(torch, acc, cos, sin, pos, H)
+    _close_bf16_flips(out, ref, scale)
+    del out, acc, ref, scale
     # Wi 768 -> 2304 + GEGLU -> 1152
     Wf = _rand(torch, (2 * I, H), 0.02, 42, torch.bfloat16).float()
     Wi = torch.empty((2 * I, H), device="cuda", dtype=torch.bfloat16)
@@ -161,8 +188,9 @@ def test_c2_gemm_sweep_full_size(torch_cuda, M):
     g = torch.empty((M, I), device="cuda", dtype=torch.bfloat16)
     j1.op_gemm(j1.EPI_GEGLU, A, Wi, out=g)
     acc = A.float() @ Wf.t()
-    _close_bf16(g, (torch.nn.functional.gelu(acc[:, :I]) * acc[:, I:]).to(torch.bfloat16).float(), atol=3e-3)
-    del acc
+    ref, scale = _geglu_ref(torch, acc, I)
+    _close_bf16_flips(g, ref, scale)
+    del acc, ref, scale
     # Wo 768 -> 768 and Wo2 1152 -> 768, each + FP32 residual + LayerNorm
     lw = 1.0 + _rand(torch, (H,), 0.1, 43, torch.float32)
     for K, src, seed in [(H, A, 44), (I, g, 46)]:
