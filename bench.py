@@ -549,7 +549,9 @@ def main():
             pool = {"value": round(JOB_ROWS * SEQ * args.steps / (p1 - p0), 1), "unit": "tokens/s",
                     "devices": world, "api": "j1_engine_create_pool + j1_engine_logits_encoded (one process)",
                     "same_logits_as_e2e": bool(np.array_equal(pl, logits))}
-        barrier()
+        # the other ranks wait on the host (gloo): an NCCL barrier would keep a kernel
+        # spinning on their GPUs, which the pool is using
+        dist.barrier(group=gloo)
 
     if rank == 0:
         hbm, tf_burst, tf_sust, kind = peaks()
