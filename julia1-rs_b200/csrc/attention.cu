@@ -57,59 +57,6 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// Every J1_ATTN_POLY-th pair of exponentials of a block with no masked key is evaluated on
-// the FMA pipe (exp2_poly2) instead of the MUFU, which the rest keep busy (0: none).
-#ifndef J1_ATTN_POLY
-#define J1_ATTN_POLY 0
-#endif
-
-// 2^x for two arguments on the FMA pipe (packed FP32), for x in [-125, 10]; smaller x give
-// 2^-125. Cody-Waite reduction: x = j + f with j = rint(x) (the 1.5 * 2^23 shifter, whose
-// low mantissa bits then hold j) and f = x - j in [-0.5, 0.5] exactly; 2^f by a degree-5
-// polynomial fitted here for minimal relative error on [-0.5, 0.5] (Remez exchange), Horner
-// with fused multiply-adds; 2^j is added to the exponent field (j << 23). Relative error
-// below 2^-22 over the range (the order of ex2.approx.f32), checked on the CPU by
-// tests/test_exp2_poly.py against exact powers of two.
-__device__ __forceinline__ void exp2_poly2(float x0, float x1, float& y0, float& y1) {
-  const uint64_t x = f2pack(fmaxf(x0, -125.f), fmaxf(x1, -125.f));
-  const uint64_t t = add2(x, f2pack(12582912.f, 12582912.f));
-  const uint64_t j = add2(t, f2pack(-12582912.f, -12582912.f));
-  const uint64_t f = fma2(j, f2pack(-1.f, -1.f), x);
-  uint64_t p = fma2(f2pack(1.3276472e-3f, 1.3276472e-3f), f, f2pack(9.6755410e-3f, 9.6755410e-3f));
-  p = fma2(p, f, f2pack(5.5507131e-2f, 5.5507131e-2f));
-  p = fma2(p, f, f2pack(2.4022120e-1f, 2.4022120e-1f));
-  p = fma2(p, f, f2pack(6.9314694e-1f, 6.9314694e-1f));
-  p = fma2(p, f, f2pack(1.0000001f, 1.0000001f));
-  float t0, t1, p0, p1;
-  f2unpack(t, t0, t1);
-  f2unpack(p, p0, p1);
-  y0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(t0) << 23));
-  y1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
-}
-
-// The block's 64 exponentials of one row, by pairs: p = 2^(s * scale - offset) (one packed
-// FMA for both exponents), the packed partial sums, and P as BF16 pairs. POLY > 0: every
-// POLY-th pair on the FMA pipe.
-template <int POLY>
-__device__ __forceinline__ void block_exps(const uint32_t (&sa)[32], const uint32_t (&sb)[32], uint64_t sc2,
-                                           uint64_t nu2, uint32_t (&pk)[32], uint64_t (&lp2)[4]) {
-#pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    const uint32_t s0 = i < 16 ? sa[2 * i] : sb[2 * i - 32];
-    const uint32_t s1 = i < 16 ? sa[2 * i + 1] : sb[2 * i - 31];
-    float a0, a1, p0, p1;
-    f2unpack(fma2(f2pack(__uint_as_float(s0), __uint_as_float(s1)), sc2, nu2), a0, a1);
-    if (POLY > 0 && i % (POLY > 0 ? POLY : 1) == (POLY > 0 ? POLY : 1) - 1) {
-      exp2_poly2(a0, a1, p0, p1);
-    } else {
-      p0 = ex2(a0);
-      p1 = ex2(a1);
-    }
-    lp2[i & 3] = add2(lp2[i & 3], f2pack(p0, p1));
-    pk[i] = pack_bf16x2(p0, p1);
-  }
-}
-
 // A bounded wait whose outcome is the same in every lane of the warp: the softmax warps
 // follow it with warp-collective tcgen05.ld/st, which all 32 lanes must reach together.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err,
@@ -477,10 +424,16 @@ __global__ void __launch_bounds__(192, 2)
         // pairs of keys: one packed FMA for both exponents, one packed add into the sums
         const uint64_t sc2 = f2pack(scale_log2, scale_log2), nu2 = f2pack(-uu, -uu);
         uint64_t lp2[4] = {0ull, 0ull, 0ull, 0ull};
-        if (full)  // no key of the block is masked for this warp's rows
-          block_exps<J1_ATTN_POLY>(sa, sb, sc2, nu2, pk, lp2);
-        else
-          block_exps<0>(sa, sb, sc2, nu2, pk, lp2);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const uint32_t s0 = i < 16 ? sa[2 * i] : sb[2 * i - 32];
+          const uint32_t s1 = i < 16 ? sa[2 * i + 1] : sb[2 * i - 31];
+          float a0, a1;
+          f2unpack(fma2(f2pack(__uint_as_float(s0), __uint_as_float(s1)), sc2, nu2), a0, a1);
+          const float p0 = ex2(a0), p1 = ex2(a1);
+          lp2[i & 3] = add2(lp2[i & 3], f2pack(p0, p1));
+          pk[i] = pack_bf16x2(p0, p1);
+        }
         float lq[8];
 #pragma unroll
         for (int k = 0; k < 4; ++k) f2unpack(lp2[k], lq[2 * k], lq[2 * k + 1]);
