@@ -94,7 +94,6 @@ __global__ void __launch_bounds__(256, 1)
   using C = RlnCfg<NG, BN>;
   constexpr int CS = C::CS;
   constexpr int NCH = BN / 32;   // residual chunks per unit
-  constexpr int NBOX = BN / 64;  // xn boxes per unit
   constexpr int H = NG * BN;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -306,54 +305,65 @@ __global__ void __launch_bounds__(256, 1)
       const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
       float w_mean = 0.f, w_m2 = 0.f, w_n = 0.f;
       // ---------------- pass 1: residual update
-#pragma unroll 1
-      for (int c = 0; c < NCH; ++c, ++gch) {
+      // One warp per SM sub-partition runs this loop, so latency is what it costs: the next
+      // chunk's accumulator columns are loaded from TMEM while this chunk is processed, and
+      // the chunk's eight 16-byte slots are all read before any is written back (written in
+      // place through a data-dependent swizzle, they could not be reordered otherwise).
+      auto pass1_chunk = [&](int c, uint32_t (&r)[32], uint32_t (&rn)[32]) {
         const uint32_t b = gch % C::NX;
-        uint32_t r[32];
-        tmem_ld32(tb + c * 32, r);
-        tmem_ld_wait();
+        tmem_ld_wait();  // chunk c's accumulator is in r
+        if (c + 1 < NCH) tmem_ld32(tb + (c + 1) * 32, rn);
         mbar_wait<true>(&xfull[b], (gch / C::NX) & 1, abort_flag, p.err, 36);
         uint8_t* xrow = sX + b * RX_CHUNK + trow * 128;  // 16-byte unit i at (i ^ (row & 7)) * 16
+        float4 o[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          o[i] = *reinterpret_cast<const float4*>(xrow + ((static_cast<uint32_t>(i) ^ (trow & 7)) << 4));
         float v[32];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          float4* slot = reinterpret_cast<float4*>(xrow + ((static_cast<uint32_t>(i) ^ (trow & 7)) << 4));
-          float4 o = *slot;
           float d0 = __uint_as_float(r[4 * i + 0]), d1 = __uint_as_float(r[4 * i + 1]);
           float d2 = __uint_as_float(r[4 * i + 2]), d3 = __uint_as_float(r[4 * i + 3]);
           bf16_round2(d0, d1);  // delta = bf16(A . W^T), as the reference's GEMM output
           bf16_round2(d2, d3);
-          o.x += d0;
-          o.y += d1;
-          o.z += d2;
-          o.w += d3;
-          if (p.bias) {
+          uint64_t lo = add2(f2pack(o[i].x, o[i].y), f2pack(d0, d1));
+          uint64_t hi = add2(f2pack(o[i].z, o[i].w), f2pack(d2, d3));
+          if (p.bias) {  // the bias after the delta
             const float4 bb = parc[c * 8 + i];
-            o.x += bb.x;
-            o.y += bb.y;
-            o.z += bb.z;
-            o.w += bb.w;
+            lo = add2(lo, f2pack(bb.x, bb.y));
+            hi = add2(hi, f2pack(bb.z, bb.w));
           }
-          *slot = o;
-          v[4 * i + 0] = o.x;
-          v[4 * i + 1] = o.y;
-          v[4 * i + 2] = o.z;
-          v[4 * i + 3] = o.w;
+          f2unpack(lo, v[4 * i + 0], v[4 * i + 1]);
+          f2unpack(hi, v[4 * i + 2], v[4 * i + 3]);
         }
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          *reinterpret_cast<float4*>(xrow + ((static_cast<uint32_t>(i) ^ (trow & 7)) << 4)) =
+              make_float4(v[4 * i + 0], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
         if constexpr (LN) {
           uint32_t vv[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) vv[j] = __float_as_uint(v[j]);
           tmem_st32(tb + c * 32, vv);  // the updated row stays on chip for pass 2
-          // chunk mean / M2 (two-pass over registers), merged into the row's running state
-          float cs4[4] = {0.f, 0.f, 0.f, 0.f};
+          // chunk mean / M2 (two passes over registers, pairs of columns at once), merged
+          // into the row's running state
+          uint64_t s2[2] = {0ull, 0ull};
 #pragma unroll
-          for (int j = 0; j < 32; ++j) cs4[j & 3] += v[j];
-          const float cm = ((cs4[0] + cs4[1]) + (cs4[2] + cs4[3])) * (1.f / 32.f);
-          float c24[4] = {0.f, 0.f, 0.f, 0.f};
+          for (int j = 0; j < 32; j += 2) s2[(j >> 1) & 1] = add2(s2[(j >> 1) & 1], f2pack(v[j], v[j + 1]));
+          float sa, sb, sc, sd;
+          f2unpack(s2[0], sa, sb);
+          f2unpack(s2[1], sc, sd);
+          const float cm = ((sa + sb) + (sc + sd)) * (1.f / 32.f);
+          const uint64_t ncm = f2pack(-cm, -cm);
+          uint64_t q2[2] = {0ull, 0ull};
 #pragma unroll
-          for (int j = 0; j < 32; ++j) c24[j & 3] += (v[j] - cm) * (v[j] - cm);
-          const float c2 = (c24[0] + c24[1]) + (c24[2] + c24[3]);
+          for (int j = 0; j < 32; j += 2) {
+            const uint64_t dv = add2(f2pack(v[j], v[j + 1]), ncm);
+            q2[(j >> 1) & 1] = fma2(dv, dv, q2[(j >> 1) & 1]);
+          }
+          f2unpack(q2[0], sa, sb);
+          f2unpack(q2[1], sc, sd);
+          const float c2 = (sa + sb) + (sc + sd);
           const float n_new = w_n + 32.f;
           const float delta = cm - w_mean;
           w_mean += delta * (32.f / n_new);
@@ -372,6 +382,17 @@ __global__ void __launch_bounds__(256, 1)
           xpend = static_cast<int>(b);
         }
         __syncwarp();
+        ++gch;
+      };
+      {
+        uint32_t ra[32], rb[32];
+        tmem_ld32(tb, ra);
+        static_assert(NCH % 2 == 0, "chunks are processed in pairs");
+#pragma unroll 1
+        for (int c = 0; c < NCH; c += 2) {
+          pass1_chunk(c, ra, rb);
+          pass1_chunk(c + 1, rb, ra);
+        }
       }
       if (lane == 0) {  // the unit's last chunk: release its slot once the store has read it
         bulk_wait_read_all();
@@ -413,46 +434,55 @@ __global__ void __launch_bounds__(256, 1)
         }
         const float rstd = rsqrtf(m2 * (1.f / static_cast<float>(H)) + p.ln_eps);
         // ---------------- pass 2: normalise from TMEM, BF16 boxes of this warp's rows out by TMA
-#pragma unroll 1
-        for (int bx = 0; bx < NBOX; ++bx) {
+        // (two chunks per 64-column box; the next chunk's TMEM load overlaps this one)
+        const uint64_t nmean = f2pack(-mean, -mean), rs2 = f2pack(rstd, rstd);
+        auto pass2_chunk = [&](int c, uint32_t (&r)[32], uint32_t (&rn)[32]) {
+          const int h = c & 1;
           uint8_t* box = sO + (q * 2 + ob) * RO_WBOX;
           uint8_t* srow = box + lane * 128;
+          tmem_ld_wait();  // chunk c's updated row is in r
+          if (c + 1 < NCH) tmem_ld32(tb + (c + 1) * 32, rn);
+          float y[32];
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int c = 2 * bx + h;
-            uint32_t r[32];
-            tmem_ld32(tb + c * 32, r);
-            tmem_ld_wait();
-            float y[32];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const float4 g = parw[c * 8 + i], be = parb[c * 8 + i];
-              y[4 * i + 0] = (__uint_as_float(r[4 * i + 0]) - mean) * rstd * g.x + be.x;
-              y[4 * i + 1] = (__uint_as_float(r[4 * i + 1]) - mean) * rstd * g.y + be.y;
-              y[4 * i + 2] = (__uint_as_float(r[4 * i + 2]) - mean) * rstd * g.z + be.z;
-              y[4 * i + 3] = (__uint_as_float(r[4 * i + 3]) - mean) * rstd * g.w + be.w;
-            }
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              uint4 w;
-              w.x = pack_bf16x2(y[8 * i + 0], y[8 * i + 1]);
-              w.y = pack_bf16x2(y[8 * i + 2], y[8 * i + 3]);
-              w.z = pack_bf16x2(y[8 * i + 4], y[8 * i + 5]);
-              w.w = pack_bf16x2(y[8 * i + 6], y[8 * i + 7]);
-              *reinterpret_cast<uint4*>(srow + ((static_cast<uint32_t>(4 * h + i) ^ (lane & 7)) << 4)) = w;
-            }
+          for (int i = 0; i < 8; ++i) {
+            const float4 g = parw[c * 8 + i], be = parb[c * 8 + i];
+            // y = ((x - mean) * rstd) * g + be, pairs of columns at once
+            const uint64_t t0 = mul2(add2(f2pack(__uint_as_float(r[4 * i + 0]), __uint_as_float(r[4 * i + 1])), nmean), rs2);
+            const uint64_t t1 = mul2(add2(f2pack(__uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3])), nmean), rs2);
+            f2unpack(fma2(t0, f2pack(g.x, g.y), f2pack(be.x, be.y)), y[4 * i + 0], y[4 * i + 1]);
+            f2unpack(fma2(t1, f2pack(g.z, g.w), f2pack(be.z, be.w)), y[4 * i + 2], y[4 * i + 3]);
           }
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            if (!*abort_flag) {
-              tma_store_2d(&tmXN, box, col0 + bx * 64, m0 + q * 32);
-              bulk_commit();
-            }
-            bulk_wait_read_1();  // the other box's store has read it: it can be rewritten next
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            uint4 w;
+            w.x = pack_bf16x2(y[8 * i + 0], y[8 * i + 1]);
+            w.y = pack_bf16x2(y[8 * i + 2], y[8 * i + 3]);
+            w.z = pack_bf16x2(y[8 * i + 4], y[8 * i + 5]);
+            w.w = pack_bf16x2(y[8 * i + 6], y[8 * i + 7]);
+            *reinterpret_cast<uint4*>(srow + ((static_cast<uint32_t>(4 * h + i) ^ (lane & 7)) << 4)) = w;
           }
-          __syncwarp();
-          ob ^= 1;
+          if (h == 1) {
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              if (!*abort_flag) {
+                tma_store_2d(&tmXN, box, col0 + (c >> 1) * 64, m0 + q * 32);
+                bulk_commit();
+              }
+              bulk_wait_read_1();  // the other box's store has read it: it can be rewritten next
+            }
+            __syncwarp();
+            ob ^= 1;
+          }
+        };
+        {
+          uint32_t ra[32], rb[32];
+          tmem_ld32(tb, ra);
+#pragma unroll 1
+          for (int c = 0; c < NCH; c += 2) {
+            pass2_chunk(c, ra, rb);
+            pass2_chunk(c + 1, rb, ra);
+          }
         }
       }
       // this warp has read its lanes of the buffer: release it to the pair's MMA
