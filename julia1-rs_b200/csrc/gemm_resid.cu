@@ -303,7 +303,10 @@ __global__ void __launch_bounds__(256, 1)
       mbar_wait<true>(&tfull[buf], (acc >> 1) & 1, abort_flag, p.err, 35);
       tc_fence_after();
       const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
-      float w_mean = 0.f, w_m2 = 0.f, w_n = 0.f;
+      // row statistics of this CTA's BN columns: sums of (x - shift) and (x - shift)^2 in
+      // column pairs, shift = the mean of the row's first chunk (so the sums stay small)
+      float shift = 0.f;
+      uint64_t ssum[2] = {0ull, 0ull}, ssq[2] = {0ull, 0ull};
       // ---------------- pass 1: residual update
       // One warp per SM sub-partition runs this loop, so latency is what it costs: the next
       // chunk's accumulator columns are loaded from TMEM while this chunk is processed, and
@@ -345,30 +348,22 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll
           for (int j = 0; j < 32; ++j) vv[j] = __float_as_uint(v[j]);
           tmem_st32(tb + c * 32, vv);  // the updated row stays on chip for pass 2
-          // chunk mean / M2 (two passes over registers, pairs of columns at once), merged
-          // into the row's running state
-          uint64_t s2[2] = {0ull, 0ull};
+          if (c == 0) {
+            uint64_t t2[2] = {0ull, 0ull};
 #pragma unroll
-          for (int j = 0; j < 32; j += 2) s2[(j >> 1) & 1] = add2(s2[(j >> 1) & 1], f2pack(v[j], v[j + 1]));
-          float sa, sb, sc, sd;
-          f2unpack(s2[0], sa, sb);
-          f2unpack(s2[1], sc, sd);
-          const float cm = ((sa + sb) + (sc + sd)) * (1.f / 32.f);
-          const uint64_t ncm = f2pack(-cm, -cm);
-          uint64_t q2[2] = {0ull, 0ull};
+            for (int j = 0; j < 32; j += 2) t2[(j >> 1) & 1] = add2(t2[(j >> 1) & 1], f2pack(v[j], v[j + 1]));
+            float sa, sb, sc, sd;
+            f2unpack(t2[0], sa, sb);
+            f2unpack(t2[1], sc, sd);
+            shift = ((sa + sb) + (sc + sd)) * (1.f / 32.f);
+          }
+          const uint64_t nsh = f2pack(-shift, -shift);
 #pragma unroll
           for (int j = 0; j < 32; j += 2) {
-            const uint64_t dv = add2(f2pack(v[j], v[j + 1]), ncm);
-            q2[(j >> 1) & 1] = fma2(dv, dv, q2[(j >> 1) & 1]);
+            const uint64_t dv = add2(f2pack(v[j], v[j + 1]), nsh);
+            ssum[(j >> 1) & 1] = add2(ssum[(j >> 1) & 1], dv);
+            ssq[(j >> 1) & 1] = fma2(dv, dv, ssq[(j >> 1) & 1]);
           }
-          f2unpack(q2[0], sa, sb);
-          f2unpack(q2[1], sc, sd);
-          const float c2 = (sa + sb) + (sc + sd);
-          const float n_new = w_n + 32.f;
-          const float delta = cm - w_mean;
-          w_mean += delta * (32.f / n_new);
-          w_m2 += c2 + delta * delta * (w_n * 32.f / n_new);
-          w_n = n_new;
         }
         fence_proxy_async_smem();
         __syncwarp();
@@ -401,6 +396,18 @@ __global__ void __launch_bounds__(256, 1)
       }
       if constexpr (LN) {
         tmem_st_wait();
+        float w_mean, w_m2;  // mean and M2 of the row's BN columns in this CTA
+        {
+          float sa, sb, sc, sd;
+          f2unpack(ssum[0], sa, sb);
+          f2unpack(ssum[1], sc, sd);
+          const float t1 = (sa + sb) + (sc + sd);
+          f2unpack(ssq[0], sa, sb);
+          f2unpack(ssq[1], sc, sd);
+          const float t2 = (sa + sb) + (sc + sd);
+          w_mean = shift + t1 * (1.f / static_cast<float>(BN));
+          w_m2 = fmaxf(t2 - t1 * t1 * (1.f / static_cast<float>(BN)), 0.f);
+        }
         // ---------------- row statistics over the pairs of the cluster
         const int su = acc & 1;
         float mean = w_mean, m2 = w_m2;
