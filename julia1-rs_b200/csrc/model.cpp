@@ -107,6 +107,8 @@ bool take_fault(int kind) {
   return false;
 }
 
+bool fault_pending(int kind) { return g_fault[kind].load() > 0; }
+
 }  // namespace j1rt
 
 using namespace j1rt;
@@ -217,7 +219,15 @@ j1_status upload_bf16(j1_model* model, SafeTensors& st, const std::string& name,
   return J1_OK;
 }
 
+void drop_forward_graphs(j1_model* model) {
+  for (auto& g : model->graphs) cudaGraphExecDestroy(g.exec);
+  model->graphs.clear();
+  model->shapes_seen.clear();
+}
+
 void free_workspace(j1_model* model) {
+  drop_forward_graphs(model);  // their kernels hold pointers into the workspace
+  ++model->ws_gen;
   for (void* p : model->ws_allocations) cudaFree(p);
   model->ws_allocations.clear();
   for (int k = 0; k < 2; ++k) {
@@ -419,7 +429,7 @@ j1_status stage_batch(j1_model* model, const BatchView& b, int slot = 0, bool sy
   return J1_OK;
 }
 
-j1_status launch_forward(j1_model* model) {
+j1_status launch_forward_direct(j1_model* model) {
   if (!model->staged) return set_error(J1_ERR_INVALID_ARG, "no staged batch");
   const ModelConfig& c = model->cfg;
   const int H = c.hidden, I = c.intermediate, FF = c.head_ff, L = c.layers;
@@ -547,6 +557,74 @@ j1_status enqueue_readback(j1_model* model) {
               "error word readback");
   J1_TRY_CUDA(cudaEventRecord(model->slot_done[slot], model->stream), "event");
   model->slot_busy[slot] = true;
+  return J1_OK;
+}
+
+bool graphs_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("J1_GRAPH");
+    return !(v && std::strcmp(v, "0") == 0);
+  }();
+  return on;
+}
+
+// The staged batch's forward: replayed from a CUDA graph when its shape has been captured,
+// captured when the shape is launched for the second time, launched kernel by kernel
+// otherwise (and while per-launch profiling or an injected launch failure is pending). A
+// graph holds the same kernels with the same arguments as the direct launches (programmatic
+// dependent launch edges included); it saves the host's per-kernel launch work and part of
+// the gaps between kernels, which matters for small micro-batches.
+j1_status launch_forward(j1_model* model) {
+  if (!graphs_enabled() || !model->staged || model->prof_on || model->t == 0 || fault_pending(J1_FAULT_LAUNCH))
+    return launch_forward_direct(model);
+  const std::array<uint64_t, 7> key = {model->t, model->m, model->nseq, model->ntiles, model->nmtiles,
+                                       static_cast<uint64_t>(model->slot), model->ws_gen};
+  for (auto& g : model->graphs)
+    if (std::equal(key.begin(), key.end(), g.key)) {
+      J1_TRY_CUDA(cudaGraphLaunch(g.exec, model->stream), "forward graph launch");
+      g.last_use = ++model->graph_tick;
+      model->launches = g.launches;
+      return J1_OK;
+    }
+  auto seen = std::find(model->shapes_seen.begin(), model->shapes_seen.end(), key);
+  if (seen == model->shapes_seen.end()) {  // first time: launch directly, remember the shape
+    if (model->shapes_seen.size() >= 16) model->shapes_seen.erase(model->shapes_seen.begin());
+    model->shapes_seen.push_back(key);
+    return launch_forward_direct(model);
+  }
+  model->shapes_seen.erase(seen);
+  // Second time: capture the launch sequence (nothing runs while capturing), then replay it.
+  J1_TRY_CUDA(cudaStreamBeginCapture(model->stream, cudaStreamCaptureModeThreadLocal), "forward graph capture");
+  const j1_status s = launch_forward_direct(model);
+  cudaGraph_t graph = nullptr;
+  const cudaError_t ec = cudaStreamEndCapture(model->stream, &graph);
+  if (s) {  // a launch failed while capturing: nothing was queued, report that launch's error
+    if (graph) cudaGraphDestroy(graph);
+    return s;
+  }
+  cudaGraphExec_t exec = nullptr;
+  cudaError_t ei = ec;
+  if (ec == cudaSuccess) ei = cudaGraphInstantiate(&exec, graph, 0);
+  if (graph) cudaGraphDestroy(graph);
+  if (ei != cudaSuccess) {  // no graph for this shape: run the forward directly
+    (void)cudaGetLastError();
+    return launch_forward_direct(model);
+  }
+  if (model->graphs.size() >= 8) {
+    auto lru = std::min_element(model->graphs.begin(), model->graphs.end(),
+                                [](const j1_model::ForwardGraph& a, const j1_model::ForwardGraph& b) {
+                                  return a.last_use < b.last_use;
+                                });
+    cudaGraphExecDestroy(lru->exec);
+    model->graphs.erase(lru);
+  }
+  j1_model::ForwardGraph g;
+  std::copy(key.begin(), key.end(), g.key);
+  g.exec = exec;
+  g.launches = model->launches;
+  g.last_use = ++model->graph_tick;
+  model->graphs.push_back(g);
+  J1_TRY_CUDA(cudaGraphLaunch(exec, model->stream), "forward graph launch");
   return J1_OK;
 }
 

@@ -2,6 +2,7 @@
 #pragma once
 #include <cuda_runtime.h>
 
+#include <array>
 #include <atomic>
 #include <exception>
 #include <functional>
@@ -23,6 +24,7 @@ j1_status cuda_error(cudaError_t e, const char* what);
 // j1_inject_fault state: remaining injected faults per kind (J1_FAULT_*).
 extern std::atomic<int> g_fault[8];
 bool take_fault(int kind);
+bool fault_pending(int kind);  // an injected fault of this kind is waiting to be taken
 
 // Every C entry point runs its body through guard(): a C++ exception (host memory
 // exhausted, a thread that could not start, ...) becomes a status and a message instead
@@ -153,6 +155,22 @@ struct j1_model {
   CUtensorMap tm_x_st, tm_ym_st;    // the same with 32-row boxes (per-warp stores of the residual GEMMs)
   CUtensorMap tm_xn_st, tm_ymb_st;  // LayerNorm outputs with 64 x 32 boxes (per-warp stores)
   int64_t launches = 0;
+
+  // ---- CUDA graphs of the forward's launch sequence, one per batch shape (t, m, nseq,
+  // query tiles, marker tiles, staging slot, workspace generation): every kernel argument
+  // (pointers, tensor maps, grids) is a function of that key, the batch's contents live in
+  // device buffers. A shape is captured the second time it is launched and replayed from
+  // then on; J1_GRAPH=0 disables this.
+  struct ForwardGraph {
+    uint64_t key[7];
+    cudaGraphExec_t exec;
+    int64_t launches;  // kernels in the graph
+    uint64_t last_use;
+  };
+  std::vector<ForwardGraph> graphs;                 // the least recently used is evicted beyond 8
+  std::vector<std::array<uint64_t, 7>> shapes_seen;  // keys launched once and not captured (at most 16)
+  uint64_t ws_gen = 0;                              // bumped whenever the workspace is freed
+  uint64_t graph_tick = 0;
 
   // ---- optional per-launch CUDA-event timing by kernel family (j1_model_profile)
   bool prof_on = false;
