@@ -88,7 +88,12 @@ J1_API j1_status j1_model_forward(j1_model* model, const uint32_t* ids, size_t t
 /* The same forward split in three so a caller can keep a batch resident on the device:
  * stage (validate + pack + async H2D of the batch metadata), launch (enqueue all
  * kernels on the model's stream; may be repeated on a staged batch), finish
- * (D2H of the scores, synchronize, device-error and nonfinite checks). */
+ * (D2H of the scores, synchronize, device-error and nonfinite checks).
+ * The second launch of a batch shape (token, marker, sequence and tile counts) captures
+ * its kernels into a CUDA graph that later launches of that shape replay (the same
+ * kernels and results; up to 8 shapes are kept, a workspace reallocation drops them;
+ * J1_GRAPH=0 in the environment turns this off). This applies to j1_model_forward and
+ * the engine's forwards too. */
 J1_API j1_status j1_model_stage(j1_model* model, const uint32_t* ids, size_t t, const uint32_t* starts,
                          const uint32_t* lens, const uint8_t* qtypes, size_t nseq, const uint32_t* marker_rows,
                          const uint32_t* marker_starts, size_t m);
