@@ -16,18 +16,21 @@
 //   warp 0      TMA producer: A (128 x 64) and W (BN/2 x 64) boxes into a 3-stage ring
 //   warp 1      TMEM allocator; in the even CTA the single-thread tcgen05.mma issuer
 //   warp 2      x producer: TMA loads of 128 x 32 FP32 residual chunks into a ring
-//   warps 4..7  epilogue, one thread per row (TMEM lane = row):
+//   warps 4..    epilogue, one thread per row (TMEM lane = row): four warps, one per TMEM
+//               lane quarter, or (few units per cluster) eight, two per lane quarter, warp
+//               (q, h) taking the quarter's even (h = 0) or odd (h = 1) chunks:
 //     pass 1: per 32-column chunk, x += bf16(acc) (+ bias), written back into the
-//             chunk (TMA store) and into TMEM over the accumulator; chunk mean / M2
-//             merged into the row's running statistics (Chan)
-//     exchange: the row's (mean, M2) over its BN columns goes to the other NG - 1 CTAs
-//             that hold the same rows by st.async (DSMEM, completing bytes on the
+//             chunk (TMA store) and into TMEM over the accumulator; sums of the row's
+//             values about its first chunk's mean accumulate the row statistics
+//     exchange: (eight warps) the two warps of a quarter merge their halves (Chan)
+//             through shared memory; the row's (mean, M2) over its BN columns goes to
+//             the other NG - 1 CTAs holding the same rows by st.async (DSMEM, completing bytes on the
 //             receiver's mbarrier); each merges the NG partials in pair order, so all
 //             of them hold the same mean and rstd for the row
 //     pass 2: the updated row is read back from TMEM, normalised, rounded to BF16 and
 //             staged in 32 x 64 boxes (128B swizzle) that leave by TMA store
-//   Each epilogue warp stores its own 32 rows of every chunk and box, so the four warps run
-//   without a common barrier.
+//   Each epilogue warp stores its own 32 rows of its chunks and boxes; the only barrier
+//   is the one between the two warps of a quarter (eight warps), once per unit.
 // Unlike a GEMM whose epilogue re-reads x from global memory, the row never leaves the
 // chip between its update and its normalisation: per row the kernel reads A and x once
 // and writes x and xn once.
@@ -58,24 +61,38 @@ constexpr int RBK = 64;                      // K per stage
 constexpr uint32_t RX_CHUNK = 128 * 32 * 4;  // one 128 x 32 FP32 residual chunk (16 KB)
 constexpr uint32_t RO_WBOX = 32 * 64 * 2;    // one warp's 32 x 64 BF16 xn box (4 KB)
 
-template <int NG, int BN>
+// Eight epilogue warps (two per TMEM lane quarter) finish a unit sooner, which pays when each
+// cluster has few units to pipeline (small micro-batches); four keep more shared-memory
+// bandwidth for the main loop at full size. Eight are used when the units are at most
+// J1_RLN_SMALL_UNITS per cluster that fits on the device.
+#ifndef J1_RLN_SMALL_UNITS
+#define J1_RLN_SMALL_UNITS 2
+#endif
+
+template <int NG, int BN, int EW>
 struct RlnCfg {
   static constexpr int CS = 2 * NG;  // CTAs per cluster
   static constexpr int STAGES = J1_RLN_STAGES;
-  static constexpr int NX = J1_RLN_NX;  // residual chunks in flight
-  static constexpr int THREADS = 256;
+  static constexpr int THREADS = 128 + EW * 32;
   static constexpr uint32_t A_BYTES = RBM * RBK * 2;
   static constexpr uint32_t W_BYTES = (BN / 2) * RBK * 2;
   static constexpr uint32_t STAGE_BYTES = A_BYTES + W_BYTES;
-  static constexpr uint32_t O_BYTES = 4 * 2 * RO_WBOX;      // two xn boxes per epilogue warp
+  static constexpr uint32_t O_BYTES = 8 * RO_WBOX;  // xn boxes: two per warp (4 warps), one per warp (8)
   static constexpr uint32_t PAR_BYTES = 3 * BN * 4;         // ln_w, ln_b, bias of this CTA's columns
   static constexpr uint32_t STAT_BYTES = 2 * NG * RBM * 8;  // [2 slots][NG pairs][128 rows] (mean, M2)
-  static constexpr uint32_t SMEM = STAGES * STAGE_BYTES + NX * RX_CHUNK + O_BYTES + PAR_BYTES + STAT_BYTES +
-                                   1024 /*align*/ + 256 /*barriers*/;
+  static constexpr uint32_t CHUNK_BYTES = (BN / 32) * RBM * 8;  // [chunk][128 rows] (mean, M2) of a unit's chunks
+  static constexpr uint32_t FIXED = STAGES * STAGE_BYTES + O_BYTES + PAR_BYTES + STAT_BYTES + CHUNK_BYTES +
+                                    1024 /*align*/ + 256 /*barriers*/;
+  // residual chunks in flight: J1_RLN_NX, or as many as fit (four pairs per cluster, hidden 1024)
+  static constexpr int NX = FIXED + J1_RLN_NX * RX_CHUNK <= 232448 ? J1_RLN_NX
+                                                                    : static_cast<int>((232448 - FIXED) / RX_CHUNK);
+  static constexpr uint32_t SMEM = FIXED + NX * RX_CHUNK;
   static constexpr uint32_t TMEM_COLS = 2 * BN;  // 256 or 512
   static_assert(SMEM <= 232448, "shared memory budget");
   static_assert(BN == 128 || BN == 256, "columns per pair");
   static_assert(CS <= 8, "portable cluster size");
+  static_assert(EW == 4 || EW == 8, "epilogue warps");
+  static_assert(NX >= 3, "residual chunks in flight");
 };
 
 // st.async of two floats into the shared memory of a CTA of the cluster, completing 8
@@ -86,12 +103,56 @@ __device__ __forceinline__ void st_async_f2(uint32_t caddr, float a, float b, ui
                : "memory");
 }
 
-template <int NG, int BN, bool LN>
-__global__ void __launch_bounds__(256, 1)
+// (mean, M2) of one row's 32 values of a chunk: the mean first, then the squared deviations
+// from it, pairs of columns at once.
+__device__ __forceinline__ float2 chunk_stats(const float (&v)[32]) {
+  uint64_t t2[2] = {0ull, 0ull};
+#pragma unroll
+  for (int j = 0; j < 32; j += 2) t2[(j >> 1) & 1] = add2(t2[(j >> 1) & 1], f2pack(v[j], v[j + 1]));
+  float sa, sb, sc, sd;
+  f2unpack(t2[0], sa, sb);
+  f2unpack(t2[1], sc, sd);
+  const float cm = ((sa + sb) + (sc + sd)) * (1.f / 32.f);
+  const uint64_t ncm = f2pack(-cm, -cm);
+  uint64_t q2[2] = {0ull, 0ull};
+#pragma unroll
+  for (int j = 0; j < 32; j += 2) {
+    const uint64_t dv = add2(f2pack(v[j], v[j + 1]), ncm);
+    q2[(j >> 1) & 1] = fma2(dv, dv, q2[(j >> 1) & 1]);
+  }
+  f2unpack(q2[0], sa, sb);
+  f2unpack(q2[1], sc, sd);
+  return make_float2(cm, (sa + sb) + (sc + sd));
+}
+
+// Chan's merge of two (mean, M2) over n values each.
+__device__ __forceinline__ float2 merge_equal(float2 a, float2 b, float n) {
+  const float d = b.x - a.x;
+  return make_float2(0.5f * (a.x + b.x), a.y + b.y + d * d * (0.5f * n));
+}
+
+// A row's (mean, M2) over its NCH chunks, merged pairwise in a fixed tree (chunks 2i and
+// 2i + 1, then pairs of pairs, ...): the same bits whichever warps computed the chunks.
+template <int NCH>
+__device__ __forceinline__ float2 merge_chunks(const float2* sChunk, int row) {
+  static_assert(NCH == 4 || NCH == 8, "chunks per unit");
+  float2 s[NCH];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) s[c] = sChunk[c * RBM + row];
+  float n = 32.f;
+#pragma unroll
+  for (int w = NCH; w > 1; w >>= 1, n *= 2.f)
+#pragma unroll
+    for (int i = 0; i < w / 2; ++i) s[i] = merge_equal(s[2 * i], s[2 * i + 1], n);
+  return s[0];
+}
+
+template <int NG, int BN, bool LN, int EW>
+__global__ void __launch_bounds__(128 + EW * 32, 1)
     resid_ln_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                     const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmXs,
                     const __grid_constant__ CUtensorMap tmXN, const EpiParams p) {
-  using C = RlnCfg<NG, BN>;
+  using C = RlnCfg<NG, BN, EW>;
   constexpr int CS = C::CS;
   constexpr int NCH = BN / 32;   // residual chunks per unit
   constexpr int H = NG * BN;
@@ -103,7 +164,8 @@ __global__ void __launch_bounds__(256, 1)
   uint8_t* sO = sX + C::NX * RX_CHUNK;                            // [warp][2] xn boxes
   float* sPar = reinterpret_cast<float*>(sO + C::O_BYTES);         // [3][BN]: ln_w, ln_b, bias
   float2* sStat = reinterpret_cast<float2*>(sO + C::O_BYTES + C::PAR_BYTES);  // [slot][pair][row]
-  uint64_t* full = reinterpret_cast<uint64_t*>(sO + C::O_BYTES + C::PAR_BYTES + C::STAT_BYTES);
+  float2* sChunk = sStat + C::STAT_BYTES / 8;                                  // [chunk][row]
+  uint64_t* full = reinterpret_cast<uint64_t*>(sO + C::O_BYTES + C::PAR_BYTES + C::STAT_BYTES + C::CHUNK_BYTES);
   uint64_t* empty = full + C::STAGES;
   uint64_t* tfull = empty + C::STAGES;  // [2]
   uint64_t* tempty = tfull + 2;         // [2] (the even CTA's: 4 arrivals from each CTA of the pair)
@@ -145,7 +207,7 @@ __global__ void __launch_bounds__(256, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 8);   // one arrival per epilogue warp of both CTAs of the pair
+      mbar_init(&tempty[b], 2 * EW);  // one arrival per epilogue warp of both CTAs of the pair
       mbar_init(&statbar[b], 1);  // the local expect_tx; the bytes come from the other pairs
     }
     for (int b = 0; b < C::NX; ++b) {
@@ -274,230 +336,394 @@ __global__ void __launch_bounds__(256, 1)
       }
     }
   } else if (warp >= 4) {
-    // ------------------------------------------------------------ epilogue (warps 4..7)
-    // Each warp owns 32 rows (its TMEM lane quarter) and works through the units on its own:
-    // it stores its rows of every residual chunk and every xn box itself (32-row TMA boxes),
-    // so no barrier couples the four warps. After an abort every wait returns at once and
-    // the loops run out without stores.
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const int trow = q * 32 + lane;
-    {  // this CTA's columns of ln_w, ln_b and bias, once
-      const int et = threadIdx.x - 128;
-      for (int j = et; j < BN; j += 128) {
-        sPar[j] = LN ? p.ln_w[col0 + j] : 0.f;
-        sPar[BN + j] = (LN && p.ln_b) ? p.ln_b[col0 + j] : 0.f;
-        sPar[2 * BN + j] = p.bias ? p.bias[col0 + j] : 0.f;
+    if constexpr (EW == 8) {
+      // ------------------------------------------------------------ epilogue (warps 4..11)
+      // Two warps per TMEM lane quarter: warp (q, hf) owns the quarter's 32 rows and the
+      // residual chunks c with c % 2 == hf, then the xn boxes with box % 2 == hf. With one warp
+      // per SM sub-partition this loop was latency-bound; two warps interleave. Each warp stores
+      // its rows of its chunks and boxes itself (32-row TMA boxes); the two warps of a quarter
+      // meet once per unit (a 64-thread named barrier) to merge their halves of the row
+      // statistics. After an abort every wait returns at once and the loops run out without
+      // stores.
+      const int q = warp & 3;          // TMEM lane quarter this warp may access
+      const int hf = (warp - 4) >> 2;  // 0: even chunks and boxes, 1: odd ones
+      const int trow = q * 32 + lane;
+      {  // this CTA's columns of ln_w, ln_b and bias, once
+        const int et = threadIdx.x - 128;
+        for (int j = et; j < BN; j += EW * 32) {
+          sPar[j] = LN ? p.ln_w[col0 + j] : 0.f;
+          sPar[BN + j] = (LN && p.ln_b) ? p.ln_b[col0 + j] : 0.f;
+          sPar[2 * BN + j] = p.bias ? p.bias[col0 + j] : 0.f;
+        }
+        named_bar_sync(1, EW * 32);
       }
-      named_bar_sync(1, 128);
-    }
-    const float4* parw = reinterpret_cast<const float4*>(sPar);
-    const float4* parb = reinterpret_cast<const float4*>(sPar + BN);
-    const float4* parc = reinterpret_cast<const float4*>(sPar + 2 * BN);
-    int acc = 0;
-    uint32_t gch = 0;  // residual chunks consumed so far
-    int xpend = -1;    // ring slot whose store (of this warp's rows) may still be reading smem
-    int ob = 0;        // this warp's xn box in use (of two)
-    for (int u = cid; u < units; u += ncl, ++acc) {
-      const int m0 = u * 2 * RBM + static_cast<int>(half) * RBM;
-      const int buf = acc & 1;
-      mbar_wait<true>(&tfull[buf], (acc >> 1) & 1, abort_flag, p.err, 35);
-      tc_fence_after();
-      const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
-      // row statistics of this CTA's BN columns: sums of (x - shift) and (x - shift)^2 in
-      // column pairs, shift = the mean of the row's first chunk (so the sums stay small)
-      float shift = 0.f;
-      uint64_t ssum[2] = {0ull, 0ull}, ssq[2] = {0ull, 0ull};
-      // ---------------- pass 1: residual update
-      // One warp per SM sub-partition runs this loop, so latency is what it costs: the next
-      // chunk's accumulator columns are loaded from TMEM while this chunk is processed, and
-      // the chunk's eight 16-byte slots are all read before any is written back (written in
-      // place through a data-dependent swizzle, they could not be reordered otherwise).
-      auto pass1_chunk = [&](int c, uint32_t (&r)[32], uint32_t (&rn)[32]) {
-        const uint32_t b = gch % C::NX;
-        tmem_ld_wait();  // chunk c's accumulator is in r
-        if (c + 1 < NCH) tmem_ld32(tb + (c + 1) * 32, rn);
-        mbar_wait<true>(&xfull[b], (gch / C::NX) & 1, abort_flag, p.err, 36);
-        uint8_t* xrow = sX + b * RX_CHUNK + trow * 128;  // 16-byte unit i at (i ^ (row & 7)) * 16
-        float4 o[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-          o[i] = *reinterpret_cast<const float4*>(xrow + ((static_cast<uint32_t>(i) ^ (trow & 7)) << 4));
-        float v[32];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          float d0 = __uint_as_float(r[4 * i + 0]), d1 = __uint_as_float(r[4 * i + 1]);
-          float d2 = __uint_as_float(r[4 * i + 2]), d3 = __uint_as_float(r[4 * i + 3]);
-          bf16_round2(d0, d1);  // delta = bf16(A . W^T), as the reference's GEMM output
-          bf16_round2(d2, d3);
-          uint64_t lo = add2(f2pack(o[i].x, o[i].y), f2pack(d0, d1));
-          uint64_t hi = add2(f2pack(o[i].z, o[i].w), f2pack(d2, d3));
-          if (p.bias) {  // the bias after the delta
-            const float4 bb = parc[c * 8 + i];
-            lo = add2(lo, f2pack(bb.x, bb.y));
-            hi = add2(hi, f2pack(bb.z, bb.w));
-          }
-          f2unpack(lo, v[4 * i + 0], v[4 * i + 1]);
-          f2unpack(hi, v[4 * i + 2], v[4 * i + 3]);
-        }
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-          *reinterpret_cast<float4*>(xrow + ((static_cast<uint32_t>(i) ^ (trow & 7)) << 4)) =
-              make_float4(v[4 * i + 0], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-        if constexpr (LN) {
-          uint32_t vv[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) vv[j] = __float_as_uint(v[j]);
-          tmem_st32(tb + c * 32, vv);  // the updated row stays on chip for pass 2
-          if (c == 0) {
-            uint64_t t2[2] = {0ull, 0ull};
-#pragma unroll
-            for (int j = 0; j < 32; j += 2) t2[(j >> 1) & 1] = add2(t2[(j >> 1) & 1], f2pack(v[j], v[j + 1]));
-            float sa, sb, sc, sd;
-            f2unpack(t2[0], sa, sb);
-            f2unpack(t2[1], sc, sd);
-            shift = ((sa + sb) + (sc + sd)) * (1.f / 32.f);
-          }
-          const uint64_t nsh = f2pack(-shift, -shift);
-#pragma unroll
-          for (int j = 0; j < 32; j += 2) {
-            const uint64_t dv = add2(f2pack(v[j], v[j + 1]), nsh);
-            ssum[(j >> 1) & 1] = add2(ssum[(j >> 1) & 1], dv);
-            ssq[(j >> 1) & 1] = fma2(dv, dv, ssq[(j >> 1) & 1]);
-          }
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          if (!*abort_flag) {
-            tma_store_2d(&tmXs, sX + b * RX_CHUNK + q * 32 * 128, col0 + c * 32, m0 + q * 32);
-            bulk_commit();
-          }
-          bulk_wait_read_1();  // this warp's previous chunk store has read its slot: release it
-          if (xpend >= 0) mbar_arrive(&xempty[xpend]);
-          xpend = static_cast<int>(b);
-        }
-        __syncwarp();
-        ++gch;
-      };
-      {
-        uint32_t ra[32], rb[32];
-        tmem_ld32(tb, ra);
-        static_assert(NCH % 2 == 0, "chunks are processed in pairs");
-#pragma unroll 1
-        for (int c = 0; c < NCH; c += 2) {
-          pass1_chunk(c, ra, rb);
-          pass1_chunk(c + 1, rb, ra);
-        }
-      }
-      if (lane == 0) {  // the unit's last chunk: release its slot once the store has read it
-        bulk_wait_read_all();
-        if (xpend >= 0) mbar_arrive(&xempty[xpend]);
-        xpend = -1;
-      }
-      if constexpr (LN) {
-        tmem_st_wait();
-        float w_mean, w_m2;  // mean and M2 of the row's BN columns in this CTA
-        {
-          float sa, sb, sc, sd;
-          f2unpack(ssum[0], sa, sb);
-          f2unpack(ssum[1], sc, sd);
-          const float t1 = (sa + sb) + (sc + sd);
-          f2unpack(ssq[0], sa, sb);
-          f2unpack(ssq[1], sc, sd);
-          const float t2 = (sa + sb) + (sc + sd);
-          w_mean = shift + t1 * (1.f / static_cast<float>(BN));
-          w_m2 = fmaxf(t2 - t1 * t1 * (1.f / static_cast<float>(BN)), 0.f);
-        }
-        // ---------------- row statistics over the pairs of the cluster
-        const int su = acc & 1;
-        float mean = w_mean, m2 = w_m2;
-        if constexpr (NG > 1) {
-          float2* mine = sStat + (su * NG + pr) * RBM + trow;
-          const uint32_t bar_local = smem_u32(&statbar[su]);
-          for (int j = 0; j < NG; ++j)
-            if (j != pr) {
-              const uint32_t dst = static_cast<uint32_t>(2 * j) + half;  // same rows, pair j
-              st_async_f2(mapa_shared(smem_u32(mine), dst), w_mean, w_m2, mapa_shared(bar_local, dst));
-            }
-          if (trow == 0) mbar_arrive_expect_tx(&statbar[su], (NG - 1) * RBM * 8);
-          mbar_wait<true>(&statbar[su], (acc >> 1) & 1, abort_flag, p.err, 37);
-          float pm[NG], pq[NG];
-#pragma unroll
-          for (int j = 0; j < NG; ++j) {
-            const float2 s2 = j == pr ? make_float2(w_mean, w_m2) : sStat[(su * NG + j) * RBM + trow];
-            pm[j] = s2.x;
-            pq[j] = s2.y;
-          }
-          float s = 0.f;
-#pragma unroll
-          for (int j = 0; j < NG; ++j) s += pm[j];
-          mean = s * (1.f / NG);
-          m2 = 0.f;
-#pragma unroll
-          for (int j = 0; j < NG; ++j) {
-            const float d = pm[j] - mean;
-            m2 += pq[j] + static_cast<float>(BN) * d * d;
-          }
-        }
-        const float rstd = rsqrtf(m2 * (1.f / static_cast<float>(H)) + p.ln_eps);
-        // ---------------- pass 2: normalise from TMEM, BF16 boxes of this warp's rows out by TMA
-        // (two chunks per 64-column box; the next chunk's TMEM load overlaps this one)
-        const uint64_t nmean = f2pack(-mean, -mean), rs2 = f2pack(rstd, rstd);
-        auto pass2_chunk = [&](int c, uint32_t (&r)[32], uint32_t (&rn)[32]) {
-          const int h = c & 1;
-          uint8_t* box = sO + (q * 2 + ob) * RO_WBOX;
-          uint8_t* srow = box + lane * 128;
-          tmem_ld_wait();  // chunk c's updated row is in r
-          if (c + 1 < NCH) tmem_ld32(tb + (c + 1) * 32, rn);
-          float y[32];
-#pragma unroll
+      const float4* parw = reinterpret_cast<const float4*>(sPar);
+      const float4* parb = reinterpret_cast<const float4*>(sPar + BN);
+      const float4* parc = reinterpret_cast<const float4*>(sPar + 2 * BN);
+      uint8_t* box = sO + (warp - 4) * RO_WBOX;  // this warp's xn box (32 rows x 64 columns)
+      uint8_t* srow = box + lane * 128;
+      int acc = 0;
+      int xpend = -1;  // ring slot whose store (of this warp's rows) may still be reading smem
+      for (int u = cid; u < units; u += ncl, ++acc) {
+        const int m0 = u * 2 * RBM + static_cast<int>(half) * RBM;
+        const int buf = acc & 1;
+        mbar_wait<true>(&tfull[buf], (acc >> 1) & 1, abort_flag, p.err, 35);
+        tc_fence_after();
+        const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
+        // ---------------- pass 1: residual update (this warp's half of the chunks)
+  #pragma unroll 1
+        for (int c = hf * (NCH / 2); c < (hf + 1) * (NCH / 2); ++c) {
+          const uint32_t g = static_cast<uint32_t>(acc * NCH + c);  // chunk in this CTA's x stream
+          const uint32_t b = g % C::NX;
+          uint32_t r[32];
+          tmem_ld32(tb + c * 32, r);
+          tmem_ld_wait();
+          mbar_wait<true>(&xfull[b], (g / C::NX) & 1, abort_flag, p.err, 36);
+          // the chunk's eight 16-byte slots of this row are all read before any is written back
+          // (in place, through a data-dependent swizzle, they could not be reordered otherwise)
+          uint8_t* xrow = sX + b * RX_CHUNK + trow * 128;  // 16-byte unit i at (i ^ (row & 7)) * 16
+          float4 o[8];
+  #pragma unroll
+          for (int i = 0; i < 8; ++i)
+            o[i] = *reinterpret_cast<const float4*>(xrow + ((static_cast<uint32_t>(i) ^ (trow & 7)) << 4));
+          float v[32];
+  #pragma unroll
           for (int i = 0; i < 8; ++i) {
-            const float4 g = parw[c * 8 + i], be = parb[c * 8 + i];
-            // y = ((x - mean) * rstd) * g + be, pairs of columns at once
-            const uint64_t t0 = mul2(add2(f2pack(__uint_as_float(r[4 * i + 0]), __uint_as_float(r[4 * i + 1])), nmean), rs2);
-            const uint64_t t1 = mul2(add2(f2pack(__uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3])), nmean), rs2);
-            f2unpack(fma2(t0, f2pack(g.x, g.y), f2pack(be.x, be.y)), y[4 * i + 0], y[4 * i + 1]);
-            f2unpack(fma2(t1, f2pack(g.z, g.w), f2pack(be.z, be.w)), y[4 * i + 2], y[4 * i + 3]);
+            float d0 = __uint_as_float(r[4 * i + 0]), d1 = __uint_as_float(r[4 * i + 1]);
+            float d2 = __uint_as_float(r[4 * i + 2]), d3 = __uint_as_float(r[4 * i + 3]);
+            bf16_round2(d0, d1);  // delta = bf16(A . W^T), as the reference's GEMM output
+            bf16_round2(d2, d3);
+            uint64_t lo = add2(f2pack(o[i].x, o[i].y), f2pack(d0, d1));
+            uint64_t hi = add2(f2pack(o[i].z, o[i].w), f2pack(d2, d3));
+            if (p.bias) {  // the bias after the delta
+              const float4 bb = parc[c * 8 + i];
+              lo = add2(lo, f2pack(bb.x, bb.y));
+              hi = add2(hi, f2pack(bb.z, bb.w));
+            }
+            f2unpack(lo, v[4 * i + 0], v[4 * i + 1]);
+            f2unpack(hi, v[4 * i + 2], v[4 * i + 3]);
           }
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            uint4 w;
-            w.x = pack_bf16x2(y[8 * i + 0], y[8 * i + 1]);
-            w.y = pack_bf16x2(y[8 * i + 2], y[8 * i + 3]);
-            w.z = pack_bf16x2(y[8 * i + 4], y[8 * i + 5]);
-            w.w = pack_bf16x2(y[8 * i + 6], y[8 * i + 7]);
-            *reinterpret_cast<uint4*>(srow + ((static_cast<uint32_t>(4 * h + i) ^ (lane & 7)) << 4)) = w;
+  #pragma unroll
+          for (int i = 0; i < 8; ++i)
+            *reinterpret_cast<float4*>(xrow + ((static_cast<uint32_t>(i) ^ (trow & 7)) << 4)) =
+                make_float4(v[4 * i + 0], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+          if constexpr (LN) {
+            uint32_t vv[32];
+  #pragma unroll
+            for (int j = 0; j < 32; ++j) vv[j] = __float_as_uint(v[j]);
+            tmem_st32(tb + c * 32, vv);  // the updated row stays on chip for pass 2
+            sChunk[c * RBM + trow] = chunk_stats(v);
           }
-          if (h == 1) {
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            if (!*abort_flag) {
+              tma_store_2d(&tmXs, sX + b * RX_CHUNK + q * 32 * 128, col0 + c * 32, m0 + q * 32);
+              bulk_commit();
+            }
+            bulk_wait_read_1();  // this warp's previous chunk store has read its slot: release it
+            if (xpend >= 0) mbar_arrive(&xempty[xpend]);
+            xpend = static_cast<int>(b);
+          }
+          __syncwarp();
+        }
+        if (lane == 0) {  // the unit's last chunk: release its slot once the store has read it
+          bulk_wait_read_all();
+          if (xpend >= 0) mbar_arrive(&xempty[xpend]);
+          xpend = -1;
+        }
+        if constexpr (LN) {
+          tmem_st_wait();
+          // ---------------- row statistics: the chunks of both warps of the quarter, merged
+          // in the fixed tree (the same bits as with four epilogue warps); the second barrier
+          // keeps either warp from overwriting the chunk statistics in the next unit before
+          // the other has read them
+          named_bar_sync(2 + q, 64);
+          const float2 ws = merge_chunks<NCH>(sChunk, trow);
+          named_bar_sync(2 + q, 64);
+          const float w_mean = ws.x, w_m2 = ws.y;  // mean and M2 of the row's BN columns in this CTA
+          // ---------------- row statistics over the pairs of the cluster
+          const int su = acc & 1;
+          float mean = w_mean, m2 = w_m2;
+          if constexpr (NG > 1) {
+            float2* mine = sStat + (su * NG + pr) * RBM + trow;
+            const uint32_t bar_local = smem_u32(&statbar[su]);
+            if (hf == 0)
+              for (int j = 0; j < NG; ++j)
+                if (j != pr) {
+                  const uint32_t dst = static_cast<uint32_t>(2 * j) + half;  // same rows, pair j
+                  st_async_f2(mapa_shared(smem_u32(mine), dst), w_mean, w_m2, mapa_shared(bar_local, dst));
+                }
+            if (trow == 0 && hf == 0) mbar_arrive_expect_tx(&statbar[su], (NG - 1) * RBM * 8);
+            mbar_wait<true>(&statbar[su], (acc >> 1) & 1, abort_flag, p.err, 37);
+            float pm[NG], pq[NG];
+  #pragma unroll
+            for (int j = 0; j < NG; ++j) {
+              const float2 st = j == pr ? make_float2(w_mean, w_m2) : sStat[(su * NG + j) * RBM + trow];
+              pm[j] = st.x;
+              pq[j] = st.y;
+            }
+            float s = 0.f;
+  #pragma unroll
+            for (int j = 0; j < NG; ++j) s += pm[j];
+            mean = s * (1.f / NG);
+            m2 = 0.f;
+  #pragma unroll
+            for (int j = 0; j < NG; ++j) {
+              const float d = pm[j] - mean;
+              m2 += pq[j] + static_cast<float>(BN) * d * d;
+            }
+          }
+          const float rstd = rsqrtf(m2 * (1.f / static_cast<float>(H)) + p.ln_eps);
+          // ---------------- pass 2: normalise from TMEM; this warp's boxes (64 columns, two
+          // chunks each) go out by TMA from its one box buffer
+          const uint64_t nmean = f2pack(-mean, -mean), rs2 = f2pack(rstd, rstd);
+  #pragma unroll 1
+          for (int bx = hf * (NCH / 4); bx < (hf + 1) * (NCH / 4); ++bx) {
+            uint32_t ra[32], rb[32];
+            tmem_ld32(tb + (2 * bx) * 32, ra);
+            tmem_ld32(tb + (2 * bx + 1) * 32, rb);
+            tmem_ld_wait();
+            uint4 w[8];
+            auto norm32 = [&](int c, const uint32_t (&r)[32], uint4* out) {
+              float y[32];
+  #pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const float4 gw = parw[c * 8 + i], be = parb[c * 8 + i];
+                // y = ((x - mean) * rstd) * g + be, pairs of columns at once
+                const uint64_t t0 = mul2(add2(f2pack(__uint_as_float(r[4 * i + 0]), __uint_as_float(r[4 * i + 1])), nmean), rs2);
+                const uint64_t t1 = mul2(add2(f2pack(__uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3])), nmean), rs2);
+                f2unpack(fma2(t0, f2pack(gw.x, gw.y), f2pack(be.x, be.y)), y[4 * i + 0], y[4 * i + 1]);
+                f2unpack(fma2(t1, f2pack(gw.z, gw.w), f2pack(be.z, be.w)), y[4 * i + 2], y[4 * i + 3]);
+              }
+  #pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                out[i].x = pack_bf16x2(y[8 * i + 0], y[8 * i + 1]);
+                out[i].y = pack_bf16x2(y[8 * i + 2], y[8 * i + 3]);
+                out[i].z = pack_bf16x2(y[8 * i + 4], y[8 * i + 5]);
+                out[i].w = pack_bf16x2(y[8 * i + 6], y[8 * i + 7]);
+              }
+            };
+            norm32(2 * bx, ra, w);
+            norm32(2 * bx + 1, rb, w + 4);
+            if (lane == 0) bulk_wait_read_all();  // the box's previous store has read it
+            __syncwarp();
+  #pragma unroll
+            for (int i = 0; i < 8; ++i)
+              *reinterpret_cast<uint4*>(srow + ((static_cast<uint32_t>(i) ^ (lane & 7)) << 4)) = w[i];
             fence_proxy_async_smem();
             __syncwarp();
-            if (lane == 0) {
-              if (!*abort_flag) {
-                tma_store_2d(&tmXN, box, col0 + (c >> 1) * 64, m0 + q * 32);
-                bulk_commit();
-              }
-              bulk_wait_read_1();  // the other box's store has read it: it can be rewritten next
+            if (lane == 0 && !*abort_flag) {
+              tma_store_2d(&tmXN, box, col0 + bx * 64, m0 + q * 32);
+              bulk_commit();
             }
             __syncwarp();
-            ob ^= 1;
           }
+        }
+        // this warp has read its lanes of the buffer: release it to the pair's MMA
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&tempty[buf]), lead));
+      }
+      if (lane == 0) bulk_wait_all();  // every store complete: this kernel's x and xn are in memory
+    } else {
+      // ------------------------------------------------------------ epilogue (warps 4..7)
+      // Each warp owns 32 rows (its TMEM lane quarter) and works through the units on its own:
+      // it stores its rows of every residual chunk and every xn box itself (32-row TMA boxes),
+      // so no barrier couples the four warps. After an abort every wait returns at once and
+      // the loops run out without stores.
+      const int q = warp & 3;  // TMEM lane quarter this warp may access
+      const int trow = q * 32 + lane;
+      {  // this CTA's columns of ln_w, ln_b and bias, once
+        const int et = threadIdx.x - 128;
+        for (int j = et; j < BN; j += 128) {
+          sPar[j] = LN ? p.ln_w[col0 + j] : 0.f;
+          sPar[BN + j] = (LN && p.ln_b) ? p.ln_b[col0 + j] : 0.f;
+          sPar[2 * BN + j] = p.bias ? p.bias[col0 + j] : 0.f;
+        }
+        named_bar_sync(1, 128);
+      }
+      const float4* parw = reinterpret_cast<const float4*>(sPar);
+      const float4* parb = reinterpret_cast<const float4*>(sPar + BN);
+      const float4* parc = reinterpret_cast<const float4*>(sPar + 2 * BN);
+      int acc = 0;
+      uint32_t gch = 0;  // residual chunks consumed so far
+      int xpend = -1;    // ring slot whose store (of this warp's rows) may still be reading smem
+      int ob = 0;        // this warp's xn box in use (of two)
+      for (int u = cid; u < units; u += ncl, ++acc) {
+        const int m0 = u * 2 * RBM + static_cast<int>(half) * RBM;
+        const int buf = acc & 1;
+        mbar_wait<true>(&tfull[buf], (acc >> 1) & 1, abort_flag, p.err, 35);
+        tc_fence_after();
+        const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
+        // ---------------- pass 1: residual update
+        // One warp per SM sub-partition runs this loop, so latency is what it costs: the next
+        // chunk's accumulator columns are loaded from TMEM while this chunk is processed, and
+        // the chunk's eight 16-byte slots are all read before any is written back (written in
+        // place through a data-dependent swizzle, they could not be reordered otherwise).
+        auto pass1_chunk = [&](int c, uint32_t (&r)[32], uint32_t (&rn)[32]) {
+          const uint32_t b = gch % C::NX;
+          tmem_ld_wait();  // chunk c's accumulator is in r
+          if (c + 1 < NCH) tmem_ld32(tb + (c + 1) * 32, rn);
+          mbar_wait<true>(&xfull[b], (gch / C::NX) & 1, abort_flag, p.err, 36);
+          uint8_t* xrow = sX + b * RX_CHUNK + trow * 128;  // 16-byte unit i at (i ^ (row & 7)) * 16
+          float4 o[8];
+  #pragma unroll
+          for (int i = 0; i < 8; ++i)
+            o[i] = *reinterpret_cast<const float4*>(xrow + ((static_cast<uint32_t>(i) ^ (trow & 7)) << 4));
+          float v[32];
+  #pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            float d0 = __uint_as_float(r[4 * i + 0]), d1 = __uint_as_float(r[4 * i + 1]);
+            float d2 = __uint_as_float(r[4 * i + 2]), d3 = __uint_as_float(r[4 * i + 3]);
+            bf16_round2(d0, d1);  // delta = bf16(A . W^T), as the reference's GEMM output
+            bf16_round2(d2, d3);
+            uint64_t lo = add2(f2pack(o[i].x, o[i].y), f2pack(d0, d1));
+            uint64_t hi = add2(f2pack(o[i].z, o[i].w), f2pack(d2, d3));
+            if (p.bias) {  // the bias after the delta
+              const float4 bb = parc[c * 8 + i];
+              lo = add2(lo, f2pack(bb.x, bb.y));
+              hi = add2(hi, f2pack(bb.z, bb.w));
+            }
+            f2unpack(lo, v[4 * i + 0], v[4 * i + 1]);
+            f2unpack(hi, v[4 * i + 2], v[4 * i + 3]);
+          }
+  #pragma unroll
+          for (int i = 0; i < 8; ++i)
+            *reinterpret_cast<float4*>(xrow + ((static_cast<uint32_t>(i) ^ (trow & 7)) << 4)) =
+                make_float4(v[4 * i + 0], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+          if constexpr (LN) {
+            uint32_t vv[32];
+  #pragma unroll
+            for (int j = 0; j < 32; ++j) vv[j] = __float_as_uint(v[j]);
+            tmem_st32(tb + c * 32, vv);  // the updated row stays on chip for pass 2
+            sChunk[c * RBM + trow] = chunk_stats(v);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            if (!*abort_flag) {
+              tma_store_2d(&tmXs, sX + b * RX_CHUNK + q * 32 * 128, col0 + c * 32, m0 + q * 32);
+              bulk_commit();
+            }
+            bulk_wait_read_1();  // this warp's previous chunk store has read its slot: release it
+            if (xpend >= 0) mbar_arrive(&xempty[xpend]);
+            xpend = static_cast<int>(b);
+          }
+          __syncwarp();
+          ++gch;
         };
         {
           uint32_t ra[32], rb[32];
           tmem_ld32(tb, ra);
-#pragma unroll 1
+          static_assert(NCH % 2 == 0, "chunks are processed in pairs");
+  #pragma unroll 1
           for (int c = 0; c < NCH; c += 2) {
-            pass2_chunk(c, ra, rb);
-            pass2_chunk(c + 1, rb, ra);
+            pass1_chunk(c, ra, rb);
+            pass1_chunk(c + 1, rb, ra);
           }
         }
+        if (lane == 0) {  // the unit's last chunk: release its slot once the store has read it
+          bulk_wait_read_all();
+          if (xpend >= 0) mbar_arrive(&xempty[xpend]);
+          xpend = -1;
+        }
+        if constexpr (LN) {
+          tmem_st_wait();
+          // the row's chunk statistics merged in the fixed tree (this thread wrote them)
+          const float2 ws = merge_chunks<NCH>(sChunk, trow);
+          const float w_mean = ws.x, w_m2 = ws.y;  // mean and M2 of the row's BN columns in this CTA
+          // ---------------- row statistics over the pairs of the cluster
+          const int su = acc & 1;
+          float mean = w_mean, m2 = w_m2;
+          if constexpr (NG > 1) {
+            float2* mine = sStat + (su * NG + pr) * RBM + trow;
+            const uint32_t bar_local = smem_u32(&statbar[su]);
+            for (int j = 0; j < NG; ++j)
+              if (j != pr) {
+                const uint32_t dst = static_cast<uint32_t>(2 * j) + half;  // same rows, pair j
+                st_async_f2(mapa_shared(smem_u32(mine), dst), w_mean, w_m2, mapa_shared(bar_local, dst));
+              }
+            if (trow == 0) mbar_arrive_expect_tx(&statbar[su], (NG - 1) * RBM * 8);
+            mbar_wait<true>(&statbar[su], (acc >> 1) & 1, abort_flag, p.err, 37);
+            float pm[NG], pq[NG];
+  #pragma unroll
+            for (int j = 0; j < NG; ++j) {
+              const float2 s2 = j == pr ? make_float2(w_mean, w_m2) : sStat[(su * NG + j) * RBM + trow];
+              pm[j] = s2.x;
+              pq[j] = s2.y;
+            }
+            float s = 0.f;
+  #pragma unroll
+            for (int j = 0; j < NG; ++j) s += pm[j];
+            mean = s * (1.f / NG);
+            m2 = 0.f;
+  #pragma unroll
+            for (int j = 0; j < NG; ++j) {
+              const float d = pm[j] - mean;
+              m2 += pq[j] + static_cast<float>(BN) * d * d;
+            }
+          }
+          const float rstd = rsqrtf(m2 * (1.f / static_cast<float>(H)) + p.ln_eps);
+          // ---------------- pass 2: normalise from TMEM, BF16 boxes of this warp's rows out by TMA
+          // (two chunks per 64-column box; the next chunk's TMEM load overlaps this one)
+          const uint64_t nmean = f2pack(-mean, -mean), rs2 = f2pack(rstd, rstd);
+          auto pass2_chunk = [&](int c, uint32_t (&r)[32], uint32_t (&rn)[32]) {
+            const int h = c & 1;
+            uint8_t* box = sO + (q * 2 + ob) * RO_WBOX;
+            uint8_t* srow = box + lane * 128;
+            tmem_ld_wait();  // chunk c's updated row is in r
+            if (c + 1 < NCH) tmem_ld32(tb + (c + 1) * 32, rn);
+            float y[32];
+  #pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const float4 g = parw[c * 8 + i], be = parb[c * 8 + i];
+              // y = ((x - mean) * rstd) * g + be, pairs of columns at once
+              const uint64_t t0 = mul2(add2(f2pack(__uint_as_float(r[4 * i + 0]), __uint_as_float(r[4 * i + 1])), nmean), rs2);
+              const uint64_t t1 = mul2(add2(f2pack(__uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3])), nmean), rs2);
+              f2unpack(fma2(t0, f2pack(g.x, g.y), f2pack(be.x, be.y)), y[4 * i + 0], y[4 * i + 1]);
+              f2unpack(fma2(t1, f2pack(g.z, g.w), f2pack(be.z, be.w)), y[4 * i + 2], y[4 * i + 3]);
+            }
+  #pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              uint4 w;
+              w.x = pack_bf16x2(y[8 * i + 0], y[8 * i + 1]);
+              w.y = pack_bf16x2(y[8 * i + 2], y[8 * i + 3]);
+              w.z = pack_bf16x2(y[8 * i + 4], y[8 * i + 5]);
+              w.w = pack_bf16x2(y[8 * i + 6], y[8 * i + 7]);
+              *reinterpret_cast<uint4*>(srow + ((static_cast<uint32_t>(4 * h + i) ^ (lane & 7)) << 4)) = w;
+            }
+            if (h == 1) {
+              fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) {
+                if (!*abort_flag) {
+                  tma_store_2d(&tmXN, box, col0 + (c >> 1) * 64, m0 + q * 32);
+                  bulk_commit();
+                }
+                bulk_wait_read_1();  // the other box's store has read it: it can be rewritten next
+              }
+              __syncwarp();
+              ob ^= 1;
+            }
+          };
+          {
+            uint32_t ra[32], rb[32];
+            tmem_ld32(tb, ra);
+  #pragma unroll 1
+            for (int c = 0; c < NCH; c += 2) {
+              pass2_chunk(c, ra, rb);
+              pass2_chunk(c + 1, rb, ra);
+            }
+          }
+        }
+        // this warp has read its lanes of the buffer: release it to the pair's MMA
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&tempty[buf]), lead));
       }
-      // this warp has read its lanes of the buffer: release it to the pair's MMA
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&tempty[buf]), lead));
+      if (lane == 0) bulk_wait_all();  // every store complete: this kernel's x and xn are in memory
     }
-    if (lane == 0) bulk_wait_all();  // every store complete: this kernel's x and xn are in memory
   }
 
   tc_fence_before();
@@ -508,17 +734,48 @@ __global__ void __launch_bounds__(256, 1)
   if (warp == 1) tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
 }
 
-template <int NG, int BN, bool LN>
-int launch_rln(const CUtensorMap& tmA, const CUtensorMap& tmW, const CUtensorMap& tmX, const CUtensorMap& tmXs,
-               const CUtensorMap& tmXN, const EpiParams& p, int grid_limit, cudaStream_t stream) {
-  using C = RlnCfg<NG, BN>;
+// Sets the kernel's shared-memory limit on the device (once) and returns how many of its
+// clusters fit on the device at once (clusters of more than two CTAs cannot always use every
+// SM: a cluster lives inside one GPC), cached per device. The limit must be set first: the
+// occupancy query counts the kernel's dynamic shared memory against it.
+template <int NG, int BN, bool LN, int EW>
+int rln_max_clusters(int dev, cudaError_t* err) {
+  using C = RlnCfg<NG, BN, EW>;
   static std::atomic<unsigned long long> configured{0};
   static std::atomic<int> max_clusters[64];
-  auto kern = resid_ln_kernel<NG, BN, LN>;
-  cudaError_t e = set_smem_once(kern, C::SMEM, configured);
+  *err = set_smem_once(resid_ln_kernel<NG, BN, LN, EW>, C::SMEM, configured);
+  if (*err != cudaSuccess) return 0;
+  int mc = (dev >= 0 && dev < 64) ? max_clusters[dev].load() : 0;
+  if (mc > 0) return mc;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = C::CS;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(C::THREADS);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cfg.gridDim = dim3(C::CS * 64);
+  if (cudaOccupancyMaxActiveClusters(&mc, resid_ln_kernel<NG, BN, LN, EW>, &cfg) != cudaSuccess || mc <= 0) {
+    (void)cudaGetLastError();
+    int sms = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    mc = sms / C::CS;
+  }
+  if (dev >= 0 && dev < 64) max_clusters[dev].store(mc);
+  return mc;
+}
+
+template <int NG, int BN, bool LN, int EW>
+int launch_rln_ew(const CUtensorMap& tmA, const CUtensorMap& tmW, const CUtensorMap& tmX, const CUtensorMap& tmXs,
+                  const CUtensorMap& tmXN, const EpiParams& p, int grid_limit, int dev, cudaStream_t stream) {
+  using C = RlnCfg<NG, BN, EW>;
+  auto kern = resid_ln_kernel<NG, BN, LN, EW>;
+  cudaError_t e = cudaSuccess;
+  const int mc = rln_max_clusters<NG, BN, LN, EW>(dev, &e);
   if (e != cudaSuccess) return static_cast<int>(e);
-  int dev = 0;
-  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return static_cast<int>(e);
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -531,20 +788,6 @@ int launch_rln(const CUtensorMap& tmA, const CUtensorMap& tmW, const CUtensorMap
   cfg.dynamicSmemBytes = C::SMEM;
   cfg.stream = stream;
   cfg.attrs = attr;
-  // clusters that fit on the device at once (clusters of more than two CTAs cannot always
-  // use every SM: a cluster lives inside one GPC)
-  int mc = (dev >= 0 && dev < 64) ? max_clusters[dev].load() : 0;
-  if (mc <= 0) {
-    cfg.gridDim = dim3(C::CS * 64);
-    cfg.numAttrs = 1;
-    if (cudaOccupancyMaxActiveClusters(&mc, kern, &cfg) != cudaSuccess || mc <= 0) {
-      (void)cudaGetLastError();
-      int sms = 0;
-      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-      mc = sms / C::CS;
-    }
-    if (dev >= 0 && dev < 64) max_clusters[dev].store(mc);
-  }
   cfg.numAttrs = 2;
   const int units = (p.M + 2 * RBM - 1) / (2 * RBM);
   int ncl = units < mc ? units : mc;
@@ -553,6 +796,21 @@ int launch_rln(const CUtensorMap& tmA, const CUtensorMap& tmW, const CUtensorMap
   if (ncl <= 0) return 0;
   cfg.gridDim = dim3(C::CS * ncl);
   return static_cast<int>(cudaLaunchKernelEx(&cfg, kern, tmA, tmW, tmX, tmXs, tmXN, p));
+}
+
+template <int NG, int BN, bool LN>
+int launch_rln(const CUtensorMap& tmA, const CUtensorMap& tmW, const CUtensorMap& tmX, const CUtensorMap& tmXs,
+               const CUtensorMap& tmXN, const EpiParams& p, int grid_limit, cudaStream_t stream) {
+  int dev = 0;
+  const cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  const int units = (p.M + 2 * RBM - 1) / (2 * RBM);
+  cudaError_t e4 = cudaSuccess;
+  const int mc = rln_max_clusters<NG, BN, LN, 4>(dev, &e4);
+  if (e4 != cudaSuccess) return static_cast<int>(e4);
+  if (units <= J1_RLN_SMALL_UNITS * mc)
+    return launch_rln_ew<NG, BN, LN, 8>(tmA, tmW, tmX, tmXs, tmXN, p, grid_limit, dev, stream);
+  return launch_rln_ew<NG, BN, LN, 4>(tmA, tmW, tmX, tmXs, tmXN, p, grid_limit, dev, stream);
 }
 
 template <bool LN>
