@@ -336,179 +336,253 @@ __global__ void __launch_bounds__(128 + EW * 32, 1)
       }
     }
   } else if (warp >= 4) {
-    if constexpr (EW == 8) {
-      // ------------------------------------------------------------ epilogue (warps 4..11)
-      // Two warps per TMEM lane quarter: warp (q, hf) owns the quarter's 32 rows and the
-      // residual chunks c with c % 2 == hf, then the xn boxes with box % 2 == hf. With one warp
-      // per SM sub-partition this loop was latency-bound; two warps interleave. Each warp stores
-      // its rows of its chunks and boxes itself (32-row TMA boxes); the two warps of a quarter
-      // meet once per unit (a 64-thread named barrier) to merge their halves of the row
-      // statistics. After an abort every wait returns at once and the loops run out without
-      // stores.
-      const int q = warp & 3;          // TMEM lane quarter this warp may access
-      const int hf = (warp - 4) >> 2;  // 0: even chunks and boxes, 1: odd ones
-      const int trow = q * 32 + lane;
-      {  // this CTA's columns of ln_w, ln_b and bias, once
-        const int et = threadIdx.x - 128;
-        for (int j = et; j < BN; j += EW * 32) {
-          sPar[j] = LN ? p.ln_w[col0 + j] : 0.f;
-          sPar[BN + j] = (LN && p.ln_b) ? p.ln_b[col0 + j] : 0.f;
-          sPar[2 * BN + j] = p.bias ? p.bias[col0 + j] : 0.f;
-        }
-        named_bar_sync(1, EW * 32);
+    // ------------------------------------------------------------ epilogue (warps 4 .. 3 + EW)
+    // One thread per row (its TMEM lane). With four warps, warp q owns lane quarter q and every
+    // chunk and xn box of its 32 rows; with eight, warps (q, 0) and (q, 1) share the quarter's
+    // rows, warp (q, h) taking chunks [h NCH/2, (h + 1) NCH/2) and the boxes over them, and the
+    // two meet once per unit (a 64-thread named barrier) around the merge of the row
+    // statistics. Each warp stores its own 32 rows of its chunks and boxes (32-row TMA boxes).
+    // After an abort every wait returns at once and the loops run out without stores.
+    constexpr int NH = EW / 4;     // warps per TMEM lane quarter
+    constexpr int CPW = NCH / NH;  // residual chunks per warp and unit
+    const int q = warp & 3;        // TMEM lane quarter this warp may access
+    const int hf = (warp - 4) >> 2;
+    const int trow = q * 32 + lane;
+    {  // this CTA's columns of ln_w, ln_b and bias, once
+      const int et = threadIdx.x - 128;
+      for (int j = et; j < BN; j += EW * 32) {
+        sPar[j] = LN ? p.ln_w[col0 + j] : 0.f;
+        sPar[BN + j] = (LN && p.ln_b) ? p.ln_b[col0 + j] : 0.f;
+        sPar[2 * BN + j] = p.bias ? p.bias[col0 + j] : 0.f;
       }
-      const float4* parw = reinterpret_cast<const float4*>(sPar);
-      const float4* parb = reinterpret_cast<const float4*>(sPar + BN);
-      const float4* parc = reinterpret_cast<const float4*>(sPar + 2 * BN);
-      uint8_t* box = sO + (warp - 4) * RO_WBOX;  // this warp's xn box (32 rows x 64 columns)
-      uint8_t* srow = box + lane * 128;
-      int acc = 0;
-      int xpend = -1;  // ring slot whose store (of this warp's rows) may still be reading smem
-      for (int u = cid; u < units; u += ncl, ++acc) {
-        const int m0 = u * 2 * RBM + static_cast<int>(half) * RBM;
-        const int buf = acc & 1;
-        mbar_wait<true>(&tfull[buf], (acc >> 1) & 1, abort_flag, p.err, 35);
-        tc_fence_after();
-        const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
-        // ---------------- pass 1: residual update (this warp's half of the chunks)
-  #pragma unroll 1
-        for (int c = hf * (NCH / 2); c < (hf + 1) * (NCH / 2); ++c) {
-          const uint32_t g = static_cast<uint32_t>(acc * NCH + c);  // chunk in this CTA's x stream
-          const uint32_t b = g % C::NX;
+      named_bar_sync(1, EW * 32);
+    }
+    const float4* parw = reinterpret_cast<const float4*>(sPar);
+    const float4* parb = reinterpret_cast<const float4*>(sPar + BN);
+    const float4* parc = reinterpret_cast<const float4*>(sPar + 2 * BN);
+    // x += bf16(acc) (+ bias) for chunk c of this row, in place in its x slot. The chunk's eight
+    // 16-byte units of the row (unit i at (i ^ (row & 7)) * 16) are all read before any is
+    // written back: written in place through a data-dependent swizzle, they could not be
+    // reordered otherwise.
+    auto update_x = [&](int c, const uint32_t (&r)[32], uint8_t* xrow, float (&v)[32]) {
+      float4 o[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        o[i] = *reinterpret_cast<const float4*>(xrow + ((static_cast<uint32_t>(i) ^ (trow & 7)) << 4));
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float d0 = __uint_as_float(r[4 * i + 0]), d1 = __uint_as_float(r[4 * i + 1]);
+        float d2 = __uint_as_float(r[4 * i + 2]), d3 = __uint_as_float(r[4 * i + 3]);
+        bf16_round2(d0, d1);  // delta = bf16(A . W^T), as the reference's GEMM output
+        bf16_round2(d2, d3);
+        uint64_t lo = add2(f2pack(o[i].x, o[i].y), f2pack(d0, d1));
+        uint64_t hi = add2(f2pack(o[i].z, o[i].w), f2pack(d2, d3));
+        if (p.bias) {  // the bias after the delta
+          const float4 bb = parc[c * 8 + i];
+          lo = add2(lo, f2pack(bb.x, bb.y));
+          hi = add2(hi, f2pack(bb.z, bb.w));
+        }
+        f2unpack(lo, v[4 * i + 0], v[4 * i + 1]);
+        f2unpack(hi, v[4 * i + 2], v[4 * i + 3]);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        *reinterpret_cast<float4*>(xrow + ((static_cast<uint32_t>(i) ^ (trow & 7)) << 4)) =
+            make_float4(v[4 * i + 0], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    };
+    // After update_x (and the TMEM store of the updated row): the warp's 32 rows of the chunk
+    // leave by TMA store; lane 0 releases the slot of the warp's previous chunk once its store
+    // has read it.
+    int xpend = -1;  // ring slot whose store (of this warp's rows) may still be reading smem
+    auto store_x = [&](uint32_t b, int c, int m0) {
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        if (!*abort_flag) {
+          tma_store_2d(&tmXs, sX + b * RX_CHUNK + q * 32 * 128, col0 + c * 32, m0 + q * 32);
+          bulk_commit();
+        }
+        bulk_wait_read_1();
+        if (xpend >= 0) mbar_arrive(&xempty[xpend]);
+        xpend = static_cast<int>(b);
+      }
+      __syncwarp();
+    };
+    // The row's (mean, rstd) over all H columns from its (mean, M2) over this CTA's BN: the
+    // row's statistics go to the NG - 1 CTAs holding the same rows in the other pairs by
+    // st.async (one warp per lane quarter sends), and every CTA merges the NG partials in pair
+    // order, so all of them normalise with the same mean and rstd.
+    auto row_stats = [&](float w_mean, float w_m2, int acc) -> float2 {
+      float mean = w_mean, m2 = w_m2;
+      if constexpr (NG > 1) {
+        const int su = acc & 1;
+        float2* mine = sStat + (su * NG + pr) * RBM + trow;
+        const uint32_t bar_local = smem_u32(&statbar[su]);
+        if (hf == 0)
+          for (int j = 0; j < NG; ++j)
+            if (j != pr) {
+              const uint32_t dst = static_cast<uint32_t>(2 * j) + half;  // same rows, pair j
+              st_async_f2(mapa_shared(smem_u32(mine), dst), w_mean, w_m2, mapa_shared(bar_local, dst));
+            }
+        if (trow == 0 && hf == 0) mbar_arrive_expect_tx(&statbar[su], (NG - 1) * RBM * 8);
+        mbar_wait<true>(&statbar[su], (acc >> 1) & 1, abort_flag, p.err, 37);
+        float pm[NG], pq[NG];
+#pragma unroll
+        for (int j = 0; j < NG; ++j) {
+          const float2 st = j == pr ? make_float2(w_mean, w_m2) : sStat[(su * NG + j) * RBM + trow];
+          pm[j] = st.x;
+          pq[j] = st.y;
+        }
+        float s = 0.f;
+#pragma unroll
+        for (int j = 0; j < NG; ++j) s += pm[j];
+        mean = s * (1.f / NG);
+        m2 = 0.f;
+#pragma unroll
+        for (int j = 0; j < NG; ++j) {
+          const float d = pm[j] - mean;
+          m2 += pq[j] + static_cast<float>(BN) * d * d;
+        }
+      }
+      return make_float2(mean, rsqrtf(m2 * (1.f / static_cast<float>(H)) + p.ln_eps));
+    };
+    // y = ((x - mean) * rstd) * g + be for chunk c of the row, pairs of columns at once, as
+    // four 16-byte units of BF16
+    auto norm32 = [&](int c, const uint32_t (&r)[32], uint64_t nmean, uint64_t rs2, uint4* out) {
+      float y[32];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 gw = parw[c * 8 + i], be = parb[c * 8 + i];
+        const uint64_t t0 = mul2(add2(f2pack(__uint_as_float(r[4 * i + 0]), __uint_as_float(r[4 * i + 1])), nmean), rs2);
+        const uint64_t t1 = mul2(add2(f2pack(__uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3])), nmean), rs2);
+        f2unpack(fma2(t0, f2pack(gw.x, gw.y), f2pack(be.x, be.y)), y[4 * i + 0], y[4 * i + 1]);
+        f2unpack(fma2(t1, f2pack(gw.z, gw.w), f2pack(be.z, be.w)), y[4 * i + 2], y[4 * i + 3]);
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        out[i].x = pack_bf16x2(y[8 * i + 0], y[8 * i + 1]);
+        out[i].y = pack_bf16x2(y[8 * i + 2], y[8 * i + 3]);
+        out[i].z = pack_bf16x2(y[8 * i + 4], y[8 * i + 5]);
+        out[i].w = pack_bf16x2(y[8 * i + 6], y[8 * i + 7]);
+      }
+    };
+    int ob = 0;  // four warps: this warp's xn box in use (of two)
+    int acc = 0;
+    for (int u = cid; u < units; u += ncl, ++acc) {
+      const int m0 = u * 2 * RBM + static_cast<int>(half) * RBM;
+      const int buf = acc & 1;
+      mbar_wait<true>(&tfull[buf], (acc >> 1) & 1, abort_flag, p.err, 35);
+      tc_fence_after();
+      const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
+      // ---------------- pass 1: residual update of this warp's chunks; each chunk's (mean, M2)
+      // goes to shared memory for the merge
+      auto pass1_chunk = [&](int c, const uint32_t (&r)[32]) {
+        const uint32_t g = static_cast<uint32_t>(acc * NCH + c);  // chunk in this CTA's x stream
+        const uint32_t b = g % C::NX;
+        mbar_wait<true>(&xfull[b], (g / C::NX) & 1, abort_flag, p.err, 36);
+        float v[32];
+        update_x(c, r, sX + b * RX_CHUNK + trow * 128, v);
+        if constexpr (LN) {
+          uint32_t vv[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) vv[j] = __float_as_uint(v[j]);
+          tmem_st32(tb + c * 32, vv);  // the updated row stays on chip for pass 2
+          sChunk[c * RBM + trow] = chunk_stats(v);
+        }
+        store_x(b, c, m0);
+      };
+      if constexpr (NH == 1) {
+        // one warp per SM sub-partition: the next chunk's accumulator columns are loaded from
+        // TMEM while this chunk is processed
+        uint32_t ra[32], rb[32];
+        tmem_ld32(tb, ra);
+        static_assert(NCH % 2 == 0, "chunks are processed in pairs");
+#pragma unroll 1
+        for (int c = 0; c < NCH; c += 2) {
+          tmem_ld_wait();
+          tmem_ld32(tb + (c + 1) * 32, rb);
+          pass1_chunk(c, ra);
+          tmem_ld_wait();
+          if (c + 2 < NCH) tmem_ld32(tb + (c + 2) * 32, ra);
+          pass1_chunk(c + 1, rb);
+        }
+      } else {
+#pragma unroll 1
+        for (int c = hf * CPW; c < (hf + 1) * CPW; ++c) {
           uint32_t r[32];
           tmem_ld32(tb + c * 32, r);
           tmem_ld_wait();
-          mbar_wait<true>(&xfull[b], (g / C::NX) & 1, abort_flag, p.err, 36);
-          // the chunk's eight 16-byte slots of this row are all read before any is written back
-          // (in place, through a data-dependent swizzle, they could not be reordered otherwise)
-          uint8_t* xrow = sX + b * RX_CHUNK + trow * 128;  // 16-byte unit i at (i ^ (row & 7)) * 16
-          float4 o[8];
-  #pragma unroll
-          for (int i = 0; i < 8; ++i)
-            o[i] = *reinterpret_cast<const float4*>(xrow + ((static_cast<uint32_t>(i) ^ (trow & 7)) << 4));
-          float v[32];
-  #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            float d0 = __uint_as_float(r[4 * i + 0]), d1 = __uint_as_float(r[4 * i + 1]);
-            float d2 = __uint_as_float(r[4 * i + 2]), d3 = __uint_as_float(r[4 * i + 3]);
-            bf16_round2(d0, d1);  // delta = bf16(A . W^T), as the reference's GEMM output
-            bf16_round2(d2, d3);
-            uint64_t lo = add2(f2pack(o[i].x, o[i].y), f2pack(d0, d1));
-            uint64_t hi = add2(f2pack(o[i].z, o[i].w), f2pack(d2, d3));
-            if (p.bias) {  // the bias after the delta
-              const float4 bb = parc[c * 8 + i];
-              lo = add2(lo, f2pack(bb.x, bb.y));
-              hi = add2(hi, f2pack(bb.z, bb.w));
-            }
-            f2unpack(lo, v[4 * i + 0], v[4 * i + 1]);
-            f2unpack(hi, v[4 * i + 2], v[4 * i + 3]);
-          }
-  #pragma unroll
-          for (int i = 0; i < 8; ++i)
-            *reinterpret_cast<float4*>(xrow + ((static_cast<uint32_t>(i) ^ (trow & 7)) << 4)) =
-                make_float4(v[4 * i + 0], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-          if constexpr (LN) {
-            uint32_t vv[32];
-  #pragma unroll
-            for (int j = 0; j < 32; ++j) vv[j] = __float_as_uint(v[j]);
-            tmem_st32(tb + c * 32, vv);  // the updated row stays on chip for pass 2
-            sChunk[c * RBM + trow] = chunk_stats(v);
-          }
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            if (!*abort_flag) {
-              tma_store_2d(&tmXs, sX + b * RX_CHUNK + q * 32 * 128, col0 + c * 32, m0 + q * 32);
-              bulk_commit();
-            }
-            bulk_wait_read_1();  // this warp's previous chunk store has read its slot: release it
-            if (xpend >= 0) mbar_arrive(&xempty[xpend]);
-            xpend = static_cast<int>(b);
-          }
-          __syncwarp();
+          pass1_chunk(c, r);
         }
-        if (lane == 0) {  // the unit's last chunk: release its slot once the store has read it
-          bulk_wait_read_all();
-          if (xpend >= 0) mbar_arrive(&xempty[xpend]);
-          xpend = -1;
-        }
-        if constexpr (LN) {
-          tmem_st_wait();
-          // ---------------- row statistics: the chunks of both warps of the quarter, merged
-          // in the fixed tree (the same bits as with four epilogue warps); the second barrier
-          // keeps either warp from overwriting the chunk statistics in the next unit before
-          // the other has read them
-          named_bar_sync(2 + q, 64);
-          const float2 ws = merge_chunks<NCH>(sChunk, trow);
-          named_bar_sync(2 + q, 64);
-          const float w_mean = ws.x, w_m2 = ws.y;  // mean and M2 of the row's BN columns in this CTA
-          // ---------------- row statistics over the pairs of the cluster
-          const int su = acc & 1;
-          float mean = w_mean, m2 = w_m2;
-          if constexpr (NG > 1) {
-            float2* mine = sStat + (su * NG + pr) * RBM + trow;
-            const uint32_t bar_local = smem_u32(&statbar[su]);
-            if (hf == 0)
-              for (int j = 0; j < NG; ++j)
-                if (j != pr) {
-                  const uint32_t dst = static_cast<uint32_t>(2 * j) + half;  // same rows, pair j
-                  st_async_f2(mapa_shared(smem_u32(mine), dst), w_mean, w_m2, mapa_shared(bar_local, dst));
-                }
-            if (trow == 0 && hf == 0) mbar_arrive_expect_tx(&statbar[su], (NG - 1) * RBM * 8);
-            mbar_wait<true>(&statbar[su], (acc >> 1) & 1, abort_flag, p.err, 37);
-            float pm[NG], pq[NG];
-  #pragma unroll
-            for (int j = 0; j < NG; ++j) {
-              const float2 st = j == pr ? make_float2(w_mean, w_m2) : sStat[(su * NG + j) * RBM + trow];
-              pm[j] = st.x;
-              pq[j] = st.y;
+      }
+      if (lane == 0) {  // the warp's last chunk of the unit: release its slot once the store has read it
+        bulk_wait_read_all();
+        if (xpend >= 0) mbar_arrive(&xempty[xpend]);
+        xpend = -1;
+      }
+      if constexpr (LN) {
+        tmem_st_wait();
+        // ---------------- row statistics: the row's chunk statistics merged in the fixed tree
+        // (the same bits with four or eight warps); with eight, the barriers make both warps'
+        // chunks visible before the merge and keep either warp from overwriting them in the
+        // next unit before the other has read them
+        if constexpr (NH == 2) named_bar_sync(2 + q, 64);
+        const float2 ws = merge_chunks<NCH>(sChunk, trow);
+        if constexpr (NH == 2) named_bar_sync(2 + q, 64);
+        const float2 mr = row_stats(ws.x, ws.y, acc);
+        const uint64_t nmean = f2pack(-mr.x, -mr.x), rs2 = f2pack(mr.y, mr.y);
+        // ---------------- pass 2: normalise from TMEM; BF16 boxes of 64 columns (two chunks)
+        // of this warp's rows out by TMA
+        if constexpr (NH == 1) {
+          // two box buffers in turn; the next chunk's TMEM load overlaps this one
+          uint32_t ra[32], rb[32];
+          tmem_ld32(tb, ra);
+#pragma unroll 1
+          for (int c = 0; c < NCH; c += 2) {
+            uint8_t* box = sO + (q * 2 + ob) * RO_WBOX;
+            uint8_t* srow = box + lane * 128;
+            uint4 w[4];
+            tmem_ld_wait();
+            tmem_ld32(tb + (c + 1) * 32, rb);
+            norm32(c, ra, nmean, rs2, w);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              *reinterpret_cast<uint4*>(srow + ((static_cast<uint32_t>(i) ^ (lane & 7)) << 4)) = w[i];
+            tmem_ld_wait();
+            if (c + 2 < NCH) tmem_ld32(tb + (c + 2) * 32, ra);
+            norm32(c + 1, rb, nmean, rs2, w);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              *reinterpret_cast<uint4*>(srow + ((static_cast<uint32_t>(4 + i) ^ (lane & 7)) << 4)) = w[i];
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              if (!*abort_flag) {
+                tma_store_2d(&tmXN, box, col0 + (c >> 1) * 64, m0 + q * 32);
+                bulk_commit();
+              }
+              bulk_wait_read_1();  // the other box's store has read it: it can be rewritten next
             }
-            float s = 0.f;
-  #pragma unroll
-            for (int j = 0; j < NG; ++j) s += pm[j];
-            mean = s * (1.f / NG);
-            m2 = 0.f;
-  #pragma unroll
-            for (int j = 0; j < NG; ++j) {
-              const float d = pm[j] - mean;
-              m2 += pq[j] + static_cast<float>(BN) * d * d;
-            }
+            __syncwarp();
+            ob ^= 1;
           }
-          const float rstd = rsqrtf(m2 * (1.f / static_cast<float>(H)) + p.ln_eps);
-          // ---------------- pass 2: normalise from TMEM; this warp's boxes (64 columns, two
-          // chunks each) go out by TMA from its one box buffer
-          const uint64_t nmean = f2pack(-mean, -mean), rs2 = f2pack(rstd, rstd);
-  #pragma unroll 1
-          for (int bx = hf * (NCH / 4); bx < (hf + 1) * (NCH / 4); ++bx) {
+        } else {
+          // one box buffer per warp: a box's two chunks are normalised before the previous
+          // store of the buffer must have read it
+          uint8_t* box = sO + (warp - 4) * RO_WBOX;
+          uint8_t* srow = box + lane * 128;
+#pragma unroll 1
+          for (int bx = hf * (CPW / 2); bx < (hf + 1) * (CPW / 2); ++bx) {
             uint32_t ra[32], rb[32];
             tmem_ld32(tb + (2 * bx) * 32, ra);
             tmem_ld32(tb + (2 * bx + 1) * 32, rb);
             tmem_ld_wait();
             uint4 w[8];
-            auto norm32 = [&](int c, const uint32_t (&r)[32], uint4* out) {
-              float y[32];
-  #pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                const float4 gw = parw[c * 8 + i], be = parb[c * 8 + i];
-                // y = ((x - mean) * rstd) * g + be, pairs of columns at once
-                const uint64_t t0 = mul2(add2(f2pack(__uint_as_float(r[4 * i + 0]), __uint_as_float(r[4 * i + 1])), nmean), rs2);
-                const uint64_t t1 = mul2(add2(f2pack(__uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3])), nmean), rs2);
-                f2unpack(fma2(t0, f2pack(gw.x, gw.y), f2pack(be.x, be.y)), y[4 * i + 0], y[4 * i + 1]);
-                f2unpack(fma2(t1, f2pack(gw.z, gw.w), f2pack(be.z, be.w)), y[4 * i + 2], y[4 * i + 3]);
-              }
-  #pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                out[i].x = pack_bf16x2(y[8 * i + 0], y[8 * i + 1]);
-                out[i].y = pack_bf16x2(y[8 * i + 2], y[8 * i + 3]);
-                out[i].z = pack_bf16x2(y[8 * i + 4], y[8 * i + 5]);
-                out[i].w = pack_bf16x2(y[8 * i + 6], y[8 * i + 7]);
-              }
-            };
-            norm32(2 * bx, ra, w);
-            norm32(2 * bx + 1, rb, w + 4);
-            if (lane == 0) bulk_wait_read_all();  // the box's previous store has read it
+            norm32(2 * bx, ra, nmean, rs2, w);
+            norm32(2 * bx + 1, rb, nmean, rs2, w + 4);
+            if (lane == 0) bulk_wait_read_all();
             __syncwarp();
-  #pragma unroll
+#pragma unroll
             for (int i = 0; i < 8; ++i)
               *reinterpret_cast<uint4*>(srow + ((static_cast<uint32_t>(i) ^ (lane & 7)) << 4)) = w[i];
             fence_proxy_async_smem();
@@ -520,210 +594,13 @@ __global__ void __launch_bounds__(128 + EW * 32, 1)
             __syncwarp();
           }
         }
-        // this warp has read its lanes of the buffer: release it to the pair's MMA
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&tempty[buf]), lead));
       }
-      if (lane == 0) bulk_wait_all();  // every store complete: this kernel's x and xn are in memory
-    } else {
-      // ------------------------------------------------------------ epilogue (warps 4..7)
-      // Each warp owns 32 rows (its TMEM lane quarter) and works through the units on its own:
-      // it stores its rows of every residual chunk and every xn box itself (32-row TMA boxes),
-      // so no barrier couples the four warps. After an abort every wait returns at once and
-      // the loops run out without stores.
-      const int q = warp & 3;  // TMEM lane quarter this warp may access
-      const int trow = q * 32 + lane;
-      {  // this CTA's columns of ln_w, ln_b and bias, once
-        const int et = threadIdx.x - 128;
-        for (int j = et; j < BN; j += 128) {
-          sPar[j] = LN ? p.ln_w[col0 + j] : 0.f;
-          sPar[BN + j] = (LN && p.ln_b) ? p.ln_b[col0 + j] : 0.f;
-          sPar[2 * BN + j] = p.bias ? p.bias[col0 + j] : 0.f;
-        }
-        named_bar_sync(1, 128);
-      }
-      const float4* parw = reinterpret_cast<const float4*>(sPar);
-      const float4* parb = reinterpret_cast<const float4*>(sPar + BN);
-      const float4* parc = reinterpret_cast<const float4*>(sPar + 2 * BN);
-      int acc = 0;
-      uint32_t gch = 0;  // residual chunks consumed so far
-      int xpend = -1;    // ring slot whose store (of this warp's rows) may still be reading smem
-      int ob = 0;        // this warp's xn box in use (of two)
-      for (int u = cid; u < units; u += ncl, ++acc) {
-        const int m0 = u * 2 * RBM + static_cast<int>(half) * RBM;
-        const int buf = acc & 1;
-        mbar_wait<true>(&tfull[buf], (acc >> 1) & 1, abort_flag, p.err, 35);
-        tc_fence_after();
-        const uint32_t tb = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
-        // ---------------- pass 1: residual update
-        // One warp per SM sub-partition runs this loop, so latency is what it costs: the next
-        // chunk's accumulator columns are loaded from TMEM while this chunk is processed, and
-        // the chunk's eight 16-byte slots are all read before any is written back (written in
-        // place through a data-dependent swizzle, they could not be reordered otherwise).
-        auto pass1_chunk = [&](int c, uint32_t (&r)[32], uint32_t (&rn)[32]) {
-          const uint32_t b = gch % C::NX;
-          tmem_ld_wait();  // chunk c's accumulator is in r
-          if (c + 1 < NCH) tmem_ld32(tb + (c + 1) * 32, rn);
-          mbar_wait<true>(&xfull[b], (gch / C::NX) & 1, abort_flag, p.err, 36);
-          uint8_t* xrow = sX + b * RX_CHUNK + trow * 128;  // 16-byte unit i at (i ^ (row & 7)) * 16
-          float4 o[8];
-  #pragma unroll
-          for (int i = 0; i < 8; ++i)
-            o[i] = *reinterpret_cast<const float4*>(xrow + ((static_cast<uint32_t>(i) ^ (trow & 7)) << 4));
-          float v[32];
-  #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            float d0 = __uint_as_float(r[4 * i + 0]), d1 = __uint_as_float(r[4 * i + 1]);
-            float d2 = __uint_as_float(r[4 * i + 2]), d3 = __uint_as_float(r[4 * i + 3]);
-            bf16_round2(d0, d1);  // delta = bf16(A . W^T), as the reference's GEMM output
-            bf16_round2(d2, d3);
-            uint64_t lo = add2(f2pack(o[i].x, o[i].y), f2pack(d0, d1));
-            uint64_t hi = add2(f2pack(o[i].z, o[i].w), f2pack(d2, d3));
-            if (p.bias) {  // the bias after the delta
-              const float4 bb = parc[c * 8 + i];
-              lo = add2(lo, f2pack(bb.x, bb.y));
-              hi = add2(hi, f2pack(bb.z, bb.w));
-            }
-            f2unpack(lo, v[4 * i + 0], v[4 * i + 1]);
-            f2unpack(hi, v[4 * i + 2], v[4 * i + 3]);
-          }
-  #pragma unroll
-          for (int i = 0; i < 8; ++i)
-            *reinterpret_cast<float4*>(xrow + ((static_cast<uint32_t>(i) ^ (trow & 7)) << 4)) =
-                make_float4(v[4 * i + 0], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-          if constexpr (LN) {
-            uint32_t vv[32];
-  #pragma unroll
-            for (int j = 0; j < 32; ++j) vv[j] = __float_as_uint(v[j]);
-            tmem_st32(tb + c * 32, vv);  // the updated row stays on chip for pass 2
-            sChunk[c * RBM + trow] = chunk_stats(v);
-          }
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            if (!*abort_flag) {
-              tma_store_2d(&tmXs, sX + b * RX_CHUNK + q * 32 * 128, col0 + c * 32, m0 + q * 32);
-              bulk_commit();
-            }
-            bulk_wait_read_1();  // this warp's previous chunk store has read its slot: release it
-            if (xpend >= 0) mbar_arrive(&xempty[xpend]);
-            xpend = static_cast<int>(b);
-          }
-          __syncwarp();
-          ++gch;
-        };
-        {
-          uint32_t ra[32], rb[32];
-          tmem_ld32(tb, ra);
-          static_assert(NCH % 2 == 0, "chunks are processed in pairs");
-  #pragma unroll 1
-          for (int c = 0; c < NCH; c += 2) {
-            pass1_chunk(c, ra, rb);
-            pass1_chunk(c + 1, rb, ra);
-          }
-        }
-        if (lane == 0) {  // the unit's last chunk: release its slot once the store has read it
-          bulk_wait_read_all();
-          if (xpend >= 0) mbar_arrive(&xempty[xpend]);
-          xpend = -1;
-        }
-        if constexpr (LN) {
-          tmem_st_wait();
-          // the row's chunk statistics merged in the fixed tree (this thread wrote them)
-          const float2 ws = merge_chunks<NCH>(sChunk, trow);
-          const float w_mean = ws.x, w_m2 = ws.y;  // mean and M2 of the row's BN columns in this CTA
-          // ---------------- row statistics over the pairs of the cluster
-          const int su = acc & 1;
-          float mean = w_mean, m2 = w_m2;
-          if constexpr (NG > 1) {
-            float2* mine = sStat + (su * NG + pr) * RBM + trow;
-            const uint32_t bar_local = smem_u32(&statbar[su]);
-            for (int j = 0; j < NG; ++j)
-              if (j != pr) {
-                const uint32_t dst = static_cast<uint32_t>(2 * j) + half;  // same rows, pair j
-                st_async_f2(mapa_shared(smem_u32(mine), dst), w_mean, w_m2, mapa_shared(bar_local, dst));
-              }
-            if (trow == 0) mbar_arrive_expect_tx(&statbar[su], (NG - 1) * RBM * 8);
-            mbar_wait<true>(&statbar[su], (acc >> 1) & 1, abort_flag, p.err, 37);
-            float pm[NG], pq[NG];
-  #pragma unroll
-            for (int j = 0; j < NG; ++j) {
-              const float2 s2 = j == pr ? make_float2(w_mean, w_m2) : sStat[(su * NG + j) * RBM + trow];
-              pm[j] = s2.x;
-              pq[j] = s2.y;
-            }
-            float s = 0.f;
-  #pragma unroll
-            for (int j = 0; j < NG; ++j) s += pm[j];
-            mean = s * (1.f / NG);
-            m2 = 0.f;
-  #pragma unroll
-            for (int j = 0; j < NG; ++j) {
-              const float d = pm[j] - mean;
-              m2 += pq[j] + static_cast<float>(BN) * d * d;
-            }
-          }
-          const float rstd = rsqrtf(m2 * (1.f / static_cast<float>(H)) + p.ln_eps);
-          // ---------------- pass 2: normalise from TMEM, BF16 boxes of this warp's rows out by TMA
-          // (two chunks per 64-column box; the next chunk's TMEM load overlaps this one)
-          const uint64_t nmean = f2pack(-mean, -mean), rs2 = f2pack(rstd, rstd);
-          auto pass2_chunk = [&](int c, uint32_t (&r)[32], uint32_t (&rn)[32]) {
-            const int h = c & 1;
-            uint8_t* box = sO + (q * 2 + ob) * RO_WBOX;
-            uint8_t* srow = box + lane * 128;
-            tmem_ld_wait();  // chunk c's updated row is in r
-            if (c + 1 < NCH) tmem_ld32(tb + (c + 1) * 32, rn);
-            float y[32];
-  #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const float4 g = parw[c * 8 + i], be = parb[c * 8 + i];
-              // y = ((x - mean) * rstd) * g + be, pairs of columns at once
-              const uint64_t t0 = mul2(add2(f2pack(__uint_as_float(r[4 * i + 0]), __uint_as_float(r[4 * i + 1])), nmean), rs2);
-              const uint64_t t1 = mul2(add2(f2pack(__uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3])), nmean), rs2);
-              f2unpack(fma2(t0, f2pack(g.x, g.y), f2pack(be.x, be.y)), y[4 * i + 0], y[4 * i + 1]);
-              f2unpack(fma2(t1, f2pack(g.z, g.w), f2pack(be.z, be.w)), y[4 * i + 2], y[4 * i + 3]);
-            }
-  #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              uint4 w;
-              w.x = pack_bf16x2(y[8 * i + 0], y[8 * i + 1]);
-              w.y = pack_bf16x2(y[8 * i + 2], y[8 * i + 3]);
-              w.z = pack_bf16x2(y[8 * i + 4], y[8 * i + 5]);
-              w.w = pack_bf16x2(y[8 * i + 6], y[8 * i + 7]);
-              *reinterpret_cast<uint4*>(srow + ((static_cast<uint32_t>(4 * h + i) ^ (lane & 7)) << 4)) = w;
-            }
-            if (h == 1) {
-              fence_proxy_async_smem();
-              __syncwarp();
-              if (lane == 0) {
-                if (!*abort_flag) {
-                  tma_store_2d(&tmXN, box, col0 + (c >> 1) * 64, m0 + q * 32);
-                  bulk_commit();
-                }
-                bulk_wait_read_1();  // the other box's store has read it: it can be rewritten next
-              }
-              __syncwarp();
-              ob ^= 1;
-            }
-          };
-          {
-            uint32_t ra[32], rb[32];
-            tmem_ld32(tb, ra);
-  #pragma unroll 1
-            for (int c = 0; c < NCH; c += 2) {
-              pass2_chunk(c, ra, rb);
-              pass2_chunk(c + 1, rb, ra);
-            }
-          }
-        }
-        // this warp has read its lanes of the buffer: release it to the pair's MMA
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&tempty[buf]), lead));
-      }
-      if (lane == 0) bulk_wait_all();  // every store complete: this kernel's x and xn are in memory
+      // this warp has read its lanes of the buffer: release it to the pair's MMA
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&tempty[buf]), lead));
     }
+    if (lane == 0) bulk_wait_all();  // every store complete: this kernel's x and xn are in memory
   }
 
   tc_fence_before();
