@@ -163,6 +163,29 @@ def test_gemm_resid_ln(torch_cuda, M, H, K, bias, ln_bias):
     _close_bf16(xn, ref.to(torch.bfloat16).float())
 
 
+@pytest.mark.parametrize("K,bias", [(768, False), (1152, True)])
+def test_gemm_resid_ln_epilogue_widths_same_bits(torch_cuda, K, bias):
+    """The residual kernel runs eight epilogue warps when each cluster has at most two 256-row
+    units (8,192 rows here) and four otherwise (32,768 rows): a row's updated x and its
+    normalised xn must not depend on which, so the first 8,192 rows of the large launch equal
+    the small launch to the last bit (tolerance 0)."""
+    torch = torch_cuda
+    M_small, M_big, H = 8192, 32768, 768
+    A = _rand(torch, (M_big, K), 1.0, 80, torch.bfloat16)
+    W = _rand(torch, (H, K), 0.02, 81, torch.bfloat16)
+    x0 = _rand(torch, (M_big, H), 1.0, 82, torch.float32)
+    b = _rand(torch, (H,), 0.1, 83, torch.float32) if bias else None
+    g = 1.0 + _rand(torch, (H,), 0.1, 84, torch.float32)
+    bb = _rand(torch, (H,), 0.1, 85, torch.float32)
+    xa, xb = x0.clone(), x0[:M_small].clone()
+    xna = torch.empty((M_big, H), device="cuda", dtype=torch.bfloat16)
+    xnb = torch.empty((M_small, H), device="cuda", dtype=torch.bfloat16)
+    j1.op_gemm(j1.EPI_RESID_LN, A, W, x=xa, bias=b, ln_w=g, ln_b=bb, xn=xna)
+    j1.op_gemm(j1.EPI_RESID_LN, A[:M_small].contiguous(), W, x=xb, bias=b, ln_w=g, ln_b=bb, xn=xnb)
+    assert torch.equal(xa[:M_small], xb)
+    assert torch.equal(xna[:M_small], xnb)
+
+
 @pytest.mark.parametrize("M", [32768, 131072])
 def test_c2_gemm_sweep_full_size(torch_cuda, M):
     """The GEMM-sweep configuration's large sizes (M = 32,768 and 131,072 rows, hidden 768):
