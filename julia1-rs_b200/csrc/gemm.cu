@@ -66,29 +66,31 @@ __device__ __forceinline__ float gelu_erf(float v) { return 0.5f * v * (1.f + er
 // GEGLU outputs gelu(h0) * g0 and gelu(h1) * g1, evaluated pairwise with packed FP32
 // arithmetic. erf(x) uses the rational approximation of the reference's CPU path
 // (src/cpu/fastmath.rs:27-43; the Eigen/XLA float erf): x clamped to [-4, 4],
-// erf = x p(x^2) / q(x^2) with p of degree 6 and q of degree 4 in x^2; the division is a
-// reciprocal estimate (about 1 ulp). It agrees with erff to about 1e-7, far below the
-// BF16 rounding of the output, at half the instructions.
+// erf = x p(x^2) / q(x^2) with p of degree 6 and q of degree 4 in x^2. Here x = h / sqrt(2)
+// is folded into the coefficients (the clamp becomes |h| <= 4 sqrt(2), coefficient k of p
+// and q is scaled by 2^-k, and p additionally by 1 / sqrt(2)), which saves the scaling of h;
+// the division is a reciprocal estimate (about 1 ulp). It agrees with erff to about 1.2e-7,
+// far below the BF16 rounding of the output.
 __device__ __forceinline__ void geglu2(float h0, float h1, float g0, float g1, float& o0, float& o1) {
-  const float x0 = fminf(fmaxf(h0 * 0.70710678118654752f, -4.f), 4.f);
-  const float x1 = fminf(fmaxf(h1 * 0.70710678118654752f, -4.f), 4.f);
-  const uint64_t x = f2pack(x0, x1), x2 = mul2(x, x);
+  constexpr float kClamp = 5.656854f;  // 4 sqrt(2)
+  const uint64_t hc = f2pack(fminf(fmaxf(h0, -kClamp), kClamp), fminf(fmaxf(h1, -kClamp), kClamp));
+  const uint64_t t = mul2(hc, hc);
   auto c2 = [](float c) { return f2pack(c, c); };
-  uint64_t p = c2(-2.7261423e-10f);
-  p = fma2(p, x2, c2(2.7706814e-8f));
-  p = fma2(p, x2, c2(-2.101024e-6f));
-  p = fma2(p, x2, c2(-5.6925064e-5f));
-  p = fma2(p, x2, c2(-7.3499063e-4f));
-  p = fma2(p, x2, c2(-2.9546e-3f));
-  p = fma2(p, x2, c2(-1.6096033e-2f));
-  uint64_t q = c2(-1.4566072e-5f);
-  q = fma2(q, x2, c2(-2.1337406e-4f));
-  q = fma2(q, x2, c2(-1.682827e-3f));
-  q = fma2(q, x2, c2(-7.373329e-3f));
-  q = fma2(q, x2, c2(-1.426474e-2f));
+  uint64_t p = c2(-3.01199018e-12f);
+  p = fma2(p, t, c2(6.1223987e-10f));
+  p = fma2(p, t, c2(-9.28530142e-08f));
+  p = fma2(p, t, c2(-5.03151205e-06f));
+  p = fma2(p, t, c2(-0.00012992922f));
+  p = fma2(p, t, c2(-0.00104460877f));
+  p = fma2(p, t, c2(-0.011381614f));
+  uint64_t q = c2(-9.10379526e-07f);
+  q = fma2(q, t, c2(-2.6671758e-05f));
+  q = fma2(q, t, c2(-0.000420706754f));
+  q = fma2(q, t, c2(-0.00368666439f));
+  q = fma2(q, t, c2(-0.01426474f));
   float q0, q1;
   f2unpack(q, q0, q1);
-  const uint64_t erf = mul2(mul2(x, p), f2pack(rcp_approx(q0), rcp_approx(q1)));
+  const uint64_t erf = mul2(mul2(hc, p), f2pack(rcp_approx(q0), rcp_approx(q1)));
   const uint64_t hh = mul2(f2pack(h0, h1), c2(0.5f));
   f2unpack(mul2(fma2(hh, erf, hh), f2pack(g0, g1)), o0, o1);
 }
