@@ -69,10 +69,14 @@ constexpr uint32_t RO_WBOX = 32 * 64 * 2;    // one warp's 32 x 64 BF16 xn box (
 #define J1_RLN_SMALL_UNITS 2
 #endif
 
-template <int NG, int BN, int EW>
+// DEEP: four A/W stages and three residual chunks in flight instead of three and five, for
+// long K (Wo2, K = 1,152: its main loop waits on A/W loads, while Wo's epilogue needs the
+// deeper residual prefetch).
+template <int NG, int BN, int EW, bool DEEP = false>
 struct RlnCfg {
   static constexpr int CS = 2 * NG;  // CTAs per cluster
-  static constexpr int STAGES = J1_RLN_STAGES;
+  static constexpr int STAGES = DEEP ? 4 : J1_RLN_STAGES;
+  static constexpr int NX_WANT = DEEP ? 3 : J1_RLN_NX;
   static constexpr int THREADS = 128 + EW * 32;
   static constexpr uint32_t A_BYTES = RBM * RBK * 2;
   static constexpr uint32_t W_BYTES = (BN / 2) * RBK * 2;
@@ -83,8 +87,8 @@ struct RlnCfg {
   static constexpr uint32_t CHUNK_BYTES = (BN / 32) * RBM * 8;  // [chunk][128 rows] (mean, M2) of a unit's chunks
   static constexpr uint32_t FIXED = STAGES * STAGE_BYTES + O_BYTES + PAR_BYTES + STAT_BYTES + CHUNK_BYTES +
                                     1024 /*align*/ + 256 /*barriers*/;
-  // residual chunks in flight: J1_RLN_NX, or as many as fit (four pairs per cluster, hidden 1024)
-  static constexpr int NX = FIXED + J1_RLN_NX * RX_CHUNK <= 232448 ? J1_RLN_NX
+  // residual chunks in flight: NX_WANT, or as many as fit (four pairs per cluster, hidden 1024)
+  static constexpr int NX = FIXED + NX_WANT * RX_CHUNK <= 232448 ? NX_WANT
                                                                     : static_cast<int>((232448 - FIXED) / RX_CHUNK);
   static constexpr uint32_t SMEM = FIXED + NX * RX_CHUNK;
   static constexpr uint32_t TMEM_COLS = 2 * BN;  // 256 or 512
@@ -92,7 +96,7 @@ struct RlnCfg {
   static_assert(BN == 128 || BN == 256, "columns per pair");
   static_assert(CS <= 8, "portable cluster size");
   static_assert(EW == 4 || EW == 8, "epilogue warps");
-  static_assert(NX >= 3, "residual chunks in flight");
+  static_assert(NX >= 2, "residual chunks in flight");
 };
 
 // st.async of two floats into the shared memory of a CTA of the cluster, completing 8
@@ -147,12 +151,12 @@ __device__ __forceinline__ float2 merge_chunks(const float2* sChunk, int row) {
   return s[0];
 }
 
-template <int NG, int BN, bool LN, int EW>
+template <int NG, int BN, bool LN, int EW, bool DEEP>
 __global__ void __launch_bounds__(128 + EW * 32, 1)
     resid_ln_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                     const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmXs,
                     const __grid_constant__ CUtensorMap tmXN, const EpiParams p) {
-  using C = RlnCfg<NG, BN, EW>;
+  using C = RlnCfg<NG, BN, EW, DEEP>;
   constexpr int CS = C::CS;
   constexpr int NCH = BN / 32;   // residual chunks per unit
   constexpr int H = NG * BN;
@@ -615,12 +619,12 @@ __global__ void __launch_bounds__(128 + EW * 32, 1)
 // clusters fit on the device at once (clusters of more than two CTAs cannot always use every
 // SM: a cluster lives inside one GPC), cached per device. The limit must be set first: the
 // occupancy query counts the kernel's dynamic shared memory against it.
-template <int NG, int BN, bool LN, int EW>
+template <int NG, int BN, bool LN, int EW, bool DEEP>
 int rln_max_clusters(int dev, cudaError_t* err) {
-  using C = RlnCfg<NG, BN, EW>;
+  using C = RlnCfg<NG, BN, EW, DEEP>;
   static std::atomic<unsigned long long> configured{0};
   static std::atomic<int> max_clusters[64];
-  *err = set_smem_once(resid_ln_kernel<NG, BN, LN, EW>, C::SMEM, configured);
+  *err = set_smem_once(resid_ln_kernel<NG, BN, LN, EW, DEEP>, C::SMEM, configured);
   if (*err != cudaSuccess) return 0;
   int mc = (dev >= 0 && dev < 64) ? max_clusters[dev].load() : 0;
   if (mc > 0) return mc;
@@ -635,7 +639,7 @@ int rln_max_clusters(int dev, cudaError_t* err) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cfg.gridDim = dim3(C::CS * 64);
-  if (cudaOccupancyMaxActiveClusters(&mc, resid_ln_kernel<NG, BN, LN, EW>, &cfg) != cudaSuccess || mc <= 0) {
+  if (cudaOccupancyMaxActiveClusters(&mc, resid_ln_kernel<NG, BN, LN, EW, DEEP>, &cfg) != cudaSuccess || mc <= 0) {
     (void)cudaGetLastError();
     int sms = 0;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -645,13 +649,13 @@ int rln_max_clusters(int dev, cudaError_t* err) {
   return mc;
 }
 
-template <int NG, int BN, bool LN, int EW>
+template <int NG, int BN, bool LN, int EW, bool DEEP>
 int launch_rln_ew(const CUtensorMap& tmA, const CUtensorMap& tmW, const CUtensorMap& tmX, const CUtensorMap& tmXs,
                   const CUtensorMap& tmXN, const EpiParams& p, int grid_limit, int dev, cudaStream_t stream) {
-  using C = RlnCfg<NG, BN, EW>;
-  auto kern = resid_ln_kernel<NG, BN, LN, EW>;
+  using C = RlnCfg<NG, BN, EW, DEEP>;
+  auto kern = resid_ln_kernel<NG, BN, LN, EW, DEEP>;
   cudaError_t e = cudaSuccess;
-  const int mc = rln_max_clusters<NG, BN, LN, EW>(dev, &e);
+  const int mc = rln_max_clusters<NG, BN, LN, EW, DEEP>(dev, &e);
   if (e != cudaSuccess) return static_cast<int>(e);
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[2];
@@ -683,11 +687,15 @@ int launch_rln(const CUtensorMap& tmA, const CUtensorMap& tmW, const CUtensorMap
   if (e != cudaSuccess) return static_cast<int>(e);
   const int units = (p.M + 2 * RBM - 1) / (2 * RBM);
   cudaError_t e4 = cudaSuccess;
-  const int mc = rln_max_clusters<NG, BN, LN, 4>(dev, &e4);
+  const int mc = rln_max_clusters<NG, BN, LN, 4, false>(dev, &e4);
   if (e4 != cudaSuccess) return static_cast<int>(e4);
   if (units <= J1_RLN_SMALL_UNITS * mc)
-    return launch_rln_ew<NG, BN, LN, 8>(tmA, tmW, tmX, tmXs, tmXN, p, grid_limit, dev, stream);
-  return launch_rln_ew<NG, BN, LN, 4>(tmA, tmW, tmX, tmXs, tmXN, p, grid_limit, dev, stream);
+    return launch_rln_ew<NG, BN, LN, 8, false>(tmA, tmW, tmX, tmXs, tmXN, p, grid_limit, dev, stream);
+  if constexpr (RlnCfg<NG, BN, 4, true>::NX >= 3) {  // the deep ring fits (not at hidden 1024)
+    if (p.K >= 1152)
+      return launch_rln_ew<NG, BN, LN, 4, true>(tmA, tmW, tmX, tmXs, tmXN, p, grid_limit, dev, stream);
+  }
+  return launch_rln_ew<NG, BN, LN, 4, false>(tmA, tmW, tmX, tmXs, tmXN, p, grid_limit, dev, stream);
 }
 
 template <bool LN>
