@@ -14,6 +14,7 @@
 // twice in TMEM: the main loop of the next unit runs while the epilogue of this one drains.
 // Per CTA:
 //   warp 0      TMA producer: A (128 x 64) and W (BN/2 x 64) boxes into a 3-stage ring
+//               (4 stages for K >= 1152, with 3 residual chunks in flight instead of 5)
 //   warp 1      TMEM allocator; in the even CTA the single-thread tcgen05.mma issuer
 //   warp 2      x producer: TMA loads of 128 x 32 FP32 residual chunks into a ring
 //   warps 4..    epilogue, one thread per row (TMEM lane = row): four warps, one per TMEM
